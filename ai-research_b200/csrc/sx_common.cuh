@@ -1,0 +1,206 @@
+// sx_common.cuh -- shared device helpers for the sm_100a decode kernels.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#define SX_DEV __device__ __forceinline__
+#define SX_HD __host__ __device__ __forceinline__
+
+namespace sx {
+
+constexpr int kWarp = 32;
+
+// ---------------------------------------------------------------------------
+// Device error word.  Every bounded wait in a kernel writes a nonzero code here
+// instead of hanging; the host reads it back after a submit.
+enum DeviceError : uint32_t {
+  kDevOk = 0,
+  kDevWaitTimeout = 1,
+  kDevBadParams = 2,
+  kDevBadSlot = 3,
+};
+
+SX_DEV void raise_error(uint32_t *err, uint32_t code) {
+  if (err) atomicCAS(err, 0u, code);
+}
+
+// ---------------------------------------------------------------------------
+// bit casts
+SX_HD float u2f(uint32_t u) {
+#ifdef __CUDA_ARCH__
+  return __uint_as_float(u);
+#else
+  float f;
+  __builtin_memcpy(&f, &u, 4);
+  return f;
+#endif
+}
+SX_HD uint32_t f2u(float f) {
+#ifdef __CUDA_ARCH__
+  return __float_as_uint(f);
+#else
+  uint32_t u;
+  __builtin_memcpy(&u, &f, 4);
+  return u;
+#endif
+}
+
+// bf16 round-to-nearest-even exactly as tensor.zig:7-13 (integer formulation).
+SX_HD uint16_t bf16_bits_rne(float v) {
+  uint32_t u = f2u(v);
+  return (uint16_t)((u + 0x7FFFu + ((u >> 16) & 1u)) >> 16);
+}
+SX_HD float bf16_bits_to_f32(uint16_t b) { return u2f((uint32_t)b << 16); }
+
+// ---------------------------------------------------------------------------
+// Synthetic-input generator.  Integer-only mixing so that host, device and the CPU
+// checker produce identical bits (splitmix64 finaliser; Irwin-Hall(4) normal).
+SX_HD uint64_t mix64(uint64_t z) {
+  z += 0x9E3779B97F4A7C15ull;
+  z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+  z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+  return z ^ (z >> 31);
+}
+SX_HD uint64_t hash3(uint64_t seed, uint64_t stream, uint64_t idx) {
+  return mix64(mix64(seed ^ (stream * 0xD1B54A32D192ED03ull)) + idx);
+}
+SX_HD float synth_normal(uint64_t seed, uint64_t stream, uint64_t idx) {
+  uint64_t h = hash3(seed, stream, idx);
+  int32_t s = (int32_t)((h & 0xFFFFu) + ((h >> 16) & 0xFFFFu) + ((h >> 32) & 0xFFFFu) +
+                        ((h >> 48) & 0xFFFFu)) -
+              131070;
+#ifdef __CUDA_ARCH__
+  return __fdiv_rn((float)s, 37837.23f);
+#else
+  return (float)s / 37837.23f;
+#endif
+}
+// f32 -> f16 -> f32 round trip, round to nearest even, subnormals kept.
+SX_HD float f16_round(float v) {
+  uint32_t x = f2u(v);
+  uint32_t sign = x & 0x80000000u;
+  uint32_t ax = x & 0x7FFFFFFFu;
+  if (ax >= 0x7F800000u) return v;
+  if (ax >= 0x477FF000u) return u2f(sign | 0x7F800000u);
+  if (ax < 0x38800000u) {
+#ifdef __CUDA_ARCH__
+    float a = __fmul_rn(u2f(ax), 16777216.0f);
+    float r = __fmul_rn(rintf(a), 1.0f / 16777216.0f);
+#else
+    float a = u2f(ax) * 16777216.0f;
+    float r = __builtin_rintf(a) * (1.0f / 16777216.0f);
+#endif
+    return u2f(sign | f2u(r));
+  }
+  uint32_t lsb = (ax >> 13) & 1u;
+  ax = (ax + 0xFFFu + lsb) & ~0x1FFFu;
+  return u2f(sign | ax);
+}
+SX_HD float synth_scale(uint64_t seed, uint64_t stream, uint64_t idx) {
+  float z = synth_normal(seed, stream, idx);
+#ifdef __CUDA_ARCH__
+  return f16_round(__fmul_rn(fabsf(z), 0.02f));
+#else
+  return f16_round((z < 0 ? -z : z) * 0.02f);
+#endif
+}
+
+// ---------------------------------------------------------------------------
+// Packed weight formats (device layout produced by the repack kernels).
+//
+// A matrix of M rows x K columns is cut into row tiles of 16 and K block pairs of 64
+// (two 32-element quant blocks).  Chunk (tile t, pair p) is one contiguous record:
+//   Q4: 512 B nibbles + 128 B scales = 640 B   (= 2 blocks x 16 rows x 20 B)
+//   Q8: 2 x 512 B int8 + 128 B scales = 1152 B (= 2 blocks x 16 rows x 36 B)
+// Lane l = 4g + c of a warp owns the 16-byte piece l of each 512-byte sub-record; it
+// holds exactly the mma.m16n8k16 A-fragment bytes of rows g and g+8 for k-slots
+// {2c, 2c+1, 2c+8, 2c+9} of both 16-wide halves of a block.  Scales: g-th 16 B =
+// {s(g, 2p), s(g+8, 2p), s(g, 2p+1), s(g+8, 2p+1)}.  The repack is a permutation of the
+// reference's nibbles/bytes and f32 scales: dequantised values are bit-identical.
+constexpr int kTileRows = 16;
+constexpr int kQ4ChunkBytes = 640;
+constexpr int kQ8ChunkBytes = 1152;
+
+SX_HD uint32_t tiles_of(uint32_t m) { return (m + kTileRows - 1) / kTileRows; }
+SX_HD uint32_t pairs_of(uint32_t k) { return (k / 32 + 1) / 2; }
+
+// ---------------------------------------------------------------------------
+// mma.sync m16n8k16 (f32 accumulate).  Used as a 16-row dot-product engine for the
+// batch-1..8 GEMV: the weights dequantise straight into A fragments.
+SX_DEV void mma_bf16_16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 "
+      "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};\n"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+SX_DEV void mma_f16_16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 "
+      "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};\n"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+SX_DEV uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
+  uint32_t r;
+  asm("prmt.b32 %0, %1, %2, %3;\n" : "=r"(r) : "r"(a), "r"(b), "r"(sel));
+  return r;
+}
+
+// Q4: eight nibbles of one packed word -> four bf16x2 holding 8 + q/2 (exact).
+// Register j holds nibble j (low half) and nibble j+4 (high half).
+SX_DEV void dq4_word(uint32_t u, uint32_t (&r)[4]) {
+  r[0] = ((u << 3) & 0x00780078u) | 0x41004100u;
+  r[1] = ((u >> 1) & 0x00780078u) | 0x41004100u;
+  r[2] = ((u >> 5) & 0x00780078u) | 0x41004100u;
+  r[3] = ((u >> 9) & 0x00780078u) | 0x41004100u;
+}
+// Q8: four int8 of one packed word -> two f16x2 holding 1024 + (q + 128) (exact).
+SX_DEV void dq8_word(uint32_t u, uint32_t &lo, uint32_t &hi) {
+  uint32_t v = u ^ 0x80808080u;
+  lo = prmt(v, 0x64646464u, 0x4140u);  // bytes 0,1 -> (1024+b0, 1024+b1)
+  hi = prmt(v, 0x64646464u, 0x4342u);  // bytes 2,3
+}
+
+// ---------------------------------------------------------------------------
+// loads
+SX_DEV uint4 ldg_stream(const void *p) {
+  uint4 v;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];\n"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p));
+  return v;
+}
+
+SX_DEV float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+SX_DEV float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+// Block-wide sum; `red` must hold >= 32 floats.  All threads get the result.
+SX_DEV float block_sum(float v, float *red) {
+  int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = (blockDim.x + 31) >> 5;
+  v = warp_sum(v);
+  __syncthreads();
+  if (lane == 0) red[wid] = v;
+  __syncthreads();
+  float t = lane < nw ? red[lane] : 0.0f;
+  t = warp_sum(t);
+  return t;
+}
+
+// Programmatic dependent launch: wait for the producer grid's memory before reading it.
+SX_DEV void pdl_wait() { asm volatile("griddepcontrol.wait;\n" ::: "memory"); }
+SX_DEV void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;\n" ::); }
+
+}  // namespace sx

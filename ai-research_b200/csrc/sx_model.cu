@@ -1,0 +1,463 @@
+// sx_model.cu -- GpuModelContext (src/gpu/model_gpu.zig:35-197) and the per-token dispatch
+// (src/gpu/model_dispatch.zig:103-147) on top of the public record API of include/sx.h.
+//
+// The decode graph is recorded exactly like recordForwardGraph/recordLayerDirect: the same
+// descriptor-set bindings (model_gpu.zig:140-168) and the same op order, then captured into
+// a CUDA graph that is replayed per token.  Quiescence gating (recordLayerIndirect) runs
+// every layer at the reference's default threshold 0.0, so all layers are recorded direct.
+#include <cmath>
+#include <cstring>
+#include <vector>
+
+#include "sx_common.cuh"
+#include "sx_host.h"
+#include "sx_internal.h"
+
+namespace {
+
+struct LayerBufs {
+  uint32_t head_dim = 0, rot = 0, num_kv = 0, q_dim = 0, kv_dim = 0, k_eq_v = 0;
+  float theta = 0.0f, layer_scalar = 1.0f;
+  sx_buffer *in_norm = nullptr, *q_norm = nullptr, *k_norm = nullptr;
+  sx_buffer *wq = nullptr, *wk = nullptr, *wv = nullptr, *wo = nullptr;
+  sx_buffer *wg = nullptr, *wu = nullptr, *wd = nullptr;
+  sx_buffer *pre_ffn = nullptr, *post_attn = nullptr, *post_ffn = nullptr;
+  sx_buffer *kc = nullptr, *vc = nullptr;
+  sx_set *s_input_norm = nullptr, *s_q = nullptr, *s_k = nullptr, *s_v = nullptr;
+  sx_set *s_qkv_rope = nullptr, *s_attn = nullptr, *s_o = nullptr, *s_gate_up = nullptr;
+  sx_set *s_down = nullptr, *s_pre_ffn = nullptr, *s_post_attn = nullptr, *s_post_ffn = nullptr;
+  sx_set *s_post_ffn_add = nullptr;
+};
+
+enum Tensor : uint32_t {
+  T_INPUT_NORM = 0, T_Q = 1, T_K = 2, T_V = 3, T_O = 4, T_QNORM = 5, T_KNORM = 6,
+  T_POST_ATTN = 7, T_PRE_FFN = 8, T_GATE = 9, T_UP = 10, T_DOWN = 11, T_POST_FFN = 12,
+  T_SCALAR = 13,
+};
+uint64_t stream_of(uint32_t layer, uint32_t kind) { return (uint64_t)(layer + 1) * 64 + kind; }
+
+}  // namespace
+
+struct sx_model {
+  sx_engine *e = nullptr;
+  sx_model_config c{};
+  uint32_t total_slots = 0, max_q = 0, max_kv = 0;
+  std::vector<LayerBufs> L;
+  sx_buffer *x = nullptr, *normed = nullptr, *q = nullptr, *k = nullptr, *v = nullptr;
+  sx_buffer *attn_out = nullptr, *slots = nullptr, *act = nullptr, *mlp_out = nullptr;
+  sx_buffer *logits = nullptr, *token = nullptr, *step = nullptr;
+  sx_buffer *lm_head = nullptr, *final_norm = nullptr;
+  sx_set *s_final_norm = nullptr, *s_logits = nullptr, *s_argmax = nullptr;
+  sx_cmd *cmd[2][2] = {{nullptr, nullptr}, {nullptr, nullptr}};  // [want_logits][io]
+  float *h_x = nullptr;
+  uint32_t *h_slots = nullptr, *h_step = nullptr, *h_token = nullptr;
+  std::vector<sx_buffer *> buffers;
+  std::vector<sx_set *> sets;
+  uint64_t weight_bytes = 0;
+};
+
+namespace {
+
+sx_status mk_buf(sx_model *m, uint64_t bytes, sx_buffer **out) {
+  sx_status st = sx_buffer_create(m->e, bytes ? bytes : 4, out);
+  if (st == SX_OK) m->buffers.push_back(*out);
+  return st;
+}
+
+sx_status mk_set(sx_model *m, std::vector<sx_buffer *> bufs, sx_set **out) {
+  sx_status st = sx_set_create(m->e, bufs.data(), (uint32_t)bufs.size(), out);
+  if (st == SX_OK) m->sets.push_back(*out);
+  return st;
+}
+
+#define M_TRY(expr)               \
+  do {                            \
+    sx_status _s = (expr);        \
+    if (_s != SX_OK) return _s;   \
+  } while (0)
+
+sx_status alloc_model(sx_model *m) {
+  const sx_model_config &c = m->c;
+  const uint32_t H = c.hidden_size, I = c.intermediate_size, V = c.vocab_size;
+  m->total_slots = c.num_anchors + c.window_size + c.num_recall;
+  m->L.resize(c.num_layers);
+  for (uint32_t l = 0; l < c.num_layers; ++l) {
+    LayerBufs &B = m->L[l];
+    // loader.zig:36-42 per-layer shapes
+    bool full = c.full_every && ((l + 1) % c.full_every == 0);
+    B.head_dim = full ? c.global_head_dim : c.head_dim;
+    B.rot = full ? B.head_dim / 4 : B.head_dim;
+    B.num_kv = full ? c.num_global_kv_heads : c.num_kv_heads;
+    B.q_dim = c.num_q_heads * B.head_dim;
+    B.kv_dim = B.num_kv * B.head_dim;
+    B.k_eq_v = (full && c.attention_k_eq_v) ? 1u : 0u;
+    B.theta = full ? c.rope_theta_full : c.rope_theta;
+    if (B.q_dim > m->max_q) m->max_q = B.q_dim;
+    if (B.kv_dim > m->max_kv) m->max_kv = B.kv_dim;
+  }
+  M_TRY(mk_buf(m, 4ull * H, &m->x));
+  M_TRY(mk_buf(m, 4ull * H, &m->normed));
+  M_TRY(mk_buf(m, 4ull * m->max_q, &m->q));
+  M_TRY(mk_buf(m, 4ull * m->max_kv, &m->k));
+  M_TRY(mk_buf(m, 4ull * m->max_kv, &m->v));
+  M_TRY(mk_buf(m, 4ull * m->max_q, &m->attn_out));
+  M_TRY(mk_buf(m, 4ull * m->total_slots, &m->slots));
+  M_TRY(mk_buf(m, 4ull * I, &m->act));
+  M_TRY(mk_buf(m, 4ull * H, &m->mlp_out));
+  M_TRY(mk_buf(m, 4ull * V, &m->logits));
+  M_TRY(mk_buf(m, 4, &m->token));
+  M_TRY(mk_buf(m, 64, &m->step));
+  const size_t kvb = c.kv_bf16 ? 2 : 4;
+  for (uint32_t l = 0; l < c.num_layers; ++l) {
+    LayerBufs &B = m->L[l];
+    M_TRY(mk_buf(m, 4ull * H, &B.in_norm));
+    M_TRY(mk_buf(m, 4ull * B.head_dim, &B.q_norm));
+    M_TRY(mk_buf(m, 4ull * B.head_dim, &B.k_norm));
+    M_TRY(mk_buf(m, 4ull * H, &B.pre_ffn));
+    M_TRY(mk_buf(m, 4ull * H, &B.post_attn));
+    M_TRY(mk_buf(m, 4ull * H, &B.post_ffn));
+    M_TRY(mk_buf(m, sx_packed_bytes(B.q_dim, H, SX_QUANT_Q4), &B.wq));
+    M_TRY(mk_buf(m, sx_packed_bytes(B.kv_dim, H, SX_QUANT_Q4), &B.wk));
+    M_TRY(mk_buf(m, sx_packed_bytes(B.kv_dim, H, SX_QUANT_Q4), &B.wv));
+    M_TRY(mk_buf(m, sx_packed_bytes(H, B.q_dim, SX_QUANT_Q4), &B.wo));
+    M_TRY(mk_buf(m, sx_packed_bytes(I, H, SX_QUANT_Q4), &B.wg));
+    M_TRY(mk_buf(m, sx_packed_bytes(I, H, SX_QUANT_Q4), &B.wu));
+    M_TRY(mk_buf(m, sx_packed_bytes(H, I, SX_QUANT_Q4), &B.wd));
+    M_TRY(mk_buf(m, (uint64_t)m->total_slots * B.kv_dim * kvb, &B.kc));
+    M_TRY(mk_buf(m, (uint64_t)m->total_slots * B.kv_dim * kvb, &B.vc));
+    m->weight_bytes += B.wq->bytes + B.wk->bytes + B.wv->bytes + B.wo->bytes + B.wg->bytes +
+                       B.wu->bytes + B.wd->bytes;
+  }
+  M_TRY(mk_buf(m, sx_packed_bytes(V, H, SX_QUANT_Q8), &m->lm_head));
+  M_TRY(mk_buf(m, 4ull * H, &m->final_norm));
+  m->weight_bytes += m->lm_head->bytes;
+
+  // descriptor sets, model_gpu.zig:140-168
+  for (uint32_t l = 0; l < c.num_layers; ++l) {
+    LayerBufs &B = m->L[l];
+    M_TRY(mk_set(m, {m->x, B.in_norm, m->normed}, &B.s_input_norm));
+    M_TRY(mk_set(m, {B.wq, m->normed, m->q}, &B.s_q));
+    M_TRY(mk_set(m, {B.wk, m->normed, m->k}, &B.s_k));
+    M_TRY(mk_set(m, {B.wv, m->normed, m->v}, &B.s_v));
+    M_TRY(mk_set(m, {m->q, m->k, m->v, B.q_norm, B.k_norm, m->q, B.kc, B.vc, m->step},
+                 &B.s_qkv_rope));
+    M_TRY(mk_set(m, {m->q, B.kc, B.vc, m->slots, m->attn_out, m->step}, &B.s_attn));
+    M_TRY(mk_set(m, {B.wo, m->attn_out, m->mlp_out}, &B.s_o));
+    M_TRY(mk_set(m, {B.wg, B.wu, m->normed, m->act}, &B.s_gate_up));
+    M_TRY(mk_set(m, {B.wd, m->act, m->mlp_out}, &B.s_down));
+    M_TRY(mk_set(m, {m->x, m->mlp_out, B.pre_ffn, m->normed}, &B.s_pre_ffn));
+    M_TRY(mk_set(m, {m->mlp_out, B.post_attn, m->mlp_out}, &B.s_post_attn));
+    M_TRY(mk_set(m, {m->mlp_out, B.post_ffn, m->mlp_out}, &B.s_post_ffn));
+    M_TRY(mk_set(m, {m->x, m->mlp_out, B.in_norm, m->normed}, &B.s_post_ffn_add));
+  }
+  M_TRY(mk_set(m, {m->x, m->final_norm, m->normed}, &m->s_final_norm));
+  M_TRY(mk_set(m, {m->lm_head, m->normed, m->logits}, &m->s_logits));
+  M_TRY(mk_set(m, {m->logits, m->token}, &m->s_argmax));
+
+  M_TRY(sx_host_cuda_status(cudaHostAlloc((void **)&m->h_x, 4ull * H, cudaHostAllocDefault),
+                            "pinned x"));
+  M_TRY(sx_host_cuda_status(
+      cudaHostAlloc((void **)&m->h_slots, 4ull * m->total_slots, cudaHostAllocDefault),
+      "pinned slots"));
+  M_TRY(sx_host_cuda_status(cudaHostAlloc((void **)&m->h_step, 64, cudaHostAllocDefault),
+                            "pinned step"));
+  M_TRY(sx_host_cuda_status(cudaHostAlloc((void **)&m->h_token, 64, cudaHostAllocDefault),
+                            "pinned token"));
+  memset(m->h_x, 0, 4ull * H);
+  memset(m->h_slots, 0, 4ull * m->total_slots);
+  memset(m->h_step, 0, 64);
+  memset(m->h_token, 0, 64);
+  return SX_OK;
+}
+
+// recordLayerDirect (model_dispatch.zig:10-43)
+void record_layer(sx_model *m, sx_cmd *cmd, uint32_t l) {
+  sx_engine *e = m->e;
+  const sx_model_config &c = m->c;
+  LayerBufs &B = m->L[l];
+  const uint32_t H = c.hidden_size, I = c.intermediate_size;
+  const float eps = c.rms_norm_eps;
+  const uint32_t gqa = c.num_q_heads / B.num_kv;
+  sx_record_rmsnorm(e, cmd, B.s_input_norm, H, eps);
+  sx_record_barrier(e, cmd);
+  sx_record_gemv(e, cmd, B.s_q, B.q_dim, H);
+  sx_record_gemv(e, cmd, B.s_k, B.kv_dim, H);
+  sx_record_gemv(e, cmd, B.s_v, B.kv_dim, H);
+  sx_record_barrier(e, cmd);
+  sx_record_qkv_rope(e, cmd, B.s_qkv_rope, c.num_q_heads, B.num_kv, B.head_dim, B.rot, B.k_eq_v,
+                     B.theta, eps, m->total_slots);
+  sx_record_barrier(e, cmd);
+  sx_record_decode_attn(e, cmd, B.s_attn, B.head_dim, B.kv_dim, gqa, c.attn_scale, c.num_q_heads,
+                        m->total_slots);
+  sx_record_barrier(e, cmd);
+  sx_record_gemv(e, cmd, B.s_o, H, B.q_dim);
+  if (c.has_post_norms) {
+    sx_record_barrier(e, cmd);
+    sx_record_rmsnorm(e, cmd, B.s_post_attn, H, eps);
+  }
+  sx_record_barrier(e, cmd);
+  sx_record_add_rmsnorm(e, cmd, B.s_pre_ffn, H, eps, 1.0f);
+  sx_record_barrier(e, cmd);
+  sx_record_gate_up(e, cmd, B.s_gate_up, I, H);
+  sx_record_barrier(e, cmd);
+  sx_record_gemv(e, cmd, B.s_down, H, I);
+  if (c.has_post_norms) {
+    sx_record_barrier(e, cmd);
+    sx_record_rmsnorm(e, cmd, B.s_post_ffn, H, eps);
+  }
+  sx_record_barrier(e, cmd);
+  sx_record_add_rmsnorm(e, cmd, B.s_post_ffn_add, H, eps, B.layer_scalar);
+  sx_record_barrier(e, cmd);
+}
+
+// recordForwardGraph (model_dispatch.zig:103-129), optionally wrapped in the per-token
+// host<->device copies of gpuDispatchForwardToken (model_dispatch.zig:136-146).
+sx_status record_forward(sx_model *m, sx_cmd *cmd, bool logits, bool io) {
+  sx_engine *e = m->e;
+  const sx_model_config &c = m->c;
+  M_TRY(sx_cmd_begin(cmd));
+  if (io) {
+    Op a{OP_H2D};
+    a.host = m->h_x; a.dev = m->x->d; a.bytes = 4ull * c.hidden_size;
+    sx_host_push_op(cmd, a);
+    Op b{OP_H2D};
+    b.host = m->h_slots; b.dev = m->slots->d; b.bytes = 4ull * m->total_slots;
+    sx_host_push_op(cmd, b);
+    Op s{OP_H2D};
+    s.host = m->h_step; s.dev = m->step->d; s.bytes = 16;
+    sx_host_push_op(cmd, s);
+  }
+  sx_record_barrier(e, cmd);
+  for (uint32_t l = 0; l < c.num_layers; ++l) record_layer(m, cmd, l);
+  if (logits) {
+    sx_record_rmsnorm(e, cmd, m->s_final_norm, c.hidden_size, c.rms_norm_eps);
+    sx_record_barrier(e, cmd);
+    sx_record_gemv_logits(e, cmd, m->s_logits, c.vocab_size, c.hidden_size);
+    sx_record_barrier(e, cmd);
+    sx_record_argmax(e, cmd, m->s_argmax, c.vocab_size);
+    if (io) {
+      Op t{OP_D2H};
+      t.host = m->h_token; t.dev = m->token->d; t.bytes = 4;
+      sx_host_push_op(cmd, t);
+    }
+  }
+  return sx_cmd_end(cmd);
+}
+
+sx_status synth_matrix(sx_model *m, sx_buffer *dst, uint32_t rows, uint32_t cols,
+                       sx_quant_mode mode, uint64_t seed, uint64_t stream, void *tmp,
+                       uint64_t tmp_bytes) {
+  const uint64_t row_bytes = sx_quantized_row_words(cols, mode) * 4;
+  uint64_t chunk = tmp_bytes / row_bytes;
+  chunk = (chunk / 16) * 16;
+  if (chunk < 16) {
+    sx_host_set_error("synth: staging buffer too small");
+    return SX_ERR_INVALID;
+  }
+  const int qt = mode == SX_QUANT_Q4 ? 4 : 8;
+  const uint64_t chunk_bytes = qt == 4 ? sx::kQ4ChunkBytes : sx::kQ8ChunkBytes;
+  for (uint64_t r0 = 0; r0 < rows; r0 += chunk) {
+    uint32_t n = (uint32_t)((rows - r0) < chunk ? (rows - r0) : chunk);
+    M_TRY(sx_host_cuda_status(sx::launch_synth_ref(qt, (uint32_t *)tmp, (uint32_t)r0, n, cols,
+                                                   seed, stream, m->e->stream),
+                              "synth launch"));
+    uint8_t *out = (uint8_t *)dst->d + (r0 / 16) * sx::pairs_of(cols) * chunk_bytes;
+    M_TRY(sx_host_cuda_status(
+        sx::launch_repack(qt, (const uint32_t *)tmp, out, n, cols, m->e->stream), "repack"));
+  }
+  return SX_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+SX_API sx_status sx_model_create(sx_engine *e, const sx_model_config *cfg, sx_model **out) {
+  if (!e || !cfg || !out) {
+    sx_host_set_error("model_create: null argument");
+    return SX_ERR_INVALID;
+  }
+  const sx_model_config &c = *cfg;
+  bool ok = c.vocab_size > 0 && c.hidden_size % 32 == 0 && c.intermediate_size % 32 == 0 &&
+            c.num_layers > 0 && c.num_q_heads > 0 && c.num_kv_heads > 0 &&
+            c.num_q_heads % c.num_kv_heads == 0 && c.window_size > 0 && c.head_dim > 0 &&
+            (c.num_q_heads * c.head_dim) % 32 == 0;
+  if (c.full_every)
+    ok = ok && c.num_global_kv_heads > 0 && c.num_q_heads % c.num_global_kv_heads == 0 &&
+         c.global_head_dim > 0;
+  if (!ok) {
+    sx_host_set_error("model_create: inconsistent config");
+    return SX_ERR_INVALID;
+  }
+  if ((c.kv_bf16 != 0) != e->kv_bf16) {
+    sx_host_set_error("model_create: config.kv_bf16 must match the engine's KV precision flag");
+    return SX_ERR_INVALID;
+  }
+  if (e->mode != SX_QUANT_Q4) {
+    sx_host_set_error("model_create: the model path is the Q4_0 engine mode");
+    return SX_ERR_UNSUPPORTED;
+  }
+  cudaSetDevice(e->device);
+  sx_model *m = new sx_model();
+  m->e = e;
+  m->c = c;
+  sx_status st = alloc_model(m);
+  for (int lg = 0; lg < 2 && st == SX_OK; ++lg)
+    for (int io = 0; io < 2 && st == SX_OK; ++io) {
+      st = sx_cmd_create(e, &m->cmd[lg][io]);
+      if (st == SX_OK) st = record_forward(m, m->cmd[lg][io], lg != 0, io != 0);
+    }
+  if (st != SX_OK) {
+    std::string msg = sx_last_error();
+    sx_model_destroy(m);
+    sx_host_set_error(msg.c_str());
+    return st;
+  }
+  *out = m;
+  return SX_OK;
+}
+
+SX_API void sx_model_destroy(sx_model *m) {
+  if (!m) return;
+  cudaSetDevice(m->e->device);
+  cudaStreamSynchronize(m->e->stream);
+  for (auto &row : m->cmd)
+    for (sx_cmd *c : row) sx_cmd_destroy(c);
+  for (sx_set *s : m->sets) sx_set_destroy(s);
+  for (sx_buffer *b : m->buffers) sx_buffer_destroy(b);
+  if (m->h_x) cudaFreeHost(m->h_x);
+  if (m->h_slots) cudaFreeHost(m->h_slots);
+  if (m->h_step) cudaFreeHost(m->h_step);
+  if (m->h_token) cudaFreeHost(m->h_token);
+  delete m;
+}
+
+SX_API sx_status sx_model_synth_weights(sx_model *m, uint64_t seed) {
+  if (!m) {
+    sx_host_set_error("model: null");
+    return SX_ERR_INVALID;
+  }
+  sx_engine *e = m->e;
+  const sx_model_config &c = m->c;
+  const uint32_t H = c.hidden_size, I = c.intermediate_size;
+  cudaSetDevice(e->device);
+  const uint64_t tmp_bytes = 64ull << 20;
+  void *tmp = nullptr;
+  M_TRY(sx_host_cuda_status(cudaMalloc(&tmp, tmp_bytes), "synth staging"));
+  sx_status st = SX_OK;
+  for (uint32_t l = 0; l < c.num_layers && st == SX_OK; ++l) {
+    LayerBufs &B = m->L[l];
+    auto gain = [&](sx_buffer *b, uint32_t n, uint32_t kind) {
+      return sx_host_cuda_status(sx::launch_synth_gain((float *)b->d, n, seed, stream_of(l, kind),
+                                                       e->stream),
+                                 "synth gain");
+    };
+    if (st == SX_OK) st = gain(B.in_norm, H, T_INPUT_NORM);
+    if (st == SX_OK) st = gain(B.post_attn, H, T_POST_ATTN);
+    if (st == SX_OK) st = gain(B.pre_ffn, H, T_PRE_FFN);
+    if (st == SX_OK) st = gain(B.post_ffn, H, T_POST_FFN);
+    if (st == SX_OK) st = gain(B.q_norm, B.head_dim, T_QNORM);
+    if (st == SX_OK) st = gain(B.k_norm, B.head_dim, T_KNORM);
+    auto mat = [&](sx_buffer *b, uint32_t rows, uint32_t cols, uint32_t kind) {
+      return synth_matrix(m, b, rows, cols, SX_QUANT_Q4, seed, stream_of(l, kind), tmp, tmp_bytes);
+    };
+    if (st == SX_OK) st = mat(B.wq, B.q_dim, H, T_Q);
+    if (st == SX_OK) st = mat(B.wk, B.kv_dim, H, T_K);
+    if (st == SX_OK) st = mat(B.wv, B.kv_dim, H, B.k_eq_v ? T_K : T_V);
+    if (st == SX_OK) st = mat(B.wo, H, B.q_dim, T_O);
+    if (st == SX_OK) st = mat(B.wg, I, H, T_GATE);
+    if (st == SX_OK) st = mat(B.wu, I, H, T_UP);
+    if (st == SX_OK) st = mat(B.wd, H, I, T_DOWN);
+    float z = sx::synth_normal(seed, stream_of(l, T_SCALAR), 0);
+    B.layer_scalar = sx::bf16_bits_to_f32(sx::bf16_bits_rne(fmaf(0.05f, z, 1.0f)));
+  }
+  if (st == SX_OK)
+    st = synth_matrix(m, m->lm_head, c.vocab_size, H, SX_QUANT_Q8, seed, 2, tmp, tmp_bytes);
+  if (st == SX_OK)
+    st = sx_host_cuda_status(
+        sx::launch_synth_gain((float *)m->final_norm->d, H, seed, 3, e->stream), "synth gain");
+  if (st == SX_OK) st = sx_host_cuda_status(cudaStreamSynchronize(e->stream), "synth sync");
+  cudaFree(tmp);
+  if (st != SX_OK) return st;
+  // layer scalars are recorded into the graphs: re-record them
+  for (int lg = 0; lg < 2 && st == SX_OK; ++lg)
+    for (int io = 0; io < 2 && st == SX_OK; ++io)
+      st = record_forward(m, m->cmd[lg][io], lg != 0, io != 0);
+  return st;
+}
+
+SX_API sx_status sx_model_fill_kv(sx_model *m, uint64_t seed) {
+  if (!m) {
+    sx_host_set_error("model: null");
+    return SX_ERR_INVALID;
+  }
+  cudaSetDevice(m->e->device);
+  for (uint32_t l = 0; l < m->c.num_layers; ++l) {
+    LayerBufs &B = m->L[l];
+    M_TRY(sx_host_cuda_status(
+        sx::launch_fill_kv(B.kc->d, B.vc->d, m->c.kv_bf16 ? 1 : 0, m->total_slots * B.num_kv,
+                           B.head_dim, m->c.rms_norm_eps, seed, l, m->e->stream),
+        "fill kv"));
+  }
+  return sx_host_cuda_status(cudaStreamSynchronize(m->e->stream), "fill kv sync");
+}
+
+SX_API sx_status sx_forward_token(sx_model *m, const float *x, uint32_t clock, uint32_t slot,
+                                  const uint32_t *active_slots, uint32_t n_active,
+                                  int want_logits, uint32_t *token_out, float *logits_out) {
+  if (!m || !x || (n_active && !active_slots)) {
+    sx_host_set_error("forward_token: null argument");
+    return SX_ERR_INVALID;
+  }
+  if (n_active > m->total_slots || slot >= m->total_slots) {
+    sx_host_set_error("forward_token: slot list larger than the ring or slot out of range");
+    return SX_ERR_INVALID;
+  }
+  memcpy(m->h_x, x, 4ull * m->c.hidden_size);
+  if (n_active) memcpy(m->h_slots, active_slots, 4ull * n_active);
+  m->h_step[0] = clock;
+  m->h_step[1] = slot;
+  m->h_step[2] = n_active;
+  m->h_step[3] = 0;
+  sx_status st = sx_submit(m->e, m->cmd[want_logits ? 1 : 0][1], 0);
+  if (token_out) *token_out = (st == SX_OK && want_logits) ? m->h_token[0] : 0u;
+  if (st == SX_OK && want_logits && logits_out)
+    st = sx_buffer_read(m->logits, 0, logits_out, 4ull * m->c.vocab_size);
+  return st;
+}
+
+SX_API sx_status sx_model_launch(sx_model *m, int want_logits) {
+  if (!m) {
+    sx_host_set_error("model: null");
+    return SX_ERR_INVALID;
+  }
+  sx_cmd *c = m->cmd[want_logits ? 1 : 0][0];
+  return sx_host_cuda_status(cudaGraphLaunch(c->exec, m->e->stream), "graph launch");
+}
+
+SX_API sx_status sx_model_get_io(sx_model *m, sx_model_io *io) {
+  if (!m || !io) {
+    sx_host_set_error("model: null");
+    return SX_ERR_INVALID;
+  }
+  io->x = (float *)m->x->d;
+  io->slots = (uint32_t *)m->slots->d;
+  io->step = (uint32_t *)m->step->d;
+  io->token = (uint32_t *)m->token->d;
+  io->logits = (float *)m->logits->d;
+  io->normed = (float *)m->normed->d;
+  return SX_OK;
+}
+
+SX_API void *sx_model_kcache(sx_model *m, uint32_t layer) {
+  return (m && layer < m->L.size()) ? m->L[layer].kc->d : nullptr;
+}
+SX_API void *sx_model_vcache(sx_model *m, uint32_t layer) {
+  return (m && layer < m->L.size()) ? m->L[layer].vc->d : nullptr;
+}
+SX_API uint64_t sx_model_weight_bytes(sx_model *m) { return m ? m->weight_bytes : 0; }
+SX_API uint32_t sx_model_kernels_per_token(sx_model *m, int want_logits) {
+  return m ? m->cmd[want_logits ? 1 : 0][0]->kernels : 0;
+}
+
+}  // extern "C"

@@ -1,0 +1,576 @@
+"""Python host binding of libsx (include/sx.h), the B200 decode hot path.
+
+This is a thin ctypes layer over the C ABI; the names follow the reference's Zig GPU
+dispatch API (src/gpu/kernels.zig ``GpuEngine.record*`` / ``submitPreRecorded``,
+src/gpu/model_gpu.zig ``GpuModelContext``, src/ring_buffer.zig ``DynamicRingBuffer``) so
+that tests read like the reference's own.  Every call goes to the CUDA library; there is
+no CPU fallback: importing this module without a built libsx.so raises.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+from pathlib import Path
+
+import numpy as np
+
+_PKG = Path(__file__).resolve().parent
+LIB_PATH = _PKG / "libsx.so"
+
+SX_OK = 0
+SX_ERR_INVALID = 1
+SX_ERR_CUDA = 2
+SX_ERR_LAUNCH = 3
+SX_ERR_TIMEOUT = 4
+SX_ERR_OOM = 5
+SX_ERR_PEER = 6
+SX_ERR_UNSUPPORTED = 7
+SX_ERR_DEVICE = 8
+
+QUANT_NONE = 0
+QUANT_Q8 = 1
+QUANT_Q4 = 2
+
+ENGINE_KV_F32 = 1
+
+
+class SxError(RuntimeError):
+    def __init__(self, status: int, message: str):
+        super().__init__(f"sx status {status}: {message}")
+        self.status = status
+        self.message = message
+
+
+class ModelConfig(C.Structure):
+    """sx_model_config (mirrors ModelConfig, src/model/types.zig:44-61)."""
+
+    _fields_ = [
+        ("vocab_size", C.c_uint32),
+        ("hidden_size", C.c_uint32),
+        ("intermediate_size", C.c_uint32),
+        ("num_layers", C.c_uint32),
+        ("num_q_heads", C.c_uint32),
+        ("num_kv_heads", C.c_uint32),
+        ("num_global_kv_heads", C.c_uint32),
+        ("head_dim", C.c_uint32),
+        ("global_head_dim", C.c_uint32),
+        ("num_anchors", C.c_uint32),
+        ("window_size", C.c_uint32),
+        ("num_recall", C.c_uint32),
+        ("kv_bf16", C.c_uint32),
+        ("has_post_norms", C.c_uint32),
+        ("full_every", C.c_uint32),
+        ("attention_k_eq_v", C.c_uint32),
+        ("rms_norm_eps", C.c_float),
+        ("rope_theta", C.c_float),
+        ("rope_theta_full", C.c_float),
+        ("attn_scale", C.c_float),
+    ]
+
+    def as_dict(self) -> dict:
+        return {name: getattr(self, name) for name, _ in self._fields_}
+
+
+class ModelIO(C.Structure):
+    _fields_ = [
+        ("x", C.c_void_p),
+        ("slots", C.c_void_p),
+        ("step", C.c_void_p),
+        ("token", C.c_void_p),
+        ("logits", C.c_void_p),
+        ("normed", C.c_void_p),
+    ]
+
+
+def model_config(**kw) -> ModelConfig:
+    """A config with the reference defaults (types.zig:44-61, main.zig:34 ring sizes)."""
+    base = dict(
+        vocab_size=262144,
+        hidden_size=1536,
+        intermediate_size=12288,
+        num_layers=35,
+        num_q_heads=8,
+        num_kv_heads=1,
+        num_global_kv_heads=1,
+        head_dim=256,
+        global_head_dim=256,
+        num_anchors=32,
+        window_size=512,
+        num_recall=96,
+        kv_bf16=1,
+        has_post_norms=1,
+        full_every=5,
+        attention_k_eq_v=0,
+        rms_norm_eps=1e-6,
+        rope_theta=10000.0,
+        rope_theta_full=1000000.0,
+        attn_scale=1.0,
+    )
+    base.update(kw)
+    return ModelConfig(**base)
+
+
+# 12B-shaped decode config
+def config_12b(**kw) -> ModelConfig:
+    d = dict(
+        vocab_size=262144,
+        hidden_size=3840,
+        intermediate_size=15360,
+        num_layers=48,
+        num_q_heads=16,
+        num_kv_heads=8,
+        num_global_kv_heads=8,
+        head_dim=256,
+        global_head_dim=256,
+    )
+    d.update(kw)
+    return model_config(**d)
+
+
+_lib = None
+
+_P = C.c_void_p
+_U32 = C.c_uint32
+_U64 = C.c_uint64
+_F = C.c_float
+_I = C.c_int
+_S = C.c_int32
+
+_SIGS = {
+    "sx_version": (C.c_char_p, []),
+    "sx_last_error": (C.c_char_p, []),
+    "sx_status_string": (C.c_char_p, [_S]),
+    "sx_quantized_row_words": (_U64, [_U32, _I]),
+    "sx_packed_bytes": (_U64, [_U32, _U32, _I]),
+    "sx_rope_inv_freq": (None, [_P, _U32, _F]),
+    "sx_synth_embed_row": (None, [_P, _U32, _U32, _U64]),
+    "sx_ring_create": (_S, [_U32, _U32, _U32, _U32, C.POINTER(_P)]),
+    "sx_ring_destroy": (None, [_P]),
+    "sx_ring_reset": (None, [_P]),
+    "sx_ring_total_slots": (_U32, [_P]),
+    "sx_ring_slot_index": (_U32, [_P, _U64]),
+    "sx_ring_activate_slot": (_U32, [_P, _U32, _U64]),
+    "sx_ring_prefill": (None, [_P, _U32, _U64]),
+    "sx_ring_write_recall": (None, [_P, _U32, _U32, _U64]),
+    "sx_ring_clear_recall": (None, [_P]),
+    "sx_ring_active_slots": (_U32, [_P, _U32, _U64, _P]),
+    "sx_engine_create": (_S, [_I, _I, _U32, C.POINTER(_P)]),
+    "sx_engine_destroy": (None, [_P]),
+    "sx_engine_set_stream": (_S, [_P, _P]),
+    "sx_engine_stream": (_P, [_P]),
+    "sx_engine_sync": (_S, [_P]),
+    "sx_buffer_create": (_S, [_P, _U64, C.POINTER(_P)]),
+    "sx_buffer_wrap": (_S, [_P, _P, _U64, C.POINTER(_P)]),
+    "sx_buffer_destroy": (None, [_P]),
+    "sx_buffer_device_ptr": (_P, [_P]),
+    "sx_buffer_size": (_U64, [_P]),
+    "sx_buffer_write": (_S, [_P, _U64, _P, _U64]),
+    "sx_buffer_read": (_S, [_P, _U64, _P, _U64]),
+    "sx_buffer_upload_weights": (_S, [_P, _P, _U32, _U32, _I]),
+    "sx_buffer_repack_device": (_S, [_P, _P, _U32, _U32, _I]),
+    "sx_set_create": (_S, [_P, _P, _U32, C.POINTER(_P)]),
+    "sx_set_destroy": (None, [_P]),
+    "sx_cmd_create": (_S, [_P, C.POINTER(_P)]),
+    "sx_cmd_destroy": (None, [_P]),
+    "sx_cmd_begin": (_S, [_P]),
+    "sx_cmd_end": (_S, [_P]),
+    "sx_record_gemv": (None, [_P, _P, _P, _U32, _U32]),
+    "sx_record_gemv_logits": (None, [_P, _P, _P, _U32, _U32]),
+    "sx_record_gate_up": (None, [_P, _P, _P, _U32, _U32]),
+    "sx_record_add_rmsnorm": (None, [_P, _P, _P, _U32, _F, _F]),
+    "sx_record_rmsnorm": (None, [_P, _P, _P, _U32, _F]),
+    "sx_record_decode_attn": (None, [_P, _P, _P, _U32, _U32, _U32, _F, _U32, _U32]),
+    "sx_record_qkv_rope": (None, [_P, _P, _P, _U32, _U32, _U32, _U32, _U32, _F, _F, _U32]),
+    "sx_record_argmax": (None, [_P, _P, _P, _U32]),
+    "sx_record_barrier": (None, [_P, _P]),
+    "sx_submit": (_S, [_P, _P, _U64]),
+    "sx_dispatch_gemv": (_S, [_P, _I, _P, _P, _P, _U32, _U32, _U32]),
+    "sx_dispatch_gate_up": (_S, [_P, _P, _P, _P, _P, _U32, _U32, _U32]),
+    "sx_dispatch_rmsnorm": (_S, [_P, _P, _P, _P, _U32, _U32, _F]),
+    "sx_dispatch_add_rmsnorm": (_S, [_P, _P, _P, _P, _P, _U32, _U32, _F, _F]),
+    "sx_dispatch_qkv_rope": (
+        _S,
+        [_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _U32, _U32, _U32, _U32, _U32, _F, _F, _U32],
+    ),
+    "sx_dispatch_decode_attn": (
+        _S,
+        [_P, _P, _P, _P, _P, _P, _P, _U32, _U32, _U32, _F, _U32, _U32],
+    ),
+    "sx_dispatch_argmax": (_S, [_P, _P, _U32, _P]),
+    "sx_dispatch_unpack_q4": (_S, [_P, _P, _P, _U32, _U32]),
+    "sx_dispatch_synth_weights": (_S, [_P, _I, _P, _U32, _U32, _U32, _U64, _U64]),
+    "sx_model_create": (_S, [_P, C.POINTER(ModelConfig), C.POINTER(_P)]),
+    "sx_model_destroy": (None, [_P]),
+    "sx_model_synth_weights": (_S, [_P, _U64]),
+    "sx_model_fill_kv": (_S, [_P, _U64]),
+    "sx_forward_token": (_S, [_P, _P, _U32, _U32, _P, _U32, _I, _P, _P]),
+    "sx_model_launch": (_S, [_P, _I]),
+    "sx_model_get_io": (_S, [_P, C.POINTER(ModelIO)]),
+    "sx_model_kcache": (_P, [_P, _U32]),
+    "sx_model_vcache": (_P, [_P, _U32]),
+    "sx_model_weight_bytes": (_U64, [_P]),
+    "sx_model_kernels_per_token": (_U32, [_P, _I]),
+}
+
+
+def lib():
+    """Load libsx.so (built by __graft_entry__.build()); raises when it is missing."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    path = os.environ.get("SX_LIB", str(LIB_PATH))
+    if not os.path.exists(path):
+        raise ImportError(
+            f"libsx.so not found at {path}: build it with __graft_entry__.build(); "
+            "the decode path has no CPU fallback"
+        )
+    L = C.CDLL(path)
+    for name, (res, args) in _SIGS.items():
+        fn = getattr(L, name)
+        fn.restype = res
+        fn.argtypes = args
+    _lib = L
+    return L
+
+
+def declared_symbols() -> list[str]:
+    return list(_SIGS)
+
+
+def last_error() -> str:
+    return lib().sx_last_error().decode()
+
+
+def check(status: int) -> None:
+    if status != SX_OK:
+        raise SxError(status, last_error())
+
+
+def _ptr(a) -> int | None:
+    """Device or host address of a numpy array, torch tensor or raw int."""
+    if a is None:
+        return None
+    if isinstance(a, int):
+        return a
+    if isinstance(a, np.ndarray):
+        return a.ctypes.data
+    if hasattr(a, "data_ptr"):
+        return a.data_ptr()
+    raise TypeError(f"cannot take the address of {type(a)}")
+
+
+# ------------------------------------------------------------------------------------
+def quantized_row_words(cols: int, mode: int) -> int:
+    return int(lib().sx_quantized_row_words(cols, mode))
+
+
+def packed_bytes(rows: int, cols: int, mode: int) -> int:
+    return int(lib().sx_packed_bytes(rows, cols, mode))
+
+
+def rope_inv_freq(rotary_dim: int, theta: float) -> np.ndarray:
+    out = np.zeros(max(rotary_dim // 2, 1), np.float32)
+    lib().sx_rope_inv_freq(out.ctypes.data, rotary_dim, theta)
+    return out[: rotary_dim // 2]
+
+
+def synth_embed_row(hidden: int, token: int, seed: int) -> np.ndarray:
+    out = np.zeros(hidden, np.float32)
+    lib().sx_synth_embed_row(out.ctypes.data, hidden, token, seed)
+    return out
+
+
+class Ring:
+    """DynamicRingBuffer slot bookkeeping (src/ring_buffer.zig:8-146)."""
+
+    def __init__(self, num_layers: int, num_anchors: int, window_size: int, num_recall: int):
+        h = C.c_void_p()
+        check(lib().sx_ring_create(num_layers, num_anchors, window_size, num_recall, C.byref(h)))
+        self.h = h
+        self.total_slots = int(lib().sx_ring_total_slots(h))
+
+    def close(self):
+        if getattr(self, "h", None):
+            lib().sx_ring_destroy(self.h)
+            self.h = None
+
+    __del__ = close
+
+    def reset(self):
+        lib().sx_ring_reset(self.h)
+
+    def get_slot_index(self, clock: int) -> int:
+        return int(lib().sx_ring_slot_index(self.h, clock))
+
+    def activate_slot(self, layer: int, clock: int) -> int:
+        return int(lib().sx_ring_activate_slot(self.h, layer, clock))
+
+    def prefill(self, layer: int, upto: int) -> None:
+        lib().sx_ring_prefill(self.h, layer, upto)
+
+    def write_recall(self, layer: int, rank: int, clock: int) -> None:
+        lib().sx_ring_write_recall(self.h, layer, rank, clock)
+
+    def clear_recall(self) -> None:
+        lib().sx_ring_clear_recall(self.h)
+
+    def get_active_slots(self, layer: int, clock: int) -> np.ndarray:
+        out = np.zeros(self.total_slots, np.uint32)
+        n = lib().sx_ring_active_slots(self.h, layer, clock, out.ctypes.data)
+        return out[:n].copy()
+
+
+class Engine:
+    """GpuEngine (src/gpu/kernels.zig:18-158) on one B200."""
+
+    def __init__(self, device: int = 0, mode: int = QUANT_Q4, kv_f32: bool = False):
+        h = C.c_void_p()
+        flags = ENGINE_KV_F32 if kv_f32 else 0
+        check(lib().sx_engine_create(device, mode, flags, C.byref(h)))
+        self.h = h
+        self.mode = mode
+        self.kv_bf16 = not kv_f32
+
+    def close(self):
+        if getattr(self, "h", None):
+            lib().sx_engine_destroy(self.h)
+            self.h = None
+
+    __del__ = close
+
+    @property
+    def stream(self) -> int:
+        return int(lib().sx_engine_stream(self.h) or 0)
+
+    def set_stream(self, stream: int | None) -> None:
+        check(lib().sx_engine_set_stream(self.h, stream))
+
+    def sync(self) -> None:
+        check(lib().sx_engine_sync(self.h))
+
+    # --- buffers / sets / command buffers
+    def buffer(self, nbytes: int) -> "Buffer":
+        return Buffer.create(self, nbytes)
+
+    def wrap(self, tensor_or_ptr, nbytes: int | None = None) -> "Buffer":
+        if nbytes is None:
+            nbytes = tensor_or_ptr.numel() * tensor_or_ptr.element_size()
+        return Buffer.wrap(self, _ptr(tensor_or_ptr), nbytes)
+
+    def set(self, *buffers: "Buffer") -> "DescriptorSet":
+        return DescriptorSet(self, buffers)
+
+    def command_buffer(self) -> "CommandBuffer":
+        return CommandBuffer(self)
+
+    # --- record API (kernels.zig:80-146)
+    def record_gemv(self, cmd, s, m, k):
+        lib().sx_record_gemv(self.h, cmd.h, s.h, m, k)
+
+    def record_gemv_logits(self, cmd, s, m, k):
+        lib().sx_record_gemv_logits(self.h, cmd.h, s.h, m, k)
+
+    def record_gate_up(self, cmd, s, m, k):
+        lib().sx_record_gate_up(self.h, cmd.h, s.h, m, k)
+
+    def record_add_rmsnorm(self, cmd, s, h, eps, scalar):
+        lib().sx_record_add_rmsnorm(self.h, cmd.h, s.h, h, eps, scalar)
+
+    def record_rmsnorm(self, cmd, s, h, eps):
+        lib().sx_record_rmsnorm(self.h, cmd.h, s.h, h, eps)
+
+    def record_decode_attn(self, cmd, s, head_dim, kv_dim, gqa_ratio, inv_sqrt_dim, num_q_heads,
+                           total_slots):
+        lib().sx_record_decode_attn(self.h, cmd.h, s.h, head_dim, kv_dim, gqa_ratio,
+                                    inv_sqrt_dim, num_q_heads, total_slots)
+
+    def record_qkv_rope(self, cmd, s, num_q, num_kv, head_dim, rotary_dim, k_eq_v, theta, eps,
+                        total_slots):
+        lib().sx_record_qkv_rope(self.h, cmd.h, s.h, num_q, num_kv, head_dim, rotary_dim,
+                                 int(k_eq_v), theta, eps, total_slots)
+
+    def record_argmax(self, cmd, s, vocab):
+        lib().sx_record_argmax(self.h, cmd.h, s.h, vocab)
+
+    def record_barrier(self, cmd):
+        lib().sx_record_barrier(self.h, cmd.h)
+
+    def submit_pre_recorded(self, cmd, timeout_ns: int = 0) -> None:
+        check(lib().sx_submit(self.h, cmd.h, timeout_ns))
+
+    # --- immediate mode (device pointers: torch tensors or ints)
+    def gemv(self, mode, w_packed, x, y, m, k, batch=1):
+        check(lib().sx_dispatch_gemv(self.h, mode, _ptr(w_packed), _ptr(x), _ptr(y), m, k, batch))
+
+    def gate_up(self, wg, wu, x, y, m, k, batch=1):
+        check(lib().sx_dispatch_gate_up(self.h, _ptr(wg), _ptr(wu), _ptr(x), _ptr(y), m, k, batch))
+
+    def rmsnorm(self, x, w, y, n, batch=1, eps=1e-6):
+        check(lib().sx_dispatch_rmsnorm(self.h, _ptr(x), _ptr(w), _ptr(y), n, batch, eps))
+
+    def add_rmsnorm(self, x, r, w, y, n, batch=1, eps=1e-6, scalar=1.0):
+        check(lib().sx_dispatch_add_rmsnorm(self.h, _ptr(x), _ptr(r), _ptr(w), _ptr(y), n, batch,
+                                            eps, scalar))
+
+    def qkv_rope(self, q_in, k_in, v_in, q_norm_w, k_norm_w, q_out, k_cache, v_cache, step,
+                 num_q, num_kv, head_dim, rotary_dim, k_eq_v, theta, eps, total_slots):
+        check(lib().sx_dispatch_qkv_rope(
+            self.h, _ptr(q_in), _ptr(k_in), _ptr(v_in), _ptr(q_norm_w), _ptr(k_norm_w),
+            _ptr(q_out), _ptr(k_cache), _ptr(v_cache), _ptr(step), num_q, num_kv, head_dim,
+            rotary_dim, int(k_eq_v), theta, eps, total_slots))
+
+    def decode_attn(self, q, k_cache, v_cache, slots, step, out, head_dim, kv_dim, gqa_ratio,
+                    scale, num_q_heads, total_slots):
+        check(lib().sx_dispatch_decode_attn(
+            self.h, _ptr(q), _ptr(k_cache), _ptr(v_cache), _ptr(slots), _ptr(step), _ptr(out),
+            head_dim, kv_dim, gqa_ratio, scale, num_q_heads, total_slots))
+
+    def argmax(self, logits, n, out):
+        check(lib().sx_dispatch_argmax(self.h, _ptr(logits), n, _ptr(out)))
+
+    def unpack_q4(self, w_packed, out, m, k):
+        check(lib().sx_dispatch_unpack_q4(self.h, _ptr(w_packed), _ptr(out), m, k))
+
+    def synth_weights(self, mode, ref_out, row0, rows, cols, seed, stream_id):
+        check(lib().sx_dispatch_synth_weights(self.h, mode, _ptr(ref_out), row0, rows, cols, seed,
+                                              stream_id))
+
+
+class Buffer:
+    """GpuBuffer (src/gpu/buffer.zig)."""
+
+    def __init__(self, engine: Engine, h, nbytes: int):
+        self.engine = engine
+        self.h = h
+        self.nbytes = nbytes
+
+    @classmethod
+    def create(cls, engine: Engine, nbytes: int) -> "Buffer":
+        h = C.c_void_p()
+        check(lib().sx_buffer_create(engine.h, nbytes, C.byref(h)))
+        return cls(engine, h, nbytes)
+
+    @classmethod
+    def wrap(cls, engine: Engine, ptr: int, nbytes: int) -> "Buffer":
+        h = C.c_void_p()
+        check(lib().sx_buffer_wrap(engine.h, ptr, nbytes, C.byref(h)))
+        return cls(engine, h, nbytes)
+
+    def close(self):
+        if getattr(self, "h", None):
+            lib().sx_buffer_destroy(self.h)
+            self.h = None
+
+    __del__ = close
+
+    @property
+    def ptr(self) -> int:
+        return int(lib().sx_buffer_device_ptr(self.h))
+
+    def write(self, arr: np.ndarray, offset: int = 0) -> None:
+        a = np.ascontiguousarray(arr)
+        check(lib().sx_buffer_write(self.h, offset, a.ctypes.data, a.nbytes))
+
+    def read(self, dtype, count: int, offset: int = 0) -> np.ndarray:
+        out = np.empty(count, dtype)
+        check(lib().sx_buffer_read(self.h, offset, out.ctypes.data, out.nbytes))
+        return out
+
+    def upload_weights(self, ref_words: np.ndarray, rows: int, cols: int, mode: int) -> None:
+        w = np.ascontiguousarray(ref_words, dtype=np.uint32)
+        check(lib().sx_buffer_upload_weights(self.h, w.ctypes.data, rows, cols, mode))
+
+    def repack_device(self, ref_ptr, rows: int, cols: int, mode: int) -> None:
+        check(lib().sx_buffer_repack_device(self.h, _ptr(ref_ptr), rows, cols, mode))
+
+
+class DescriptorSet:
+    def __init__(self, engine: Engine, buffers):
+        self.buffers = list(buffers)  # keep alive
+        arr = (C.c_void_p * len(self.buffers))(*[b.h.value for b in self.buffers])
+        h = C.c_void_p()
+        check(lib().sx_set_create(engine.h, arr, len(self.buffers), C.byref(h)))
+        self.h = h
+
+    def close(self):
+        if getattr(self, "h", None):
+            lib().sx_set_destroy(self.h)
+            self.h = None
+
+    __del__ = close
+
+
+class CommandBuffer:
+    def __init__(self, engine: Engine):
+        h = C.c_void_p()
+        check(lib().sx_cmd_create(engine.h, C.byref(h)))
+        self.h = h
+
+    def close(self):
+        if getattr(self, "h", None):
+            lib().sx_cmd_destroy(self.h)
+            self.h = None
+
+    __del__ = close
+
+    def begin(self):
+        check(lib().sx_cmd_begin(self.h))
+
+    def end(self):
+        check(lib().sx_cmd_end(self.h))
+
+
+class Model:
+    """GpuModelContext (src/gpu/model_gpu.zig:35-197) + gpuDispatchForwardToken."""
+
+    def __init__(self, engine: Engine, cfg: ModelConfig):
+        h = C.c_void_p()
+        self.cfg = cfg
+        check(lib().sx_model_create(engine.h, C.byref(cfg), C.byref(h)))
+        self.h = h
+        self.engine = engine
+        self.total_slots = cfg.num_anchors + cfg.window_size + cfg.num_recall
+
+    def close(self):
+        if getattr(self, "h", None):
+            lib().sx_model_destroy(self.h)
+            self.h = None
+
+    __del__ = close
+
+    def synth_weights(self, seed: int) -> None:
+        check(lib().sx_model_synth_weights(self.h, seed))
+
+    def fill_kv(self, seed: int) -> None:
+        check(lib().sx_model_fill_kv(self.h, seed))
+
+    def forward_token(self, x: np.ndarray, clock: int, slot: int, active_slots: np.ndarray,
+                      want_logits: bool = True, logits_out: np.ndarray | None = None) -> int:
+        xs = np.ascontiguousarray(x, np.float32)
+        sl = np.ascontiguousarray(active_slots, np.uint32)
+        tok = C.c_uint32(0)
+        check(lib().sx_forward_token(self.h, xs.ctypes.data, clock, slot, sl.ctypes.data,
+                                     len(sl), int(want_logits), C.byref(tok),
+                                     None if logits_out is None else logits_out.ctypes.data))
+        return int(tok.value)
+
+    def launch(self, want_logits: bool = True) -> None:
+        check(lib().sx_model_launch(self.h, int(want_logits)))
+
+    def io(self) -> ModelIO:
+        io = ModelIO()
+        check(lib().sx_model_get_io(self.h, C.byref(io)))
+        return io
+
+    def kcache_ptr(self, layer: int) -> int:
+        return int(lib().sx_model_kcache(self.h, layer))
+
+    def vcache_ptr(self, layer: int) -> int:
+        return int(lib().sx_model_vcache(self.h, layer))
+
+    @property
+    def weight_bytes(self) -> int:
+        return int(lib().sx_model_weight_bytes(self.h))
+
+    def kernels_per_token(self, want_logits: bool = True) -> int:
+        return int(lib().sx_model_kernels_per_token(self.h, int(want_logits)))

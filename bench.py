@@ -1,0 +1,415 @@
+"""Benchmark: 12B-shaped Q4_0 batch-1 greedy decode on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
+
+One step = one decode token of the 48-layer 12B-shaped model (Q4_0 layers, Q8_0 LM head,
+640-slot ring with every slot live) on synthetic weights.  Prints one JSON line.
+
+value : tokens/s with the step's inputs resident in HBM (device-timed CUDA graph replays)
+e2e   : tokens/s through the public C ABI sx_forward_token (gpuDispatchForwardToken) with
+        host buffers: the per-token host->device copy of x / slot list / step params and the
+        device->host read of the sampled token are inside the timed region
+roofline : dominant kernel (fused gate+up GeGLU Q4 GEMV) bytes / CUDA-event launch time
+cpu_baseline : the CPU checker (restatement of the reference's CPU path) on the host cores
+
+N > 1: one process per GPU (torchrun), each rank decodes its own replica of the model
+(independent sessions, no collective); value is the sum over ranks.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import re
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT / "ai-research_b200"))
+sys.path.insert(0, str(ROOT))
+
+METRIC = "12B-shape Q4_0 decode tok/s"
+UNIT = "tok/s"
+SEED = 1234 + 4
+START_CLOCK = 50000
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="sx", choices=["sx", "reference"])
+    ap.add_argument("--layers", type=int, default=48)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+def model_cfg_dict(layers=48):
+    return dict(
+        vocab_size=262144, hidden_size=3840, intermediate_size=15360, num_layers=layers,
+        num_q_heads=16, num_kv_heads=8, num_global_kv_heads=8, head_dim=256, global_head_dim=256,
+        num_anchors=32, window_size=512, num_recall=96, kv_bf16=1, has_post_norms=1, full_every=5,
+        attention_k_eq_v=0, rms_norm_eps=1e-6, rope_theta=10000.0, rope_theta_full=1000000.0,
+        attn_scale=1.0,
+    )
+
+
+def algorithmic_bytes_per_token(cfg) -> dict:
+    H, I, V, L = cfg["hidden_size"], cfg["intermediate_size"], cfg["vocab_size"], cfg["num_layers"]
+    q = cfg["num_q_heads"] * cfg["head_dim"]
+    kv = cfg["num_kv_heads"] * cfg["head_dim"]
+    q4 = lambda r, c: r * c // 32 * 20  # noqa: E731
+    layer_w = q4(q, H) + 2 * q4(kv, H) + q4(H, q) + 2 * q4(I, H) + q4(H, I)
+    head = V * H // 32 * 36
+    slots = cfg["num_anchors"] + cfg["window_size"] + cfg["num_recall"]
+    kv_bytes = L * slots * kv * 2 * 2  # K and V, bf16
+    norms = L * (6 * H + 2 * cfg["head_dim"]) * 4 + H * 4
+    return dict(weights=L * layer_w, lm_head=head, kv=kv_bytes, norms=norms,
+                total=L * layer_w + head + kv_bytes + norms)
+
+
+def load_peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def profiled_traffic():
+    """dram read+write bytes per launch of the GeGLU kernel from the committed ncu summary."""
+    f = ROOT / "profiles" / "gate_up_geglu_q4_12b.md"
+    if not f.exists():
+        return None
+    m = re.search(r"traffic_bytes_per_launch:\s*([0-9]+)", f.read_text())
+    return int(m.group(1)) if m else None
+
+
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device: int):
+        self.device = device
+        self.lines: list[str] = []
+        self.proc = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200", "-i", str(self.device)],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except OSError:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx.append(float(parts[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(mx) if mx else None, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ----------------------------------------------------------------------------------------
+class CpuSample:
+    """The CPU checker (restatement of the reference's Q4 decode path) on a bounded sample of
+    one token: two 12B-width layers (one sliding, one full attention, 640 live slots) and
+    16384 of the 262144 LM-head rows, extrapolated x24 (layers) and x16 (head)."""
+
+    def __init__(self):
+        from oracle import oracle as orc
+
+        self.orc = orc
+        self.cores = os.cpu_count() or 1
+        cfg = model_cfg_dict(2)
+        cfg["vocab_size"] = 16  # the head is timed separately on a row sample
+        cfg["full_every"] = 2
+        self.m = orc.Model(cfg, SEED, nthreads=self.cores)
+        self.m.fill_kv(SEED)
+        self.m.ring.prefill(0, START_CLOCK)
+        self.m.synth_recall(START_CLOCK, 96, SEED)
+        self.head_rows = 262144 // 16
+        self.w8 = orc.synth_q8(self.head_rows, 3840, SEED, 2)
+        self.x = orc.synth_embed_row(3840, 5, SEED)
+        self.k = 0
+
+    def step(self) -> float:
+        """Seconds per token extrapolated from one sample."""
+        t0 = time.perf_counter()
+        self.m.forward(self.x, START_CLOCK + self.k, want_logits=False)
+        t1 = time.perf_counter()
+        self.orc.gemv_q8(self.w8, self.x, self.head_rows, 3840)
+        t2 = time.perf_counter()
+        self.k += 1
+        return 24 * (t1 - t0) + 16 * (t2 - t1)
+
+    def describe(self, n) -> str:
+        return (f"{n} samples of 2 of 48 12B-width layers + 16384 of 262144 LM-head rows "
+                f"(CPU checker, {self.cores} threads), extrapolated x24 / x16 to one token")
+
+
+def cpu_baseline(budget_s: float = 20.0) -> dict:
+    cs = CpuSample()
+    times = []
+    t_end = time.perf_counter() + budget_s
+    while time.perf_counter() < t_end and len(times) < 20:
+        times.append(cs.step())
+    per_token = statistics.median(times)
+    return {"value": 1.0 / per_token, "unit": UNIT, "cores": cs.cores, "kind": "port",
+            "sample": cs.describe(len(times))}
+
+
+def run_reference(args, rank, world):
+    if rank != 0:
+        return
+    cs = CpuSample()
+    for _ in range(args.warmup):
+        cs.step()
+    steps = [cs.step() for _ in range(args.steps)]
+    per_token = sum(steps) / len(steps)
+    value = 1.0 / per_token
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": per_token * 1e3,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic",
+        "config": {"workload": "c4: 12B-shape Q4_0 decode, batch 1, 48 layers, H 3840, "
+                               "16q/8kv x 256, I 15360, vocab 262144, 640 live ring slots",
+                   "parallelism": "cpu"},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": cs.cores, "kind": "port",
+                         "sample": cs.describe(args.steps)},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "note": ("the reference's own CPU path is Zig and cannot be built here (no zig "
+                 "toolchain); timed the C restatement of its Q4 decode path instead"),
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ----------------------------------------------------------------------------------------
+def main():
+    args = parse()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        run_reference(args, rank, world)
+        return
+
+    import torch
+
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    import sx
+
+    cfgd = model_cfg_dict(args.layers)
+    eng = sx.Engine(local)
+    stream = torch.cuda.ExternalStream(eng.stream)
+    model = sx.Model(eng, sx.model_config(**cfgd))
+    model.synth_weights(SEED + rank)
+    model.fill_kv(SEED + rank)
+    total_slots = model.total_slots
+    ring = sx.Ring(1, 32, 512, 96)
+    ring.prefill(0, START_CLOCK)
+    rng = np.random.default_rng(SEED + rank)
+    for r in range(96):  # synthetic recall tier: every slot live (640)
+        ring.write_recall(0, r, int(rng.integers(0, START_CLOCK)))
+
+    # ---- per-step inputs staged in HBM (value run)
+    nsteps = args.warmup + args.steps
+    H = cfgd["hidden_size"]
+    xs = np.stack([sx.synth_embed_row(H, int(rng.integers(0, 262144)), SEED) for _ in range(nsteps)])
+    slot_tab = np.zeros((nsteps, total_slots), np.uint32)
+    step_tab = np.zeros((nsteps, 4), np.uint32)
+    vring = sx.Ring(1, 32, 512, 96)
+    vring.prefill(0, START_CLOCK)
+    for r in range(96):
+        vring.write_recall(0, r, START_CLOCK - 1 - r)
+    for i in range(nsteps):
+        c = START_CLOCK + i
+        s = vring.activate_slot(0, c)
+        a = vring.get_active_slots(0, c)
+        slot_tab[i, : len(a)] = a
+        step_tab[i] = (c, s, len(a), 0)
+    d_x = torch.from_numpy(xs.astype(np.float32)).cuda()
+    d_slots = torch.from_numpy(slot_tab.view(np.int32)).cuda()
+    d_step = torch.from_numpy(step_tab.view(np.int32)).cuda()
+    io = model.io()
+
+    import ctypes
+
+    cudart = ctypes.CDLL("libcudart.so.12")
+    cudart.cudaMemcpyAsync.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t,
+                                       ctypes.c_int, ctypes.c_void_p]
+    cudart.cudaMemcpyAsync.restype = ctypes.c_int
+    copies = []
+    for i in range(nsteps):
+        copies.append(((io.x, d_x[i].data_ptr(), 4 * H),
+                       (io.slots, d_slots[i].data_ptr(), 4 * total_slots),
+                       (io.step, d_step[i].data_ptr(), 16)))
+
+    def stage(i):
+        # device-to-device staging of this step's resident inputs on the engine stream
+        for dst, src, nb in copies[i]:
+            rc = cudart.cudaMemcpyAsync(dst, src, nb, 3, eng.stream)
+            if rc != 0:
+                raise RuntimeError(f"cudaMemcpyAsync failed ({rc})")
+
+    kernels_per_token = model.kernels_per_token(True)
+    for i in range(args.warmup):
+        stage(i)
+        model.launch(True)
+    eng.sync()
+    if dist is not None:
+        dist.barrier()
+    clocks = ClockSampler(local)
+    clocks.start()
+    torch.cuda.synchronize()
+    ev0 = torch.cuda.Event(enable_timing=True)
+    ev1 = torch.cuda.Event(enable_timing=True)
+    ev0.record(stream)
+    for i in range(args.warmup, nsteps):
+        stage(i)
+        model.launch(True)
+    ev1.record(stream)
+    eng.sync()
+    torch.cuda.synchronize()
+    ms = ev0.elapsed_time(ev1)
+    clk = clocks.stop()
+    ms_max = ms
+    if dist is not None:
+        t = torch.tensor([ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms_max = float(t.item())
+    value = world * args.steps / (ms_max / 1e3)
+
+    # ---- e2e through the public API (host buffers, copies inside the timed region)
+    token = 7
+    if dist is not None:
+        dist.barrier()
+    torch.cuda.synchronize()
+    for i in range(args.warmup):
+        c = START_CLOCK + nsteps + i
+        x = sx.synth_embed_row(H, token, SEED)
+        s = ring.activate_slot(0, c)
+        token = model.forward_token(x, c, s, ring.get_active_slots(0, c), True)
+    t0 = time.perf_counter()
+    for i in range(args.steps):
+        c = START_CLOCK + nsteps + args.warmup + i
+        x = sx.synth_embed_row(H, token, SEED)
+        s = ring.activate_slot(0, c)
+        token = model.forward_token(x, c, s, ring.get_active_slots(0, c), True)
+    e2e_s = time.perf_counter() - t0
+    if dist is not None:
+        t = torch.tensor([e2e_s], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_s = float(t.item())
+    e2e = world * args.steps / e2e_s
+
+    # ---- roofline of the dominant kernel: fused gate+up GeGLU over the layers' weights
+    peak, peak_kind = load_peaks()
+    I = cfgd["intermediate_size"]
+    gu_bytes = 2 * (I * H // 32 * 20) + H * 4 + I * 4
+    roof_layers = min(args.layers, 24)
+    wbufs = []
+    for l in range(roof_layers):
+        g = eng.buffer(sx.packed_bytes(I, H, sx.QUANT_Q4))
+        u = eng.buffer(sx.packed_bytes(I, H, sx.QUANT_Q4))
+        wbufs.append((g, u))
+    xin = torch.randn(H, device="cuda")
+    yout = torch.empty(I, device="cuda")
+    torch.cuda.synchronize()
+    reps = 4
+    with torch.cuda.stream(stream):
+        for g, u in wbufs:
+            eng.gate_up(g.ptr, u.ptr, xin, yout, I, H, 1)
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(reps):
+            for g, u in wbufs:
+                eng.gate_up(g.ptr, u.ptr, xin, yout, I, H, 1)
+        e1.record(stream)
+    eng.sync()
+    launch_ms = e0.elapsed_time(e1) / (reps * len(wbufs))
+    achieved = gu_bytes / (launch_ms / 1e3) / 1e9
+    traffic = profiled_traffic()
+
+    alg = algorithmic_bytes_per_token(cfgd)
+    line = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32 (Q4_0/Q8_0 weights)",
+        "data": "synthetic (seeded random-init 12B-shaped weights, BASELINE distributions)",
+        "config": {
+            "workload": f"c4: 12B-shape Q4_0 greedy decode, batch 1, {args.layers} layers, H 3840, "
+                        "16q/8kv x 256, I 15360, vocab 262144 (Q8_0 head), 640 live ring slots",
+            "global_batch": world, "seq_len": total_slots,
+            "parallelism": "replicas" if world > 1 else "single",
+            "l2": "inputs larger than L2 (8.1 GB of weights+KV read per step)",
+            "algorithmic_bytes_per_token": alg["total"],
+            "hbm_gbs_per_token_rate": alg["total"] * value / world / 1e9,
+        },
+        "e2e": {"value": e2e, "unit": UNIT,
+                "h2d_bytes_per_step": 4 * H + 4 * total_slots + 16, "d2h_bytes_per_step": 4},
+        "gpu_launches": kernels_per_token * args.steps,
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                     "frac": achieved / peak, "traffic": traffic,
+                     "kernel": "gemv_kernel<4,2,1> fused gate+up GeGLU, 2 x 15360x3840 Q4_0",
+                     "algorithmic_bytes_per_launch": gu_bytes, "launch_ms": launch_ms,
+                     "peak_kind": peak_kind + " (burst copy)"},
+        "clocks": clk,
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline()
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    model.close()
+    eng.close()
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

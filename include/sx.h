@@ -1,0 +1,272 @@
+/*
+ * sx.h -- C ABI of libsx, the B200 (sm_100a) decode hot path of the Sullux/ai-research
+ * inference engine.
+ *
+ * The reference's Zig host drives its GPU through `GpuEngine` (src/gpu/kernels.zig): it
+ * records every per-token op into a command buffer once at init (`record*` calls bound to
+ * descriptor sets of storage buffers, src/gpu/model_dispatch.zig:10-129) and re-submits that
+ * buffer once per token (`submitPreRecorded`).  This header is the drop-in replacement for
+ * that API: the same record calls with the same arguments, recorded into a CUDA graph and
+ * replayed per token.  Each declaration cites the reference interface it replaces.
+ *
+ * Conventions: every function that can fail returns an sx_status (0 = success) and never
+ * throws; sx_last_error() gives a message for the calling thread.  Record calls return void
+ * exactly like the reference; a bad record call poisons the command buffer and the error is
+ * returned by sx_cmd_end.  No torch types cross this boundary: plain pointers and sizes.
+ */
+#ifndef SX_H
+#define SX_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define SX_API __attribute__((visibility("default")))
+
+typedef int32_t sx_status;
+#define SX_OK 0
+#define SX_ERR_INVALID 1     /* bad argument or unsupported shape                      */
+#define SX_ERR_CUDA 2        /* CUDA runtime error (message in sx_last_error)          */
+#define SX_ERR_LAUNCH 3      /* kernel launch failed (VkQueueSubmitFailed)             */
+#define SX_ERR_TIMEOUT 4     /* submit did not finish in time (VkFenceTimeout)         */
+#define SX_ERR_OOM 5         /* device allocation failed                               */
+#define SX_ERR_PEER 6        /* multi-GPU exchange failed                              */
+#define SX_ERR_UNSUPPORTED 7 /* valid request this build does not implement            */
+#define SX_ERR_DEVICE 8      /* a kernel reported a device-side error (bad slot, ...)  */
+
+/* quant.zig:3-13 QuantMode */
+typedef enum { SX_QUANT_NONE = 0, SX_QUANT_Q8 = 1, SX_QUANT_Q4 = 2 } sx_quant_mode;
+
+/* engine flags */
+#define SX_ENGINE_KV_F32 1u /* keep the KV cache in f32 like model_gpu.zig:133 (default bf16) */
+
+SX_API const char *sx_version(void);
+SX_API const char *sx_last_error(void);
+SX_API const char *sx_status_string(sx_status s);
+
+/* ---------------------------------------------------------------------------------------
+ * Formats (host only, no GPU needed)
+ * ------------------------------------------------------------------------------------- */
+/* quant.zig:164-171 getQuantizedRowWords */
+SX_API uint64_t sx_quantized_row_words(uint32_t cols, sx_quant_mode mode);
+/* Bytes of the packed device layout sx_buffer_upload_weights produces for a rows x cols
+ * matrix (equal to the reference's 20 B / 36 B per block when rows % 16 == 0 and
+ * cols % 64 == 0). */
+SX_API uint64_t sx_packed_bytes(uint32_t rows, uint32_t cols, sx_quant_mode mode);
+/* kernels.zig:138 RoPE inverse frequencies 1 / pow(theta, 2i / rotary_dim), i < rot/2 */
+SX_API void sx_rope_inv_freq(float *out, uint32_t rotary_dim, float theta);
+/* forward.zig:33-37 synthetic-checkpoint embedding row times sqrt(hidden) */
+SX_API void sx_synth_embed_row(float *x, uint32_t hidden, uint32_t token, uint64_t seed);
+
+/* ---------------------------------------------------------------------------------------
+ * Ring buffer bookkeeping (host), ring_buffer.zig:8-146 DynamicRingBuffer.  Only slot
+ * clocks and liveness live here; K/V live in device caches.
+ * ------------------------------------------------------------------------------------- */
+typedef struct sx_ring sx_ring;
+/* ring_buffer.zig:20-37 init */
+SX_API sx_status sx_ring_create(uint32_t num_layers, uint32_t num_anchors, uint32_t window_size,
+                                uint32_t num_recall, sx_ring **out);
+/* ring_buffer.zig:39-43 deinit */
+SX_API void sx_ring_destroy(sx_ring *r);
+/* ring_buffer.zig:45-49 reset */
+SX_API void sx_ring_reset(sx_ring *r);
+SX_API uint32_t sx_ring_total_slots(const sx_ring *r);
+/* ring_buffer.zig:56-59 getSlotIndex */
+SX_API uint32_t sx_ring_slot_index(const sx_ring *r, uint64_t clock);
+/* ring_buffer.zig:61-68 activateSlot */
+SX_API uint32_t sx_ring_activate_slot(sx_ring *r, uint32_t layer, uint64_t clock);
+/* activateSlot for every clock below `upto` (history of a session that ran to `upto`) */
+SX_API void sx_ring_prefill(sx_ring *r, uint32_t layer, uint64_t upto);
+/* ring_buffer.zig:90-99 writeRecallKV (bookkeeping part) */
+SX_API void sx_ring_write_recall(sx_ring *r, uint32_t layer, uint32_t rank, uint64_t clock);
+/* ring_buffer.zig:82-88 clearRecall */
+SX_API void sx_ring_clear_recall(sx_ring *r);
+/* ring_buffer.zig:101-136 getActiveSlots; returns the count written to out */
+SX_API uint32_t sx_ring_active_slots(const sx_ring *r, uint32_t layer, uint64_t clock,
+                                     uint32_t *out);
+
+/* ---------------------------------------------------------------------------------------
+ * Engine, buffers, descriptor sets (gpu/context.zig, gpu/buffer.zig, gpu/descriptors.zig)
+ * ------------------------------------------------------------------------------------- */
+typedef struct sx_engine sx_engine;
+typedef struct sx_buffer sx_buffer;
+typedef struct sx_set sx_set;
+typedef struct sx_cmd sx_cmd;
+
+/* GpuContext.init + GpuEngine.init (context.zig:17, kernels.zig:35-68).  `mode` selects
+ * the layer GEMV format; with SX_QUANT_Q4 the logits GEMV is Q8 (kernels.zig:38). */
+SX_API sx_status sx_engine_create(int device, sx_quant_mode mode, uint32_t flags,
+                                  sx_engine **out);
+/* GpuEngine.deinit (kernels.zig:70-78) */
+SX_API void sx_engine_destroy(sx_engine *e);
+/* Run subsequent work on an external cudaStream_t (NULL restores the engine's own). */
+SX_API sx_status sx_engine_set_stream(sx_engine *e, void *cuda_stream);
+SX_API void *sx_engine_stream(sx_engine *e);
+/* Wait for the engine stream, then report any device-side error word. */
+SX_API sx_status sx_engine_sync(sx_engine *e);
+
+/* GpuBuffer.init (buffer.zig:13) -- device memory */
+SX_API sx_status sx_buffer_create(sx_engine *e, uint64_t bytes, sx_buffer **out);
+/* Wrap caller-owned device memory (not freed by sx_buffer_destroy). */
+SX_API sx_status sx_buffer_wrap(sx_engine *e, void *device_ptr, uint64_t bytes,
+                                sx_buffer **out);
+/* GpuBuffer.deinit (buffer.zig:56) */
+SX_API void sx_buffer_destroy(sx_buffer *b);
+SX_API void *sx_buffer_device_ptr(sx_buffer *b);
+SX_API uint64_t sx_buffer_size(const sx_buffer *b);
+/* asSlice writes/reads (buffer.zig:64-67); synchronous on the engine stream */
+SX_API sx_status sx_buffer_write(sx_buffer *b, uint64_t offset, const void *src, uint64_t bytes);
+SX_API sx_status sx_buffer_read(sx_buffer *b, uint64_t offset, void *dst, uint64_t bytes);
+/* createWeightBuffer (model_gpu.zig:51-62): take a rows x cols matrix in the reference's
+ * quantised block layout (quantizeMatrix output: Q4 5 words / Q8 9 words per 32 values) and
+ * store it in `dst` in the packed device layout (lossless permutation; dst must hold
+ * sx_packed_bytes).  mode NONE is rejected. */
+SX_API sx_status sx_buffer_upload_weights(sx_buffer *dst, const uint32_t *ref_words,
+                                          uint32_t rows, uint32_t cols, sx_quant_mode mode);
+/* Same, from reference-layout words already in device memory. */
+SX_API sx_status sx_buffer_repack_device(sx_buffer *dst, const void *ref_words_device,
+                                         uint32_t rows, uint32_t cols, sx_quant_mode mode);
+
+/* DescriptorManager.allocateSet + bindBuffers (descriptors.zig:27-103): an ordered tuple of
+ * buffers; aliasing allowed (model_gpu.zig:144,153-154). */
+SX_API sx_status sx_set_create(sx_engine *e, sx_buffer *const *buffers, uint32_t count,
+                               sx_set **out);
+SX_API void sx_set_destroy(sx_set *s);
+
+/* ---------------------------------------------------------------------------------------
+ * Command buffers: record once, submit per token (kernels.zig:80-157)
+ * ------------------------------------------------------------------------------------- */
+SX_API sx_status sx_cmd_create(sx_engine *e, sx_cmd **out);
+SX_API void sx_cmd_destroy(sx_cmd *c);
+/* vkBeginCommandBuffer (model_dispatch.zig:110) */
+SX_API sx_status sx_cmd_begin(sx_cmd *c);
+/* vkEndCommandBuffer (model_dispatch.zig:128): instantiates the CUDA graph */
+SX_API sx_status sx_cmd_end(sx_cmd *c);
+
+/* recordGemv (kernels.zig:80-83): set {W, X, Y}, Y[m] = W[m x k] . X[k] in the engine mode */
+SX_API void sx_record_gemv(sx_engine *e, sx_cmd *c, sx_set *set, uint32_t m, uint32_t k);
+/* recordGemvLogits (kernels.zig:88-91): set {W, X, Y}; Q8 weights when the mode is Q4 */
+SX_API void sx_record_gemv_logits(sx_engine *e, sx_cmd *c, sx_set *set, uint32_t m, uint32_t k);
+/* recordGateUpSwiGlu (kernels.zig:92-95): set {W_gate, W_up, X, Y},
+ * Y[r] = gelu_tanh(W_gate[r] . X) * (W_up[r] . X) */
+SX_API void sx_record_gate_up(sx_engine *e, sx_cmd *c, sx_set *set, uint32_t m, uint32_t k);
+/* recordAddRmsNorm (kernels.zig:100-103): set {X, R, W, Y}; X = (X + R) * scalar,
+ * Y = X * rsqrt(mean(X^2) + eps) * W */
+SX_API void sx_record_add_rmsnorm(sx_engine *e, sx_cmd *c, sx_set *set, uint32_t h, float eps,
+                                  float scalar);
+/* recordRmsNorm (kernels.zig:108-111): set {X, W, Y} */
+SX_API void sx_record_rmsnorm(sx_engine *e, sx_cmd *c, sx_set *set, uint32_t h, float eps);
+/* recordDecodeAttn (kernels.zig:116-119): set {Q, K_cache, V_cache, Active_slots, Attn_out,
+ * Step_params}; Step_params = u32 {clock, slot, n_active, 0}.  total_slots sizes the caches
+ * (the reference hard-codes 1024, model_gpu.zig:86). */
+SX_API void sx_record_decode_attn(sx_engine *e, sx_cmd *c, sx_set *set, uint32_t head_dim,
+                                  uint32_t kv_dim, uint32_t gqa_ratio, float inv_sqrt_dim,
+                                  uint32_t num_q_heads, uint32_t total_slots);
+/* recordQkvRope (kernels.zig:124-129): set {Q_in, K_in, V_in, Q_norm_w, K_norm_w, Q_out,
+ * K_cache, V_cache, Step_params} */
+SX_API void sx_record_qkv_rope(sx_engine *e, sx_cmd *c, sx_set *set, uint32_t num_q,
+                               uint32_t num_kv, uint32_t head_dim, uint32_t rotary_dim,
+                               uint32_t k_eq_v, float theta, float eps, uint32_t total_slots);
+/* recordArgmax (kernels.zig:139-142): set {Logits, OutToken}; first index of the maximum
+ * (the CPU rule, kernels.zig:164-174) */
+SX_API void sx_record_argmax(sx_engine *e, sx_cmd *c, sx_set *set, uint32_t vocab);
+/* recordBarrier (kernels.zig:143-146): ordering is implicit in the graph; kept for parity */
+SX_API void sx_record_barrier(sx_engine *e, sx_cmd *c);
+/* submitPreRecorded (kernels.zig:147-157): launch and poll to a deadline
+ * (timeout_ns == 0 -> the reference's 5 s).  SX_ERR_TIMEOUT like VkFenceTimeout. */
+SX_API sx_status sx_submit(sx_engine *e, sx_cmd *c, uint64_t timeout_ns);
+
+/* ---------------------------------------------------------------------------------------
+ * Immediate-mode dispatch on device pointers (ComputePipeline.dispatch, pipeline.zig:143-158,
+ * as used by test_q4_exec.zig:77-85).  Asynchronous on the engine stream.  Packed weights
+ * come from sx_buffer_upload_weights / sx_buffer_repack_device.  Batch rows are contiguous
+ * with strides k (inputs) and m (outputs).
+ * ------------------------------------------------------------------------------------- */
+SX_API sx_status sx_dispatch_gemv(sx_engine *e, sx_quant_mode mode, const void *w_packed,
+                                  const float *x, float *y, uint32_t m, uint32_t k,
+                                  uint32_t batch);
+SX_API sx_status sx_dispatch_gate_up(sx_engine *e, const void *wg_packed, const void *wu_packed,
+                                     const float *x, float *y, uint32_t m, uint32_t k,
+                                     uint32_t batch);
+SX_API sx_status sx_dispatch_rmsnorm(sx_engine *e, const float *x, const float *w, float *y,
+                                     uint32_t n, uint32_t batch, float eps);
+SX_API sx_status sx_dispatch_add_rmsnorm(sx_engine *e, float *x, const float *r, const float *w,
+                                         float *y, uint32_t n, uint32_t batch, float eps,
+                                         float scalar);
+SX_API sx_status sx_dispatch_qkv_rope(sx_engine *e, const float *q_in, const float *k_in,
+                                      const float *v_in, const float *q_norm_w,
+                                      const float *k_norm_w, float *q_out, void *k_cache,
+                                      void *v_cache, const uint32_t *step_params,
+                                      uint32_t num_q, uint32_t num_kv, uint32_t head_dim,
+                                      uint32_t rotary_dim, uint32_t k_eq_v, float theta,
+                                      float eps, uint32_t total_slots);
+SX_API sx_status sx_dispatch_decode_attn(sx_engine *e, const float *q, const void *k_cache,
+                                         const void *v_cache, const uint32_t *active_slots,
+                                         const uint32_t *step_params, float *out,
+                                         uint32_t head_dim, uint32_t kv_dim, uint32_t gqa_ratio,
+                                         float scale, uint32_t num_q_heads,
+                                         uint32_t total_slots);
+SX_API sx_status sx_dispatch_argmax(sx_engine *e, const float *logits, uint32_t n,
+                                    uint32_t *out_token);
+/* Dequantise a packed Q4 matrix to f32 (nib - 8) * d in reference element order. */
+SX_API sx_status sx_dispatch_unpack_q4(sx_engine *e, const void *w_packed, float *out,
+                                       uint32_t m, uint32_t k);
+/* Synthetic reference-layout blocks (BASELINE distributions), rows [row0, row0 + rows). */
+SX_API sx_status sx_dispatch_synth_weights(sx_engine *e, sx_quant_mode mode, uint32_t *ref_out,
+                                           uint32_t row0, uint32_t rows, uint32_t cols,
+                                           uint64_t seed, uint64_t stream_id);
+
+/* ---------------------------------------------------------------------------------------
+ * Model: GpuModelContext (model_gpu.zig:35-197) + gpuDispatchForwardToken
+ * (model_dispatch.zig:131-147) for a Q4_0 model with a Q8_0 LM head.
+ * ------------------------------------------------------------------------------------- */
+typedef struct {
+  uint32_t vocab_size, hidden_size, intermediate_size, num_layers;
+  uint32_t num_q_heads, num_kv_heads, num_global_kv_heads, head_dim, global_head_dim;
+  uint32_t num_anchors, window_size, num_recall;
+  uint32_t kv_bf16;          /* 1: bf16 KV cache (build default), 0: f32 (reference)    */
+  uint32_t has_post_norms;   /* post_attention / post_feedforward layernorms present     */
+  uint32_t full_every;       /* layer l is full attention when (l+1) % full_every == 0  */
+  uint32_t attention_k_eq_v; /* types.zig:58                                            */
+  float rms_norm_eps, rope_theta, rope_theta_full, attn_scale;
+} sx_model_config;
+
+typedef struct sx_model sx_model;
+/* GpuModelContext.init without weights: allocates every device buffer and records the
+ * decode and prefill graphs (model_gpu.zig:75-185). */
+SX_API sx_status sx_model_create(sx_engine *e, const sx_model_config *cfg, sx_model **out);
+SX_API void sx_model_destroy(sx_model *m);
+/* Fill all weights with the synthetic checkpoint (seeded, BASELINE distributions). */
+SX_API sx_status sx_model_synth_weights(sx_model *m, uint64_t seed);
+/* Fill every KV slot with a synthetic past (K = bf16 N(0,1), V unit-RMS). */
+SX_API sx_status sx_model_fill_kv(sx_model *m, uint64_t seed);
+/* gpuDispatchForwardToken (model_dispatch.zig:131-147): host x[hidden], clock, slot and the
+ * active-slot list in; greedy token out (and the logits when logits_out != NULL).
+ * want_logits == 0 runs the prefill graph (no LM head).  Host<->device copies included. */
+SX_API sx_status sx_forward_token(sx_model *m, const float *x, uint32_t clock, uint32_t slot,
+                                  const uint32_t *active_slots, uint32_t n_active,
+                                  int want_logits, uint32_t *token_out, float *logits_out);
+/* Device-resident replay: inputs already in the model's device buffers (sx_model_io). */
+SX_API sx_status sx_model_launch(sx_model *m, int want_logits);
+typedef struct {
+  float *x;            /* device f32[hidden]                  */
+  uint32_t *slots;     /* device u32[total_slots]             */
+  uint32_t *step;      /* device u32[4] {clock, slot, n, 0}   */
+  uint32_t *token;     /* device u32[1]                       */
+  float *logits;       /* device f32[vocab]                   */
+  float *normed;       /* device f32[hidden]                  */
+} sx_model_io;
+SX_API sx_status sx_model_get_io(sx_model *m, sx_model_io *io);
+/* Device pointers of layer weights / caches (tests and benchmarks). */
+SX_API void *sx_model_kcache(sx_model *m, uint32_t layer);
+SX_API void *sx_model_vcache(sx_model *m, uint32_t layer);
+SX_API uint64_t sx_model_weight_bytes(sx_model *m);
+SX_API uint32_t sx_model_kernels_per_token(sx_model *m, int want_logits);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* SX_H */

@@ -1,0 +1,231 @@
+"""Model-level parity on a B200: the record API replaying recordLayerDirect, and whole-token
+greedy decode through sx_forward_token (gpuDispatchForwardToken), against the CPU checker's
+decode in the GPU graph's op order."""
+import ctypes
+import math
+
+import numpy as np
+import pytest
+
+import sx
+from oracle import oracle as orc
+from tests.conftest import assert_close
+
+pytestmark = pytest.mark.gpu
+
+torch = pytest.importorskip("torch")
+
+_libm = ctypes.CDLL("libm.so.6")
+_libm.fmaf.restype = ctypes.c_float
+_libm.fmaf.argtypes = [ctypes.c_float] * 3
+
+
+def tiny_cfg(**kw):
+    cfg = dict(
+        vocab_size=4096, hidden_size=256, intermediate_size=640, num_layers=3,
+        num_q_heads=4, num_kv_heads=2, num_global_kv_heads=2, head_dim=64, global_head_dim=64,
+        num_anchors=4, window_size=8, num_recall=4, kv_bf16=1, has_post_norms=1, full_every=3,
+        attention_k_eq_v=0, rms_norm_eps=1e-6, rope_theta=10000.0, rope_theta_full=1000000.0,
+        attn_scale=1.0,
+    )
+    cfg.update(kw)
+    return cfg
+
+
+def margin_top2(logits):
+    s = np.sort(logits)
+    return float(s[-1] - s[-2])
+
+
+def run_decode(engine, cfg, seed, steps, start_clock, n_recall=0):
+    """Greedy decode on both sides, feeding the GPU's token back to both."""
+    model = sx.Model(engine, sx.model_config(**cfg))
+    model.synth_weights(seed)
+    model.fill_kv(seed)
+    ref = orc.Model(cfg, seed)
+    ref.fill_kv(seed)
+    ring = sx.Ring(1, cfg["num_anchors"], cfg["window_size"], cfg["num_recall"])
+    ring.prefill(0, start_clock)
+    ref.ring.prefill(0, start_clock)
+    rng = np.random.default_rng(seed)
+    for r in range(n_recall):
+        c = int(rng.integers(0, max(start_clock, 1)))
+        ring.write_recall(0, r, c)
+        ref.ring.write_recall(0, r, c)
+    token = 17
+    results = []
+    for t in range(steps):
+        clock = start_clock + t
+        x = sx.synth_embed_row(cfg["hidden_size"], token, seed)
+        assert np.array_equal(x, orc.synth_embed_row(cfg["hidden_size"], token, seed))
+        slot = ring.activate_slot(0, clock)
+        slots = ring.get_active_slots(0, clock)
+        logits = np.zeros(cfg["vocab_size"], np.float32)
+        tok = model.forward_token(x, clock, slot, slots, True, logits)
+        rtok, rlogits, _ = ref.forward(x, clock, True)
+        assert np.array_equal(slots, ref.ring.get_active_slots(0, clock))
+        results.append((tok, rtok, logits, rlogits))
+        token = tok
+    return results
+
+
+@pytest.mark.parametrize("kv_f32", [False, True])
+def test_greedy_decode_matches_checker(engine, engine_f32kv, kv_f32):
+    eng = engine_f32kv if kv_f32 else engine
+    cfg = tiny_cfg(kv_bf16=0 if kv_f32 else 1)
+    res = run_decode(eng, cfg, seed=3, steps=24, start_clock=0)  # window wraps twice
+    for i, (tok, rtok, lg, rlg) in enumerate(res):
+        assert_close(lg, rlg, what=f"logits step {i}")
+        if tok != rtok:
+            assert margin_top2(rlg) < 1e-3, f"step {i}: token {tok} vs {rtok}"
+
+
+def test_greedy_decode_with_recall_and_large_clock(engine):
+    cfg = tiny_cfg()
+    res = run_decode(engine, cfg, seed=9, steps=6, start_clock=90000, n_recall=3)
+    for i, (tok, rtok, lg, rlg) in enumerate(res):
+        assert_close(lg, rlg, what=f"logits step {i}")
+        if tok != rtok:
+            assert margin_top2(rlg) < 1e-3
+
+
+def test_12b_width_two_layers_full_vocab(engine):
+    # 12B layer shapes and full vocabulary with two layers (one sliding, one full attention)
+    cfg = tiny_cfg(vocab_size=262144, hidden_size=3840, intermediate_size=15360, num_layers=2,
+                   num_q_heads=16, num_kv_heads=8, num_global_kv_heads=8, head_dim=256,
+                   global_head_dim=256, num_anchors=32, window_size=512, num_recall=96,
+                   full_every=2)
+    res = run_decode(engine, cfg, seed=5, steps=2, start_clock=5000, n_recall=96)
+    for i, (tok, rtok, lg, rlg) in enumerate(res):
+        assert_close(lg, rlg, what=f"logits step {i}")
+        if tok != rtok:
+            assert margin_top2(rlg) < 1e-3
+
+
+def test_prefill_graph_skips_logits(engine):
+    cfg = tiny_cfg()
+    model = sx.Model(engine, sx.model_config(**cfg))
+    model.synth_weights(1)
+    ring = sx.Ring(1, 4, 8, 4)
+    x = sx.synth_embed_row(256, 3, 1)
+    slot = ring.activate_slot(0, 0)
+    tok = model.forward_token(x, 0, slot, ring.get_active_slots(0, 0), want_logits=False)
+    assert tok == 0
+    assert model.kernels_per_token(False) < model.kernels_per_token(True)
+
+
+def test_forward_token_rejects_oversized_slot_list(engine):
+    cfg = tiny_cfg()
+    model = sx.Model(engine, sx.model_config(**cfg))
+    with pytest.raises(sx.SxError):
+        model.forward_token(np.zeros(256, np.float32), 0, 0, np.zeros(100, np.uint32))
+
+
+def test_record_api_layer_matches_checker(engine):
+    """recordLayerDirect (model_dispatch.zig:10-43) written with the record API directly,
+    bound like model_gpu.zig:140-156, against one checker layer."""
+    cfg = tiny_cfg(num_layers=1, full_every=0)
+    seed, clock = 4, 30
+    H, I, D, nq, nkv = 256, 640, 64, 4, 2
+    qd, kvd, total = nq * D, nkv * D, 16
+    eps = cfg["rms_norm_eps"]
+    E = engine
+
+    def stream(kind):
+        return 64 + kind
+
+    def buf_f32(arr):
+        b = E.buffer(arr.nbytes)
+        b.write(arr.astype(np.float32))
+        return b
+
+    def wbuf(rows, cols, kind):
+        b = E.buffer(sx.packed_bytes(rows, cols, sx.QUANT_Q4))
+        b.upload_weights(orc.synth_q4(rows, cols, seed, stream(kind)), rows, cols, sx.QUANT_Q4)
+        return b
+
+    x0 = sx.synth_embed_row(H, 21, seed)
+    x = buf_f32(x0)
+    normed, q = E.buffer(4 * H), E.buffer(4 * qd)
+    k, v, attn = E.buffer(4 * kvd), E.buffer(4 * kvd), E.buffer(4 * qd)
+    act, mlp = E.buffer(4 * I), E.buffer(4 * H)
+    kc, vc = E.buffer(2 * total * kvd), E.buffer(2 * total * kvd)
+    in_norm = buf_f32(orc.synth_gain(H, seed, stream(0)))
+    qn, kn = buf_f32(orc.synth_gain(D, seed, stream(5))), buf_f32(orc.synth_gain(D, seed, stream(6)))
+    post_attn = buf_f32(orc.synth_gain(H, seed, stream(7)))
+    pre_ffn = buf_f32(orc.synth_gain(H, seed, stream(8)))
+    post_ffn = buf_f32(orc.synth_gain(H, seed, stream(12)))
+    wq, wk, wv = wbuf(qd, H, 1), wbuf(kvd, H, 2), wbuf(kvd, H, 3)
+    wo, wg, wu, wd = wbuf(H, qd, 4), wbuf(I, H, 9), wbuf(I, H, 10), wbuf(H, I, 11)
+    z = orc.synth_normal(seed, stream(13), 0)
+    scalar = orc.bf16_round(np.array([_libm.fmaf(0.05, z, 1.0)], np.float32))[0]
+
+    ring = sx.Ring(1, 4, 8, 4)
+    ring.prefill(0, clock)
+    slot = ring.activate_slot(0, clock)
+    slots = ring.get_active_slots(0, clock)
+    slot_buf = E.buffer(4 * total)
+    slot_buf.write(np.concatenate([slots, np.zeros(total - len(slots), np.uint32)]))
+    step = E.buffer(16)
+    step.write(np.array([clock, slot, len(slots), 0], np.uint32))
+
+    S = E.set
+    cmd = E.command_buffer()
+    cmd.begin()
+    E.record_rmsnorm(cmd, S(x, in_norm, normed), H, eps)
+    E.record_barrier(cmd)
+    E.record_gemv(cmd, S(wq, normed, q), qd, H)
+    E.record_gemv(cmd, S(wk, normed, k), kvd, H)
+    E.record_gemv(cmd, S(wv, normed, v), kvd, H)
+    E.record_barrier(cmd)
+    E.record_qkv_rope(cmd, S(q, k, v, qn, kn, q, kc, vc, step), nq, nkv, D, D, 0,
+                      cfg["rope_theta"], eps, total)
+    E.record_barrier(cmd)
+    E.record_decode_attn(cmd, S(q, kc, vc, slot_buf, attn, step), D, kvd, nq // nkv, 1.0, nq,
+                         total)
+    E.record_barrier(cmd)
+    E.record_gemv(cmd, S(wo, attn, mlp), H, qd)
+    E.record_rmsnorm(cmd, S(mlp, post_attn, mlp), H, eps)
+    E.record_add_rmsnorm(cmd, S(x, mlp, pre_ffn, normed), H, eps, 1.0)
+    E.record_gate_up(cmd, S(wg, wu, normed, act), I, H)
+    E.record_gemv(cmd, S(wd, act, mlp), H, I)
+    E.record_rmsnorm(cmd, S(mlp, post_ffn, mlp), H, eps)
+    E.record_add_rmsnorm(cmd, S(x, mlp, in_norm, normed), H, eps, float(scalar))
+    E.record_barrier(cmd)
+    cmd.end()
+    E.submit_pre_recorded(cmd)
+    got = x.read(np.float32, H)
+
+    ref = orc.Model(cfg, seed)
+    ref.ring.prefill(0, clock)
+    _, _, rx = ref.forward(x0, clock, want_logits=False)
+    assert_close(got, rx, what="residual after one layer")
+
+
+def test_record_on_unbegun_command_buffer_fails_at_end(engine):
+    cmd = engine.command_buffer()
+    b = engine.buffer(64)
+    engine.record_rmsnorm(cmd, engine.set(b, b, b), 16, 1e-6)  # not recording yet
+    cmd.begin()
+    engine.record_rmsnorm(cmd, engine.set(b, b), 16, 1e-6)  # too few buffers
+    with pytest.raises(sx.SxError):
+        cmd.end()
+
+
+def test_submit_deadline_returns_timeout_not_hang(engine):
+    """submitPreRecorded's bounded fence wait (kernels.zig:151-156): a deadline that cannot be
+    met returns SX_ERR_TIMEOUT instead of blocking; the work still completes afterwards."""
+    m, k = 262144, 3840
+    E = engine
+    w = E.buffer(sx.packed_bytes(m, k, sx.QUANT_Q8))
+    x, y = E.buffer(4 * k), E.buffer(4 * m)
+    cmd = E.command_buffer()
+    cmd.begin()
+    for _ in range(8):
+        E.record_gemv_logits(cmd, E.set(w, x, y), m, k)
+    cmd.end()
+    with pytest.raises(sx.SxError) as ei:
+        E.submit_pre_recorded(cmd, timeout_ns=1000)
+    assert ei.value.status == sx.SX_ERR_TIMEOUT
+    E.sync()
+    E.submit_pre_recorded(cmd)  # default 5 s deadline is met
