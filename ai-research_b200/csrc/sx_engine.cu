@@ -107,6 +107,8 @@ sx_status do_gemv(sx_engine *e, cudaStream_t s, int qt, bool geglu, const void *
   if (st != SX_OK) return st;
   SX_CHECK_ARG(qt == 4 || qt == 8, "gemv: unsupported quant mode (bf16 GEMV is not built)");
   SX_CHECK_ARG(w0 && x && y && (!geglu || w1), "gemv: null pointer");
+  SX_CHECK_ARG(((uintptr_t)w0 | (uintptr_t)(geglu ? w1 : w0)) % 16 == 0,
+               "gemv: packed weights must be 16-byte aligned");
   sx::GemvArgs a{w0, w1, x, y, m, k, batch, k, m};
   return cuda_status(sx::launch_gemv(qt, geglu, a, e->num_sms, s), "gemv launch");
 }
@@ -147,6 +149,9 @@ sx_status do_attn(sx_engine *e, cudaStream_t s, const float *q, const void *kc, 
   SX_CHECK_ARG(num_q % gqa == 0 && (num_q / gqa) * head_dim <= kv_dim,
                "decode_attn: num_q_heads/gqa_ratio kv heads do not fit kv_dim");
   SX_CHECK_ARG(total_slots > 0, "decode_attn: total_slots must be > 0");
+  SX_CHECK_ARG(q && kc && vc && slots && step && out, "decode_attn: null pointer");
+  SX_CHECK_ARG(((uintptr_t)kc | (uintptr_t)vc) % 16 == 0 && kv_dim % 8 == 0,
+               "decode_attn: caches must be 16-byte aligned with kv_dim a multiple of 8");
   size_t need = sx::attn_scratch_bytes(num_q, total_slots, head_dim);
   if (need + sx::argmax_scratch_bytes() > e->scratch_bytes) {
     set_error("decode_attn: needs %zu B scratch, engine has %zu", need, e->scratch_bytes);
@@ -167,7 +172,7 @@ sx_status do_argmax(sx_engine *e, cudaStream_t s, const float *logits, uint32_t 
                      "argmax launch");
 }
 
-void *bp(sx_set *s, size_t i) { return s->b[i]->d; }
+
 
 sx_status run_op(sx_engine *e, cudaStream_t s, const Op &op, uint32_t *kernels) {
   switch (op.kind) {
@@ -175,37 +180,37 @@ sx_status run_op(sx_engine *e, cudaStream_t s, const Op &op, uint32_t *kernels) 
     case OP_GEMV_LOGITS: {
       int qt = op.kind == OP_GEMV_LOGITS ? 8 : qt_of(e->mode);
       *kernels += 1;
-      return do_gemv(e, s, qt, false, bp(op.set, 0), nullptr, (const float *)bp(op.set, 1),
-                     (float *)bp(op.set, 2), op.u[0], op.u[1], 1);
+      return do_gemv(e, s, qt, false, op.bind.at(0), nullptr, (const float *)op.bind.at(1),
+                     (float *)op.bind.at(2), op.u[0], op.u[1], 1);
     }
     case OP_GATE_UP:
       *kernels += 1;
-      return do_gemv(e, s, qt_of(e->mode), true, bp(op.set, 0), bp(op.set, 1),
-                     (const float *)bp(op.set, 2), (float *)bp(op.set, 3), op.u[0], op.u[1], 1);
+      return do_gemv(e, s, qt_of(e->mode), true, op.bind.at(0), op.bind.at(1),
+                     (const float *)op.bind.at(2), (float *)op.bind.at(3), op.u[0], op.u[1], 1);
     case OP_ADD_RMSNORM:
       *kernels += 1;
-      return do_norm(s, true, (float *)bp(op.set, 0), (const float *)bp(op.set, 1),
-                     (const float *)bp(op.set, 2), (float *)bp(op.set, 3), op.u[0], 1, op.f[0],
+      return do_norm(s, true, (float *)op.bind.at(0), (const float *)op.bind.at(1),
+                     (const float *)op.bind.at(2), (float *)op.bind.at(3), op.u[0], 1, op.f[0],
                      op.f[1]);
     case OP_RMSNORM:
       *kernels += 1;
-      return do_norm(s, false, (float *)bp(op.set, 0), nullptr, (const float *)bp(op.set, 1),
-                     (float *)bp(op.set, 2), op.u[0], 1, op.f[0], 1.0f);
+      return do_norm(s, false, (float *)op.bind.at(0), nullptr, (const float *)op.bind.at(1),
+                     (float *)op.bind.at(2), op.u[0], 1, op.f[0], 1.0f);
     case OP_ATTN:
       *kernels += 2;
-      return do_attn(e, s, (const float *)bp(op.set, 0), bp(op.set, 1), bp(op.set, 2),
-                     (const uint32_t *)bp(op.set, 3), (const uint32_t *)bp(op.set, 5),
-                     (float *)bp(op.set, 4), op.u[0], op.u[1], op.u[2], op.f[0], op.u[3], op.u[4]);
+      return do_attn(e, s, (const float *)op.bind.at(0), op.bind.at(1), op.bind.at(2),
+                     (const uint32_t *)op.bind.at(3), (const uint32_t *)op.bind.at(5),
+                     (float *)op.bind.at(4), op.u[0], op.u[1], op.u[2], op.f[0], op.u[3], op.u[4]);
     case OP_QKV_ROPE:
       *kernels += 1;
-      return do_qkv_rope(e, s, (const float *)bp(op.set, 0), (const float *)bp(op.set, 1),
-                         (const float *)bp(op.set, 2), (const float *)bp(op.set, 3),
-                         (const float *)bp(op.set, 4), (float *)bp(op.set, 5), bp(op.set, 6),
-                         bp(op.set, 7), (const uint32_t *)bp(op.set, 8), op.u[0], op.u[1],
+      return do_qkv_rope(e, s, (const float *)op.bind.at(0), (const float *)op.bind.at(1),
+                         (const float *)op.bind.at(2), (const float *)op.bind.at(3),
+                         (const float *)op.bind.at(4), (float *)op.bind.at(5), op.bind.at(6),
+                         op.bind.at(7), (const uint32_t *)op.bind.at(8), op.u[0], op.u[1],
                          op.u[2], op.u[3], op.u[4], op.f[0], op.f[1], op.u[5]);
     case OP_ARGMAX:
       *kernels += 2;
-      return do_argmax(e, s, (const float *)bp(op.set, 0), op.u[0], (uint32_t *)bp(op.set, 1));
+      return do_argmax(e, s, (const float *)op.bind.at(0), op.u[0], (uint32_t *)op.bind.at(1));
     case OP_H2D:
       return cuda_status(cudaMemcpyAsync(op.dev, op.host, op.bytes, cudaMemcpyHostToDevice, s),
                          "h2d copy");
@@ -458,6 +463,10 @@ SX_API sx_status sx_engine_create(int device, sx_quant_mode mode, uint32_t flags
     if (st) break;
     e->scratch_bytes = 32u << 20;
     st = cuda_status(cudaMalloc(&e->scratch, e->scratch_bytes), "engine scratch");
+    if (st) break;
+    st = cuda_status(sx::prepare_gemv_kernels(), "gemv kernel attributes");
+    if (st) break;
+    st = cuda_status(sx::prepare_ops_kernels(), "attention kernel attributes");
   } while (0);
   if (st != SX_OK) {
     sx_engine_destroy(e);
@@ -649,6 +658,12 @@ SX_API sx_status sx_cmd_end(sx_cmd *c) {
   }
   sx_engine *e = c->e;
   SX_TRY_CUDA(cudaSetDevice(e->device), "cudaSetDevice");
+  // device-side tables are created before capture (no allocation inside a capture)
+  for (const Op &op : c->ops) {
+    if (op.kind != OP_QKV_ROPE) continue;
+    sx_status fst = SX_OK;
+    if (!engine_inv_freq(e, op.u[3], op.f[0], &fst)) return fst;
+  }
   cudaStream_t cs = e->capture_stream;
   SX_TRY_CUDA(cudaStreamBeginCapture(cs, cudaStreamCaptureModeThreadLocal), "begin capture");
   sx_status st = SX_OK;
@@ -680,70 +695,66 @@ SX_API sx_status sx_cmd_end(sx_cmd *c) {
 }
 
 extern "C++" void sx_host_push_op(sx_cmd *c, const Op &op) { c->ops.push_back(op); }
-static void push_op(sx_cmd *c, const Op &op) { sx_host_push_op(c, op); }
+static void push_op(sx_cmd *c, Op op, sx_set *set) {
+  for (sx_buffer *b : set->b) op.bind.push_back(b ? b->d : nullptr);
+  sx_host_push_op(c, op);
+}
 
 SX_API void sx_record_gemv(sx_engine *e, sx_cmd *c, sx_set *set, uint32_t m, uint32_t k) {
   if (!record_guard(e, c, set, 3, "record_gemv")) return;
   Op op{OP_GEMV};
-  op.set = set;
   op.u[0] = m;
   op.u[1] = k;
-  push_op(c, op);
+  push_op(c, op, set);
 }
 SX_API void sx_record_gemv_logits(sx_engine *e, sx_cmd *c, sx_set *set, uint32_t m, uint32_t k) {
   if (!record_guard(e, c, set, 3, "record_gemv_logits")) return;
   Op op{OP_GEMV_LOGITS};
-  op.set = set;
   op.u[0] = m;
   op.u[1] = k;
-  push_op(c, op);
+  push_op(c, op, set);
 }
 SX_API void sx_record_gate_up(sx_engine *e, sx_cmd *c, sx_set *set, uint32_t m, uint32_t k) {
   if (!record_guard(e, c, set, 4, "record_gate_up")) return;
   Op op{OP_GATE_UP};
-  op.set = set;
   op.u[0] = m;
   op.u[1] = k;
-  push_op(c, op);
+  push_op(c, op, set);
 }
 SX_API void sx_record_add_rmsnorm(sx_engine *e, sx_cmd *c, sx_set *set, uint32_t h, float eps,
                                   float scalar) {
   if (!record_guard(e, c, set, 4, "record_add_rmsnorm")) return;
   Op op{OP_ADD_RMSNORM};
-  op.set = set;
   op.u[0] = h;
   op.f[0] = eps;
   op.f[1] = scalar;
-  push_op(c, op);
+  push_op(c, op, set);
 }
 SX_API void sx_record_rmsnorm(sx_engine *e, sx_cmd *c, sx_set *set, uint32_t h, float eps) {
   if (!record_guard(e, c, set, 3, "record_rmsnorm")) return;
   Op op{OP_RMSNORM};
-  op.set = set;
   op.u[0] = h;
   op.f[0] = eps;
-  push_op(c, op);
+  push_op(c, op, set);
 }
 SX_API void sx_record_decode_attn(sx_engine *e, sx_cmd *c, sx_set *set, uint32_t head_dim,
                                   uint32_t kv_dim, uint32_t gqa_ratio, float inv_sqrt_dim,
                                   uint32_t num_q_heads, uint32_t total_slots) {
   if (!record_guard(e, c, set, 6, "record_decode_attn")) return;
   Op op{OP_ATTN};
-  op.set = set;
   op.u[0] = head_dim;
   op.u[1] = kv_dim;
   op.u[2] = gqa_ratio;
   op.u[3] = num_q_heads;
   op.u[4] = total_slots;
   op.f[0] = inv_sqrt_dim;
-  push_op(c, op);
+  push_op(c, op, set);
 }
 SX_API void sx_record_qkv_rope(sx_engine *e, sx_cmd *c, sx_set *set, uint32_t num_q,
                                uint32_t num_kv, uint32_t head_dim, uint32_t rotary_dim,
                                uint32_t k_eq_v, float theta, float eps, uint32_t total_slots) {
   if (!record_guard(e, c, set, 9, "record_qkv_rope")) return;
   Op op{OP_QKV_ROPE};
-  op.set = set;
   op.u[0] = num_q;
   op.u[1] = num_kv;
   op.u[2] = head_dim;
@@ -752,14 +763,13 @@ SX_API void sx_record_qkv_rope(sx_engine *e, sx_cmd *c, sx_set *set, uint32_t nu
   op.u[5] = total_slots;
   op.f[0] = theta;
   op.f[1] = eps;
-  push_op(c, op);
+  push_op(c, op, set);
 }
 SX_API void sx_record_argmax(sx_engine *e, sx_cmd *c, sx_set *set, uint32_t vocab) {
   if (!record_guard(e, c, set, 2, "record_argmax")) return;
   Op op{OP_ARGMAX};
-  op.set = set;
   op.u[0] = vocab;
-  push_op(c, op);
+  push_op(c, op, set);
 }
 SX_API void sx_record_barrier(sx_engine *e, sx_cmd *c) {
   // Ops in one command buffer execute in stream order; the barrier is implicit.

@@ -287,9 +287,6 @@ template <int QT, int NMAT, int NSETS>
 cudaError_t launch_t(const GemvArgs &a, int num_sms, cudaStream_t s) {
   const SmemLayout L = smem_layout(a.k, a.batch, NMAT);
   auto kern = gemv_kernel<QT, NMAT, NSETS>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       (int)L.total);
-  if (e != cudaSuccess) return e;
   uint32_t T = tiles_of(a.m);
   uint32_t cap = (uint32_t)num_sms * 8;
   uint32_t grid = T < cap ? T : cap;
@@ -297,7 +294,23 @@ cudaError_t launch_t(const GemvArgs &a, int num_sms, cudaStream_t s) {
   return cudaGetLastError();
 }
 
+template <int QT, int NMAT, int NSETS>
+cudaError_t prepare_t() {
+  return cudaFuncSetAttribute(gemv_kernel<QT, NMAT, NSETS>,
+                              cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+}
+
 }  // namespace
+
+cudaError_t prepare_gemv_kernels() {
+  cudaError_t e = cudaSuccess;
+  cudaError_t r[8] = {prepare_t<4, 1, 1>(), prepare_t<4, 1, 2>(), prepare_t<4, 2, 1>(),
+                      prepare_t<4, 2, 2>(), prepare_t<8, 1, 1>(), prepare_t<8, 1, 2>(),
+                      prepare_t<8, 2, 1>(), prepare_t<8, 2, 2>()};
+  for (cudaError_t x : r)
+    if (x != cudaSuccess) e = x;
+  return e;
+}
 
 size_t gemv_smem_bytes(int qt, uint32_t k, uint32_t batch) {
   (void)qt;

@@ -56,7 +56,9 @@ enum OpKind {
 
 struct Op {
   OpKind kind;
-  sx_set *set = nullptr;
+  // device addresses of the bound buffers, copied from the descriptor set when the op is
+  // recorded (the set itself may be destroyed afterwards; the buffers must stay alive)
+  std::vector<void *> bind;
   uint32_t u[8] = {0, 0, 0, 0, 0, 0, 0, 0};
   float f[4] = {0, 0, 0, 0};
   void *host = nullptr;    // OP_H2D / OP_D2H

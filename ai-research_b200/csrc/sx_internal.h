@@ -15,6 +15,11 @@ struct GemvArgs {
   uint32_t ldx, ldy;
 };
 
+// Per-device kernel attributes (dynamic shared memory limits); called at engine creation,
+// never inside a stream capture.
+cudaError_t prepare_gemv_kernels();
+cudaError_t prepare_ops_kernels();
+
 // qt: 4 or 8.  geglu: fused gate+up with gelu_tanh(gate) * up epilogue.
 cudaError_t launch_gemv(int qt, bool geglu, const GemvArgs &a, int num_sms, cudaStream_t s);
 size_t gemv_smem_bytes(int qt, uint32_t k, uint32_t batch);

@@ -120,26 +120,44 @@ __global__ void __launch_bounds__(128) qkv_rope_kernel(QkvRopeArgs a) {
 constexpr int kAttnChunk = 32;
 constexpr int kAttnWarps = 4;
 
+// Lane `lane` owns elements [lane*DPL, lane*DPL + DPL) of a head row; the load width matches
+// DPL so every access is naturally aligned (DPL*2 or DPL*4 bytes per lane).
 template <int DPL, bool BF16>
 SX_DEV void load_row(const void *cache, size_t off, int lane, float (&v)[DPL]) {
   if (BF16) {
-    const uint16_t *p = reinterpret_cast<const uint16_t *>(cache) + off + lane * DPL;
+    const uint16_t *p = reinterpret_cast<const uint16_t *>(cache) + off + (size_t)lane * DPL;
+    if constexpr (DPL % 8 == 0) {
 #pragma unroll
-    for (int i = 0; i < DPL; i += 8) {
-      uint4 u = *reinterpret_cast<const uint4 *>(p + i);
-      uint32_t w[4] = {u.x, u.y, u.z, u.w};
+      for (int i = 0; i < DPL; i += 8) {
+        uint4 u = *reinterpret_cast<const uint4 *>(p + i);
+        uint32_t w[4] = {u.x, u.y, u.z, u.w};
 #pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        v[i + 2 * k] = u2f(w[k] << 16);
-        v[i + 2 * k + 1] = u2f(w[k] & 0xFFFF0000u);
+        for (int k = 0; k < 4; ++k) {
+          v[i + 2 * k] = u2f(w[k] << 16);
+          v[i + 2 * k + 1] = u2f(w[k] & 0xFFFF0000u);
+        }
       }
+    } else if constexpr (DPL == 4) {
+      uint2 u = *reinterpret_cast<const uint2 *>(p);
+      v[0] = u2f(u.x << 16); v[1] = u2f(u.x & 0xFFFF0000u);
+      v[2] = u2f(u.y << 16); v[3] = u2f(u.y & 0xFFFF0000u);
+    } else {
+      static_assert(DPL == 2, "head_dim must be 64, 128, 256 or 512");
+      uint32_t u = *reinterpret_cast<const uint32_t *>(p);
+      v[0] = u2f(u << 16); v[1] = u2f(u & 0xFFFF0000u);
     }
   } else {
-    const float *p = reinterpret_cast<const float *>(cache) + off + lane * DPL;
+    const float *p = reinterpret_cast<const float *>(cache) + off + (size_t)lane * DPL;
+    if constexpr (DPL % 4 == 0) {
 #pragma unroll
-    for (int i = 0; i < DPL; i += 4) {
-      float4 u = *reinterpret_cast<const float4 *>(p + i);
-      v[i] = u.x; v[i + 1] = u.y; v[i + 2] = u.z; v[i + 3] = u.w;
+      for (int i = 0; i < DPL; i += 4) {
+        float4 u = *reinterpret_cast<const float4 *>(p + i);
+        v[i] = u.x; v[i + 1] = u.y; v[i + 2] = u.z; v[i + 3] = u.w;
+      }
+    } else {
+      static_assert(DPL == 2, "head_dim must be 64, 128, 256 or 512");
+      float2 u = *reinterpret_cast<const float2 *>(p);
+      v[0] = u.x; v[1] = u.y;
     }
   }
 }
@@ -259,14 +277,29 @@ cudaError_t launch_attn_t(const AttnArgs &a, cudaStream_t s) {
   size_t smem = sizeof(float) * (G * a.head_dim + 2 * kAttnWarps * G +
                                  (size_t)kAttnWarps * G * a.head_dim);
   auto kern = a.kv_bf16 ? attn_split_kernel<DPL, G, true> : attn_split_kernel<DPL, G, false>;
-  cudaError_t e =
-      cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  if (e != cudaSuccess) return e;
   kern<<<dim3(num_kv, nchunks), kAttnWarps * 32, smem, s>>>(a);
-  e = cudaGetLastError();
+  cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   attn_combine_kernel<<<a.num_q, 256, 0, s>>>(a, nchunks);
   return cudaGetLastError();
+}
+
+template <int DPL, int G>
+cudaError_t prepare_attn_t() {
+  cudaError_t a = cudaFuncSetAttribute(attn_split_kernel<DPL, G, true>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+  cudaError_t b = cudaFuncSetAttribute(attn_split_kernel<DPL, G, false>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+  return a != cudaSuccess ? a : b;
+}
+
+template <int DPL>
+cudaError_t prepare_attn_d() {
+  cudaError_t r[4] = {prepare_attn_t<DPL, 1>(), prepare_attn_t<DPL, 2>(),
+                      prepare_attn_t<DPL, 4>(), prepare_attn_t<DPL, 8>()};
+  for (cudaError_t x : r)
+    if (x != cudaSuccess) return x;
+  return cudaSuccess;
 }
 
 template <int DPL>
@@ -368,6 +401,14 @@ __global__ void argmax_final_kernel(const float *x, const float2 *part, uint32_t
 }
 
 }  // namespace
+
+cudaError_t prepare_ops_kernels() {
+  cudaError_t r[4] = {prepare_attn_d<2>(), prepare_attn_d<4>(), prepare_attn_d<8>(),
+                      prepare_attn_d<16>()};
+  for (cudaError_t x : r)
+    if (x != cudaSuccess) return x;
+  return cudaSuccess;
+}
 
 cudaError_t launch_rmsnorm(bool add, const NormArgs &a, cudaStream_t s) {
   uint32_t threads = a.n >= 1024 ? 1024 : ((a.n + 31) / 32) * 32;

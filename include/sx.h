@@ -131,7 +131,9 @@ SX_API sx_status sx_buffer_repack_device(sx_buffer *dst, const void *ref_words_d
                                          uint32_t rows, uint32_t cols, sx_quant_mode mode);
 
 /* DescriptorManager.allocateSet + bindBuffers (descriptors.zig:27-103): an ordered tuple of
- * buffers; aliasing allowed (model_gpu.zig:144,153-154). */
+ * buffers; aliasing allowed (model_gpu.zig:144,153-154).  A record call copies the set's
+ * device addresses, so the set may be destroyed after recording; the buffers themselves must
+ * outlive every command buffer that uses them. */
 SX_API sx_status sx_set_create(sx_engine *e, sx_buffer *const *buffers, uint32_t count,
                                sx_set **out);
 SX_API void sx_set_destroy(sx_set *s);
