@@ -197,6 +197,10 @@ _SIGS = {
         [_P, _P, _P, _P, _P, _P, _P, _U32, _U32, _U32, _F, _U32, _U32],
     ),
     "sx_dispatch_argmax": (_S, [_P, _P, _U32, _P]),
+    "sx_decode_attn_noalloc": (
+        _S,
+        [_P, _P, _P, _P, _P, _P, _U32, _U32, _U32, _F, _U32, _U32, _U32, _P],
+    ),
     "sx_dispatch_unpack_q4": (_S, [_P, _P, _P, _U32, _U32]),
     "sx_dispatch_synth_weights": (_S, [_P, _I, _P, _U32, _U32, _U32, _U64, _U64]),
     "sx_model_create": (_S, [_P, C.POINTER(ModelConfig), C.POINTER(_P)]),

@@ -213,6 +213,24 @@ SX_API sx_status sx_dispatch_decode_attn(sx_engine *e, const float *q, const voi
                                          uint32_t total_slots);
 SX_API sx_status sx_dispatch_argmax(sx_engine *e, const float *logits, uint32_t n,
                                     uint32_t *out_token);
+/* No counterpart in the reference.  Decode attention that allocates nothing, for callers that
+ * may not call cudaMalloc while serving (device memory owned by another allocator or a fixed
+ * arena, or allocation forbidden after start-up) and so cannot create an engine.  Same math and
+ * arguments as sx_dispatch_decode_attn plus the KV precision (kv_bf16: 1 bf16, 0 f32) and the
+ * cudaStream_t to run on.  Its split-over-slots partials live in a fixed 1 MiB array inside
+ * the library's device image, held by every GPU that loads libsx until the process exits:
+ * requests needing num_q_heads * ceil(total_slots / 32) * (head_dim + 2) * 4 bytes above 1 MiB
+ * are rejected with SX_ERR_INVALID.  The first call on a device looks the array's address up
+ * (cudaGetSymbolAddress) and sets kernel attributes, so make that first call outside any stream
+ * capture.  All calls share the array: calls whose GPU work overlaps (different streams, or
+ * threads) race on it.  Every partial is written before it is read, so nothing in it needs to
+ * start at zero.  Device-side slot checks skip bad slots but have no error word to report to. */
+SX_API sx_status sx_decode_attn_noalloc(const float *q, const void *k_cache, const void *v_cache,
+                                        const uint32_t *active_slots,
+                                        const uint32_t *step_params, float *out,
+                                        uint32_t head_dim, uint32_t kv_dim, uint32_t gqa_ratio,
+                                        float scale, uint32_t num_q_heads, uint32_t total_slots,
+                                        uint32_t kv_bf16, void *cuda_stream);
 /* Dequantise a packed Q4 matrix to f32 (nib - 8) * d in reference element order. */
 SX_API sx_status sx_dispatch_unpack_q4(sx_engine *e, const void *w_packed, float *out,
                                        uint32_t m, uint32_t k);
