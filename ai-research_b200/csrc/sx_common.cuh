@@ -199,6 +199,45 @@ SX_DEV float block_sum(float v, float *red) {
   return t;
 }
 
+// ---------------------------------------------------------------------------
+// mbarrier + bulk async copy (TMA, non-tensor form).  Waits are bounded: a wait that does
+// not complete within ~1 s of SM clock returns false instead of spinning forever.
+SX_DEV uint32_t smem_u32(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
+SX_DEV void mbar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;\n" ::"r"(bar), "r"(count) : "memory");
+}
+SX_DEV void fence_mbar_init() { asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory"); }
+SX_DEV void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory"); }
+SX_DEV void mbar_arrive_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(bar), "r"(bytes)
+               : "memory");
+}
+SX_DEV bool mbar_try_wait(uint32_t bar, uint32_t phase) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+      " selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(bar), "r"(phase)
+      : "memory");
+  return ok != 0;
+}
+constexpr long long kWaitCycles = 2000000000ll;  // ~1 s at 1.9 GHz
+SX_DEV bool mbar_wait_bounded(uint32_t bar, uint32_t phase) {
+  if (mbar_try_wait(bar, phase)) return true;
+  long long t0 = clock64();
+  while (!mbar_try_wait(bar, phase))
+    if (clock64() - t0 > kWaitCycles) return false;
+  return true;
+}
+// global -> shared bulk copy completing on an mbarrier (16-B aligned, size % 16 == 0)
+SX_DEV void bulk_g2s(uint32_t dst, const void *src, uint32_t bytes, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n" ::"r"(dst),
+      "l"(src), "r"(bytes), "r"(bar)
+      : "memory");
+}
+
 // Programmatic dependent launch: wait for the producer grid's memory before reading it.
 SX_DEV void pdl_wait() { asm volatile("griddepcontrol.wait;\n" ::: "memory"); }
 SX_DEV void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;\n" ::); }

@@ -62,6 +62,20 @@ sx_status cuda_status(cudaError_t e, const char *what) {
 }  // namespace
 
 void sx_host_set_error(const char *msg) { g_last_error = msg; }
+
+void sx_host_bind_scratch(sx_engine *e, sx::GemvArgs &a) {
+  a.part = e->gemv_part;
+  a.tile_cnt = e->tile_cnt;
+  a.best_v = e->best_v;
+  a.best_i = e->best_i;
+  a.done_cnt = e->done_cnt;
+  a.err = e->err_dev;
+}
+void sx_host_bind_scratch(sx_engine *e, sx::AttnFusedArgs &a) {
+  a.part = e->attn_part;
+  a.cnt = e->attn_cnt;
+  a.err = e->err_dev;
+}
 sx_status sx_host_cuda_status(cudaError_t e, const char *what) { return cuda_status(e, what); }
 
 namespace {
@@ -87,12 +101,20 @@ float *engine_inv_freq(sx_engine *e, uint32_t rot, float theta, sx_status *st) {
   return d;
 }
 
+}  // namespace
+float *sx_host_inv_freq(sx_engine *e, uint32_t rot, float theta, sx_status *st) {
+  return engine_inv_freq(e, rot, theta, st);
+}
+namespace {
+
 int qt_of(sx_quant_mode m) { return m == SX_QUANT_Q4 ? 4 : m == SX_QUANT_Q8 ? 8 : 0; }
 
-sx_status check_gemv_shape(uint32_t m, uint32_t k, uint32_t batch) {
+sx_status check_gemv_shape(int qt, bool geglu, bool pro, uint32_t m, uint32_t k,
+                           uint32_t batch) {
   SX_CHECK_ARG(m > 0 && k > 0 && (k % 32) == 0, "gemv: need m > 0 and k a multiple of 32 (m=%u k=%u)", m, k);
   SX_CHECK_ARG(batch >= 1 && batch <= 8, "gemv: batch must be 1..8 (got %u)", batch);
-  size_t smem = sx::gemv_smem_bytes(4, k, batch);
+  SX_CHECK_ARG(sx::tiles_of(m) <= sx::kMaxGemvTiles, "gemv: at most %u rows", sx::kMaxGemvTiles * 16);
+  size_t smem = sx::gemv_smem_bytes(qt, k, batch, geglu, pro);
   if (smem > 227 * 1024) {
     set_error("gemv: k=%u with batch %u needs %zu B of shared memory (max 227 KB)", k, batch, smem);
     return SX_ERR_UNSUPPORTED;
@@ -100,17 +122,37 @@ sx_status check_gemv_shape(uint32_t m, uint32_t k, uint32_t batch) {
   return SX_OK;
 }
 
+}  // namespace
+sx_status sx_host_check_gemv(int qt, bool geglu, bool pro, uint32_t m, uint32_t k,
+                             uint32_t batch) {
+  return check_gemv_shape(qt, geglu, pro, m, k, batch);
+}
+namespace {
+
 sx_status do_gemv(sx_engine *e, cudaStream_t s, int qt, bool geglu, const void *w0,
                   const void *w1, const float *x, float *y, uint32_t m, uint32_t k,
                   uint32_t batch) {
-  sx_status st = check_gemv_shape(m, k, batch);
-  if (st != SX_OK) return st;
   SX_CHECK_ARG(qt == 4 || qt == 8, "gemv: unsupported quant mode (bf16 GEMV is not built)");
+  sx_status st = check_gemv_shape(qt, geglu, false, m, k, batch);
+  if (st != SX_OK) return st;
   SX_CHECK_ARG(w0 && x && y && (!geglu || w1), "gemv: null pointer");
   SX_CHECK_ARG(((uintptr_t)w0 | (uintptr_t)(geglu ? w1 : w0)) % 16 == 0,
                "gemv: packed weights must be 16-byte aligned");
-  sx::GemvArgs a{w0, w1, x, y, m, k, batch, k, m};
-  return cuda_status(sx::launch_gemv(qt, geglu, a, e->num_sms, s), "gemv launch");
+  sx::GemvArgs a{};
+  a.w[0][0] = w0;
+  a.w[0][1] = geglu ? w1 : w0;
+  a.y[0] = y;
+  a.rows[0] = m;
+  a.tiles[0] = sx::tiles_of(m);
+  a.k = k;
+  a.batch = batch;
+  a.ldy = m;
+  a.x = x;
+  a.ldx = k;
+  a.pro = sx::kProNone;
+  a.epi = sx::kEpiPlain;
+  sx_host_bind_scratch(e, a);
+  return cuda_status(sx::launch_gemv(qt, geglu, a, e->num_sms, s, true), "gemv launch");
 }
 
 sx_status do_norm(cudaStream_t s, bool add, float *x, const float *r, const float *w, float *y,
@@ -153,11 +195,11 @@ sx_status do_attn(sx_engine *e, cudaStream_t s, const float *q, const void *kc, 
   SX_CHECK_ARG(((uintptr_t)kc | (uintptr_t)vc) % 16 == 0 && kv_dim % 8 == 0,
                "decode_attn: caches must be 16-byte aligned with kv_dim a multiple of 8");
   size_t need = sx::attn_scratch_bytes(num_q, total_slots, head_dim);
-  if (need + sx::argmax_scratch_bytes() > e->scratch_bytes) {
-    set_error("decode_attn: needs %zu B scratch, engine has %zu", need, e->scratch_bytes);
+  if (need > e->attn_part_bytes) {
+    set_error("decode_attn: needs %zu B scratch, engine has %zu", need, e->attn_part_bytes);
     return SX_ERR_UNSUPPORTED;
   }
-  sx::AttnArgs a{q, kc, vc, slots, step, out, static_cast<float *>(e->scratch), head_dim, kv_dim,
+  sx::AttnArgs a{q, kc, vc, slots, step, out, e->attn_part, head_dim, kv_dim,
                  gqa, num_q, total_slots, e->kv_bf16 ? 1u : 0u, scale, e->err_dev};
   return cuda_status(sx::launch_decode_attn(a, s), "decode_attn launch");
 }
@@ -165,11 +207,9 @@ sx_status do_attn(sx_engine *e, cudaStream_t s, const float *q, const void *kc, 
 sx_status do_argmax(sx_engine *e, cudaStream_t s, const float *logits, uint32_t n,
                     uint32_t *out) {
   SX_CHECK_ARG(n > 0 && logits && out, "argmax: empty input");
-  // argmax partials live after the attention partials region
-  size_t off = e->scratch_bytes - sx::argmax_scratch_bytes();
-  return cuda_status(sx::launch_argmax(logits, n, out, static_cast<uint8_t *>(e->scratch) + off,
-                                       sx::argmax_scratch_bytes(), s),
-                     "argmax launch");
+  return cuda_status(
+      sx::launch_argmax(logits, n, out, e->argmax_part, sx::argmax_scratch_bytes(), s),
+      "argmax launch");
 }
 
 
@@ -211,6 +251,18 @@ sx_status run_op(sx_engine *e, cudaStream_t s, const Op &op, uint32_t *kernels) 
     case OP_ARGMAX:
       *kernels += 2;
       return do_argmax(e, s, (const float *)op.bind.at(0), op.u[0], (uint32_t *)op.bind.at(1));
+    case OP_GEMV_FUSED:
+      *kernels += 1;
+      return cuda_status(sx::launch_gemv(op.qt, op.geglu, op.gemv, e->num_sms, s, true),
+                         "fused gemv launch");
+    case OP_ATTN_FUSED: {
+      *kernels += 1;
+      sx::AttnFusedArgs a = op.attnf;
+      sx_status fst = SX_OK;
+      a.inv_freq = engine_inv_freq(e, op.attn_rot, op.attn_theta, &fst);
+      if (!a.inv_freq) return fst;
+      return cuda_status(sx::launch_attn_fused(a, s, true), "fused attention launch");
+    }
     case OP_H2D:
       return cuda_status(cudaMemcpyAsync(op.dev, op.host, op.bytes, cudaMemcpyHostToDevice, s),
                          "h2d copy");
@@ -461,9 +513,38 @@ SX_API sx_status sx_engine_create(int device, sx_quant_mode mode, uint32_t flags
     st = cuda_status(cudaHostGetDevicePointer((void **)&e->err_dev, e->err_host, 0),
                      "error word mapping");
     if (st) break;
-    e->scratch_bytes = 32u << 20;
-    st = cuda_status(cudaMalloc(&e->scratch, e->scratch_bytes), "engine scratch");
-    if (st) break;
+    {
+      // scratch regions, 256-byte aligned
+      size_t off = 0;
+      auto take = [&](size_t bytes) {
+        size_t o = off;
+        off = (off + bytes + 255) & ~(size_t)255;
+        return o;
+      };
+      const size_t nw_max = (size_t)e->num_sms * 2 * 8;
+      size_t o_attn = take(e->attn_part_bytes = 8u << 20);
+      size_t o_acnt = take(4096 * 4);
+      size_t o_gpart = take(sx::gemv_part_bytes(e->num_sms));
+      size_t o_tcnt = take((size_t)sx::kMaxGemvTiles * 4);
+      size_t o_bv = take(nw_max * 8 * 4);
+      size_t o_bi = take(nw_max * 8 * 4);
+      size_t o_done = take(256);
+      size_t o_amax = take(sx::argmax_scratch_bytes());
+      e->scratch_bytes = off;
+      st = cuda_status(cudaMalloc(&e->scratch, e->scratch_bytes), "engine scratch");
+      if (st) break;
+      uint8_t *b = static_cast<uint8_t *>(e->scratch);
+      e->attn_part = reinterpret_cast<float *>(b + o_attn);
+      e->attn_cnt = reinterpret_cast<uint32_t *>(b + o_acnt);
+      e->gemv_part = reinterpret_cast<float *>(b + o_gpart);
+      e->tile_cnt = reinterpret_cast<uint32_t *>(b + o_tcnt);
+      e->best_v = reinterpret_cast<float *>(b + o_bv);
+      e->best_i = reinterpret_cast<uint32_t *>(b + o_bi);
+      e->done_cnt = reinterpret_cast<uint32_t *>(b + o_done);
+      e->argmax_part = b + o_amax;
+      st = cuda_status(cudaMemset(e->scratch, 0, e->scratch_bytes), "engine scratch zero");
+      if (st) break;
+    }
     st = cuda_status(sx::prepare_gemv_kernels(), "gemv kernel attributes");
     if (st) break;
     st = cuda_status(sx::prepare_ops_kernels(), "attention kernel attributes");
@@ -660,9 +741,10 @@ SX_API sx_status sx_cmd_end(sx_cmd *c) {
   SX_TRY_CUDA(cudaSetDevice(e->device), "cudaSetDevice");
   // device-side tables are created before capture (no allocation inside a capture)
   for (const Op &op : c->ops) {
-    if (op.kind != OP_QKV_ROPE) continue;
     sx_status fst = SX_OK;
-    if (!engine_inv_freq(e, op.u[3], op.f[0], &fst)) return fst;
+    if (op.kind == OP_QKV_ROPE && !engine_inv_freq(e, op.u[3], op.f[0], &fst)) return fst;
+    if (op.kind == OP_ATTN_FUSED && !engine_inv_freq(e, op.attn_rot, op.attn_theta, &fst))
+      return fst;
   }
   cudaStream_t cs = e->capture_stream;
   SX_TRY_CUDA(cudaStreamBeginCapture(cs, cudaStreamCaptureModeThreadLocal), "begin capture");

@@ -1,18 +1,27 @@
-// sx_gemv.cu -- Q4_0 / Q8_0 GEMV (batch 1..8) and the fused gate+up GeGLU for sm_100a.
+// sx_gemv.cu -- Q4_0 / Q8_0 GEMV (batch 1..8), fused gate+up GeGLU, fused input norms and
+// fused argmax for sm_100a.
 //
-// Replaces gemv_q4.wgsl, gemv_q8.wgsl and fused_mlp_q4.wgsl (reference dispatch:
-// src/gpu/kernels.zig:80-95).  Semantics: y[r] = sum_b sum_e ((q - 8) * d_b) * x[e] for Q4,
-// (q * d_b) * x[e] for Q8; fused: y[r] = gelu_tanh(Wg[r].x) * (Wu[r].x) (kernels.zig:94-115).
+// Replaces gemv_q4.wgsl, gemv_q8.wgsl, fused_mlp_q4.wgsl and argmax.wgsl (reference dispatch:
+// src/gpu/kernels.zig:80-95,139-142).  Semantics: y[r] = sum_b sum_e ((q - 8) * d_b) * x[e]
+// for Q4, (q * d_b) * x[e] for Q8; GeGLU: y[r] = gelu_tanh(Wg[r].x) * (Wu[r].x)
+// (kernels.zig:94-115); argmax = first index of the maximum (kernels.zig:164-174).
 //
-// Design.  Decode GEMVs are HBM-bound (20 B per 32 weights), so the kernel must spend few
-// instructions per weight.  Each warp streams 16-row x 64-column chunks of the packed
-// matrix with 128-bit no-L1-allocate loads and dequantises nibbles straight into
-// mma.m16n8k16 A fragments with one shift + one LOP3 per two weights (bf16 value 8 + q/2,
-// exact).  The activation enters as the B operand split into bf16 hi + lo parts (16-bit
-// significand, ~2^-17 relative), one column pair per batch row, so the tensor core does the
-// 32-element block dot products; the per-block f32 scale and the constant offset are applied
-// on the f32 accumulator:  sum_e (q_e - 8) x_e = 2 * (D - 12 * sum_e x_e).
-// Q8 uses f16 values 1024 + (q + 128) (exact) and a per-vector power-of-two prescale of x.
+// Work split.  The matrix (or the concatenation of up to three matrices, e.g. q|k|v) is a
+// sequence of N = tiles x pairs 640-byte chunks (16 rows x 64 columns; 1152 B for Q8).  Every
+// warp of a persistent grid is a worker that owns a contiguous range of N / (CTAs x 8) chunks
+// ("stream-K"), so the load is balanced for any shape.  Each warp streams its chunks through
+// its own 8-stage shared-memory ring with cp.async.bulk + mbarrier (the first stages are
+// issued before the programmatic-dependent-launch wait, i.e. while the previous kernel is
+// still finishing).  A tile covered by one worker is written directly; a tile split between
+// workers is reduced by the last worker to arrive, summing the partial records in worker
+// order (deterministic; no atomics on the data).
+//
+// Dequantisation.  Nibbles become mma.m16n8k16 A fragments with one shift + one LOP3 per two
+// weights (bf16 value 8 + q/2, exact).  The f32 activation enters as the B operand split into
+// bf16 hi + lo (16 significant bits), one column pair per batch row, so the tensor core forms
+// the 32-element block dot products; the per-block f32 scale and the offset are applied on
+// the f32 accumulator: sum_e (q_e - 8) x_e = 2 * (D - 12 * sum_e x_e).  Q8 uses f16 values
+// 1024 + (q + 128) (exact) with a per-vector power-of-two prescale of x.
 #include "sx_common.cuh"
 #include "sx_internal.h"
 
@@ -20,8 +29,9 @@ namespace sx {
 
 namespace {
 
-constexpr int kGemvThreads = 256;
-constexpr int kGemvWarps = kGemvThreads / 32;
+constexpr int kThreads = 256;
+constexpr int kWarps = kThreads / 32;
+constexpr int kStages = 8;
 
 SX_HD uint32_t nv_of(uint32_t batch) {
   return batch <= 1 ? 2u : batch <= 2 ? 4u : batch <= 4 ? 8u : 16u;
@@ -42,18 +52,23 @@ struct QTraits<8> {
   static constexpr float kCorr = 1152.0f;
 };
 
-struct SmemLayout {
-  uint32_t xfrag_bytes, corr_off, red_off, scale_off, total;
+struct Layout {
+  uint32_t xfrag, corr, misc, xin, ring, bars, total;
 };
 
-SX_HD SmemLayout smem_layout(uint32_t k, uint32_t batch, int nmat) {
-  SmemLayout L;
+// xfrag | corr | misc (xscale[8], xexp[8], red[32]) | xin (fused prologue) | ring | mbarriers
+SX_HD Layout layout_of(uint32_t k, uint32_t batch, int nmat, int qt, bool pro) {
+  Layout L;
   uint32_t nblk = 2 * pairs_of(k);
-  L.xfrag_bytes = nblk * nv_of(batch) * 4 * 16;
-  L.corr_off = L.xfrag_bytes;
-  L.red_off = L.corr_off + nblk * 8 * 4;
-  L.scale_off = L.red_off + kGemvWarps * nmat * 16 * 8 * 4;
-  L.total = L.scale_off + 8 * 4;
+  L.xfrag = 0;
+  L.corr = nblk * nv_of(batch) * 64;
+  L.misc = L.corr + ((nblk * batch * 4 + 15) & ~15u);
+  L.xin = L.misc + 48 * 4;
+  uint32_t xin_bytes = pro ? batch * k * 4 : 0;
+  L.ring = (L.xin + xin_bytes + 127) & ~127u;
+  uint32_t chunk = qt == 4 ? kQ4ChunkBytes : kQ8ChunkBytes;
+  L.bars = L.ring + kWarps * kStages * nmat * chunk;
+  L.total = L.bars + kWarps * kStages * 8;
   return L;
 }
 
@@ -64,30 +79,88 @@ SX_DEV float gelu_tanh_dev(float x) {
   return __fmul_rn(__fmul_rn(0.5f, x), __fadd_rn(1.0f, tanhf(inner)));
 }
 
+// ---------------------------------------------------------------------------------------
+// Fused input prologues (replace a separate norm launch).  Each CTA computes the GEMV input
+// for all batch rows into shared memory:
+//   kProNorm:  xin = rmsnorm(x, w)                                   (rmsnorm.wgsl)
+//   kProResid: v = post_w ? rmsnorm(mlp, post_w) : mlp; xn = (x + v) * scalar;
+//              CTA 0 writes xn to x_out; xin = rmsnorm(xn, w)         (add_rmsnorm.wgsl)
+SX_DEV float cta_sum(float v, float *red) { return block_sum(v, red); }
+
+SX_DEV float inv_rms(float ss, uint32_t n, float eps) {
+  return __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)n), eps)));
+}
+
+SX_DEV void run_prologue(const GemvArgs &a, float *xin, float *red) {
+  const uint32_t K = a.k;
+  for (uint32_t j = 0; j < a.batch; ++j) {
+    float *xo = xin + (size_t)j * K;
+    const float *x = a.x + (size_t)j * a.ldx;
+    if (a.pro == kProNorm) {
+      float ss = 0.0f;
+      for (uint32_t i = threadIdx.x; i < K; i += blockDim.x) {
+        float v = x[i];
+        ss = fmaf(v, v, ss);
+      }
+      float r = inv_rms(cta_sum(ss, red), K, a.eps);
+      for (uint32_t i = threadIdx.x; i < K; i += blockDim.x)
+        xo[i] = __fmul_rn(__fmul_rn(x[i], r), a.pro_w[i]);
+    } else {
+      const float *mlp = a.pro_mlp + (size_t)j * a.ldx;
+      float rm = 1.0f;
+      if (a.pro_post_w) {
+        float ss = 0.0f;
+        for (uint32_t i = threadIdx.x; i < K; i += blockDim.x) {
+          float v = mlp[i];
+          ss = fmaf(v, v, ss);
+        }
+        rm = inv_rms(cta_sum(ss, red), K, a.eps);
+      }
+      float ss = 0.0f;
+      for (uint32_t i = threadIdx.x; i < K; i += blockDim.x) {
+        float v = mlp[i];
+        if (a.pro_post_w) v = __fmul_rn(__fmul_rn(v, rm), a.pro_post_w[i]);
+        float xn = __fmul_rn(__fadd_rn(x[i], v), a.pro_scalar);
+        xo[i] = xn;
+        ss = fmaf(xn, xn, ss);
+      }
+      float r = inv_rms(cta_sum(ss, red), K, a.eps);
+      for (uint32_t i = threadIdx.x; i < K; i += blockDim.x) {
+        float xn = xo[i];
+        if (blockIdx.x == 0) a.pro_x_out[(size_t)j * a.ldx + i] = xn;
+        xo[i] = __fmul_rn(__fmul_rn(xn, r), a.pro_w[i]);
+      }
+    }
+    __syncthreads();
+  }
+}
+
 // Activation -> B fragments.  Item (blk, j, c, jj) converts elements 32*blk + 8*jj + 2c,+1
 // of batch row j into the hi/lo pair words and reduces the block sum for the offset term.
 template <int QT>
-SX_DEV void stage_x(const GemvArgs &a, uint8_t *smem, const SmemLayout &L) {
-  uint32_t *xf = reinterpret_cast<uint32_t *>(smem);
-  float *corr = reinterpret_cast<float *>(smem + L.corr_off);
-  float *xscale = reinterpret_cast<float *>(smem + L.scale_off);
-  int *xexp = reinterpret_cast<int *>(smem + L.red_off);  // red area is free here
+SX_DEV void stage_x(const GemvArgs &a, const float *src, uint32_t ld, uint8_t *smem,
+                    const Layout &L) {
+  uint32_t *xf = reinterpret_cast<uint32_t *>(smem + L.xfrag);
+  float *corr = reinterpret_cast<float *>(smem + L.corr);
+  float *xscale = reinterpret_cast<float *>(smem + L.misc);
+  int *xexp = reinterpret_cast<int *>(smem + L.misc + 32);
+  float *red = reinterpret_cast<float *>(smem + L.misc + 64);
   const uint32_t nb = a.k / 32, nblk = 2 * pairs_of(a.k), nv = nv_of(a.batch);
   const int tid = threadIdx.x;
 
   if (QT == 8) {
-    // Per-row power-of-two prescale so that the f16 hi/lo split neither overflows nor
-    // loses precision: max |x| * 2^e < 2^15.
+    // Per-row power-of-two prescale so that the f16 hi/lo split neither overflows nor loses
+    // precision: max |x| * 2^e < 2^15.
     for (uint32_t j = 0; j < a.batch; ++j) {
       float mx = 0.0f;
-      for (uint32_t i = tid; i < a.k; i += blockDim.x) mx = fmaxf(mx, fabsf(a.x[j * a.ldx + i]));
+      for (uint32_t i = tid; i < a.k; i += blockDim.x) mx = fmaxf(mx, fabsf(src[j * ld + i]));
       mx = warp_max(mx);
       __syncthreads();
-      if ((tid & 31) == 0) xscale[tid >> 5] = mx;
+      if ((tid & 31) == 0) red[tid >> 5] = mx;
       __syncthreads();
       if (tid == 0) {
         float m = 0.0f;
-        for (int w = 0; w < (int)(blockDim.x >> 5); ++w) m = fmaxf(m, xscale[w]);
+        for (int w = 0; w < (int)(blockDim.x >> 5); ++w) m = fmaxf(m, red[w]);
         int e = 0;
         if (m > 0.0f && isfinite(m)) {
           int ex;
@@ -96,12 +169,16 @@ SX_DEV void stage_x(const GemvArgs &a, uint8_t *smem, const SmemLayout &L) {
           e = e > 100 ? 100 : (e < -100 ? -100 : e);
         }
         xexp[j] = e;
+        xscale[j] = ldexpf(1.0f, -e);
       }
       __syncthreads();
     }
-    if (tid < (int)a.batch) xscale[tid] = ldexpf(1.0f, -xexp[tid]);
   } else {
-    if (tid < (int)a.batch) xscale[tid] = 2.0f;
+    if (tid < (int)a.batch) {
+      xscale[tid] = 2.0f;
+      xexp[tid] = 0;
+    }
+    __syncthreads();
   }
 
   const uint32_t items = nblk * a.batch * 16;
@@ -114,8 +191,8 @@ SX_DEV void stage_x(const GemvArgs &a, uint8_t *smem, const SmemLayout &L) {
       uint32_t e0 = blk * 32 + jj * 8 + 2 * c;
       float x0 = 0.0f, x1 = 0.0f;
       if (blk < nb) {
-        x0 = a.x[j * a.ldx + e0];
-        x1 = a.x[j * a.ldx + e0 + 1];
+        x0 = src[j * ld + e0];
+        x1 = src[j * ld + e0 + 1];
       }
       uint32_t hw, lw;
       if (QT == 4) {
@@ -145,7 +222,7 @@ SX_DEV void stage_x(const GemvArgs &a, uint8_t *smem, const SmemLayout &L) {
     part += __shfl_xor_sync(0xffffffffu, part, 4);
     part += __shfl_xor_sync(0xffffffffu, part, 2);
     part += __shfl_xor_sync(0xffffffffu, part, 1);
-    if (it < items && (it & 15) == 0) corr[blk * 8 + j] = QTraits<QT>::kCorr * part;
+    if (it < items && (it & 15) == 0) corr[blk * a.batch + j] = QTraits<QT>::kCorr * part;
   }
   __syncthreads();
 }
@@ -161,7 +238,7 @@ SX_DEV void block_mma(const uint32_t (&a0)[4], const uint32_t (&a1)[4], const ui
     uint4 xb = make_uint4(0, 0, 0, 0);
     if (v < 2 * batch) xb = xf4[(blk * nv + v) * 4 + c];
     uint32_t j = 4 * s + c;
-    float cr = j < batch ? corr[blk * 8 + j] : 0.0f;
+    float cr = j < batch ? corr[blk * batch + j] : 0.0f;
     float d[4] = {-cr, 0.0f, -cr, 0.0f};
     if (QT == 4) {
       mma_bf16_16816(d, a0, xb.x, xb.y);
@@ -175,123 +252,308 @@ SX_DEV void block_mma(const uint32_t (&a0)[4], const uint32_t (&a1)[4], const ui
   }
 }
 
+// worker ranges: worker w owns chunks [N*w/NW, N*(w+1)/NW)
+SX_DEV uint64_t wstart(uint64_t N, uint32_t NW, uint32_t w) { return N * w / NW; }
+SX_DEV uint32_t wowner(uint64_t N, uint32_t NW, uint64_t c) {
+  return (uint32_t)(((c + 1) * NW - 1) / N);
+}
+
+struct Best {
+  float v;
+  uint32_t i;
+};
+SX_DEV bool better(float v, uint32_t i, float bv, uint32_t bi) {
+  return v > bv || (v == bv && i < bi);
+}
+
 template <int QT, int NMAT, int NSETS>
-__global__ void __launch_bounds__(kGemvThreads) gemv_kernel(GemvArgs a) {
-  extern __shared__ __align__(16) uint8_t smem[];
-  const SmemLayout L = smem_layout(a.k, a.batch, NMAT);
-  stage_x<QT>(a, smem, L);
-
-  const uint4 *xf4 = reinterpret_cast<const uint4 *>(smem);
-  const float *corr = reinterpret_cast<const float *>(smem + L.corr_off);
-  float *red = reinterpret_cast<float *>(smem + L.red_off);
-  const float *xscale = reinterpret_cast<const float *>(smem + L.scale_off);
-
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, c = lane & 3;
-  const uint32_t T = tiles_of(a.m), P = pairs_of(a.k), nv = nv_of(a.batch);
+__global__ void __launch_bounds__(kThreads, 2) gemv_kernel(GemvArgs a) {
+  extern __shared__ __align__(128) uint8_t smem[];
   constexpr int CB = QTraits<QT>::kChunk;
   constexpr int SO = QTraits<QT>::kScaleOff;
-  constexpr int U = NMAT == 1 ? 4 : 2;
-  const uint8_t *wbase[2] = {static_cast<const uint8_t *>(a.w0),
-                             static_cast<const uint8_t *>(NMAT == 2 ? a.w1 : a.w0)};
+  constexpr int STAGE = NMAT * CB;
+  const Layout L = layout_of(a.k, a.batch, NMAT, QT, a.pro != kProNone);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, c = lane & 3;
+  const uint32_t P = pairs_of(a.k), nv = nv_of(a.batch);
+  const uint32_t T = a.tiles[0] + a.tiles[1] + a.tiles[2];
+  const uint64_t N = (uint64_t)T * P;
+  const uint32_t NW = gridDim.x * kWarps, wid = blockIdx.x * kWarps + warp;
+  const uint64_t c0 = wstart(N, NW, wid), c1 = wstart(N, NW, wid + 1);
 
-  for (uint32_t t = blockIdx.x; t < T; t += gridDim.x) {
-    float acc[NMAT][NSETS][2];
+  uint8_t *ring = smem + L.ring + warp * kStages * STAGE;
+  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + L.bars) + warp * kStages;
+
+  auto seg_of = [&](uint32_t tt, uint32_t &t) {
+    int s = 0;
+    t = tt;
+    if (t >= a.tiles[0]) {
+      t -= a.tiles[0];
+      s = 1;
+      if (t >= a.tiles[1]) {
+        t -= a.tiles[1];
+        s = 2;
+      }
+    }
+    return s;
+  };
+  auto issue = [&](int st, uint64_t cc) {
+    uint32_t t;
+    int s = seg_of((uint32_t)(cc / P), t);
+    uint64_t off = ((uint64_t)t * P + cc % P) * CB;
+    uint32_t bar = smem_u32(&bars[st]);
+    mbar_arrive_expect_tx(bar, STAGE);
 #pragma unroll
     for (int m = 0; m < NMAT; ++m)
-#pragma unroll
-      for (int s = 0; s < NSETS; ++s) acc[m][s][0] = acc[m][s][1] = 0.0f;
+      bulk_g2s(smem_u32(ring + st * STAGE + m * CB),
+               static_cast<const uint8_t *>(a.w[s][m]) + off, CB, bar);
+  };
 
-    for (uint32_t p0 = warp; p0 < P; p0 += kGemvWarps * U) {
-      uint4 wq[U][NMAT][QT == 4 ? 1 : 2];
-      float4 sc[U][NMAT];
+  // 1. per-warp pipeline start: weights do not depend on the previous kernel
+  if (lane == 0) {
+    for (int st = 0; st < kStages; ++st) mbar_init(smem_u32(&bars[st]), 1);
+    fence_mbar_init();
+    for (int st = 0; st < kStages && c0 + st < c1; ++st) issue(st, c0 + st);
+  }
+  __syncwarp();
+  pdl_launch_dependents();
+  // 2. wait for the producer of x, then stage it
+  pdl_wait();
+  const float *xsrc = a.x;
+  uint32_t xld = a.ldx;
+  if (a.pro != kProNone) {
+    float *xin = reinterpret_cast<float *>(smem + L.xin);
+    run_prologue(a, xin, reinterpret_cast<float *>(smem + L.misc + 64));
+    xsrc = xin;
+    xld = a.k;
+  }
+  stage_x<QT>(a, xsrc, xld, smem, L);
+
+  const uint4 *xf4 = reinterpret_cast<const uint4 *>(smem + L.xfrag);
+  const float *corr = reinterpret_cast<const float *>(smem + L.corr);
+  const float *xscale = reinterpret_cast<const float *>(smem + L.misc);
+
+  Best best[NSETS];
 #pragma unroll
-      for (int u = 0; u < U; ++u) {
-        uint32_t p = p0 + u * kGemvWarps;
-        if (p < P) {
+  for (int s = 0; s < NSETS; ++s) best[s] = {-INFINITY, 0xFFFFFFFFu};
+
+  // epilogue for one (row, batch) value pair set: apply factor, GeGLU, write, track argmax
+  auto emit = [&](uint32_t tt, uint32_t row, uint32_t j, const float (&v)[NMAT], int s_idx) {
+    uint32_t t;
+    int s = seg_of(tt, t);
+    uint32_t r = t * 16 + row;
+    if (r >= a.rows[s] || j >= a.batch) return;
+    float out = v[0] * xscale[j];
+    if (NMAT == 2) out = __fmul_rn(gelu_tanh_dev(out), v[NMAT - 1] * xscale[j]);
+    a.y[s][(size_t)j * a.ldy + r] = out;
+    if (a.epi == kEpiArgmax) {
+      uint32_t gi = a.row_base[s] + r;
+      float ov = isnan(out) ? -INFINITY : out;
+      if (best[s_idx].i == 0xFFFFFFFFu || better(ov, gi, best[s_idx].v, best[s_idx].i))
+        best[s_idx] = {ov, gi};
+    }
+  };
+
+  float acc[NMAT][NSETS][2];
 #pragma unroll
-          for (int m = 0; m < NMAT; ++m) {
-            const uint8_t *ch = wbase[m] + ((size_t)t * P + p) * CB;
-            wq[u][m][0] = ldg_stream(ch + lane * 16);
-            if (QT == 8) wq[u][m][QT == 4 ? 0 : 1] = ldg_stream(ch + 512 + lane * 16);
-            sc[u][m] = __ldg(reinterpret_cast<const float4 *>(ch + SO + g * 16));
-          }
+  for (int m = 0; m < NMAT; ++m)
+#pragma unroll
+    for (int s = 0; s < NSETS; ++s) acc[m][s][0] = acc[m][s][1] = 0.0f;
+
+  bool ok = true;
+  uint64_t fail_cc = 0;
+  uint64_t issued = c0 + kStages < c1 ? c0 + kStages : c1;  // chunks whose copy was issued
+  for (uint64_t cc = c0; cc < c1; ++cc) {
+    const uint64_t i = cc - c0;
+    const int st = (int)(i % kStages);
+    const uint32_t phase = (uint32_t)(i / kStages) & 1u;
+    if (!mbar_wait_bounded(smem_u32(&bars[st]), phase)) {
+      raise_error(a.err, kDevWaitTimeout);
+      ok = false;
+      fail_cc = cc;
+      break;
+    }
+    const uint8_t *chunk = ring + st * STAGE;
+    const uint32_t p = (uint32_t)(cc % P);
+#pragma unroll
+    for (int m = 0; m < NMAT; ++m) {
+      const uint8_t *ch = chunk + m * CB;
+      const float4 sc = *reinterpret_cast<const float4 *>(ch + SO + g * 16);
+#pragma unroll
+      for (int hb = 0; hb < 2; ++hb) {
+        uint32_t a0[4], a1[4];
+        if (QT == 4) {
+          const uint4 nib = *reinterpret_cast<const uint4 *>(ch + lane * 16);
+          uint32_t rg[4], rg8[4];
+          dq4_word(hb ? nib.z : nib.x, rg);
+          dq4_word(hb ? nib.w : nib.y, rg8);
+          a0[0] = rg[0]; a0[1] = rg8[0]; a0[2] = rg[1]; a0[3] = rg8[1];
+          a1[0] = rg[2]; a1[1] = rg8[2]; a1[2] = rg[3]; a1[3] = rg8[3];
+        } else {
+          const uint4 q = *reinterpret_cast<const uint4 *>(ch + hb * 512 + lane * 16);
+          uint32_t g0l, g0h, g1l, g1h, h0l, h0h, h1l, h1h;
+          dq8_word(q.x, g0l, g0h);
+          dq8_word(q.y, g1l, g1h);
+          dq8_word(q.z, h0l, h0h);
+          dq8_word(q.w, h1l, h1h);
+          a0[0] = g0l; a0[1] = h0l; a0[2] = g0h; a0[3] = h0h;
+          a1[0] = g1l; a1[1] = h1l; a1[2] = g1h; a1[3] = h1h;
         }
+        block_mma<QT, NSETS>(a0, a1, xf4, corr, 2 * p + hb, nv, a.batch, g, c,
+                             hb ? sc.z : sc.x, hb ? sc.w : sc.y, acc[m]);
       }
+    }
+    // refill this stage (its data has been consumed into registers and used)
+    __syncwarp();
+    if (cc + kStages < c1) {
+      if (lane == 0) {
+        fence_proxy_async();
+        issue(st, cc + kStages);
+      }
+      issued = cc + kStages + 1;
+    }
+    // tile boundary
+    const uint32_t tt = (uint32_t)(cc / P);
+    if (p == P - 1 || cc + 1 == c1) {
+      const uint64_t tb = (uint64_t)tt * P, te = tb + P;
+      if (tb >= c0 && te <= c1) {
+        // the whole tile is ours: write it directly
 #pragma unroll
-      for (int u = 0; u < U; ++u) {
-        uint32_t p = p0 + u * kGemvWarps;
-        if (p >= P) break;
+        for (int s = 0; s < NSETS; ++s)
 #pragma unroll
-        for (int m = 0; m < NMAT; ++m) {
+          for (int h = 0; h < 2; ++h) {
+            float v[NMAT];
 #pragma unroll
-          for (int hb = 0; hb < 2; ++hb) {
-            uint32_t a0[4], a1[4];
-            if (QT == 4) {
-              uint32_t rg[4], rg8[4];
-              dq4_word(hb ? wq[u][m][0].z : wq[u][m][0].x, rg);
-              dq4_word(hb ? wq[u][m][0].w : wq[u][m][0].y, rg8);
-              a0[0] = rg[0]; a0[1] = rg8[0]; a0[2] = rg[1]; a0[3] = rg8[1];
-              a1[0] = rg[2]; a1[1] = rg8[2]; a1[2] = rg[3]; a1[3] = rg8[3];
-            } else {
-              const uint4 q = wq[u][m][QT == 4 ? 0 : hb];
-              uint32_t g0l, g0h, g1l, g1h, h0l, h0h, h1l, h1h;
-              dq8_word(q.x, g0l, g0h);
-              dq8_word(q.y, g1l, g1h);
-              dq8_word(q.z, h0l, h0h);
-              dq8_word(q.w, h1l, h1h);
-              a0[0] = g0l; a0[1] = h0l; a0[2] = g0h; a0[3] = h0h;
-              a1[0] = g1l; a1[1] = h1l; a1[2] = g1h; a1[3] = h1h;
+            for (int m = 0; m < NMAT; ++m) v[m] = acc[m][s][h];
+            emit(tt, g + 8 * h, 4 * s + c, v, s);
+          }
+      } else {
+        // partial tile: publish, and reduce if we are the last contributor
+        const int slot = (tt == (uint32_t)(c0 / P)) ? 0 : 1;
+        float *rec = a.part + ((size_t)wid * 2 + slot) * NMAT * 128;
+#pragma unroll
+        for (int m = 0; m < NMAT; ++m)
+#pragma unroll
+          for (int s = 0; s < NSETS; ++s) {
+            uint32_t j = 4 * s + c;
+            if (j < 8) {
+              rec[m * 128 + g * 8 + j] = acc[m][s][0];
+              rec[m * 128 + (g + 8) * 8 + j] = acc[m][s][1];
             }
-            float sg = hb ? sc[u][m].z : sc[u][m].x;
-            float sg8 = hb ? sc[u][m].w : sc[u][m].y;
-            block_mma<QT, NSETS>(a0, a1, xf4, corr, 2 * p + hb, nv, a.batch, g, c, sg, sg8,
-                                 acc[m]);
           }
+        __threadfence();
+        __syncwarp();
+        uint32_t wlo = wowner(N, NW, tb), whi = wowner(N, NW, te - 1);
+        uint32_t expected = 0;
+        for (uint32_t w = wlo; w <= whi; ++w)
+          if (wstart(N, NW, w) < wstart(N, NW, w + 1)) ++expected;
+        uint32_t old = 0;
+        if (lane == 0) old = atomicAdd(&a.tile_cnt[tt], 1u);
+        old = __shfl_sync(0xffffffffu, old, 0);
+        if (old + 1 == expected) {
+          __threadfence();
+          // lanes own (row, j) pairs: 16 rows x 8 batch slots = 128 -> 4 per lane
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            uint32_t idx = lane + 32 * q, row = idx >> 3, j = idx & 7;
+            float v[NMAT];
+#pragma unroll
+            for (int m = 0; m < NMAT; ++m) v[m] = 0.0f;
+            for (uint32_t w = wlo; w <= whi; ++w) {
+              uint64_t ws = wstart(N, NW, w);
+              if (ws >= wstart(N, NW, w + 1)) continue;
+              int sl = (tt == (uint32_t)(ws / P)) ? 0 : 1;
+              const float *r = a.part + ((size_t)w * 2 + sl) * NMAT * 128;
+#pragma unroll
+              for (int m = 0; m < NMAT; ++m) v[m] += __ldcg(r + m * 128 + idx);
+            }
+            emit(tt, row, j, v, j >= 4 ? NSETS - 1 : 0);
+          }
+          if (lane == 0) a.tile_cnt[tt] = 0;
         }
       }
+#pragma unroll
+      for (int m = 0; m < NMAT; ++m)
+#pragma unroll
+        for (int s = 0; s < NSETS; ++s) acc[m][s][0] = acc[m][s][1] = 0.0f;
     }
+  }
+  if (!ok) {
+    // a copy never completed: wait (bounded) for this warp's other copies still in flight so
+    // that none lands after the CTA exits, then leave; the host sees kDevWaitTimeout
+    for (uint64_t cc = fail_cc; cc < issued; ++cc) {
+      uint64_t i = cc - c0;
+      mbar_wait_bounded(smem_u32(&bars[i % kStages]), (uint32_t)(i / kStages) & 1u);
+    }
+    return;
+  }
 
-    // cross-warp reduction: red[warp][m][row][batch]
+  if (a.epi == kEpiArgmax) {
+    // Per batch row j: lane (g, c) tracked rows of batch row 4s + c in best[s].  Reduce over
+    // the warp, publish per worker, and let the last worker to arrive merge all workers.
+    for (uint32_t j = 0; j < a.batch; ++j) {
+      Best b = {-INFINITY, 0xFFFFFFFFu};
 #pragma unroll
-    for (int m = 0; m < NMAT; ++m)
+      for (int s = 0; s < NSETS; ++s)
+        if ((uint32_t)(4 * s + c) == j) b = best[s];
 #pragma unroll
-      for (int s = 0; s < NSETS; ++s) {
-        uint32_t j = 4 * s + c;
-        if (j < a.batch) {
-          red[((warp * NMAT + m) * 16 + g) * 8 + j] = acc[m][s][0];
-          red[((warp * NMAT + m) * 16 + g + 8) * 8 + j] = acc[m][s][1];
-        }
+      for (int o = 16; o > 0; o >>= 1) {
+        float ov = __shfl_xor_sync(0xffffffffu, b.v, o);
+        uint32_t oi = __shfl_xor_sync(0xffffffffu, b.i, o);
+        if (oi != 0xFFFFFFFFu && (b.i == 0xFFFFFFFFu || better(ov, oi, b.v, b.i))) b = {ov, oi};
       }
-    __syncthreads();
-    for (uint32_t i = tid; i < 16 * a.batch; i += blockDim.x) {
-      uint32_t row = i & 15, j = i >> 4;
-      float v[NMAT];
-#pragma unroll
-      for (int m = 0; m < NMAT; ++m) {
-        float s = 0.0f;
-        for (int w = 0; w < kGemvWarps; ++w) s += red[((w * NMAT + m) * 16 + row) * 8 + j];
-        v[m] = s * xscale[j];
-      }
-      uint32_t r = t * 16 + row;
-      if (r < a.m) {
-        float out = v[0];
-        if (NMAT == 2) out = __fmul_rn(gelu_tanh_dev(v[0]), v[NMAT - 1]);
-        a.y[(size_t)j * a.ldy + r] = out;
+      if (lane == 0) {
+        a.best_v[(size_t)wid * 8 + j] = b.v;
+        a.best_i[(size_t)wid * 8 + j] = b.i;
       }
     }
-    __syncthreads();
+    __threadfence();
+    __syncwarp();
+    uint32_t old = 0;
+    if (lane == 0) old = atomicAdd(a.done_cnt, 1u);
+    old = __shfl_sync(0xffffffffu, old, 0);
+    if (old + 1 == NW) {
+      __threadfence();
+      for (uint32_t j = 0; j < a.batch; ++j) {
+        Best r = {-INFINITY, 0xFFFFFFFFu};
+        for (uint32_t w = lane; w < NW; w += 32) {
+          float v = __ldcg(a.best_v + (size_t)w * 8 + j);
+          uint32_t ix = __ldcg(a.best_i + (size_t)w * 8 + j);
+          if (ix != 0xFFFFFFFFu && (r.i == 0xFFFFFFFFu || better(v, ix, r.v, r.i))) r = {v, ix};
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+          float ov = __shfl_xor_sync(0xffffffffu, r.v, o);
+          uint32_t oi = __shfl_xor_sync(0xffffffffu, r.i, o);
+          if (oi != 0xFFFFFFFFu && (r.i == 0xFFFFFFFFu || better(ov, oi, r.v, r.i))) r = {ov, oi};
+        }
+        if (lane == 0) {
+          uint32_t tok = r.i == 0xFFFFFFFFu ? 0u : r.i;
+          // the CPU rule starts from logits[0]: a NaN there is never beaten
+          if (isnan(__ldcg(a.y[0] + (size_t)j * a.ldy))) tok = 0;
+          a.token[j] = tok;
+        }
+      }
+      if (lane == 0) *a.done_cnt = 0;
+    }
   }
 }
 
 template <int QT, int NMAT, int NSETS>
-cudaError_t launch_t(const GemvArgs &a, int num_sms, cudaStream_t s) {
-  const SmemLayout L = smem_layout(a.k, a.batch, NMAT);
+cudaError_t launch_t(const GemvArgs &a, int num_sms, cudaStream_t s, bool pdl) {
+  const Layout L = layout_of(a.k, a.batch, NMAT, QT, a.pro != kProNone);
   auto kern = gemv_kernel<QT, NMAT, NSETS>;
-  uint32_t T = tiles_of(a.m);
-  uint32_t cap = (uint32_t)num_sms * 8;
-  uint32_t grid = T < cap ? T : cap;
-  kern<<<grid, kGemvThreads, L.total, s>>>(a);
-  return cudaGetLastError();
+  int per_sm = L.total <= 110 * 1024 ? 2 : 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(num_sms * per_sm);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = L.total;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kern, a);
 }
 
 template <int QT, int NMAT, int NSETS>
@@ -312,19 +574,24 @@ cudaError_t prepare_gemv_kernels() {
   return e;
 }
 
-size_t gemv_smem_bytes(int qt, uint32_t k, uint32_t batch) {
-  (void)qt;
-  return smem_layout(k, batch, 2).total;
+size_t gemv_smem_bytes(int qt, uint32_t k, uint32_t batch, bool geglu, bool prologue) {
+  return layout_of(k, batch, geglu ? 2 : 1, qt, prologue).total;
 }
 
-cudaError_t launch_gemv(int qt, bool geglu, const GemvArgs &a, int num_sms, cudaStream_t s) {
+size_t gemv_part_bytes(int num_sms) { return (size_t)num_sms * 2 * kWarps * 2 * 2 * 128 * 4; }
+size_t gemv_best_bytes(int num_sms) { return (size_t)num_sms * 2 * kWarps * 8; }
+
+cudaError_t launch_gemv(int qt, bool geglu, const GemvArgs &a, int num_sms, cudaStream_t s,
+                        bool pdl) {
   bool two = a.batch > 4;
   if (qt == 4) {
-    if (geglu) return two ? launch_t<4, 2, 2>(a, num_sms, s) : launch_t<4, 2, 1>(a, num_sms, s);
-    return two ? launch_t<4, 1, 2>(a, num_sms, s) : launch_t<4, 1, 1>(a, num_sms, s);
+    if (geglu)
+      return two ? launch_t<4, 2, 2>(a, num_sms, s, pdl) : launch_t<4, 2, 1>(a, num_sms, s, pdl);
+    return two ? launch_t<4, 1, 2>(a, num_sms, s, pdl) : launch_t<4, 1, 1>(a, num_sms, s, pdl);
   }
-  if (geglu) return two ? launch_t<8, 2, 2>(a, num_sms, s) : launch_t<8, 2, 1>(a, num_sms, s);
-  return two ? launch_t<8, 1, 2>(a, num_sms, s) : launch_t<8, 1, 1>(a, num_sms, s);
+  if (geglu)
+    return two ? launch_t<8, 2, 2>(a, num_sms, s, pdl) : launch_t<8, 2, 1>(a, num_sms, s, pdl);
+  return two ? launch_t<8, 1, 2>(a, num_sms, s, pdl) : launch_t<8, 1, 1>(a, num_sms, s, pdl);
 }
 
 }  // namespace sx

@@ -10,6 +10,7 @@
 #include <vector>
 
 #include "../../include/sx.h"
+#include "sx_internal.h"
 
 // ---------------------------------------------------------------------------------------
 // objects
@@ -25,6 +26,16 @@ struct sx_engine {
   uint32_t *err_dev = nullptr;
   void *scratch = nullptr;
   size_t scratch_bytes = 0;
+  // carved out of `scratch` (counters are zero at rest; kernels that use them reset them)
+  float *attn_part = nullptr;
+  size_t attn_part_bytes = 0;
+  uint32_t *attn_cnt = nullptr;
+  float *gemv_part = nullptr;
+  uint32_t *tile_cnt = nullptr;
+  float *best_v = nullptr;
+  uint32_t *best_i = nullptr;
+  uint32_t *done_cnt = nullptr;
+  void *argmax_part = nullptr;
   int num_sms = 148;
   std::mutex freq_mu;
   std::map<std::pair<uint32_t, uint32_t>, float *> inv_freq;  // (rot, theta bits)
@@ -52,6 +63,8 @@ enum OpKind {
   OP_ARGMAX,
   OP_H2D,
   OP_D2H,
+  OP_GEMV_FUSED,  // multi-segment GEMV with fused prologue / epilogue (model graph)
+  OP_ATTN_FUSED,  // qkv_rope + decode attention + combine (model graph)
 };
 
 struct Op {
@@ -64,6 +77,13 @@ struct Op {
   void *host = nullptr;    // OP_H2D / OP_D2H
   void *dev = nullptr;
   uint64_t bytes = 0;
+  // OP_GEMV_FUSED / OP_ATTN_FUSED: complete kernel arguments fixed at record time
+  int qt = 4;
+  bool geglu = false;
+  sx::GemvArgs gemv{};
+  sx::AttnFusedArgs attnf{};
+  uint32_t attn_rot = 0;
+  float attn_theta = 0.0f;
 };
 
 struct sx_cmd {
@@ -81,4 +101,13 @@ struct sx_cmd {
 // Append an op (including the internal host<->device copy ops) to a recording command buffer.
 void sx_host_push_op(sx_cmd *c, const Op &op);
 void sx_host_set_error(const char *msg);
+// Shape / shared-memory validation of a GEMV launch (sets the error message).
+sx_status sx_host_check_gemv(int qt, bool geglu, bool pro, uint32_t m, uint32_t k,
+                             uint32_t batch);
+// Fill the scratch / error-word fields of GEMV and fused-attention arguments.
+void sx_host_bind_scratch(sx_engine *e, sx::GemvArgs &a);
+void sx_host_bind_scratch(sx_engine *e, sx::AttnFusedArgs &a);
+// Device RoPE inverse-frequency table for (rotary_dim, theta); created on first use, never
+// inside a stream capture.
+float *sx_host_inv_freq(sx_engine *e, uint32_t rot, float theta, sx_status *st);
 sx_status sx_host_cuda_status(cudaError_t e, const char *what);

@@ -6,13 +6,38 @@
 
 namespace sx {
 
+// GEMV input prologues and epilogues (see sx_gemv.cu)
+enum GemvPrologue : int { kProNone = 0, kProNorm = 1, kProResid = 2 };
+enum GemvEpilogue : int { kEpiPlain = 0, kEpiArgmax = 2 };
+
 struct GemvArgs {
-  const void *w0;      // packed matrix (gate matrix for the fused GeGLU)
-  const void *w1;      // packed up matrix (fused GeGLU only)
-  const float *x;      // [batch][ldx]
-  float *y;            // [batch][ldy]
-  uint32_t m, k, batch;
-  uint32_t ldx, ldy;
+  // up to three row-concatenated matrices (e.g. q | k | v); w[s][1] is the up matrix of the
+  // fused GeGLU; y[s] receives the rows of segment s
+  const void *w[3][2];
+  float *y[3];
+  uint32_t rows[3];
+  uint32_t tiles[3];      // tiles_of(rows[s]); 0 for unused segments
+  uint32_t row_base[3];   // global row index of segment s (argmax ids)
+  uint32_t k, batch, ldy;
+  const float *x;         // [batch][ldx] input, or the residual stream for kProResid
+  uint32_t ldx;
+  int pro;
+  const float *pro_w;       // norm gain
+  const float *pro_mlp;     // kProResid: sublayer output added to x
+  const float *pro_post_w;  // kProResid: optional post-norm gain of the sublayer output
+  float *pro_x_out;         // kProResid: updated residual stream (must not alias x)
+  float pro_scalar;         // kProResid: layer scalar
+  float eps;
+  int epi;
+  uint32_t *token;          // kEpiArgmax: [batch] greedy ids
+  // scratch (engine-owned): split-tile records, per-tile arrival counters (zero at rest),
+  // per-worker argmax candidates, the argmax arrival counter (zero at rest)
+  float *part;
+  uint32_t *tile_cnt;
+  float *best_v;
+  uint32_t *best_i;
+  uint32_t *done_cnt;
+  uint32_t *err;
 };
 
 // Per-device kernel attributes (dynamic shared memory limits); called at engine creation,
@@ -20,9 +45,14 @@ struct GemvArgs {
 cudaError_t prepare_gemv_kernels();
 cudaError_t prepare_ops_kernels();
 
-// qt: 4 or 8.  geglu: fused gate+up with gelu_tanh(gate) * up epilogue.
-cudaError_t launch_gemv(int qt, bool geglu, const GemvArgs &a, int num_sms, cudaStream_t s);
-size_t gemv_smem_bytes(int qt, uint32_t k, uint32_t batch);
+// qt: 4 or 8.  geglu: fused gate+up with gelu_tanh(gate) * up epilogue.  pdl: launch with
+// programmatic stream serialization (the kernel prefetches weights before waiting).
+cudaError_t launch_gemv(int qt, bool geglu, const GemvArgs &a, int num_sms, cudaStream_t s,
+                        bool pdl);
+size_t gemv_smem_bytes(int qt, uint32_t k, uint32_t batch, bool geglu, bool prologue);
+size_t gemv_part_bytes(int num_sms);
+size_t gemv_best_bytes(int num_sms);
+constexpr uint32_t kMaxGemvTiles = 262144;
 
 cudaError_t launch_repack(int qt, const uint32_t *ref, void *packed, uint32_t m, uint32_t k,
                           cudaStream_t s);
@@ -71,6 +101,21 @@ struct AttnArgs {
 };
 size_t attn_scratch_bytes(uint32_t num_q, uint32_t total_slots, uint32_t head_dim);
 cudaError_t launch_decode_attn(const AttnArgs &a, cudaStream_t s);
+
+struct AttnFusedArgs {
+  const float *q, *k, *v;          // raw projections of this token
+  const float *q_norm_w, *k_norm_w;
+  const float *inv_freq;
+  void *k_cache, *v_cache;
+  const uint32_t *slots, *step;
+  float *out;
+  float *part;                     // [num_q][nchunks][head_dim + 2]
+  uint32_t *cnt;                   // [num_kv], zero at rest
+  uint32_t head_dim, kv_dim, num_q, num_kv, rotary_dim, k_eq_v, kv_bf16, total_slots;
+  float scale, eps;
+  uint32_t *err;
+};
+cudaError_t launch_attn_fused(const AttnFusedArgs &a, cudaStream_t s, bool pdl);
 
 cudaError_t launch_argmax(const float *logits, uint32_t n, uint32_t *out, void *scratch,
                           size_t scratch_bytes, cudaStream_t s);

@@ -43,7 +43,7 @@ struct sx_model {
   sx_model_config c{};
   uint32_t total_slots = 0, max_q = 0, max_kv = 0;
   std::vector<LayerBufs> L;
-  sx_buffer *x = nullptr, *normed = nullptr, *q = nullptr, *k = nullptr, *v = nullptr;
+  sx_buffer *x = nullptr, *x2 = nullptr, *normed = nullptr, *q = nullptr, *k = nullptr, *v = nullptr;
   sx_buffer *attn_out = nullptr, *slots = nullptr, *act = nullptr, *mlp_out = nullptr;
   sx_buffer *logits = nullptr, *token = nullptr, *step = nullptr;
   sx_buffer *lm_head = nullptr, *final_norm = nullptr;
@@ -96,6 +96,7 @@ sx_status alloc_model(sx_model *m) {
     if (B.kv_dim > m->max_kv) m->max_kv = B.kv_dim;
   }
   M_TRY(mk_buf(m, 4ull * H, &m->x));
+  M_TRY(mk_buf(m, 4ull * H, &m->x2));
   M_TRY(mk_buf(m, 4ull * H, &m->normed));
   M_TRY(mk_buf(m, 4ull * m->max_q, &m->q));
   M_TRY(mk_buf(m, 4ull * m->max_kv, &m->k));
@@ -244,6 +245,175 @@ sx_status record_forward(sx_model *m, sx_cmd *cmd, bool logits, bool io) {
   return sx_cmd_end(cmd);
 }
 
+// The fused decode graph: per layer
+//   [prologue: residual update of the previous layer + input RMSNorm] q|k|v GEMV
+//   -> fused qkv_rope + decode attention -> o GEMV
+//   -> [prologue: residual + pre-FFN RMSNorm] gate+up GeGLU GEMV -> down GEMV
+// and a Q8 LM head whose prologue applies the last residual update and the final norm and
+// whose epilogue is the argmax.  Same arithmetic as recordLayerDirect, 5 launches per layer
+// instead of 14, all chained with programmatic dependent launch.
+void push_gemv(sx_model *m, sx_cmd *cmd, const sx::GemvArgs &a, int qt, bool geglu) {
+  Op op{OP_GEMV_FUSED};
+  op.qt = qt;
+  op.geglu = geglu;
+  op.gemv = a;
+  sx_host_bind_scratch(m->e, op.gemv);
+  sx_host_push_op(cmd, op);
+}
+
+sx::GemvArgs gemv1(const sx_buffer *w, const sx_buffer *x, sx_buffer *y, uint32_t rows,
+                   uint32_t k) {
+  sx::GemvArgs a{};
+  a.w[0][0] = a.w[0][1] = w->d;
+  a.y[0] = (float *)y->d;
+  a.rows[0] = rows;
+  a.tiles[0] = sx::tiles_of(rows);
+  a.k = k;
+  a.batch = 1;
+  a.ldy = rows;
+  a.x = (const float *)x->d;
+  a.ldx = k;
+  a.pro = sx::kProNone;
+  a.epi = sx::kEpiPlain;
+  return a;
+}
+
+sx_status record_forward_fused(sx_model *m, sx_cmd *cmd, bool logits, bool io) {
+  const sx_model_config &c = m->c;
+  const uint32_t H = c.hidden_size, I = c.intermediate_size, L = c.num_layers;
+  const float eps = c.rms_norm_eps;
+  M_TRY(sx_cmd_begin(cmd));
+  if (io) {
+    Op a{OP_H2D};
+    a.host = m->h_x; a.dev = m->x->d; a.bytes = 4ull * H;
+    sx_host_push_op(cmd, a);
+    Op b{OP_H2D};
+    b.host = m->h_slots; b.dev = m->slots->d; b.bytes = 4ull * m->total_slots;
+    sx_host_push_op(cmd, b);
+    Op s{OP_H2D};
+    s.host = m->h_step; s.dev = m->step->d; s.bytes = 16;
+    sx_host_push_op(cmd, s);
+  }
+  for (uint32_t l = 0; l < L; ++l) {
+    LayerBufs &B = m->L[l];
+    // q | k | v with the input norm (and, after layer 0, the previous layer's residual)
+    sx::GemvArgs q{};
+    const sx_buffer *w3[3] = {B.wq, B.wk, B.wv};
+    sx_buffer *y3[3] = {m->q, m->k, m->v};
+    uint32_t r3[3] = {B.q_dim, B.kv_dim, B.kv_dim};
+    uint32_t base = 0;
+    for (int s = 0; s < 3; ++s) {
+      q.w[s][0] = q.w[s][1] = w3[s]->d;
+      q.y[s] = (float *)y3[s]->d;
+      q.rows[s] = r3[s];
+      q.tiles[s] = sx::tiles_of(r3[s]);
+      q.row_base[s] = base;
+      base += r3[s];
+    }
+    q.k = H;
+    q.batch = 1;
+    q.ldy = base;
+    q.ldx = H;
+    q.eps = eps;
+    q.pro_w = (const float *)B.in_norm->d;
+    if (l == 0) {
+      q.pro = sx::kProNorm;
+      q.x = (const float *)m->x->d;
+    } else {
+      LayerBufs &P = m->L[l - 1];
+      q.pro = sx::kProResid;
+      q.x = (const float *)m->x2->d;
+      q.pro_mlp = (const float *)m->mlp_out->d;
+      q.pro_post_w = c.has_post_norms ? (const float *)P.post_ffn->d : nullptr;
+      q.pro_scalar = P.layer_scalar;
+      q.pro_x_out = (float *)m->x->d;
+    }
+    q.epi = sx::kEpiPlain;
+    M_TRY(sx_host_check_gemv(4, false, true, B.q_dim + 2 * B.kv_dim, H, 1));
+    push_gemv(m, cmd, q, 4, false);
+
+    // fused qkv_rope + attention
+    Op at{OP_ATTN_FUSED};
+    sx::AttnFusedArgs &A = at.attnf;
+    A.q = (const float *)m->q->d;
+    A.k = (const float *)m->k->d;
+    A.v = (const float *)m->v->d;
+    A.q_norm_w = (const float *)B.q_norm->d;
+    A.k_norm_w = (const float *)B.k_norm->d;
+    A.k_cache = B.kc->d;
+    A.v_cache = B.vc->d;
+    A.slots = (const uint32_t *)m->slots->d;
+    A.step = (const uint32_t *)m->step->d;
+    A.out = (float *)m->attn_out->d;
+    A.head_dim = B.head_dim;
+    A.kv_dim = B.kv_dim;
+    A.num_q = c.num_q_heads;
+    A.num_kv = B.num_kv;
+    A.rotary_dim = B.rot;
+    A.k_eq_v = B.k_eq_v;
+    A.kv_bf16 = c.kv_bf16 ? 1u : 0u;
+    A.total_slots = m->total_slots;
+    A.scale = c.attn_scale;
+    A.eps = eps;
+    at.attn_rot = B.rot;
+    at.attn_theta = B.theta;
+    sx_host_bind_scratch(m->e, A);
+    if (sx::attn_scratch_bytes(c.num_q_heads, m->total_slots, B.head_dim) > m->e->attn_part_bytes ||
+        B.num_kv > 4096) {
+      sx_host_set_error("model: attention scratch too small for this ring / head count");
+      return SX_ERR_UNSUPPORTED;
+    }
+    sx_host_push_op(cmd, at);
+
+    // o projection
+    M_TRY(sx_host_check_gemv(4, false, false, H, B.q_dim, 1));
+    push_gemv(m, cmd, gemv1(B.wo, m->attn_out, m->mlp_out, H, B.q_dim), 4, false);
+
+    // gate+up GeGLU with the post-attention residual and pre-FFN norm
+    sx::GemvArgs g = gemv1(B.wg, m->x, m->act, I, H);
+    g.w[0][1] = B.wu->d;
+    g.pro = sx::kProResid;
+    g.pro_mlp = (const float *)m->mlp_out->d;
+    g.pro_post_w = c.has_post_norms ? (const float *)B.post_attn->d : nullptr;
+    g.pro_scalar = 1.0f;
+    g.pro_w = (const float *)B.pre_ffn->d;
+    g.pro_x_out = (float *)m->x2->d;
+    g.eps = eps;
+    M_TRY(sx_host_check_gemv(4, true, true, I, H, 1));
+    push_gemv(m, cmd, g, 4, true);
+
+    // down projection
+    M_TRY(sx_host_check_gemv(4, false, false, H, I, 1));
+    push_gemv(m, cmd, gemv1(B.wd, m->act, m->mlp_out, H, I), 4, false);
+  }
+  if (logits) {
+    LayerBufs &P = m->L[L - 1];
+    sx::GemvArgs h = gemv1(m->lm_head, m->x2, m->logits, c.vocab_size, H);
+    h.pro = sx::kProResid;
+    h.pro_mlp = (const float *)m->mlp_out->d;
+    h.pro_post_w = c.has_post_norms ? (const float *)P.post_ffn->d : nullptr;
+    h.pro_scalar = P.layer_scalar;
+    h.pro_w = (const float *)m->final_norm->d;
+    h.pro_x_out = (float *)m->x->d;
+    h.eps = eps;
+    h.epi = sx::kEpiArgmax;
+    h.token = (uint32_t *)m->token->d;
+    M_TRY(sx_host_check_gemv(8, false, true, c.vocab_size, H, 1));
+    push_gemv(m, cmd, h, 8, false);
+    if (io) {
+      Op t{OP_D2H};
+      t.host = m->h_token; t.dev = m->token->d; t.bytes = 4;
+      sx_host_push_op(cmd, t);
+    }
+  }
+  return sx_cmd_end(cmd);
+}
+
+sx_status record_graph(sx_model *m, sx_cmd *cmd, bool logits, bool io) {
+  return m->c.reference_graph ? record_forward(m, cmd, logits, io)
+                              : record_forward_fused(m, cmd, logits, io);
+}
+
 sx_status synth_matrix(sx_model *m, sx_buffer *dst, uint32_t rows, uint32_t cols,
                        sx_quant_mode mode, uint64_t seed, uint64_t stream, void *tmp,
                        uint64_t tmp_bytes) {
@@ -305,7 +475,7 @@ SX_API sx_status sx_model_create(sx_engine *e, const sx_model_config *cfg, sx_mo
   for (int lg = 0; lg < 2 && st == SX_OK; ++lg)
     for (int io = 0; io < 2 && st == SX_OK; ++io) {
       st = sx_cmd_create(e, &m->cmd[lg][io]);
-      if (st == SX_OK) st = record_forward(m, m->cmd[lg][io], lg != 0, io != 0);
+      if (st == SX_OK) st = record_graph(m, m->cmd[lg][io], lg != 0, io != 0);
     }
   if (st != SX_OK) {
     std::string msg = sx_last_error();
@@ -382,7 +552,7 @@ SX_API sx_status sx_model_synth_weights(sx_model *m, uint64_t seed) {
   // layer scalars are recorded into the graphs: re-record them
   for (int lg = 0; lg < 2 && st == SX_OK; ++lg)
     for (int io = 0; io < 2 && st == SX_OK; ++io)
-      st = record_forward(m, m->cmd[lg][io], lg != 0, io != 0);
+      st = record_graph(m, m->cmd[lg][io], lg != 0, io != 0);
   return st;
 }
 

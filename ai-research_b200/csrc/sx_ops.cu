@@ -3,9 +3,29 @@
 #include "sx_common.cuh"
 #include "sx_internal.h"
 
+#include <utility>
+
 namespace sx {
 
 namespace {
+
+// Launch with programmatic stream serialization: every kernel here calls
+// griddepcontrol.wait before it touches data written by the previous kernel.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                       cudaStream_t s, Args &&...args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+}
 
 // ---------------------------------------------------------------------------
 // rmsnorm.wgsl:352-387 and add_rmsnorm.wgsl:303-338.
@@ -15,6 +35,8 @@ namespace {
 template <bool ADD>
 __global__ void __launch_bounds__(1024) rmsnorm_kernel(NormArgs a) {
   __shared__ float red[32];
+  pdl_launch_dependents();
+  pdl_wait();
   float *x = a.x + (size_t)blockIdx.x * a.ld;
   const float *r = ADD ? a.r + (size_t)blockIdx.x * a.ld : nullptr;
   float *y = a.y + (size_t)blockIdx.x * a.ld;
@@ -42,6 +64,8 @@ __global__ void __launch_bounds__(1024) rmsnorm_kernel(NormArgs a) {
 // table 1/pow(theta, 2i/rot) (kernels.zig:138) so CPU and GPU angles agree bit for bit.
 __global__ void __launch_bounds__(128) qkv_rope_kernel(QkvRopeArgs a) {
   extern __shared__ float sh[];  // head_dim floats + 32 reduction slots
+  pdl_launch_dependents();
+  pdl_wait();
   float *vec = sh;
   float *red = sh + a.head_dim;
   const uint32_t D = a.head_dim, half = a.rotary_dim / 2;
@@ -165,6 +189,8 @@ SX_DEV void load_row(const void *cache, size_t off, int lane, float (&v)[DPL]) {
 template <int DPL, int G, bool BF16>
 __global__ void __launch_bounds__(kAttnWarps * 32) attn_split_kernel(AttnArgs a) {
   extern __shared__ float sh[];
+  pdl_launch_dependents();
+  pdl_wait();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t D = a.head_dim;  // == 32 * DPL
   const uint32_t kvh = blockIdx.x, chunk = blockIdx.y, nchunks = gridDim.y;
@@ -252,6 +278,8 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_split_kernel(AttnArgs a)
 }
 
 __global__ void attn_combine_kernel(AttnArgs a, uint32_t nchunks) {
+  pdl_launch_dependents();
+  pdl_wait();
   const uint32_t qh = blockIdx.x, D = a.head_dim;
   const float *base = a.part + (size_t)qh * nchunks * (D + 2);
   float M = -INFINITY;
@@ -270,6 +298,229 @@ __global__ void attn_combine_kernel(AttnArgs a, uint32_t nchunks) {
   }
 }
 
+// ---------------------------------------------------------------------------
+// Fused decode attention for the model graph: qkv_rope + decode_attn (+ the combine) in one
+// launch.  CTA (kv head h, slot chunk) normalises and rotates the q heads of its GQA group and
+// the new k/v of head h (qkv_rope.wgsl semantics, identical rounding to the cache), chunk 0
+// stores the new K/V at the current slot, every CTA runs the online softmax over its 32 slots
+// (taking the current slot's K/V from shared memory rather than the cache), and the last CTA
+// of the head to finish merges the chunk partials in chunk order.
+template <int DPL, int G, bool BF16>
+__global__ void __launch_bounds__(kAttnWarps * 32) attn_fused_kernel(AttnFusedArgs a) {
+  extern __shared__ float sh[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t D = 32 * DPL;
+  const uint32_t kvh = blockIdx.x, chunk = blockIdx.y, nchunks = gridDim.y;
+  float *qs = sh;                       // [G][D] normalised, rotated q
+  float *kn = qs + G * D;               // [D] new K (cache precision)
+  float *vn = kn + D;                   // [D] new V (cache precision)
+  float *red = vn + D;                  // [32]
+  float *wm = red + 32;                 // [warps][G]
+  float *wl = wm + kAttnWarps * G;      // [warps][G]
+  float *wo = wl + kAttnWarps * G;      // [warps][G][D]
+  __shared__ uint32_t last_flag;
+
+  pdl_launch_dependents();
+  pdl_wait();
+  const uint32_t clock = a.step[0], slot = a.step[1];
+  uint32_t S = a.step[2];
+  if (S > a.total_slots || slot >= a.total_slots) {
+    if (threadIdx.x == 0 && chunk == 0 && kvh == 0) raise_error(a.err, kDevBadParams);
+    S = S > a.total_slots ? a.total_slots : S;
+  }
+  const bool slot_ok = slot < a.total_slots;
+  const uint32_t half = a.rotary_dim / 2;
+  const float fclock = (float)clock;
+
+  // normalise + rotate one head vector held in buf (in place); w = gain or nullptr (unit norm)
+  auto norm_rope = [&](float *buf, const float *w, bool rope) {
+    float ss = 0.0f;
+    for (uint32_t d = threadIdx.x; d < D; d += blockDim.x) ss = fmaf(buf[d], buf[d], ss);
+    ss = block_sum(ss, red);
+    float rs = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)D), a.eps)));
+    __syncthreads();
+    for (uint32_t d = threadIdx.x; d < D; d += blockDim.x)
+      buf[d] = w ? __fmul_rn(__fmul_rn(buf[d], rs), w[d]) : __fmul_rn(buf[d], rs);
+    __syncthreads();
+    if (rope) {
+      for (uint32_t i = threadIdx.x; i < half; i += blockDim.x) {
+        float ang = __fmul_rn(fclock, a.inv_freq[i]);
+        float sn, cs;
+        sincosf(ang, &sn, &cs);
+        float v0 = buf[i], v1 = buf[i + half];
+        buf[i] = __fsub_rn(__fmul_rn(v0, cs), __fmul_rn(v1, sn));
+        buf[i + half] = __fadd_rn(__fmul_rn(v0, sn), __fmul_rn(v1, cs));
+      }
+      __syncthreads();
+    }
+  };
+  for (int h = 0; h < G; ++h) {
+    for (uint32_t d = threadIdx.x; d < D; d += blockDim.x)
+      qs[h * D + d] = a.q[(size_t)(kvh * G + h) * D + d];
+    __syncthreads();
+    norm_rope(qs + h * D, a.q_norm_w, true);
+  }
+  for (uint32_t d = threadIdx.x; d < D; d += blockDim.x) {
+    kn[d] = a.k[(size_t)kvh * D + d];
+    vn[d] = (a.k_eq_v ? a.k : a.v)[(size_t)kvh * D + d];
+  }
+  __syncthreads();
+  norm_rope(kn, a.k_norm_w, true);
+  norm_rope(vn, nullptr, false);
+  const size_t new_off = ((size_t)slot * a.num_kv + kvh) * D;
+  for (uint32_t d = threadIdx.x; d < D; d += blockDim.x) {
+    if (BF16) {
+      uint16_t kb = bf16_bits_rne(kn[d]), vb = bf16_bits_rne(vn[d]);
+      kn[d] = bf16_bits_to_f32(kb);
+      vn[d] = bf16_bits_to_f32(vb);
+      if (chunk == 0 && slot_ok) {
+        reinterpret_cast<uint16_t *>(a.k_cache)[new_off + d] = kb;
+        reinterpret_cast<uint16_t *>(a.v_cache)[new_off + d] = vb;
+      }
+    } else if (chunk == 0 && slot_ok) {
+      reinterpret_cast<float *>(a.k_cache)[new_off + d] = kn[d];
+      reinterpret_cast<float *>(a.v_cache)[new_off + d] = vn[d];
+    }
+  }
+  __syncthreads();
+
+  float m[G], l[G], o[G][DPL], qr[G][DPL];
+#pragma unroll
+  for (int h = 0; h < G; ++h) {
+    m[h] = -INFINITY;
+    l[h] = 0.0f;
+#pragma unroll
+    for (int i = 0; i < DPL; ++i) {
+      o[h][i] = 0.0f;
+      qr[h][i] = qs[h * D + lane * DPL + i];
+    }
+  }
+  const uint32_t s0 = chunk * kAttnChunk, s1 = min(S, s0 + kAttnChunk);
+  for (uint32_t si = s0 + warp; si < s1; si += kAttnWarps) {
+    uint32_t sl = a.slots[si];
+    if (sl >= a.total_slots) {
+      if (lane == 0) raise_error(a.err, kDevBadSlot);
+      continue;
+    }
+    float kr[DPL], vr[DPL];
+    if (sl == slot) {
+#pragma unroll
+      for (int i = 0; i < DPL; ++i) {
+        kr[i] = kn[lane * DPL + i];
+        vr[i] = vn[lane * DPL + i];
+      }
+    } else {
+      size_t off = (size_t)sl * a.kv_dim + (size_t)kvh * D;
+      load_row<DPL, BF16>(a.k_cache, off, lane, kr);
+      load_row<DPL, BF16>(a.v_cache, off, lane, vr);
+    }
+#pragma unroll
+    for (int h = 0; h < G; ++h) {
+      float part = 0.0f;
+#pragma unroll
+      for (int i = 0; i < DPL; ++i) part = fmaf(qr[h][i], kr[i], part);
+      float sc = warp_sum(part) * a.scale;
+      float mn = fmaxf(m[h], sc);
+      float corr = expf(m[h] - mn);
+      float p = expf(sc - mn);
+      l[h] = fmaf(l[h], corr, p);
+#pragma unroll
+      for (int i = 0; i < DPL; ++i) o[h][i] = fmaf(o[h][i], corr, p * vr[i]);
+      m[h] = mn;
+    }
+  }
+#pragma unroll
+  for (int h = 0; h < G; ++h) {
+    if (lane == 0) {
+      wm[warp * G + h] = m[h];
+      wl[warp * G + h] = l[h];
+    }
+#pragma unroll
+    for (int i = 0; i < DPL; ++i) wo[(warp * G + h) * D + lane * DPL + i] = o[h][i];
+  }
+  __syncthreads();
+  for (uint32_t idx = threadIdx.x; idx < G * D; idx += blockDim.x) {
+    uint32_t h = idx / D, d = idx % D;
+    float M = -INFINITY;
+    for (int w = 0; w < kAttnWarps; ++w) M = fmaxf(M, wm[w * G + h]);
+    float Lsum = 0.0f, O = 0.0f;
+    for (int w = 0; w < kAttnWarps; ++w) {
+      float f = M == -INFINITY ? 0.0f : expf(wm[w * G + h] - M);
+      Lsum = fmaf(wl[w * G + h], f, Lsum);
+      O = fmaf(wo[(w * G + h) * D + d], f, O);
+    }
+    float *rec = a.part + ((size_t)(kvh * G + h) * nchunks + chunk) * (D + 2);
+    rec[2 + d] = O;
+    if (d == 0) {
+      rec[0] = M;
+      rec[1] = Lsum;
+    }
+  }
+  // last CTA of this kv head merges the chunks
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) last_flag = (atomicAdd(&a.cnt[kvh], 1u) + 1 == nchunks) ? 1u : 0u;
+  __syncthreads();
+  if (!last_flag) return;
+  __threadfence();
+  for (uint32_t idx = threadIdx.x; idx < G * D; idx += blockDim.x) {
+    uint32_t h = idx / D, d = idx % D;
+    const float *base = a.part + (size_t)(kvh * G + h) * nchunks * (D + 2);
+    float M = -INFINITY;
+    for (uint32_t c = 0; c < nchunks; ++c) M = fmaxf(M, __ldcg(base + (size_t)c * (D + 2)));
+    float L = 0.0f, O = 0.0f;
+    if (M != -INFINITY) {
+      for (uint32_t c = 0; c < nchunks; ++c) {
+        const float *rec = base + (size_t)c * (D + 2);
+        float f = expf(__ldcg(rec) - M);
+        L = fmaf(__ldcg(rec + 1), f, L);
+        O = fmaf(__ldcg(rec + 2 + d), f, O);
+      }
+    }
+    a.out[(size_t)(kvh * G + h) * D + d] = L > 0.0f ? O / L : 0.0f;
+  }
+  if (threadIdx.x == 0) a.cnt[kvh] = 0;
+}
+
+template <int DPL, int G>
+cudaError_t launch_attn_fused_t(const AttnFusedArgs &a, cudaStream_t s, bool pdl) {
+  uint32_t nchunks = (a.total_slots + kAttnChunk - 1) / kAttnChunk;
+  size_t D = 32 * DPL;
+  size_t smem = sizeof(float) * (G * D + 2 * D + 32 + 2 * kAttnWarps * G + kAttnWarps * G * D);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(a.num_kv, nchunks);
+  cfg.blockDim = dim3(kAttnWarps * 32);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  if (a.kv_bf16) return cudaLaunchKernelEx(&cfg, attn_fused_kernel<DPL, G, true>, a);
+  return cudaLaunchKernelEx(&cfg, attn_fused_kernel<DPL, G, false>, a);
+}
+
+template <int DPL>
+cudaError_t launch_attn_fused_d(const AttnFusedArgs &a, cudaStream_t s, bool pdl) {
+  switch (a.num_q / a.num_kv) {
+    case 1: return launch_attn_fused_t<DPL, 1>(a, s, pdl);
+    case 2: return launch_attn_fused_t<DPL, 2>(a, s, pdl);
+    case 4: return launch_attn_fused_t<DPL, 4>(a, s, pdl);
+    case 8: return launch_attn_fused_t<DPL, 8>(a, s, pdl);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+template <int DPL, int G>
+cudaError_t prepare_attn_fused_t() {
+  cudaError_t a = cudaFuncSetAttribute(attn_fused_kernel<DPL, G, true>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+  cudaError_t b = cudaFuncSetAttribute(attn_fused_kernel<DPL, G, false>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+  return a != cudaSuccess ? a : b;
+}
+
 template <int DPL, int G>
 cudaError_t launch_attn_t(const AttnArgs &a, cudaStream_t s) {
   uint32_t num_kv = a.num_q / G;
@@ -277,11 +528,9 @@ cudaError_t launch_attn_t(const AttnArgs &a, cudaStream_t s) {
   size_t smem = sizeof(float) * (G * a.head_dim + 2 * kAttnWarps * G +
                                  (size_t)kAttnWarps * G * a.head_dim);
   auto kern = a.kv_bf16 ? attn_split_kernel<DPL, G, true> : attn_split_kernel<DPL, G, false>;
-  kern<<<dim3(num_kv, nchunks), kAttnWarps * 32, smem, s>>>(a);
-  cudaError_t e = cudaGetLastError();
+  cudaError_t e = launch_pdl(kern, dim3(num_kv, nchunks), dim3(kAttnWarps * 32), smem, s, a);
   if (e != cudaSuccess) return e;
-  attn_combine_kernel<<<a.num_q, 256, 0, s>>>(a, nchunks);
-  return cudaGetLastError();
+  return launch_pdl(attn_combine_kernel, dim3(a.num_q), dim3(256), 0, s, a, nchunks);
 }
 
 template <int DPL, int G>
@@ -295,8 +544,10 @@ cudaError_t prepare_attn_t() {
 
 template <int DPL>
 cudaError_t prepare_attn_d() {
-  cudaError_t r[4] = {prepare_attn_t<DPL, 1>(), prepare_attn_t<DPL, 2>(),
-                      prepare_attn_t<DPL, 4>(), prepare_attn_t<DPL, 8>()};
+  cudaError_t r[8] = {prepare_attn_t<DPL, 1>(),       prepare_attn_t<DPL, 2>(),
+                      prepare_attn_t<DPL, 4>(),       prepare_attn_t<DPL, 8>(),
+                      prepare_attn_fused_t<DPL, 1>(), prepare_attn_fused_t<DPL, 2>(),
+                      prepare_attn_fused_t<DPL, 4>(), prepare_attn_fused_t<DPL, 8>()};
   for (cudaError_t x : r)
     if (x != cudaSuccess) return x;
   return cudaSuccess;
@@ -328,6 +579,8 @@ __global__ void __launch_bounds__(kArgmaxThreads) argmax_partial_kernel(const fl
                                                                          uint32_t n,
                                                                          float2 *part) {
   __shared__ float sv[kArgmaxThreads];
+  pdl_launch_dependents();
+  pdl_wait();
   __shared__ uint32_t si[kArgmaxThreads];
   uint32_t i0 = blockIdx.x * blockDim.x + threadIdx.x, stride = gridDim.x * blockDim.x;
   float bv = -INFINITY;
@@ -365,6 +618,8 @@ __global__ void __launch_bounds__(kArgmaxThreads) argmax_partial_kernel(const fl
 __global__ void argmax_final_kernel(const float *x, const float2 *part, uint32_t nparts,
                                     uint32_t *out) {
   __shared__ float sv[kArgmaxThreads];
+  pdl_launch_dependents();
+  pdl_wait();
   __shared__ uint32_t si[kArgmaxThreads];
   float bv = -INFINITY;
   uint32_t bi = 0xFFFFFFFFu;
@@ -413,17 +668,13 @@ cudaError_t prepare_ops_kernels() {
 cudaError_t launch_rmsnorm(bool add, const NormArgs &a, cudaStream_t s) {
   uint32_t threads = a.n >= 1024 ? 1024 : ((a.n + 31) / 32) * 32;
   if (threads == 0) threads = 32;
-  if (add)
-    rmsnorm_kernel<true><<<a.batch, threads, 0, s>>>(a);
-  else
-    rmsnorm_kernel<false><<<a.batch, threads, 0, s>>>(a);
-  return cudaGetLastError();
+  if (add) return launch_pdl(rmsnorm_kernel<true>, dim3(a.batch), dim3(threads), 0, s, a);
+  return launch_pdl(rmsnorm_kernel<false>, dim3(a.batch), dim3(threads), 0, s, a);
 }
 
 cudaError_t launch_qkv_rope(const QkvRopeArgs &a, cudaStream_t s) {
   size_t smem = sizeof(float) * (a.head_dim + 32);
-  qkv_rope_kernel<<<a.num_q + a.num_kv, 128, smem, s>>>(a);
-  return cudaGetLastError();
+  return launch_pdl(qkv_rope_kernel, dim3(a.num_q + a.num_kv), dim3(128), smem, s, a);
 }
 
 size_t attn_scratch_bytes(uint32_t num_q, uint32_t total_slots, uint32_t head_dim) {
@@ -441,17 +692,28 @@ cudaError_t launch_decode_attn(const AttnArgs &a, cudaStream_t s) {
   }
 }
 
+cudaError_t launch_attn_fused(const AttnFusedArgs &a, cudaStream_t s, bool pdl) {
+  if (a.num_kv == 0 || a.num_q % a.num_kv != 0) return cudaErrorInvalidValue;
+  switch (a.head_dim) {
+    case 64: return launch_attn_fused_d<2>(a, s, pdl);
+    case 128: return launch_attn_fused_d<4>(a, s, pdl);
+    case 256: return launch_attn_fused_d<8>(a, s, pdl);
+    case 512: return launch_attn_fused_d<16>(a, s, pdl);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
 size_t argmax_scratch_bytes() { return sizeof(float2) * kArgmaxBlocks; }
 
 cudaError_t launch_argmax(const float *logits, uint32_t n, uint32_t *out, void *scratch,
                           size_t scratch_bytes, cudaStream_t s) {
   if (scratch_bytes < argmax_scratch_bytes() || n == 0) return cudaErrorInvalidValue;
   float2 *part = static_cast<float2 *>(scratch);
-  argmax_partial_kernel<<<kArgmaxBlocks, kArgmaxThreads, 0, s>>>(logits, n, part);
-  cudaError_t e = cudaGetLastError();
+  cudaError_t e = launch_pdl(argmax_partial_kernel, dim3(kArgmaxBlocks), dim3(kArgmaxThreads), 0,
+                             s, logits, n, part);
   if (e != cudaSuccess) return e;
-  argmax_final_kernel<<<1, kArgmaxThreads, 0, s>>>(logits, part, kArgmaxBlocks, out);
-  return cudaGetLastError();
+  return launch_pdl(argmax_final_kernel, dim3(1), dim3(kArgmaxThreads), 0, s, logits,
+                    (const float2 *)part, (uint32_t)kArgmaxBlocks, out);
 }
 
 }  // namespace sx

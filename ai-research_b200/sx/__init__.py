@@ -65,6 +65,7 @@ class ModelConfig(C.Structure):
         ("rope_theta", C.c_float),
         ("rope_theta_full", C.c_float),
         ("attn_scale", C.c_float),
+        ("reference_graph", C.c_uint32),
     ]
 
     def as_dict(self) -> dict:
@@ -105,6 +106,7 @@ def model_config(**kw) -> ModelConfig:
         rope_theta=10000.0,
         rope_theta_full=1000000.0,
         attn_scale=1.0,
+        reference_graph=0,
     )
     base.update(kw)
     return ModelConfig(**base)

@@ -252,6 +252,8 @@ typedef struct {
   uint32_t full_every;       /* layer l is full attention when (l+1) % full_every == 0  */
   uint32_t attention_k_eq_v; /* types.zig:58                                            */
   float rms_norm_eps, rope_theta, rope_theta_full, attn_scale;
+  uint32_t reference_graph;  /* 1: record the reference's op-by-op graph through the record
+                                API (14 launches per layer); 0: the fused graph (5 per layer) */
 } sx_model_config;
 
 typedef struct sx_model sx_model;

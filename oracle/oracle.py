@@ -342,7 +342,8 @@ class Model:
     """Whole-model decode in the GPU graph's op order (model_dispatch.zig)."""
 
     def __init__(self, cfg: dict, seed: int, nthreads: int | None = None):
-        c = OrcConfig(**cfg)
+        names = {f for f, _ in OrcConfig._fields_}
+        c = OrcConfig(**{k: v for k, v in cfg.items() if k in names})
         self.cfg = dict(cfg)
         self.h = lib().orc_model_create(C.byref(c), seed, nthreads or threads())
         self.ring = Ring.borrow(lib().orc_model_ring(self.h))

@@ -68,6 +68,10 @@ GEMV_Q4_CASES = [
     (1536, 6144, 4),
     (6144, 1536, 8),   # BASELINE config 2 batch 8
     (1536, 6144, 8),
+    (16, 15360, 1),    # one tile split across hundreds of stream-K workers
+    (1, 4096, 1),      # a single row
+    (262144, 64, 1),   # many tiles, one pair each
+    (48, 1536, 5),
 ]
 
 

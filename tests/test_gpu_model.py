@@ -69,10 +69,11 @@ def run_decode(engine, cfg, seed, steps, start_clock, n_recall=0):
     return results
 
 
+@pytest.mark.parametrize("reference_graph", [0, 1])
 @pytest.mark.parametrize("kv_f32", [False, True])
-def test_greedy_decode_matches_checker(engine, engine_f32kv, kv_f32):
+def test_greedy_decode_matches_checker(engine, engine_f32kv, kv_f32, reference_graph):
     eng = engine_f32kv if kv_f32 else engine
-    cfg = tiny_cfg(kv_bf16=0 if kv_f32 else 1)
+    cfg = tiny_cfg(kv_bf16=0 if kv_f32 else 1, reference_graph=reference_graph)
     res = run_decode(eng, cfg, seed=3, steps=24, start_clock=0)  # window wraps twice
     for i, (tok, rtok, lg, rlg) in enumerate(res):
         assert_close(lg, rlg, what=f"logits step {i}")
@@ -80,8 +81,9 @@ def test_greedy_decode_matches_checker(engine, engine_f32kv, kv_f32):
             assert margin_top2(rlg) < 1e-3, f"step {i}: token {tok} vs {rtok}"
 
 
-def test_greedy_decode_with_recall_and_large_clock(engine):
-    cfg = tiny_cfg()
+@pytest.mark.parametrize("reference_graph", [0, 1])
+def test_greedy_decode_with_recall_and_large_clock(engine, reference_graph):
+    cfg = tiny_cfg(reference_graph=reference_graph)
     res = run_decode(engine, cfg, seed=9, steps=6, start_clock=90000, n_recall=3)
     for i, (tok, rtok, lg, rlg) in enumerate(res):
         assert_close(lg, rlg, what=f"logits step {i}")
@@ -102,8 +104,9 @@ def test_12b_width_two_layers_full_vocab(engine):
             assert margin_top2(rlg) < 1e-3
 
 
-def test_prefill_graph_skips_logits(engine):
-    cfg = tiny_cfg()
+@pytest.mark.parametrize("reference_graph", [0, 1])
+def test_prefill_graph_skips_logits(engine, reference_graph):
+    cfg = tiny_cfg(reference_graph=reference_graph)
     model = sx.Model(engine, sx.model_config(**cfg))
     model.synth_weights(1)
     ring = sx.Ring(1, 4, 8, 4)
@@ -112,6 +115,8 @@ def test_prefill_graph_skips_logits(engine):
     tok = model.forward_token(x, 0, slot, ring.get_active_slots(0, 0), want_logits=False)
     assert tok == 0
     assert model.kernels_per_token(False) < model.kernels_per_token(True)
+    per_layer = 14 if reference_graph else 5
+    assert model.kernels_per_token(False) == per_layer * cfg["num_layers"]
 
 
 def test_forward_token_rejects_oversized_slot_list(engine):
