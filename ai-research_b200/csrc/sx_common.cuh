@@ -238,6 +238,31 @@ SX_DEV void bulk_g2s(uint32_t dst, const void *src, uint32_t bytes, uint32_t bar
       : "memory");
 }
 
+// Ampere-style asynchronous 16-byte copies (LDGSTS), L1-bypassing, grouped per thread.
+SX_DEV void cp_async16(uint32_t dst, const void *src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(dst), "l"(src) : "memory");
+}
+SX_DEV void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
+template <int N>
+SX_DEV void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory");
+}
+
+// Allow a kernel the device's opt-in shared memory maximum minus its static shared memory.
+template <typename K>
+inline cudaError_t allow_max_dynamic_smem(K kernel) {
+  int dev = 0, optin = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  e = cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+  if (e != cudaSuccess) return e;
+  cudaFuncAttributes fa;
+  e = cudaFuncGetAttributes(&fa, kernel);
+  if (e != cudaSuccess) return e;
+  return cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                              optin - (int)fa.sharedSizeBytes);
+}
+
 // Programmatic dependent launch: wait for the producer grid's memory before reading it.
 SX_DEV void pdl_wait() { asm volatile("griddepcontrol.wait;\n" ::: "memory"); }
 SX_DEV void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;\n" ::); }

@@ -114,6 +114,8 @@ sx_status check_gemv_shape(int qt, bool geglu, bool pro, uint32_t m, uint32_t k,
   SX_CHECK_ARG(m > 0 && k > 0 && (k % 32) == 0, "gemv: need m > 0 and k a multiple of 32 (m=%u k=%u)", m, k);
   SX_CHECK_ARG(batch >= 1 && batch <= 8, "gemv: batch must be 1..8 (got %u)", batch);
   SX_CHECK_ARG(sx::tiles_of(m) <= sx::kMaxGemvTiles, "gemv: at most %u rows", sx::kMaxGemvTiles * 16);
+  SX_CHECK_ARG(!pro || k <= sx::kGemvPrologueMaxK, "gemv: fused norm prologue needs k <= %u",
+               sx::kGemvPrologueMaxK);
   size_t smem = sx::gemv_smem_bytes(qt, k, batch, geglu, pro);
   if (smem > 227 * 1024) {
     set_error("gemv: k=%u with batch %u needs %zu B of shared memory (max 227 KB)", k, batch, smem);
@@ -136,8 +138,8 @@ sx_status do_gemv(sx_engine *e, cudaStream_t s, int qt, bool geglu, const void *
   sx_status st = check_gemv_shape(qt, geglu, false, m, k, batch);
   if (st != SX_OK) return st;
   SX_CHECK_ARG(w0 && x && y && (!geglu || w1), "gemv: null pointer");
-  SX_CHECK_ARG(((uintptr_t)w0 | (uintptr_t)(geglu ? w1 : w0)) % 16 == 0,
-               "gemv: packed weights must be 16-byte aligned");
+  SX_CHECK_ARG(((uintptr_t)w0 | (uintptr_t)(geglu ? w1 : w0) | (uintptr_t)x) % 16 == 0,
+               "gemv: packed weights and x must be 16-byte aligned");
   sx::GemvArgs a{};
   a.w[0][0] = w0;
   a.w[0][1] = geglu ? w1 : w0;
@@ -521,7 +523,7 @@ SX_API sx_status sx_engine_create(int device, sx_quant_mode mode, uint32_t flags
         off = (off + bytes + 255) & ~(size_t)255;
         return o;
       };
-      const size_t nw_max = (size_t)e->num_sms * 2 * 8;
+      const size_t nw_max = sx::gemv_workers(e->num_sms);
       size_t o_attn = take(e->attn_part_bytes = 8u << 20);
       size_t o_acnt = take(4096 * 4);
       size_t o_gpart = take(sx::gemv_part_bytes(e->num_sms));

@@ -7,14 +7,14 @@
 // (kernels.zig:94-115); argmax = first index of the maximum (kernels.zig:164-174).
 //
 // Work split.  The matrix (or the concatenation of up to three matrices, e.g. q|k|v) is a
-// sequence of N = tiles x pairs 640-byte chunks (16 rows x 64 columns; 1152 B for Q8).  Every
-// warp of a persistent grid is a worker that owns a contiguous range of N / (CTAs x 8) chunks
-// ("stream-K"), so the load is balanced for any shape.  Each warp streams its chunks through
-// its own 8-stage shared-memory ring with cp.async.bulk + mbarrier (the first stages are
-// issued before the programmatic-dependent-launch wait, i.e. while the previous kernel is
-// still finishing).  A tile covered by one worker is written directly; a tile split between
-// workers is reduced by the last worker to arrive, summing the partial records in worker
-// order (deterministic; no atomics on the data).
+// sequence of N = tiles x pairs 640-byte chunks (16 rows x 64 columns; 1152 B for Q8).  One
+// persistent 512-thread CTA runs per SM and each of its 16 warps is a worker that owns a
+// contiguous range of N / (CTAs x 16) chunks ("stream-K"), so the load is balanced for any
+// shape.  Each warp streams its chunks through its own shared-memory ring of S stages with
+// 16-byte cp.async copies; the first S chunks are issued before the programmatic-dependent-
+// launch wait, i.e. while the previous kernel is still finishing.  A tile covered by one
+// worker is written directly; a tile split between workers is reduced by the last worker to
+// arrive, summing the partial records in worker order (deterministic; no atomics on data).
 //
 // Dequantisation.  Nibbles become mma.m16n8k16 A fragments with one shift + one LOP3 per two
 // weights (bf16 value 8 + q/2, exact).  The f32 activation enters as the B operand split into
@@ -29,9 +29,9 @@ namespace sx {
 
 namespace {
 
-constexpr int kThreads = 256;
+constexpr int kThreads = 512;  // one persistent CTA per SM, 16 stream-K workers
 constexpr int kWarps = kThreads / 32;
-constexpr int kStages = 8;
+constexpr uint32_t kSmemLimit = 227 * 1024;
 
 SX_HD uint32_t nv_of(uint32_t batch) {
   return batch <= 1 ? 2u : batch <= 2 ? 4u : batch <= 4 ? 8u : 16u;
@@ -53,23 +53,38 @@ struct QTraits<8> {
 };
 
 struct Layout {
-  uint32_t xfrag, corr, misc, xin, ring, bars, total;
+  uint32_t xfrag, corr, misc, xin, xin_bytes, ring, total;
 };
 
-// xfrag | corr | misc (xscale[8], xexp[8], red[32]) | xin (fused prologue) | ring | mbarriers
-SX_HD Layout layout_of(uint32_t k, uint32_t batch, int nmat, int qt, bool pro) {
+// xfrag | corr | misc (xscale[8], xexp[8], red[32]) | xin (f32 activation) | ring
+SX_HD Layout layout_of(uint32_t k, uint32_t batch, int nmat, int qt, bool with_xin, int stages) {
   Layout L;
   uint32_t nblk = 2 * pairs_of(k);
   L.xfrag = 0;
   L.corr = nblk * nv_of(batch) * 64;
   L.misc = L.corr + ((nblk * batch * 4 + 15) & ~15u);
   L.xin = L.misc + 48 * 4;
-  uint32_t xin_bytes = pro ? batch * k * 4 : 0;
-  L.ring = (L.xin + xin_bytes + 127) & ~127u;
+  L.xin_bytes = with_xin ? batch * k * 4 : 0;
+  L.ring = (L.xin + L.xin_bytes + 127) & ~127u;
   uint32_t chunk = qt == 4 ? kQ4ChunkBytes : kQ8ChunkBytes;
-  L.bars = L.ring + kWarps * kStages * nmat * chunk;
-  L.total = L.bars + kWarps * kStages * 8;
+  L.total = L.ring + kWarps * stages * nmat * chunk;
   return L;
+}
+
+// Deepest ring (8, 4 or 2 stages per warp) that fits in shared memory; 0 if none does.  x
+// gets its own staging area whenever it fits (the fused prologues require it).
+SX_HD int stages_for(uint32_t k, uint32_t batch, int nmat, int qt, bool pro) {
+  const int opts[3] = {8, 4, 2};
+  for (int s : opts)
+    if (layout_of(k, batch, nmat, qt, true, s).total <= kSmemLimit) return s;
+  if (!pro)
+    for (int s : opts)
+      if (layout_of(k, batch, nmat, qt, false, s).total <= kSmemLimit) return s;
+  return 0;
+}
+SX_HD Layout layout_for(uint32_t k, uint32_t batch, int nmat, int qt, int s) {
+  Layout L = layout_of(k, batch, nmat, qt, true, s);
+  return L.total <= kSmemLimit ? L : layout_of(k, batch, nmat, qt, false, s);
 }
 
 SX_DEV float gelu_tanh_dev(float x) {
@@ -79,57 +94,67 @@ SX_DEV float gelu_tanh_dev(float x) {
   return __fmul_rn(__fmul_rn(0.5f, x), __fadd_rn(1.0f, tanhf(inner)));
 }
 
-// ---------------------------------------------------------------------------------------
-// Fused input prologues (replace a separate norm launch).  Each CTA computes the GEMV input
-// for all batch rows into shared memory:
-//   kProNorm:  xin = rmsnorm(x, w)                                   (rmsnorm.wgsl)
-//   kProResid: v = post_w ? rmsnorm(mlp, post_w) : mlp; xn = (x + v) * scalar;
-//              CTA 0 writes xn to x_out; xin = rmsnorm(xn, w)         (add_rmsnorm.wgsl)
-SX_DEV float cta_sum(float v, float *red) { return block_sum(v, red); }
-
 SX_DEV float inv_rms(float ss, uint32_t n, float eps) {
   return __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)n), eps)));
 }
+
+// ---------------------------------------------------------------------------------------
+// Fused input prologues (replace a separate norm launch).  Each CTA computes the GEMV input
+// for all batch rows into shared memory with one round trip to global memory:
+//   kProNorm:  xin = rmsnorm(x, w)                                   (rmsnorm.wgsl)
+//   kProResid: v = post_w ? rmsnorm(mlp, post_w) : mlp; xn = (x + v) * scalar;
+//              CTA 0 writes xn to x_out; xin = rmsnorm(xn, w)         (add_rmsnorm.wgsl)
+constexpr int kProPer = 8;  // elements per thread held in registers: K <= 512 * 8
 
 SX_DEV void run_prologue(const GemvArgs &a, float *xin, float *red) {
   const uint32_t K = a.k;
   for (uint32_t j = 0; j < a.batch; ++j) {
     float *xo = xin + (size_t)j * K;
     const float *x = a.x + (size_t)j * a.ldx;
-    if (a.pro == kProNorm) {
-      float ss = 0.0f;
-      for (uint32_t i = threadIdx.x; i < K; i += blockDim.x) {
-        float v = x[i];
-        ss = fmaf(v, v, ss);
+    float xv[kProPer], mv[kProPer], pw[kProPer], nw[kProPer];
+#pragma unroll
+    for (int q = 0; q < kProPer; ++q) {
+      uint32_t i = threadIdx.x + q * blockDim.x;
+      bool in = i < K;
+      xv[q] = in ? x[i] : 0.0f;
+      nw[q] = in ? a.pro_w[i] : 0.0f;
+      mv[q] = 0.0f;
+      pw[q] = 0.0f;
+      if (a.pro == kProResid) {
+        mv[q] = in ? a.pro_mlp[(size_t)j * a.ldx + i] : 0.0f;
+        pw[q] = (in && a.pro_post_w) ? a.pro_post_w[i] : 0.0f;
       }
-      float r = inv_rms(cta_sum(ss, red), K, a.eps);
-      for (uint32_t i = threadIdx.x; i < K; i += blockDim.x)
-        xo[i] = __fmul_rn(__fmul_rn(x[i], r), a.pro_w[i]);
-    } else {
-      const float *mlp = a.pro_mlp + (size_t)j * a.ldx;
+    }
+    if (a.pro == kProResid) {
       float rm = 1.0f;
       if (a.pro_post_w) {
         float ss = 0.0f;
-        for (uint32_t i = threadIdx.x; i < K; i += blockDim.x) {
-          float v = mlp[i];
-          ss = fmaf(v, v, ss);
+#pragma unroll
+        for (int q = 0; q < kProPer; ++q) ss = fmaf(mv[q], mv[q], ss);
+        rm = inv_rms(block_sum(ss, red), K, a.eps);
+      }
+#pragma unroll
+      for (int q = 0; q < kProPer; ++q) {
+        float v = mv[q];
+        if (a.pro_post_w) v = __fmul_rn(__fmul_rn(v, rm), pw[q]);
+        xv[q] = __fmul_rn(__fadd_rn(xv[q], v), a.pro_scalar);
+      }
+      if (blockIdx.x == 0) {
+#pragma unroll
+        for (int q = 0; q < kProPer; ++q) {
+          uint32_t i = threadIdx.x + q * blockDim.x;
+          if (i < K) a.pro_x_out[(size_t)j * a.ldx + i] = xv[q];
         }
-        rm = inv_rms(cta_sum(ss, red), K, a.eps);
       }
-      float ss = 0.0f;
-      for (uint32_t i = threadIdx.x; i < K; i += blockDim.x) {
-        float v = mlp[i];
-        if (a.pro_post_w) v = __fmul_rn(__fmul_rn(v, rm), a.pro_post_w[i]);
-        float xn = __fmul_rn(__fadd_rn(x[i], v), a.pro_scalar);
-        xo[i] = xn;
-        ss = fmaf(xn, xn, ss);
-      }
-      float r = inv_rms(cta_sum(ss, red), K, a.eps);
-      for (uint32_t i = threadIdx.x; i < K; i += blockDim.x) {
-        float xn = xo[i];
-        if (blockIdx.x == 0) a.pro_x_out[(size_t)j * a.ldx + i] = xn;
-        xo[i] = __fmul_rn(__fmul_rn(xn, r), a.pro_w[i]);
-      }
+    }
+    float ss = 0.0f;
+#pragma unroll
+    for (int q = 0; q < kProPer; ++q) ss = fmaf(xv[q], xv[q], ss);
+    float r = inv_rms(block_sum(ss, red), K, a.eps);
+#pragma unroll
+    for (int q = 0; q < kProPer; ++q) {
+      uint32_t i = threadIdx.x + q * blockDim.x;
+      if (i < K) xo[i] = __fmul_rn(__fmul_rn(xv[q], r), nw[q]);
     }
     __syncthreads();
   }
@@ -227,35 +252,29 @@ SX_DEV void stage_x(const GemvArgs &a, const float *src, uint32_t ld, uint8_t *s
   __syncthreads();
 }
 
-// One 32-element block of one 16-row tile against the staged activation.
-template <int QT, int NSETS>
-SX_DEV void block_mma(const uint32_t (&a0)[4], const uint32_t (&a1)[4], const uint4 *xf4,
-                      const float *corr, uint32_t blk, uint32_t nv, uint32_t batch, int g, int c,
-                      float sg, float sg8, float (&acc)[NSETS][2]) {
-#pragma unroll
-  for (int s = 0; s < NSETS; ++s) {
-    uint32_t v = 8 * s + g;
-    uint4 xb = make_uint4(0, 0, 0, 0);
-    if (v < 2 * batch) xb = xf4[(blk * nv + v) * 4 + c];
-    uint32_t j = 4 * s + c;
-    float cr = j < batch ? corr[blk * batch + j] : 0.0f;
-    float d[4] = {-cr, 0.0f, -cr, 0.0f};
-    if (QT == 4) {
-      mma_bf16_16816(d, a0, xb.x, xb.y);
-      mma_bf16_16816(d, a1, xb.z, xb.w);
-    } else {
-      mma_f16_16816(d, a0, xb.x, xb.y);
-      mma_f16_16816(d, a1, xb.z, xb.w);
-    }
-    acc[s][0] = fmaf(sg, d[0] + d[1], acc[s][0]);
-    acc[s][1] = fmaf(sg8, d[2] + d[3], acc[s][1]);
+// One 32-element block of one 16-row tile: two chained m16n8k16 MMAs per column set, the
+// offset term enters as the C operand, the block scale is applied to the f32 result.
+template <int QT>
+SX_DEV void block_mma(const uint32_t (&a0)[4], const uint32_t (&a1)[4], uint4 xb, float cr,
+                      float sg, float sg8, float (&acc)[2]) {
+  float d[4] = {-cr, 0.0f, -cr, 0.0f};
+  if (QT == 4) {
+    mma_bf16_16816(d, a0, xb.x, xb.y);
+    mma_bf16_16816(d, a1, xb.z, xb.w);
+  } else {
+    mma_f16_16816(d, a0, xb.x, xb.y);
+    mma_f16_16816(d, a1, xb.z, xb.w);
   }
+  acc[0] = fmaf(sg, d[0] + d[1], acc[0]);
+  acc[1] = fmaf(sg8, d[2] + d[3], acc[1]);
 }
 
 // worker ranges: worker w owns chunks [N*w/NW, N*(w+1)/NW)
-SX_DEV uint64_t wstart(uint64_t N, uint32_t NW, uint32_t w) { return N * w / NW; }
-SX_DEV uint32_t wowner(uint64_t N, uint32_t NW, uint64_t c) {
-  return (uint32_t)(((c + 1) * NW - 1) / N);
+SX_DEV uint32_t wstart(uint32_t N, uint32_t NW, uint32_t w) {
+  return (uint32_t)((uint64_t)N * w / NW);
+}
+SX_DEV uint32_t wowner(uint32_t N, uint32_t NW, uint32_t c) {
+  return (uint32_t)(((uint64_t)(c + 1) * NW - 1) / N);
 }
 
 struct Best {
@@ -266,22 +285,23 @@ SX_DEV bool better(float v, uint32_t i, float bv, uint32_t bi) {
   return v > bv || (v == bv && i < bi);
 }
 
-template <int QT, int NMAT, int NSETS>
-__global__ void __launch_bounds__(kThreads, 2) gemv_kernel(GemvArgs a) {
+template <int QT, int NMAT, int NSETS, int S>
+__global__ void __launch_bounds__(kThreads, 1) gemv_kernel(GemvArgs a) {
   extern __shared__ __align__(128) uint8_t smem[];
   constexpr int CB = QTraits<QT>::kChunk;
   constexpr int SO = QTraits<QT>::kScaleOff;
   constexpr int STAGE = NMAT * CB;
-  const Layout L = layout_of(a.k, a.batch, NMAT, QT, a.pro != kProNone);
+  const bool pro = a.pro != kProNone;
+  const Layout L = layout_for(a.k, a.batch, NMAT, QT, S);
+  const bool have_xin = L.xin_bytes != 0;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, c = lane & 3;
-  const uint32_t P = pairs_of(a.k), nv = nv_of(a.batch);
+  const uint32_t P = pairs_of(a.k), nv = nv_of(a.batch), batch = a.batch;
   const uint32_t T = a.tiles[0] + a.tiles[1] + a.tiles[2];
-  const uint64_t N = (uint64_t)T * P;
+  const uint32_t N = T * P;
   const uint32_t NW = gridDim.x * kWarps, wid = blockIdx.x * kWarps + warp;
-  const uint64_t c0 = wstart(N, NW, wid), c1 = wstart(N, NW, wid + 1);
+  const uint32_t c0 = wstart(N, NW, wid), c1 = wstart(N, NW, wid + 1);
 
-  uint8_t *ring = smem + L.ring + warp * kStages * STAGE;
-  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + L.bars) + warp * kStages;
+  uint8_t *const ring = smem + L.ring + warp * S * STAGE;
 
   auto seg_of = [&](uint32_t tt, uint32_t &t) {
     int s = 0;
@@ -296,52 +316,102 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(GemvArgs a) {
     }
     return s;
   };
-  auto issue = [&](int st, uint64_t cc) {
-    uint32_t t;
-    int s = seg_of((uint32_t)(cc / P), t);
-    uint64_t off = ((uint64_t)t * P + cc % P) * CB;
-    uint32_t bar = smem_u32(&bars[st]);
-    mbar_arrive_expect_tx(bar, STAGE);
+
+  // ---- issue pointer: chunks of a segment are contiguous, so copies walk a pointer ----
+  uint32_t ileft = c1 - c0;  // chunks still to issue
+  uint32_t iseg_left = 0;    // chunks left in the current segment
+  int iseg = 0;
+  const uint8_t *isrc[NMAT];
 #pragma unroll
-    for (int m = 0; m < NMAT; ++m)
-      bulk_g2s(smem_u32(ring + st * STAGE + m * CB),
-               static_cast<const uint8_t *>(a.w[s][m]) + off, CB, bar);
+  for (int m = 0; m < NMAT; ++m) isrc[m] = nullptr;
+  if (ileft) {
+    uint32_t t;
+    iseg = seg_of(c0 / P, t);
+    uint32_t p0 = c0 % P;
+    uint64_t off = ((uint64_t)t * P + p0) * CB;
+#pragma unroll
+    for (int m = 0; m < NMAT; ++m) isrc[m] = static_cast<const uint8_t *>(a.w[iseg][m]) + off;
+    iseg_left = (a.tiles[iseg] - t) * P - p0;
+  }
+  // copy the next chunk into dst_stage: every lane moves 16 B of each 512-B sub-record, lanes
+  // 0..7 the 128 B of scales; one commit group per chunk (empty groups keep counts uniform)
+  auto issue_next = [&](uint8_t *dst_stage) {
+    if (ileft) {
+#pragma unroll
+      for (int m = 0; m < NMAT; ++m) {
+        uint32_t dst = smem_u32(dst_stage + m * CB);
+#pragma unroll
+        for (int sub = 0; sub < CB / 512; ++sub)
+          cp_async16(dst + sub * 512 + lane * 16, isrc[m] + sub * 512 + lane * 16);
+        if (lane < 8) cp_async16(dst + SO + lane * 16, isrc[m] + SO + lane * 16);
+        isrc[m] += CB;
+      }
+      --ileft;
+      if (--iseg_left == 0 && ileft) {
+        do {
+          ++iseg;
+        } while (iseg < 2 && a.tiles[iseg] == 0);
+#pragma unroll
+        for (int m = 0; m < NMAT; ++m) isrc[m] = static_cast<const uint8_t *>(a.w[iseg][m]);
+        iseg_left = a.tiles[iseg] * P;
+      }
+    }
+    cp_async_commit();
   };
 
-  // 1. per-warp pipeline start: weights do not depend on the previous kernel
-  if (lane == 0) {
-    for (int st = 0; st < kStages; ++st) mbar_init(smem_u32(&bars[st]), 1);
-    fence_mbar_init();
-    for (int st = 0; st < kStages && c0 + st < c1; ++st) issue(st, c0 + st);
-  }
-  __syncwarp();
+  // 1. the weights do not depend on the previous kernel: start streaming them now
+#pragma unroll
+  for (int st = 0; st < S; ++st) issue_next(ring + st * STAGE);
   pdl_launch_dependents();
-  // 2. wait for the producer of x, then stage it
+
+  // 2. wait for the producer of x, bring x into shared memory and build the B fragments
   pdl_wait();
+  float *xin = reinterpret_cast<float *>(smem + L.xin);
   const float *xsrc = a.x;
   uint32_t xld = a.ldx;
-  if (a.pro != kProNone) {
-    float *xin = reinterpret_cast<float *>(smem + L.xin);
+  if (pro) {
     run_prologue(a, xin, reinterpret_cast<float *>(smem + L.misc + 64));
+    xsrc = xin;
+    xld = a.k;
+  } else if (have_xin) {
+    // one batch of independent 16-byte copies instead of a dependent round trip per element
+    const uint32_t per_row = a.k / 4;
+    for (uint32_t q = tid; q < batch * per_row; q += blockDim.x) {
+      uint32_t j = q / per_row, i = q % per_row;
+      cp_async16(smem_u32(xin + (size_t)j * a.k + 4 * i), a.x + (size_t)j * a.ldx + 4 * i);
+    }
+    cp_async_commit();
+    cp_async_wait<0>();
+    __syncthreads();
     xsrc = xin;
     xld = a.k;
   }
   stage_x<QT>(a, xsrc, xld, smem, L);
 
-  const uint4 *xf4 = reinterpret_cast<const uint4 *>(smem + L.xfrag);
-  const float *corr = reinterpret_cast<const float *>(smem + L.corr);
-  const float *xscale = reinterpret_cast<const float *>(smem + L.misc);
+  const uint4 *const xf4 = reinterpret_cast<const uint4 *>(smem + L.xfrag);
+  const float *const corr = reinterpret_cast<const float *>(smem + L.corr);
+  const float *const xscale = reinterpret_cast<const float *>(smem + L.misc);
+
+  // lane constants: column set s uses B variant 8s + g and batch row 4s + c
+  uint32_t xoff[NSETS];
+  bool xvalid[NSETS], cvalid[NSETS];
+#pragma unroll
+  for (int s = 0; s < NSETS; ++s) {
+    xoff[s] = (8 * s + g) * 4 + c;
+    xvalid[s] = (uint32_t)(8 * s + g) < 2 * batch;
+    cvalid[s] = (uint32_t)(4 * s + c) < batch;
+  }
 
   Best best[NSETS];
 #pragma unroll
   for (int s = 0; s < NSETS; ++s) best[s] = {-INFINITY, 0xFFFFFFFFu};
 
-  // epilogue for one (row, batch) value pair set: apply factor, GeGLU, write, track argmax
+  // epilogue for one (row, batch) value: apply the factor, GeGLU, write, track the argmax
   auto emit = [&](uint32_t tt, uint32_t row, uint32_t j, const float (&v)[NMAT], int s_idx) {
     uint32_t t;
     int s = seg_of(tt, t);
     uint32_t r = t * 16 + row;
-    if (r >= a.rows[s] || j >= a.batch) return;
+    if (r >= a.rows[s] || j >= batch) return;
     float out = v[0] * xscale[j];
     if (NMAT == 2) out = __fmul_rn(gelu_tanh_dev(out), v[NMAT - 1] * xscale[j]);
     a.y[s][(size_t)j * a.ldy + r] = out;
@@ -359,37 +429,41 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(GemvArgs a) {
 #pragma unroll
     for (int s = 0; s < NSETS; ++s) acc[m][s][0] = acc[m][s][1] = 0.0f;
 
-  bool ok = true;
-  uint64_t fail_cc = 0;
-  uint64_t issued = c0 + kStages < c1 ? c0 + kStages : c1;  // chunks whose copy was issued
-  for (uint64_t cc = c0; cc < c1; ++cc) {
-    const uint64_t i = cc - c0;
-    const int st = (int)(i % kStages);
-    const uint32_t phase = (uint32_t)(i / kStages) & 1u;
-    if (!mbar_wait_bounded(smem_u32(&bars[st]), phase)) {
-      raise_error(a.err, kDevWaitTimeout);
-      ok = false;
-      fail_cc = cc;
-      break;
-    }
-    const uint8_t *chunk = ring + st * STAGE;
-    const uint32_t p = (uint32_t)(cc % P);
+  // ---- main loop: one 16-row x 64-column chunk per iteration ----
+  uint32_t tt = c0 / P, p = c0 % P;
+  const uint4 *xp = xf4 + 2 * p * nv * 4;  // B fragments of pair p
+  const float *cp = corr + 2 * p * batch;   // offset terms of pair p
+  uint8_t *cur = ring;
+  for (uint32_t cc = c0; cc < c1; ++cc) {
+    cp_async_wait<S - 1>();  // this lane's copies of chunk cc have landed
+    __syncwarp();            // ... and every other lane's
+    uint4 xb[2][NSETS];
+    float cr[2][NSETS];
+#pragma unroll
+    for (int hb = 0; hb < 2; ++hb)
+#pragma unroll
+      for (int s = 0; s < NSETS; ++s) {
+        xb[hb][s] = xvalid[s] ? xp[hb * nv * 4 + xoff[s]] : make_uint4(0, 0, 0, 0);
+        cr[hb][s] = cvalid[s] ? cp[hb * batch + 4 * s + c] : 0.0f;
+      }
 #pragma unroll
     for (int m = 0; m < NMAT; ++m) {
-      const uint8_t *ch = chunk + m * CB;
+      const uint8_t *ch = cur + m * CB;
       const float4 sc = *reinterpret_cast<const float4 *>(ch + SO + g * 16);
+      uint4 wq[QT == 4 ? 1 : 2];
+      wq[0] = *reinterpret_cast<const uint4 *>(ch + lane * 16);
+      if (QT == 8) wq[QT == 4 ? 0 : 1] = *reinterpret_cast<const uint4 *>(ch + 512 + lane * 16);
 #pragma unroll
       for (int hb = 0; hb < 2; ++hb) {
         uint32_t a0[4], a1[4];
         if (QT == 4) {
-          const uint4 nib = *reinterpret_cast<const uint4 *>(ch + lane * 16);
           uint32_t rg[4], rg8[4];
-          dq4_word(hb ? nib.z : nib.x, rg);
-          dq4_word(hb ? nib.w : nib.y, rg8);
+          dq4_word(hb ? wq[0].z : wq[0].x, rg);
+          dq4_word(hb ? wq[0].w : wq[0].y, rg8);
           a0[0] = rg[0]; a0[1] = rg8[0]; a0[2] = rg[1]; a0[3] = rg8[1];
           a1[0] = rg[2]; a1[1] = rg8[2]; a1[2] = rg[3]; a1[3] = rg8[3];
         } else {
-          const uint4 q = *reinterpret_cast<const uint4 *>(ch + hb * 512 + lane * 16);
+          const uint4 q = wq[QT == 4 ? 0 : hb];
           uint32_t g0l, g0h, g1l, g1h, h0l, h0h, h1l, h1h;
           dq8_word(q.x, g0l, g0h);
           dq8_word(q.y, g1l, g1h);
@@ -398,23 +472,23 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(GemvArgs a) {
           a0[0] = g0l; a0[1] = h0l; a0[2] = g0h; a0[3] = h0h;
           a1[0] = g1l; a1[1] = h1l; a1[2] = g1h; a1[3] = h1h;
         }
-        block_mma<QT, NSETS>(a0, a1, xf4, corr, 2 * p + hb, nv, a.batch, g, c,
-                             hb ? sc.z : sc.x, hb ? sc.w : sc.y, acc[m]);
+        const float sg = hb ? sc.z : sc.x, sg8 = hb ? sc.w : sc.y;
+#pragma unroll
+        for (int s = 0; s < NSETS; ++s)
+          block_mma<QT>(a0, a1, xb[hb][s], cr[hb][s], sg, sg8, acc[m][s]);
       }
     }
-    // refill this stage (its data has been consumed into registers and used)
-    __syncwarp();
-    if (cc + kStages < c1) {
-      if (lane == 0) {
-        fence_proxy_async();
-        issue(st, cc + kStages);
-      }
-      issued = cc + kStages + 1;
-    }
-    // tile boundary
-    const uint32_t tt = (uint32_t)(cc / P);
-    if (p == P - 1 || cc + 1 == c1) {
-      const uint64_t tb = (uint64_t)tt * P, te = tb + P;
+    __syncwarp();  // every lane has read this stage: refill it
+    issue_next(cur);
+    cur += STAGE;
+    if (cur == ring + S * STAGE) cur = ring;
+    xp += 2 * nv * 4;
+    cp += 2 * batch;
+
+    // ---- tile boundary ----
+    const bool tile_end = (p == P - 1);
+    if (tile_end || cc + 1 == c1) {
+      const uint32_t tb = tt * P, te = tb + P;
       if (tb >= c0 && te <= c1) {
         // the whole tile is ours: write it directly
 #pragma unroll
@@ -427,46 +501,55 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(GemvArgs a) {
             emit(tt, g + 8 * h, 4 * s + c, v, s);
           }
       } else {
-        // partial tile: publish, and reduce if we are the last contributor
-        const int slot = (tt == (uint32_t)(c0 / P)) ? 0 : 1;
+        // partial tile: publish a record; the last contributor reduces all of them in
+        // worker order.  slot 0 = the tile holds this worker's first chunk, 1 = its last.
+        const int slot = c0 >= tb ? 0 : 1;
         float *rec = a.part + ((size_t)wid * 2 + slot) * NMAT * 128;
 #pragma unroll
         for (int m = 0; m < NMAT; ++m)
 #pragma unroll
           for (int s = 0; s < NSETS; ++s) {
             uint32_t j = 4 * s + c;
-            if (j < 8) {
-              rec[m * 128 + g * 8 + j] = acc[m][s][0];
-              rec[m * 128 + (g + 8) * 8 + j] = acc[m][s][1];
-            }
+            rec[m * 128 + g * 8 + j] = acc[m][s][0];
+            rec[m * 128 + (g + 8) * 8 + j] = acc[m][s][1];
           }
         __threadfence();
         __syncwarp();
-        uint32_t wlo = wowner(N, NW, tb), whi = wowner(N, NW, te - 1);
-        uint32_t expected = 0;
-        for (uint32_t w = wlo; w <= whi; ++w)
-          if (wstart(N, NW, w) < wstart(N, NW, w + 1)) ++expected;
+        // contributors: N >= NW -> every worker owns >= 1 chunk, so they are the owners
+        // wlo..whi of the tile's first and last chunks; N < NW -> every worker owns at most
+        // one chunk, so each of the tile's P chunks has its own owner
+        const bool dense = N >= NW;
+        uint32_t wlo = 0, whi = 0, expected = P;
+        if (dense) {
+          wlo = wowner(N, NW, tb);
+          whi = wowner(N, NW, te - 1);
+          expected = whi - wlo + 1;
+        }
         uint32_t old = 0;
         if (lane == 0) old = atomicAdd(&a.tile_cnt[tt], 1u);
         old = __shfl_sync(0xffffffffu, old, 0);
         if (old + 1 == expected) {
           __threadfence();
-          // lanes own (row, j) pairs: 16 rows x 8 batch slots = 128 -> 4 per lane
+          const bool lo_tail = dense && wstart(N, NW, wlo) < tb;  // wlo started earlier
+          float v[4][NMAT];
+#pragma unroll
+          for (int q = 0; q < 4; ++q)
+#pragma unroll
+            for (int m = 0; m < NMAT; ++m) v[q][m] = 0.0f;
+          for (uint32_t k = 0; k < expected; ++k) {
+            uint32_t w = dense ? wlo + k : wowner(N, NW, tb + k);
+            int sl = (dense && k == 0 && lo_tail) ? 1 : 0;
+            const float *r = a.part + ((size_t)w * 2 + sl) * NMAT * 128;
+#pragma unroll
+            for (int q = 0; q < 4; ++q)
+#pragma unroll
+              for (int m = 0; m < NMAT; ++m) v[q][m] += __ldcg(r + m * 128 + lane + 32 * q);
+          }
+          // lane owns (row, j) = ((lane + 32 q) / 8, lane % 8)
 #pragma unroll
           for (int q = 0; q < 4; ++q) {
             uint32_t idx = lane + 32 * q, row = idx >> 3, j = idx & 7;
-            float v[NMAT];
-#pragma unroll
-            for (int m = 0; m < NMAT; ++m) v[m] = 0.0f;
-            for (uint32_t w = wlo; w <= whi; ++w) {
-              uint64_t ws = wstart(N, NW, w);
-              if (ws >= wstart(N, NW, w + 1)) continue;
-              int sl = (tt == (uint32_t)(ws / P)) ? 0 : 1;
-              const float *r = a.part + ((size_t)w * 2 + sl) * NMAT * 128;
-#pragma unroll
-              for (int m = 0; m < NMAT; ++m) v[m] += __ldcg(r + m * 128 + idx);
-            }
-            emit(tt, row, j, v, j >= 4 ? NSETS - 1 : 0);
+            emit(tt, row, j, v[q], j >= 4 ? NSETS - 1 : 0);
           }
           if (lane == 0) a.tile_cnt[tt] = 0;
         }
@@ -476,21 +559,21 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(GemvArgs a) {
 #pragma unroll
         for (int s = 0; s < NSETS; ++s) acc[m][s][0] = acc[m][s][1] = 0.0f;
     }
-  }
-  if (!ok) {
-    // a copy never completed: wait (bounded) for this warp's other copies still in flight so
-    // that none lands after the CTA exits, then leave; the host sees kDevWaitTimeout
-    for (uint64_t cc = fail_cc; cc < issued; ++cc) {
-      uint64_t i = cc - c0;
-      mbar_wait_bounded(smem_u32(&bars[i % kStages]), (uint32_t)(i / kStages) & 1u);
+    if (tile_end) {
+      p = 0;
+      ++tt;
+      xp = xf4;
+      cp = corr;
+    } else {
+      ++p;
     }
-    return;
   }
+  cp_async_wait<0>();
 
   if (a.epi == kEpiArgmax) {
     // Per batch row j: lane (g, c) tracked rows of batch row 4s + c in best[s].  Reduce over
     // the warp, publish per worker, and let the last worker to arrive merge all workers.
-    for (uint32_t j = 0; j < a.batch; ++j) {
+    for (uint32_t j = 0; j < batch; ++j) {
       Best b = {-INFINITY, 0xFFFFFFFFu};
 #pragma unroll
       for (int s = 0; s < NSETS; ++s)
@@ -513,7 +596,7 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(GemvArgs a) {
     old = __shfl_sync(0xffffffffu, old, 0);
     if (old + 1 == NW) {
       __threadfence();
-      for (uint32_t j = 0; j < a.batch; ++j) {
+      for (uint32_t j = 0; j < batch; ++j) {
         Best r = {-INFINITY, 0xFFFFFFFFu};
         for (uint32_t w = lane; w < NW; w += 32) {
           float v = __ldcg(a.best_v + (size_t)w * 8 + j);
@@ -538,13 +621,11 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(GemvArgs a) {
   }
 }
 
-template <int QT, int NMAT, int NSETS>
-cudaError_t launch_t(const GemvArgs &a, int num_sms, cudaStream_t s, bool pdl) {
-  const Layout L = layout_of(a.k, a.batch, NMAT, QT, a.pro != kProNone);
-  auto kern = gemv_kernel<QT, NMAT, NSETS>;
-  int per_sm = L.total <= 110 * 1024 ? 2 : 1;
+template <int QT, int NMAT, int NSETS, int S>
+cudaError_t launch_s(const GemvArgs &a, int num_sms, cudaStream_t s, bool pdl) {
+  const Layout L = layout_for(a.k, a.batch, NMAT, QT, S);
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(num_sms * per_sm);
+  cfg.gridDim = dim3(num_sms);
   cfg.blockDim = dim3(kThreads);
   cfg.dynamicSmemBytes = L.total;
   cfg.stream = s;
@@ -553,13 +634,27 @@ cudaError_t launch_t(const GemvArgs &a, int num_sms, cudaStream_t s, bool pdl) {
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 1 : 0;
-  return cudaLaunchKernelEx(&cfg, kern, a);
+  return cudaLaunchKernelEx(&cfg, gemv_kernel<QT, NMAT, NSETS, S>, a);
+}
+
+template <int QT, int NMAT, int NSETS>
+cudaError_t launch_t(const GemvArgs &a, int num_sms, cudaStream_t s, bool pdl) {
+  switch (stages_for(a.k, a.batch, NMAT, QT, a.pro != kProNone)) {
+    case 8: return launch_s<QT, NMAT, NSETS, 8>(a, num_sms, s, pdl);
+    case 4: return launch_s<QT, NMAT, NSETS, 4>(a, num_sms, s, pdl);
+    case 2: return launch_s<QT, NMAT, NSETS, 2>(a, num_sms, s, pdl);
+    default: return cudaErrorInvalidValue;
+  }
 }
 
 template <int QT, int NMAT, int NSETS>
 cudaError_t prepare_t() {
-  return cudaFuncSetAttribute(gemv_kernel<QT, NMAT, NSETS>,
-                              cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+  cudaError_t e[3] = {allow_max_dynamic_smem(gemv_kernel<QT, NMAT, NSETS, 8>),
+                      allow_max_dynamic_smem(gemv_kernel<QT, NMAT, NSETS, 4>),
+                      allow_max_dynamic_smem(gemv_kernel<QT, NMAT, NSETS, 2>)};
+  for (cudaError_t x : e)
+    if (x != cudaSuccess) return x;
+  return cudaSuccess;
 }
 
 }  // namespace
@@ -575,11 +670,12 @@ cudaError_t prepare_gemv_kernels() {
 }
 
 size_t gemv_smem_bytes(int qt, uint32_t k, uint32_t batch, bool geglu, bool prologue) {
-  return layout_of(k, batch, geglu ? 2 : 1, qt, prologue).total;
+  int st = stages_for(k, batch, geglu ? 2 : 1, qt, prologue);
+  return st ? layout_for(k, batch, geglu ? 2 : 1, qt, st).total : (size_t)-1;
 }
 
-size_t gemv_part_bytes(int num_sms) { return (size_t)num_sms * 2 * kWarps * 2 * 2 * 128 * 4; }
-size_t gemv_best_bytes(int num_sms) { return (size_t)num_sms * 2 * kWarps * 8; }
+size_t gemv_part_bytes(int num_sms) { return (size_t)num_sms * kWarps * 2 * 2 * 128 * 4; }
+size_t gemv_workers(int num_sms) { return (size_t)num_sms * kWarps; }
 
 cudaError_t launch_gemv(int qt, bool geglu, const GemvArgs &a, int num_sms, cudaStream_t s,
                         bool pdl) {

@@ -51,7 +51,8 @@ cudaError_t launch_gemv(int qt, bool geglu, const GemvArgs &a, int num_sms, cuda
                         bool pdl);
 size_t gemv_smem_bytes(int qt, uint32_t k, uint32_t batch, bool geglu, bool prologue);
 size_t gemv_part_bytes(int num_sms);
-size_t gemv_best_bytes(int num_sms);
+size_t gemv_workers(int num_sms);
+constexpr uint32_t kGemvPrologueMaxK = 4096;  // fused norm prologues hold K / 512 <= 8 per thread
 constexpr uint32_t kMaxGemvTiles = 262144;
 
 cudaError_t launch_repack(int qt, const uint32_t *ref, void *packed, uint32_t m, uint32_t k,

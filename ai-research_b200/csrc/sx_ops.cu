@@ -514,10 +514,8 @@ cudaError_t launch_attn_fused_d(const AttnFusedArgs &a, cudaStream_t s, bool pdl
 
 template <int DPL, int G>
 cudaError_t prepare_attn_fused_t() {
-  cudaError_t a = cudaFuncSetAttribute(attn_fused_kernel<DPL, G, true>,
-                                       cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
-  cudaError_t b = cudaFuncSetAttribute(attn_fused_kernel<DPL, G, false>,
-                                       cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+  cudaError_t a = allow_max_dynamic_smem(attn_fused_kernel<DPL, G, true>);
+  cudaError_t b = allow_max_dynamic_smem(attn_fused_kernel<DPL, G, false>);
   return a != cudaSuccess ? a : b;
 }
 
@@ -535,10 +533,8 @@ cudaError_t launch_attn_t(const AttnArgs &a, cudaStream_t s) {
 
 template <int DPL, int G>
 cudaError_t prepare_attn_t() {
-  cudaError_t a = cudaFuncSetAttribute(attn_split_kernel<DPL, G, true>,
-                                       cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
-  cudaError_t b = cudaFuncSetAttribute(attn_split_kernel<DPL, G, false>,
-                                       cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+  cudaError_t a = allow_max_dynamic_smem(attn_split_kernel<DPL, G, true>);
+  cudaError_t b = allow_max_dynamic_smem(attn_split_kernel<DPL, G, false>);
   return a != cudaSuccess ? a : b;
 }
 
