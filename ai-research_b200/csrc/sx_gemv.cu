@@ -536,14 +536,35 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(GemvArgs a) {
           for (int q = 0; q < 4; ++q)
 #pragma unroll
             for (int m = 0; m < NMAT; ++m) v[q][m] = 0.0f;
-          for (uint32_t k = 0; k < expected; ++k) {
-            uint32_t w = dense ? wlo + k : wowner(N, NW, tb + k);
-            int sl = (dense && k == 0 && lo_tail) ? 1 : 0;
-            const float *r = a.part + ((size_t)w * 2 + sl) * NMAT * 128;
+          // lane owns (row, j) = ((lane + 32 q) / 8, lane % 8); only j < batch is read.
+          // Records are fetched four contributors at a time so their L2 round trips
+          // overlap; the additions stay in contributor order.
+          const bool jlive = (uint32_t)(lane & 7) < batch;
+          for (uint32_t k0 = 0; k0 < expected; k0 += 4) {
+            float t[4][4][NMAT];
 #pragma unroll
-            for (int q = 0; q < 4; ++q)
+            for (int u = 0; u < 4; ++u) {
+              const uint32_t k = k0 + u;
+              const bool live = jlive && k < expected;
+              uint32_t w = 0;
+              int sl = 0;
+              if (live) {
+                w = dense ? wlo + k : wowner(N, NW, tb + k);
+                sl = (dense && k == 0 && lo_tail) ? 1 : 0;
+              }
+              const float *r = a.part + ((size_t)w * 2 + sl) * NMAT * 128;
 #pragma unroll
-              for (int m = 0; m < NMAT; ++m) v[q][m] += __ldcg(r + m * 128 + lane + 32 * q);
+              for (int q = 0; q < 4; ++q)
+#pragma unroll
+                for (int m = 0; m < NMAT; ++m)
+                  t[u][q][m] = live ? __ldcg(r + m * 128 + lane + 32 * q) : 0.0f;
+            }
+#pragma unroll
+            for (int u = 0; u < 4; ++u)
+#pragma unroll
+              for (int q = 0; q < 4; ++q)
+#pragma unroll
+                for (int m = 0; m < NMAT; ++m) v[q][m] += t[u][q][m];
           }
           // lane owns (row, j) = ((lane + 32 q) / 8, lane % 8)
 #pragma unroll
