@@ -153,11 +153,19 @@ SX_DEV uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
 
 // Q4: eight nibbles of one packed word -> four bf16x2 holding 8 + q/2 (exact).
 // Register j holds nibble j (low half) and nibble j+4 (high half).
+// (a & b) | c in one LOP3 (truth table 0xEA); b and c are registers, so a constant mask and
+// magic number are materialised once instead of costing a second logic op per use
+SX_DEV uint32_t and_or(uint32_t a, uint32_t b, uint32_t c) {
+  uint32_t d;
+  asm("lop3.b32 %0, %1, %2, %3, 0xEA;\n" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+  return d;
+}
 SX_DEV void dq4_word(uint32_t u, uint32_t (&r)[4]) {
-  r[0] = ((u << 3) & 0x00780078u) | 0x41004100u;
-  r[1] = ((u >> 1) & 0x00780078u) | 0x41004100u;
-  r[2] = ((u >> 5) & 0x00780078u) | 0x41004100u;
-  r[3] = ((u >> 9) & 0x00780078u) | 0x41004100u;
+  const uint32_t m = 0x00780078u, e = 0x41004100u;
+  r[0] = and_or(u << 3, m, e);
+  r[1] = and_or(u >> 1, m, e);
+  r[2] = and_or(u >> 5, m, e);
+  r[3] = and_or(u >> 9, m, e);
 }
 // Q8: four int8 of one packed word -> two f16x2 holding 1024 + (q + 128) (exact).
 SX_DEV void dq8_word(uint32_t u, uint32_t &lo, uint32_t &hi) {
@@ -241,6 +249,14 @@ SX_DEV void bulk_g2s(uint32_t dst, const void *src, uint32_t bytes, uint32_t bar
 // Ampere-style asynchronous 16-byte copies (LDGSTS), L1-bypassing, grouped per thread.
 SX_DEV void cp_async16(uint32_t dst, const void *src) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(dst), "l"(src) : "memory");
+}
+// predicated form: no copy (and no read of src) when p is false
+SX_DEV void cp_async16_if(uint32_t dst, const void *src, bool p) {
+  asm volatile(
+      "{\n .reg .pred q;\n setp.ne.b32 q, %2, 0;\n"
+      " @q cp.async.cg.shared.global [%0], [%1], 16;\n}\n" ::"r"(dst),
+      "l"(src), "r"((uint32_t)p)
+      : "memory");
 }
 SX_DEV void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
 template <int N>

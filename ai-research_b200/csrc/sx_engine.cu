@@ -255,6 +255,10 @@ sx_status run_op(sx_engine *e, cudaStream_t s, const Op &op, uint32_t *kernels) 
       return do_argmax(e, s, (const float *)op.bind.at(0), op.u[0], (uint32_t *)op.bind.at(1));
     case OP_GEMV_FUSED:
       *kernels += 1;
+      if (!sx::gemv_segments_contiguous(op.gemv, op.qt, op.geglu ? 2 : 1)) {
+        set_error("fused gemv: the segments of a multi-segment call must lie back to back");
+        return SX_ERR_UNSUPPORTED;
+      }
       return cuda_status(sx::launch_gemv(op.qt, op.geglu, op.gemv, e->num_sms, s, true),
                          "fused gemv launch");
     case OP_ATTN_FUSED: {

@@ -32,6 +32,9 @@ namespace {
 constexpr int kThreads = 512;  // one persistent CTA per SM, 16 stream-K workers
 constexpr int kWarps = kThreads / 32;
 constexpr uint32_t kSmemLimit = 227 * 1024;
+// Lane-private scale copies (four per stage) remove the per-chunk warp synchronisation but
+// quadruple the scale bytes written to and read from shared memory; the shared copy is used.
+constexpr bool kPrivScales = false;
 
 SX_HD uint32_t nv_of(uint32_t batch) {
   return batch <= 1 ? 2u : batch <= 2 ? 4u : batch <= 4 ? 8u : 16u;
@@ -43,12 +46,16 @@ template <>
 struct QTraits<4> {
   static constexpr int kChunk = kQ4ChunkBytes;
   static constexpr int kScaleOff = 512;
+  static constexpr int kStage = 512 + 512;  // quants + four copies of the scales
+  static constexpr int kStageShared = 512 + 128;  // quants + one shared copy
   static constexpr float kCorr = 12.0f;
 };
 template <>
 struct QTraits<8> {
   static constexpr int kChunk = kQ8ChunkBytes;
   static constexpr int kScaleOff = 1024;
+  static constexpr int kStage = 1024 + 512;
+  static constexpr int kStageShared = 1024 + 128;
   static constexpr float kCorr = 1152.0f;
 };
 
@@ -66,15 +73,20 @@ SX_HD Layout layout_of(uint32_t k, uint32_t batch, int nmat, int qt, bool with_x
   L.xin = L.misc + 48 * 4;
   L.xin_bytes = with_xin ? batch * k * 4 : 0;
   L.ring = (L.xin + L.xin_bytes + 127) & ~127u;
-  uint32_t chunk = qt == 4 ? kQ4ChunkBytes : kQ8ChunkBytes;
-  L.total = L.ring + kWarps * stages * nmat * chunk;
+  // a ring stage holds the chunk's quants and, for one column set, one copy of its 128 B of
+  // scales per lane of a row group (every lane then reads only bytes it copied itself); with
+  // two column sets the x fragments are large and the warp shares a single copy
+  const bool priv = kPrivScales && batch <= 4;
+  uint32_t stage = qt == 4 ? (priv ? QTraits<4>::kStage : QTraits<4>::kStageShared)
+                           : (priv ? QTraits<8>::kStage : QTraits<8>::kStageShared);
+  L.total = L.ring + kWarps * stages * nmat * stage;
   return L;
 }
 
-// Deepest ring (8, 4 or 2 stages per warp) that fits in shared memory; 0 if none does.  x
+// Deepest ring (8, 6, 4 or 2 stages per warp) that fits in shared memory; 0 if none does.  x
 // gets its own staging area whenever it fits (the fused prologues require it).
 SX_HD int stages_for(uint32_t k, uint32_t batch, int nmat, int qt, bool pro) {
-  const int opts[3] = {8, 4, 2};
+  const int opts[4] = {8, 6, 4, 2};
   for (int s : opts)
     if (layout_of(k, batch, nmat, qt, true, s).total <= kSmemLimit) return s;
   if (!pro)
@@ -239,15 +251,16 @@ SX_DEV void stage_x(const GemvArgs &a, const float *src, uint32_t ld, uint8_t *s
         lw = (uint32_t)__half_as_ushort(l0) | ((uint32_t)__half_as_ushort(l1) << 16);
         part = (__half2float(h0) + __half2float(l0)) + (__half2float(h1) + __half2float(l1));
       }
-      // uint4 index (blk * nv + v) * 4 + c, word jj
-      xf[(((blk * nv + 2 * j) * 4 + c) << 2) + jj] = hw;
-      xf[(((blk * nv + 2 * j + 1) * 4 + c) << 2) + jj] = lw;
+      // per pair (blk / 2): uint4 index ((variant * 4 + c) * 2 + half), word jj
+      const uint32_t pr = blk >> 1, hb = blk & 1;
+      xf[(((((pr * nv + 2 * j) * 4 + c) << 1) + hb) << 2) + jj] = hw;
+      xf[(((((pr * nv + 2 * j + 1) * 4 + c) << 1) + hb) << 2) + jj] = lw;
     }
     part += __shfl_xor_sync(0xffffffffu, part, 8);
     part += __shfl_xor_sync(0xffffffffu, part, 4);
     part += __shfl_xor_sync(0xffffffffu, part, 2);
     part += __shfl_xor_sync(0xffffffffu, part, 1);
-    if (it < items && (it & 15) == 0) corr[blk * a.batch + j] = QTraits<QT>::kCorr * part;
+    if (it < items && (it & 15) == 0) corr[((blk >> 1) * a.batch + j) * 2 + (blk & 1)] = QTraits<QT>::kCorr * part;
   }
   __syncthreads();
 }
@@ -257,7 +270,7 @@ SX_DEV void stage_x(const GemvArgs &a, const float *src, uint32_t ld, uint8_t *s
 template <int QT>
 SX_DEV void block_mma(const uint32_t (&a0)[4], const uint32_t (&a1)[4], uint4 xb, float cr,
                       float sg, float sg8, float (&acc)[2]) {
-  float d[4] = {-cr, 0.0f, -cr, 0.0f};
+  float d[4] = {0.0f, 0.0f, 0.0f, 0.0f};
   if (QT == 4) {
     mma_bf16_16816(d, a0, xb.x, xb.y);
     mma_bf16_16816(d, a1, xb.z, xb.w);
@@ -265,8 +278,8 @@ SX_DEV void block_mma(const uint32_t (&a0)[4], const uint32_t (&a1)[4], uint4 xb
     mma_f16_16816(d, a0, xb.x, xb.y);
     mma_f16_16816(d, a1, xb.z, xb.w);
   }
-  acc[0] = fmaf(sg, d[0] + d[1], acc[0]);
-  acc[1] = fmaf(sg8, d[2] + d[3], acc[1]);
+  acc[0] = fmaf(sg, (d[0] + d[1]) - cr, acc[0]);
+  acc[1] = fmaf(sg8, (d[2] + d[3]) - cr, acc[1]);
 }
 
 // worker ranges: worker w owns chunks [N*w/NW, N*(w+1)/NW)
@@ -290,7 +303,9 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(GemvArgs a) {
   extern __shared__ __align__(128) uint8_t smem[];
   constexpr int CB = QTraits<QT>::kChunk;
   constexpr int SO = QTraits<QT>::kScaleOff;
-  constexpr int STAGE = NMAT * CB;
+  constexpr bool PRIV = kPrivScales && NSETS == 1;  // lane-private scale copies
+  constexpr int KS = PRIV ? QTraits<QT>::kStage : QTraits<QT>::kStageShared;
+  constexpr int STAGE = NMAT * KS;
   const bool pro = a.pro != kProNone;
   const Layout L = layout_for(a.k, a.batch, NMAT, QT, S);
   const bool have_xin = L.xin_bytes != 0;
@@ -317,51 +332,42 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(GemvArgs a) {
     return s;
   };
 
-  // ---- issue pointer: chunks of a segment are contiguous, so copies walk a pointer ----
-  uint32_t ileft = c1 - c0;  // chunks still to issue
-  uint32_t iseg_left = 0;    // chunks left in the current segment
-  int iseg = 0;
-  const uint8_t *isrc[NMAT];
+  // ---- copies: the chunks of the call form one contiguous stream (the segments of a
+  // multi-segment call lie back to back in memory, which the host checks), so chunk i of this
+  // worker starts at w[0][m] + (c0 + i) * CB ----
+  const uint32_t n = c1 - c0;
+  const uint8_t *wsrc[NMAT];
 #pragma unroll
-  for (int m = 0; m < NMAT; ++m) isrc[m] = nullptr;
-  if (ileft) {
-    uint32_t t;
-    iseg = seg_of(c0 / P, t);
-    uint32_t p0 = c0 % P;
-    uint64_t off = ((uint64_t)t * P + p0) * CB;
+  for (int m = 0; m < NMAT; ++m) wsrc[m] = static_cast<const uint8_t *>(a.w[0][m]) + (size_t)c0 * CB;
+  // lane (g, c) copies bytes [16 lane, 16 lane + 16) of every 512-B quant sub-record and
+  // reads back exactly those.  PRIV: it also copies the 16 B of scales of row group g into its
+  // own copy c of the scale record, so no lane waits on another lane's copies; otherwise lanes
+  // 0..7 copy the one shared scale record and the warp synchronises once per chunk.
+  const uint32_t ring_s = smem_u32(ring);
+  const uint32_t q_dst = ring_s + lane * 16;
+  const uint32_t s_dst = PRIV ? ring_s + SO + c * 128 + g * 16 : ring_s + SO + lane * 16;
+  const uint32_t q_src = lane * 16, s_src = PRIV ? SO + g * 16 : SO + lane * 16;
+  const bool s_lane = PRIV || lane < 8;
+  // copy chunk i into stage i mod S; one commit group per chunk (empty past the end, so the
+  // group count stays uniform)
+  auto issue = [&](uint32_t i) {
+    const bool live = i < n;
+    const uint32_t stage = (i % S) * STAGE;
 #pragma unroll
-    for (int m = 0; m < NMAT; ++m) isrc[m] = static_cast<const uint8_t *>(a.w[iseg][m]) + off;
-    iseg_left = (a.tiles[iseg] - t) * P - p0;
-  }
-  // copy the next chunk into dst_stage: every lane moves 16 B of each 512-B sub-record, lanes
-  // 0..7 the 128 B of scales; one commit group per chunk (empty groups keep counts uniform)
-  auto issue_next = [&](uint8_t *dst_stage) {
-    if (ileft) {
+    for (int m = 0; m < NMAT; ++m) {
+      const uint8_t *s = wsrc[m] + (size_t)i * CB;
 #pragma unroll
-      for (int m = 0; m < NMAT; ++m) {
-        uint32_t dst = smem_u32(dst_stage + m * CB);
-#pragma unroll
-        for (int sub = 0; sub < CB / 512; ++sub)
-          cp_async16(dst + sub * 512 + lane * 16, isrc[m] + sub * 512 + lane * 16);
-        if (lane < 8) cp_async16(dst + SO + lane * 16, isrc[m] + SO + lane * 16);
-        isrc[m] += CB;
-      }
-      --ileft;
-      if (--iseg_left == 0 && ileft) {
-        do {
-          ++iseg;
-        } while (iseg < 2 && a.tiles[iseg] == 0);
-#pragma unroll
-        for (int m = 0; m < NMAT; ++m) isrc[m] = static_cast<const uint8_t *>(a.w[iseg][m]);
-        iseg_left = a.tiles[iseg] * P;
-      }
+      for (int sub = 0; sub < CB / 512; ++sub)
+        cp_async16_if(q_dst + stage + m * KS + sub * 512, s + q_src + sub * 512, live);
+      cp_async16_if(s_dst + stage + m * KS, s + s_src, live && s_lane);
     }
     cp_async_commit();
   };
 
-  // 1. the weights do not depend on the previous kernel: start streaming them now
+  // 1. the weights do not depend on the previous kernel: start streaming them now (chunk
+  // S - 1 is issued by the first loop iteration)
 #pragma unroll
-  for (int st = 0; st < S; ++st) issue_next(ring + st * STAGE);
+  for (int st = 0; st < S - 1; ++st) issue(st);
   pdl_launch_dependents();
 
   // 2. wait for the producer of x, bring x into shared memory and build the B fragments
@@ -392,15 +398,19 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(GemvArgs a) {
   const float *const corr = reinterpret_cast<const float *>(smem + L.corr);
   const float *const xscale = reinterpret_cast<const float *>(smem + L.misc);
 
-  // lane constants: column set s uses B variant 8s + g and batch row 4s + c
-  uint32_t xoff[NSETS];
+  // lane constants: column set s uses B variant 8s + g and batch row 4s + c.  Per pair the
+  // fragments are [variant][c][half] uint4 and the offset terms [batch row][half] floats, so a
+  // lane's two halves are adjacent.
+  uint32_t xoff[NSETS], coff[NSETS];
   bool xvalid[NSETS], cvalid[NSETS];
 #pragma unroll
   for (int s = 0; s < NSETS; ++s) {
-    xoff[s] = (8 * s + g) * 4 + c;
+    xoff[s] = ((8 * s + g) * 4 + c) * 2;
+    coff[s] = (4 * s + c) * 2;
     xvalid[s] = (uint32_t)(8 * s + g) < 2 * batch;
     cvalid[s] = (uint32_t)(4 * s + c) < batch;
   }
+  const uint32_t xstride = nv * 8, cstride = batch * 2;  // per pair
 
   Best best[NSETS];
 #pragma unroll
@@ -429,65 +439,80 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(GemvArgs a) {
 #pragma unroll
     for (int s = 0; s < NSETS; ++s) acc[m][s][0] = acc[m][s][1] = 0.0f;
 
-  // ---- main loop: one 16-row x 64-column chunk per iteration ----
-  uint32_t tt = c0 / P, p = c0 % P;
-  const uint4 *xp = xf4 + 2 * p * nv * 4;  // B fragments of pair p
-  const float *cp = corr + 2 * p * batch;   // offset terms of pair p
-  uint8_t *cur = ring;
-  for (uint32_t cc = c0; cc < c1; ++cc) {
-    cp_async_wait<S - 1>();  // this lane's copies of chunk cc have landed
-    __syncwarp();            // ... and every other lane's
-    uint4 xb[2][NSETS];
-    float cr[2][NSETS];
+  // ---- main loop: one 16-row x 64-column chunk per iteration, flushing the accumulators
+  // at the end of a tile or of the range ----
+  uint32_t tt = c0 / P;
+  const uint32_t p0 = c0 % P;
+  const uint4 *xp = xf4 + p0 * xstride;
+  const float *cp = corr + p0 * cstride;
+  uint32_t flush_at = min(P - 1 - p0, n - 1);
+  const uint8_t *const q_rd = ring + lane * 16;
+  const uint8_t *const s_rd = ring + SO + (PRIV ? c * 128 : 0) + g * 16;
+  // B fragments and offset terms of unused columns / batch rows are never loaded: those
+  // lanes keep zeros (their D columns are never emitted), with no per-chunk re-zeroing
+  uint4 xb[2][NSETS];
+  float cr[2][NSETS];
 #pragma unroll
-    for (int hb = 0; hb < 2; ++hb)
+  for (int s = 0; s < NSETS; ++s) {
+    xb[0][s] = xb[1][s] = make_uint4(0, 0, 0, 0);
+    cr[0][s] = cr[1][s] = 0.0f;
+  }
+  uint32_t i = 0;
+  while (i < n) {
+#pragma unroll 1
+    for (; i <= flush_at; ++i) {
+      cp_async_wait<S - 2>();  // this lane's copies of chunk i have landed
+      if (!PRIV) __syncwarp();  // ... and every other lane's; all finished chunk i - 1
+      issue(i + S - 1);         // refill the stage of chunk i - 1
+      const uint32_t st_off = (i % S) * STAGE;
 #pragma unroll
       for (int s = 0; s < NSETS; ++s) {
-        xb[hb][s] = xvalid[s] ? xp[hb * nv * 4 + xoff[s]] : make_uint4(0, 0, 0, 0);
-        cr[hb][s] = cvalid[s] ? cp[hb * batch + 4 * s + c] : 0.0f;
-      }
-#pragma unroll
-    for (int m = 0; m < NMAT; ++m) {
-      const uint8_t *ch = cur + m * CB;
-      const float4 sc = *reinterpret_cast<const float4 *>(ch + SO + g * 16);
-      uint4 wq[QT == 4 ? 1 : 2];
-      wq[0] = *reinterpret_cast<const uint4 *>(ch + lane * 16);
-      if (QT == 8) wq[QT == 4 ? 0 : 1] = *reinterpret_cast<const uint4 *>(ch + 512 + lane * 16);
-#pragma unroll
-      for (int hb = 0; hb < 2; ++hb) {
-        uint32_t a0[4], a1[4];
-        if (QT == 4) {
-          uint32_t rg[4], rg8[4];
-          dq4_word(hb ? wq[0].z : wq[0].x, rg);
-          dq4_word(hb ? wq[0].w : wq[0].y, rg8);
-          a0[0] = rg[0]; a0[1] = rg8[0]; a0[2] = rg[1]; a0[3] = rg8[1];
-          a1[0] = rg[2]; a1[1] = rg8[2]; a1[2] = rg[3]; a1[3] = rg8[3];
-        } else {
-          const uint4 q = wq[QT == 4 ? 0 : hb];
-          uint32_t g0l, g0h, g1l, g1h, h0l, h0h, h1l, h1h;
-          dq8_word(q.x, g0l, g0h);
-          dq8_word(q.y, g1l, g1h);
-          dq8_word(q.z, h0l, h0h);
-          dq8_word(q.w, h1l, h1h);
-          a0[0] = g0l; a0[1] = h0l; a0[2] = g0h; a0[3] = h0h;
-          a1[0] = g1l; a1[1] = h1l; a1[2] = g1h; a1[3] = h1h;
+        if (xvalid[s]) {
+          xb[0][s] = xp[xoff[s]];
+          xb[1][s] = xp[xoff[s] + 1];
         }
-        const float sg = hb ? sc.z : sc.x, sg8 = hb ? sc.w : sc.y;
-#pragma unroll
-        for (int s = 0; s < NSETS; ++s)
-          block_mma<QT>(a0, a1, xb[hb][s], cr[hb][s], sg, sg8, acc[m][s]);
+        if (cvalid[s]) {
+          const float2 c2 = *reinterpret_cast<const float2 *>(cp + coff[s]);
+          cr[0][s] = c2.x;
+          cr[1][s] = c2.y;
+        }
       }
+#pragma unroll
+      for (int m = 0; m < NMAT; ++m) {
+        const float4 sc = *reinterpret_cast<const float4 *>(s_rd + st_off + m * KS);
+        uint4 wq[QT == 4 ? 1 : 2];
+        wq[0] = *reinterpret_cast<const uint4 *>(q_rd + st_off + m * KS);
+        if (QT == 8) wq[QT == 4 ? 0 : 1] = *reinterpret_cast<const uint4 *>(q_rd + st_off + m * KS + 512);
+#pragma unroll
+        for (int hb = 0; hb < 2; ++hb) {
+          uint32_t a0[4], a1[4];
+          if (QT == 4) {
+            uint32_t rg[4], rg8[4];
+            dq4_word(hb ? wq[0].z : wq[0].x, rg);
+            dq4_word(hb ? wq[0].w : wq[0].y, rg8);
+            a0[0] = rg[0]; a0[1] = rg8[0]; a0[2] = rg[1]; a0[3] = rg8[1];
+            a1[0] = rg[2]; a1[1] = rg8[2]; a1[2] = rg[3]; a1[3] = rg8[3];
+          } else {
+            const uint4 q = wq[QT == 4 ? 0 : hb];
+            uint32_t g0l, g0h, g1l, g1h, h0l, h0h, h1l, h1h;
+            dq8_word(q.x, g0l, g0h);
+            dq8_word(q.y, g1l, g1h);
+            dq8_word(q.z, h0l, h0h);
+            dq8_word(q.w, h1l, h1h);
+            a0[0] = g0l; a0[1] = h0l; a0[2] = g0h; a0[3] = h0h;
+            a1[0] = g1l; a1[1] = h1l; a1[2] = g1h; a1[3] = h1h;
+          }
+          const float sg = hb ? sc.z : sc.x, sg8 = hb ? sc.w : sc.y;
+#pragma unroll
+          for (int s = 0; s < NSETS; ++s)
+            block_mma<QT>(a0, a1, xb[hb][s], cr[hb][s], sg, sg8, acc[m][s]);
+        }
+      }
+      xp += xstride;
+      cp += cstride;
     }
-    __syncwarp();  // every lane has read this stage: refill it
-    issue_next(cur);
-    cur += STAGE;
-    if (cur == ring + S * STAGE) cur = ring;
-    xp += 2 * nv * 4;
-    cp += 2 * batch;
 
-    // ---- tile boundary ----
-    const bool tile_end = (p == P - 1);
-    if (tile_end || cc + 1 == c1) {
+    {
       const uint32_t tb = tt * P, te = tb + P;
       if (tb >= c0 && te <= c1) {
         // the whole tile is ours: write it directly
@@ -566,7 +591,6 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(GemvArgs a) {
 #pragma unroll
                 for (int m = 0; m < NMAT; ++m) v[q][m] += t[u][q][m];
           }
-          // lane owns (row, j) = ((lane + 32 q) / 8, lane % 8)
 #pragma unroll
           for (int q = 0; q < 4; ++q) {
             uint32_t idx = lane + 32 * q, row = idx >> 3, j = idx & 7;
@@ -579,14 +603,11 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(GemvArgs a) {
       for (int m = 0; m < NMAT; ++m)
 #pragma unroll
         for (int s = 0; s < NSETS; ++s) acc[m][s][0] = acc[m][s][1] = 0.0f;
-    }
-    if (tile_end) {
-      p = 0;
+      // next tile starts at pair 0
       ++tt;
       xp = xf4;
       cp = corr;
-    } else {
-      ++p;
+      flush_at = min(flush_at + P, n - 1);
     }
   }
   cp_async_wait<0>();
@@ -662,6 +683,7 @@ template <int QT, int NMAT, int NSETS>
 cudaError_t launch_t(const GemvArgs &a, int num_sms, cudaStream_t s, bool pdl) {
   switch (stages_for(a.k, a.batch, NMAT, QT, a.pro != kProNone)) {
     case 8: return launch_s<QT, NMAT, NSETS, 8>(a, num_sms, s, pdl);
+    case 6: return launch_s<QT, NMAT, NSETS, 6>(a, num_sms, s, pdl);
     case 4: return launch_s<QT, NMAT, NSETS, 4>(a, num_sms, s, pdl);
     case 2: return launch_s<QT, NMAT, NSETS, 2>(a, num_sms, s, pdl);
     default: return cudaErrorInvalidValue;
@@ -670,7 +692,8 @@ cudaError_t launch_t(const GemvArgs &a, int num_sms, cudaStream_t s, bool pdl) {
 
 template <int QT, int NMAT, int NSETS>
 cudaError_t prepare_t() {
-  cudaError_t e[3] = {allow_max_dynamic_smem(gemv_kernel<QT, NMAT, NSETS, 8>),
+  cudaError_t e[4] = {allow_max_dynamic_smem(gemv_kernel<QT, NMAT, NSETS, 8>),
+                      allow_max_dynamic_smem(gemv_kernel<QT, NMAT, NSETS, 6>),
                       allow_max_dynamic_smem(gemv_kernel<QT, NMAT, NSETS, 4>),
                       allow_max_dynamic_smem(gemv_kernel<QT, NMAT, NSETS, 2>)};
   for (cudaError_t x : e)
@@ -693,6 +716,21 @@ cudaError_t prepare_gemv_kernels() {
 size_t gemv_smem_bytes(int qt, uint32_t k, uint32_t batch, bool geglu, bool prologue) {
   int st = stages_for(k, batch, geglu ? 2 : 1, qt, prologue);
   return st ? layout_for(k, batch, geglu ? 2 : 1, qt, st).total : (size_t)-1;
+}
+
+bool gemv_segments_contiguous(const GemvArgs &a, int qt, int nmat) {
+  const uint64_t chunk = qt == 8 ? kQ8ChunkBytes : kQ4ChunkBytes;
+  const uint64_t per_tile = (uint64_t)pairs_of(a.k) * chunk;
+  for (int m = 0; m < nmat; ++m) {
+    uint64_t off = 0;
+    for (int s = 0; s < 3; ++s) {
+      if (a.tiles[s] == 0) continue;
+      if (reinterpret_cast<uintptr_t>(a.w[s][m]) != reinterpret_cast<uintptr_t>(a.w[0][m]) + off)
+        return false;
+      off += a.tiles[s] * per_tile;
+    }
+  }
+  return true;
 }
 
 size_t gemv_part_bytes(int num_sms) { return (size_t)num_sms * kWarps * 2 * 2 * 128 * 4; }

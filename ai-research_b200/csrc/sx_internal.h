@@ -51,6 +51,9 @@ cudaError_t launch_gemv(int qt, bool geglu, const GemvArgs &a, int num_sms, cuda
                         bool pdl);
 size_t gemv_smem_bytes(int qt, uint32_t k, uint32_t batch, bool geglu, bool prologue);
 size_t gemv_part_bytes(int num_sms);
+// The kernel streams the chunks of all segments as one run starting at w[0][m]: segment s
+// must begin where segment s - 1 ends.
+bool gemv_segments_contiguous(const GemvArgs &a, int qt, int nmat);
 size_t gemv_workers(int num_sms);
 constexpr uint32_t kGemvPrologueMaxK = 4096;  // fused norm prologues hold K / 512 <= 8 per thread
 constexpr uint32_t kMaxGemvTiles = 262144;

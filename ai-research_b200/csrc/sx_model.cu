@@ -64,6 +64,13 @@ sx_status mk_buf(sx_model *m, uint64_t bytes, sx_buffer **out) {
   return st;
 }
 
+// a non-owning window [off, off + bytes) of an allocation made with mk_buf
+sx_status mk_view(sx_model *m, sx_buffer *base, uint64_t off, uint64_t bytes, sx_buffer **out) {
+  sx_status st = sx_buffer_wrap(m->e, static_cast<uint8_t *>(base->d) + off, bytes, out);
+  if (st == SX_OK) m->buffers.push_back(*out);
+  return st;
+}
+
 sx_status mk_set(sx_model *m, std::vector<sx_buffer *> bufs, sx_set **out) {
   sx_status st = sx_set_create(m->e, bufs.data(), (uint32_t)bufs.size(), out);
   if (st == SX_OK) m->sets.push_back(*out);
@@ -117,9 +124,14 @@ sx_status alloc_model(sx_model *m) {
     M_TRY(mk_buf(m, 4ull * H, &B.pre_ffn));
     M_TRY(mk_buf(m, 4ull * H, &B.post_attn));
     M_TRY(mk_buf(m, 4ull * H, &B.post_ffn));
-    M_TRY(mk_buf(m, sx_packed_bytes(B.q_dim, H, SX_QUANT_Q4), &B.wq));
-    M_TRY(mk_buf(m, sx_packed_bytes(B.kv_dim, H, SX_QUANT_Q4), &B.wk));
-    M_TRY(mk_buf(m, sx_packed_bytes(B.kv_dim, H, SX_QUANT_Q4), &B.wv));
+    // q | k | v back to back: the fused projection streams them as one run of chunks
+    const uint64_t qb = sx_packed_bytes(B.q_dim, H, SX_QUANT_Q4);
+    const uint64_t kvb_w = sx_packed_bytes(B.kv_dim, H, SX_QUANT_Q4);
+    sx_buffer *qkv = nullptr;
+    M_TRY(mk_buf(m, qb + 2 * kvb_w, &qkv));
+    M_TRY(mk_view(m, qkv, 0, qb, &B.wq));
+    M_TRY(mk_view(m, qkv, qb, kvb_w, &B.wk));
+    M_TRY(mk_view(m, qkv, qb + kvb_w, kvb_w, &B.wv));
     M_TRY(mk_buf(m, sx_packed_bytes(H, B.q_dim, SX_QUANT_Q4), &B.wo));
     M_TRY(mk_buf(m, sx_packed_bytes(I, H, SX_QUANT_Q4), &B.wg));
     M_TRY(mk_buf(m, sx_packed_bytes(I, H, SX_QUANT_Q4), &B.wu));
