@@ -151,8 +151,6 @@ SX_DEV uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
   return r;
 }
 
-// Q4: eight nibbles of one packed word -> four bf16x2 holding 8 + q/2 (exact).
-// Register j holds nibble j (low half) and nibble j+4 (high half).
 // (a & b) | c in one LOP3 (truth table 0xEA); b and c are registers, so a constant mask and
 // magic number are materialised once instead of costing a second logic op per use
 SX_DEV uint32_t and_or(uint32_t a, uint32_t b, uint32_t c) {
@@ -160,6 +158,9 @@ SX_DEV uint32_t and_or(uint32_t a, uint32_t b, uint32_t c) {
   asm("lop3.b32 %0, %1, %2, %3, 0xEA;\n" : "=r"(d) : "r"(a), "r"(b), "r"(c));
   return d;
 }
+// Q4: the eight nibbles of one packed word -> four bf16x2 A-fragment registers holding
+// 8 + q/2 (exact): register j holds nibble slot j (low half) and slot j + 4 (high half) in
+// mantissa bits 3..6; one shift and one LOP3 per register.
 SX_DEV void dq4_word(uint32_t u, uint32_t (&r)[4]) {
   const uint32_t m = 0x00780078u, e = 0x41004100u;
   r[0] = and_or(u << 3, m, e);

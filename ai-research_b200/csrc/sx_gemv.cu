@@ -11,17 +11,22 @@
 // persistent 512-thread CTA runs per SM and each of its 16 warps is a worker that owns a
 // contiguous range of N / (CTAs x 16) chunks ("stream-K"), so the load is balanced for any
 // shape.  Each warp streams its chunks through its own shared-memory ring of S stages with
-// 16-byte cp.async copies; the first S chunks are issued before the programmatic-dependent-
-// launch wait, i.e. while the previous kernel is still finishing.  A tile covered by one
-// worker is written directly; a tile split between workers is reduced by the last worker to
-// arrive, summing the partial records in worker order (deterministic; no atomics on data).
+// 16-byte cp.async copies; the first S - 1 chunks are issued before the programmatic-
+// dependent-launch wait, i.e. while the previous kernel is still finishing.  The chunks of a
+// call form one contiguous stream (the segments of a q|k|v call lie back to back), each lane
+// copies and reads back the same 16 bytes of every quant record, and the warp synchronises once
+// per chunk for the shared scale record.  A tile covered by one worker is written directly; a
+// tile split between workers is reduced by the last worker to arrive, summing the partial
+// records in worker order (deterministic; no atomics on data).
 //
 // Dequantisation.  Nibbles become mma.m16n8k16 A fragments with one shift + one LOP3 per two
 // weights (bf16 value 8 + q/2, exact).  The f32 activation enters as the B operand split into
 // bf16 hi + lo (16 significant bits), one column pair per batch row, so the tensor core forms
 // the 32-element block dot products; the per-block f32 scale and the offset are applied on
-// the f32 accumulator: sum_e (q_e - 8) x_e = 2 * (D - 12 * sum_e x_e).  Q8 uses f16 values
-// 1024 + (q + 128) (exact) with a per-vector power-of-two prescale of x.
+// the f32 result: sum_e (q_e - 8) x_e = 2 * (D - 12 * sum_e x_e).  (A 1024-magic f16 form
+// needs fewer logic ops but carries an offset ~200x the signal through the f32 sums, costing
+// about 1e-3 relative accuracy on the outputs; the bf16 form keeps the offset near 5x.)  Q8
+// uses f16 values 1024 + (q + 128) (exact) with a per-vector power-of-two prescale of x.
 #include "sx_common.cuh"
 #include "sx_internal.h"
 
@@ -48,7 +53,6 @@ struct QTraits<4> {
   static constexpr int kScaleOff = 512;
   static constexpr int kStage = 512 + 512;  // quants + four copies of the scales
   static constexpr int kStageShared = 512 + 128;  // quants + one shared copy
-  static constexpr float kCorr = 12.0f;
 };
 template <>
 struct QTraits<8> {
@@ -56,7 +60,6 @@ struct QTraits<8> {
   static constexpr int kScaleOff = 1024;
   static constexpr int kStage = 1024 + 512;
   static constexpr int kStageShared = 1024 + 128;
-  static constexpr float kCorr = 1152.0f;
 };
 
 struct Layout {
@@ -238,8 +241,9 @@ SX_DEV void stage_x(const GemvArgs &a, const float *src, uint32_t ld, uint8_t *s
         __nv_bfloat16 l0 = __float2bfloat16_rn(r0), l1 = __float2bfloat16_rn(r1);
         hw = (uint32_t)__bfloat16_as_ushort(h0) | ((uint32_t)__bfloat16_as_ushort(h1) << 16);
         lw = (uint32_t)__bfloat16_as_ushort(l0) | ((uint32_t)__bfloat16_as_ushort(l1) << 16);
-        part = (__bfloat162float(h0) + __bfloat162float(l0)) +
-               (__bfloat162float(h1) + __bfloat162float(l1));
+        // Q4 value 8 + q / 2 = (q - 8) / 2 + 12
+        part = 12.0f * ((__bfloat162float(h0) + __bfloat162float(l0)) +
+                        (__bfloat162float(h1) + __bfloat162float(l1)));
       } else {
         int e = xexp[j];
         x0 = ldexpf(x0, e);
@@ -249,7 +253,8 @@ SX_DEV void stage_x(const GemvArgs &a, const float *src, uint32_t ld, uint8_t *s
         __half l0 = __float2half_rn(r0), l1 = __float2half_rn(r1);
         hw = (uint32_t)__half_as_ushort(h0) | ((uint32_t)__half_as_ushort(h1) << 16);
         lw = (uint32_t)__half_as_ushort(l0) | ((uint32_t)__half_as_ushort(l1) << 16);
-        part = (__half2float(h0) + __half2float(l0)) + (__half2float(h1) + __half2float(l1));
+        // Q8 value 1024 + (q + 128) = q + 1152
+        part = 1152.0f * ((__half2float(h0) + __half2float(l0)) + (__half2float(h1) + __half2float(l1)));
       }
       // per pair (blk / 2): uint4 index ((variant * 4 + c) * 2 + half), word jj
       const uint32_t pr = blk >> 1, hb = blk & 1;
@@ -260,7 +265,7 @@ SX_DEV void stage_x(const GemvArgs &a, const float *src, uint32_t ld, uint8_t *s
     part += __shfl_xor_sync(0xffffffffu, part, 4);
     part += __shfl_xor_sync(0xffffffffu, part, 2);
     part += __shfl_xor_sync(0xffffffffu, part, 1);
-    if (it < items && (it & 15) == 0) corr[((blk >> 1) * a.batch + j) * 2 + (blk & 1)] = QTraits<QT>::kCorr * part;
+    if (it < items && (it & 15) == 0) corr[((blk >> 1) * a.batch + j) * 2 + (blk & 1)] = part;
   }
   __syncthreads();
 }
