@@ -221,51 +221,67 @@ SX_DEV void stage_x(const GemvArgs &a, const float *src, uint32_t ld, uint8_t *s
     __syncthreads();
   }
 
-  const uint32_t items = nblk * a.batch * 16;
-  const uint32_t items_pad = (items + 31) & ~31u;
-  for (uint32_t it = tid; it < items_pad; it += blockDim.x) {
-    float part = 0.0f;
-    uint32_t c = it & 3, jj = (it >> 2) & 3, rest = it >> 4;
-    uint32_t j = rest % a.batch, blk = rest / a.batch;
-    if (it < items) {
-      uint32_t e0 = blk * 32 + jj * 8 + 2 * c;
-      float x0 = 0.0f, x1 = 0.0f;
-      if (blk < nb) {
-        x0 = src[j * ld + e0];
-        x1 = src[j * ld + e0 + 1];
+  // One thread per group of 8 consecutive elements (block blk, word jj of each of the four
+  // lane columns c): packed conversions, four scattered fragment words per variant, and the
+  // block sum for the offset term over the block's four groups (adjacent lanes).
+  const uint32_t groups = nblk * 4;
+  const uint32_t gpad = (groups + 31) & ~31u;
+  for (uint32_t j = 0; j < a.batch; ++j) {
+    // Q8: multiply by 2^e (exact for a power of two, e in [-100, 100])
+    const float p2 = QT == 8 ? __int_as_float((xexp[j] + 127) << 23) : 1.0f;
+    for (uint32_t gi = tid; gi < gpad; gi += blockDim.x) {
+      const uint32_t blk = gi >> 2, jj = gi & 3;
+      float part = 0.0f;
+      if (gi < groups) {
+        float v[8];
+        if (blk < nb) {
+          const float4 u0 = *reinterpret_cast<const float4 *>(src + (size_t)j * ld + blk * 32 + jj * 8);
+          const float4 u1 = *reinterpret_cast<const float4 *>(src + (size_t)j * ld + blk * 32 + jj * 8 + 4);
+          v[0] = u0.x; v[1] = u0.y; v[2] = u0.z; v[3] = u0.w;
+          v[4] = u1.x; v[5] = u1.y; v[6] = u1.z; v[7] = u1.w;
+        } else {
+#pragma unroll
+          for (int q = 0; q < 8; ++q) v[q] = 0.0f;
+        }
+        const uint32_t pr = blk >> 1, hb = blk & 1;
+        // word jj of uint4 ((variant * 4 + c) * 2 + hb) of pair pr; c steps 8 words
+        uint32_t *hi_w = xf + ((((pr * nv + 2 * j) * 4) * 2 + hb) * 4 + jj);
+        uint32_t *lo_w = xf + ((((pr * nv + 2 * j + 1) * 4) * 2 + hb) * 4 + jj);
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          const float x0 = v[2 * c] * p2, x1 = v[2 * c + 1] * p2;
+          uint32_t hw, lw;
+          float h0, h1, l0, l1;
+          if (QT == 4) {
+            const __nv_bfloat162 h = __floats2bfloat162_rn(x0, x1);
+            h0 = __low2float(h);
+            h1 = __high2float(h);
+            const __nv_bfloat162 l = __floats2bfloat162_rn(__fsub_rn(x0, h0), __fsub_rn(x1, h1));
+            l0 = __low2float(l);
+            l1 = __high2float(l);
+            hw = *reinterpret_cast<const uint32_t *>(&h);
+            lw = *reinterpret_cast<const uint32_t *>(&l);
+          } else {
+            const __half2 h = __floats2half2_rn(x0, x1);
+            h0 = __low2float(h);
+            h1 = __high2float(h);
+            const __half2 l = __floats2half2_rn(__fsub_rn(x0, h0), __fsub_rn(x1, h1));
+            l0 = __low2float(l);
+            l1 = __high2float(l);
+            hw = *reinterpret_cast<const uint32_t *>(&h);
+            lw = *reinterpret_cast<const uint32_t *>(&l);
+          }
+          hi_w[c * 8] = hw;
+          lo_w[c * 8] = lw;
+          part += (h0 + l0) + (h1 + l1);
+        }
       }
-      uint32_t hw, lw;
-      if (QT == 4) {
-        __nv_bfloat16 h0 = __float2bfloat16_rn(x0), h1 = __float2bfloat16_rn(x1);
-        float r0 = __fsub_rn(x0, __bfloat162float(h0)), r1 = __fsub_rn(x1, __bfloat162float(h1));
-        __nv_bfloat16 l0 = __float2bfloat16_rn(r0), l1 = __float2bfloat16_rn(r1);
-        hw = (uint32_t)__bfloat16_as_ushort(h0) | ((uint32_t)__bfloat16_as_ushort(h1) << 16);
-        lw = (uint32_t)__bfloat16_as_ushort(l0) | ((uint32_t)__bfloat16_as_ushort(l1) << 16);
-        // Q4 value 8 + q / 2 = (q - 8) / 2 + 12
-        part = 12.0f * ((__bfloat162float(h0) + __bfloat162float(l0)) +
-                        (__bfloat162float(h1) + __bfloat162float(l1)));
-      } else {
-        int e = xexp[j];
-        x0 = ldexpf(x0, e);
-        x1 = ldexpf(x1, e);
-        __half h0 = __float2half_rn(x0), h1 = __float2half_rn(x1);
-        float r0 = __fsub_rn(x0, __half2float(h0)), r1 = __fsub_rn(x1, __half2float(h1));
-        __half l0 = __float2half_rn(r0), l1 = __float2half_rn(r1);
-        hw = (uint32_t)__half_as_ushort(h0) | ((uint32_t)__half_as_ushort(h1) << 16);
-        lw = (uint32_t)__half_as_ushort(l0) | ((uint32_t)__half_as_ushort(l1) << 16);
-        // Q8 value 1024 + (q + 128) = q + 1152
-        part = 1152.0f * ((__half2float(h0) + __half2float(l0)) + (__half2float(h1) + __half2float(l1)));
-      }
-      // per pair (blk / 2): uint4 index ((variant * 4 + c) * 2 + half), word jj
-      const uint32_t pr = blk >> 1, hb = blk & 1;
-      xf[(((((pr * nv + 2 * j) * 4 + c) << 1) + hb) << 2) + jj] = hw;
-      xf[(((((pr * nv + 2 * j + 1) * 4 + c) << 1) + hb) << 2) + jj] = lw;
+      part += __shfl_xor_sync(0xffffffffu, part, 1);
+      part += __shfl_xor_sync(0xffffffffu, part, 2);
+      // Q4 value 8 + q / 2 = (q - 8) / 2 + 12; Q8 value 1024 + (q + 128) = q + 1152
+      if (gi < groups && jj == 0)
+        corr[((blk >> 1) * a.batch + j) * 2 + (blk & 1)] = (QT == 4 ? 12.0f : 1152.0f) * part;
     }
-    part += __shfl_xor_sync(0xffffffffu, part, 8);
-    part += __shfl_xor_sync(0xffffffffu, part, 4);
-    part += __shfl_xor_sync(0xffffffffu, part, 2);
-    part += __shfl_xor_sync(0xffffffffu, part, 1);
-    if (it < items && (it & 15) == 0) corr[((blk >> 1) * a.batch + j) * 2 + (blk & 1)] = part;
   }
   __syncthreads();
 }
