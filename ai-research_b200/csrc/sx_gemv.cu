@@ -7,17 +7,17 @@
 // (kernels.zig:94-115); argmax = first index of the maximum (kernels.zig:164-174).
 //
 // Work split.  The matrix (or the concatenation of up to three matrices, e.g. q|k|v) is a
-// sequence of N = tiles x pairs 640-byte chunks (16 rows x 64 columns; 1152 B for Q8).  One
-// persistent 512-thread CTA runs per SM and each of its 16 warps is a worker that owns a
-// contiguous range of N / (CTAs x 16) chunks ("stream-K"), so the load is balanced for any
-// shape.  Each warp streams its chunks through its own shared-memory ring of S stages with
-// 16-byte cp.async copies; the first S - 1 chunks are issued before the programmatic-
-// dependent-launch wait, i.e. while the previous kernel is still finishing.  The chunks of a
-// call form one contiguous stream (the segments of a q|k|v call lie back to back), each lane
-// copies and reads back the same 16 bytes of every quant record, and the warp synchronises once
-// per chunk for the shared scale record.  A tile covered by one worker is written directly; a
-// tile split between workers is reduced by the last worker to arrive, summing the partial
-// records in worker order (deterministic; no atomics on data).
+// sequence of tiles x pairs 640-byte chunks (16 rows x 64 columns; 1152 B for Q8).  One
+// persistent 512-thread CTA runs per SM and owns a contiguous run of whole tiles (tile counts
+// balanced to within one); its 16 warps split the run's chunks evenly.  Each warp streams its
+// chunks through its own shared-memory ring of S stages with 16-byte cp.async copies; the first
+// S - 1 chunks are issued before the programmatic-dependent-launch wait, i.e. while the previous
+// kernel is still finishing.  The chunks of a call form one contiguous stream (the segments of a
+// q|k|v call lie back to back), each lane copies and reads back the same 16 bytes of every quant
+// record, and the warp synchronises once per chunk for the shared scale record.  A tile held by
+// one warp is written directly; the partial sums of a tile shared by several warps of the CTA
+// meet in shared memory after the loop and are added in warp order (deterministic; no global
+// scratch, fences or atomics).
 //
 // Dequantisation.  Nibbles become mma.m16n8k16 A fragments with one shift + one LOP3 per two
 // weights (bf16 value 8 + q/2, exact).  The f32 activation enters as the B operand split into
@@ -333,9 +333,13 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(GemvArgs a) {
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, c = lane & 3;
   const uint32_t P = pairs_of(a.k), nv = nv_of(a.batch), batch = a.batch;
   const uint32_t T = a.tiles[0] + a.tiles[1] + a.tiles[2];
-  const uint32_t N = T * P;
   const uint32_t NW = gridDim.x * kWarps, wid = blockIdx.x * kWarps + warp;
-  const uint32_t c0 = wstart(N, NW, wid), c1 = wstart(N, NW, wid + 1);
+  // CTA b owns whole tiles [ct0, ct1) (counts balanced to within one); its warps split the
+  // run's chunks evenly, warp w taking [cbase + ncta w / 16, cbase + ncta (w + 1) / 16)
+  const uint32_t ct0 = (uint32_t)((uint64_t)T * blockIdx.x / gridDim.x);
+  const uint32_t ct1 = (uint32_t)((uint64_t)T * (blockIdx.x + 1) / gridDim.x);
+  const uint32_t cbase = ct0 * P, ncta = (ct1 - ct0) * P;
+  const uint32_t c0 = cbase + wstart(ncta, kWarps, warp), c1 = cbase + wstart(ncta, kWarps, warp + 1);
 
   uint8_t *const ring = smem + L.ring + warp * S * STAGE;
 
@@ -455,6 +459,10 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(GemvArgs a) {
   };
 
   float acc[NMAT][NSETS][2];
+  // sums of the tiles this warp shares with other warps: slot 0 = the tile holding its first
+  // chunk, slot 1 = the tile holding its last chunk
+  float part0[NMAT][NSETS][2], part1[NMAT][NSETS][2];
+  bool has0 = false, has1 = false;
 #pragma unroll
   for (int m = 0; m < NMAT; ++m)
 #pragma unroll
@@ -546,79 +554,18 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(GemvArgs a) {
             for (int m = 0; m < NMAT; ++m) v[m] = acc[m][s][h];
             emit(tt, g + 8 * h, 4 * s + c, v, s);
           }
-      } else {
-        // partial tile: publish a record; the last contributor reduces all of them in
-        // worker order.  slot 0 = the tile holds this worker's first chunk, 1 = its last.
-        const int slot = c0 >= tb ? 0 : 1;
-        float *rec = a.part + ((size_t)wid * 2 + slot) * NMAT * 128;
+      } else if (c0 >= tb) {
 #pragma unroll
         for (int m = 0; m < NMAT; ++m)
 #pragma unroll
-          for (int s = 0; s < NSETS; ++s) {
-            uint32_t j = 4 * s + c;
-            rec[m * 128 + g * 8 + j] = acc[m][s][0];
-            rec[m * 128 + (g + 8) * 8 + j] = acc[m][s][1];
-          }
-        __threadfence();
-        __syncwarp();
-        // contributors: N >= NW -> every worker owns >= 1 chunk, so they are the owners
-        // wlo..whi of the tile's first and last chunks; N < NW -> every worker owns at most
-        // one chunk, so each of the tile's P chunks has its own owner
-        const bool dense = N >= NW;
-        uint32_t wlo = 0, whi = 0, expected = P;
-        if (dense) {
-          wlo = wowner(N, NW, tb);
-          whi = wowner(N, NW, te - 1);
-          expected = whi - wlo + 1;
-        }
-        uint32_t old = 0;
-        if (lane == 0) old = atomicAdd(&a.tile_cnt[tt], 1u);
-        old = __shfl_sync(0xffffffffu, old, 0);
-        if (old + 1 == expected) {
-          __threadfence();
-          const bool lo_tail = dense && wstart(N, NW, wlo) < tb;  // wlo started earlier
-          float v[4][NMAT];
+          for (int s = 0; s < NSETS; ++s) part0[m][s][0] = acc[m][s][0], part0[m][s][1] = acc[m][s][1];
+        has0 = true;
+      } else {
 #pragma unroll
-          for (int q = 0; q < 4; ++q)
+        for (int m = 0; m < NMAT; ++m)
 #pragma unroll
-            for (int m = 0; m < NMAT; ++m) v[q][m] = 0.0f;
-          // lane owns (row, j) = ((lane + 32 q) / 8, lane % 8); only j < batch is read.
-          // Records are fetched four contributors at a time so their L2 round trips
-          // overlap; the additions stay in contributor order.
-          const bool jlive = (uint32_t)(lane & 7) < batch;
-          for (uint32_t k0 = 0; k0 < expected; k0 += 4) {
-            float t[4][4][NMAT];
-#pragma unroll
-            for (int u = 0; u < 4; ++u) {
-              const uint32_t k = k0 + u;
-              const bool live = jlive && k < expected;
-              uint32_t w = 0;
-              int sl = 0;
-              if (live) {
-                w = dense ? wlo + k : wowner(N, NW, tb + k);
-                sl = (dense && k == 0 && lo_tail) ? 1 : 0;
-              }
-              const float *r = a.part + ((size_t)w * 2 + sl) * NMAT * 128;
-#pragma unroll
-              for (int q = 0; q < 4; ++q)
-#pragma unroll
-                for (int m = 0; m < NMAT; ++m)
-                  t[u][q][m] = live ? __ldcg(r + m * 128 + lane + 32 * q) : 0.0f;
-            }
-#pragma unroll
-            for (int u = 0; u < 4; ++u)
-#pragma unroll
-              for (int q = 0; q < 4; ++q)
-#pragma unroll
-                for (int m = 0; m < NMAT; ++m) v[q][m] += t[u][q][m];
-          }
-#pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            uint32_t idx = lane + 32 * q, row = idx >> 3, j = idx & 7;
-            emit(tt, row, j, v[q], j >= 4 ? NSETS - 1 : 0);
-          }
-          if (lane == 0) a.tile_cnt[tt] = 0;
-        }
+          for (int s = 0; s < NSETS; ++s) part1[m][s][0] = acc[m][s][0], part1[m][s][1] = acc[m][s][1];
+        has1 = true;
       }
 #pragma unroll
       for (int m = 0; m < NMAT; ++m)
@@ -632,6 +579,53 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(GemvArgs a) {
     }
   }
   cp_async_wait<0>();
+
+  // ---- tiles shared by several warps of this CTA: the partial sums meet in shared memory
+  // (each warp's own ring, free now) and the warp (t - ct0) mod 16 adds them in warp order ----
+  {
+    float *own = reinterpret_cast<float *>(ring);  // slot sl at own + sl * NMAT * 128
+#pragma unroll
+    for (int m = 0; m < NMAT; ++m)
+#pragma unroll
+      for (int s = 0; s < NSETS; ++s) {
+        const uint32_t j = 4 * s + c;
+        if (has0) {
+          own[m * 128 + g * 8 + j] = part0[m][s][0];
+          own[m * 128 + (g + 8) * 8 + j] = part0[m][s][1];
+        }
+        if (has1) {
+          own[(NMAT + m) * 128 + g * 8 + j] = part1[m][s][0];
+          own[(NMAT + m) * 128 + (g + 8) * 8 + j] = part1[m][s][1];
+        }
+      }
+  }
+  __syncthreads();
+  for (uint32_t t = ct0 + warp; t < ct1; t += kWarps) {
+    const uint32_t fc = (t - ct0) * P, lc = fc + P - 1;  // relative to cbase
+    const uint32_t wlo = wowner(ncta, kWarps, fc), whi = wowner(ncta, kWarps, lc);
+    if (wlo == whi) continue;  // one warp held the whole tile and wrote it
+    float v[4][NMAT];
+#pragma unroll
+    for (int q = 0; q < 4; ++q)
+#pragma unroll
+      for (int m = 0; m < NMAT; ++m) v[q][m] = 0.0f;
+    for (uint32_t w = wlo; w <= whi; ++w) {
+      if (wstart(ncta, kWarps, w) == wstart(ncta, kWarps, w + 1)) continue;  // empty range
+      // the tile is w's last tile only for the first contributor when it started earlier
+      const int sl = (w == wlo && wstart(ncta, kWarps, w) < fc) ? 1 : 0;
+      const float *r = reinterpret_cast<const float *>(smem + L.ring + w * S * STAGE) + sl * NMAT * 128;
+#pragma unroll
+      for (int q = 0; q < 4; ++q)
+#pragma unroll
+        for (int m = 0; m < NMAT; ++m) v[q][m] += r[m * 128 + lane + 32 * q];
+    }
+    // lane owns (row, j) = ((lane + 32 q) / 8, lane % 8)
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const uint32_t idx = lane + 32 * q, row = idx >> 3, j = idx & 7;
+      emit(t, row, j, v[q], j >= 4 ? NSETS - 1 : 0);
+    }
+  }
 
   if (a.epi == kEpiArgmax) {
     // Per batch row j: lane (g, c) tracked rows of batch row 4s + c in best[s].  Reduce over
