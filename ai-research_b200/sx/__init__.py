@@ -131,6 +131,14 @@ def config_12b(**kw) -> ModelConfig:
 
 _lib = None
 
+
+def _quiet_close(obj):
+    """__del__: release the handle; at interpreter exit the module may already be torn down."""
+    try:
+        obj.close()
+    except Exception:
+        pass
+
 _P = C.c_void_p
 _U32 = C.c_uint32
 _U64 = C.c_uint64
@@ -300,7 +308,7 @@ class Ring:
             lib().sx_ring_destroy(self.h)
             self.h = None
 
-    __del__ = close
+    __del__ = _quiet_close
 
     def reset(self):
         lib().sx_ring_reset(self.h)
@@ -342,7 +350,7 @@ class Engine:
             lib().sx_engine_destroy(self.h)
             self.h = None
 
-    __del__ = close
+    __del__ = _quiet_close
 
     @property
     def stream(self) -> int:
@@ -467,7 +475,7 @@ class Buffer:
             lib().sx_buffer_destroy(self.h)
             self.h = None
 
-    __del__ = close
+    __del__ = _quiet_close
 
     @property
     def ptr(self) -> int:
@@ -503,7 +511,7 @@ class DescriptorSet:
             lib().sx_set_destroy(self.h)
             self.h = None
 
-    __del__ = close
+    __del__ = _quiet_close
 
 
 class CommandBuffer:
@@ -517,7 +525,7 @@ class CommandBuffer:
             lib().sx_cmd_destroy(self.h)
             self.h = None
 
-    __del__ = close
+    __del__ = _quiet_close
 
     def begin(self):
         check(lib().sx_cmd_begin(self.h))
@@ -542,7 +550,7 @@ class Model:
             lib().sx_model_destroy(self.h)
             self.h = None
 
-    __del__ = close
+    __del__ = _quiet_close
 
     def synth_weights(self, seed: int) -> None:
         check(lib().sx_model_synth_weights(self.h, seed))

@@ -48,7 +48,56 @@ def parse():
     ap.add_argument("--impl", default="sx", choices=["sx", "reference"])
     ap.add_argument("--layers", type=int, default=48)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--case", choices=["geglu", "q4_head", "attn"],
+                    help="profiling case: launch one kernel of the step standalone "
+                         "(--launches times) on synthetic data and exit; prints no JSON line")
+    ap.add_argument("--launches", type=int, default=3)
     return ap.parse_args()
+
+
+def run_case(args):
+    """Small standalone workloads for ncu captures of the step's kernels:
+    geglu   -- the fused gate+up GeGLU GEMV of one 12B layer (2 x 15360 x 3840 Q4_0, 73.8 MB)
+    q4_head -- a 262144 x 3840 Q4_0 GEMV (629 MB), the steady-state streaming case
+    attn    -- one 12B-width layer token (16 q / 8 kv heads x 256, 640 live slots), whose
+               second kernel is the fused attention"""
+    import torch
+    import sx
+
+    eng = sx.Engine(0)
+    g = torch.Generator(device="cuda").manual_seed(SEED)
+
+    def packed(m, k):
+        n = sx.packed_bytes(m, k, sx.QUANT_Q4)
+        return torch.randint(0, 256, (n,), dtype=torch.uint8, device="cuda", generator=g)
+
+    if args.case == "attn":
+        cfg = model_cfg_dict(1)
+        cfg["vocab_size"] = 4096
+        model = sx.Model(eng, sx.model_config(**cfg))
+        model.synth_weights(SEED)
+        model.fill_kv(SEED)
+        ring = sx.Ring(1, 32, 512, 96)
+        ring.prefill(0, START_CLOCK)
+        for r in range(96):
+            ring.write_recall(0, r, START_CLOCK - 1 - r)
+        for t in range(args.launches):
+            c = START_CLOCK + t
+            s = ring.activate_slot(0, c)
+            model.forward_token(sx.synth_embed_row(3840, 5, SEED), c, s,
+                                ring.get_active_slots(0, c), want_logits=False)
+    else:
+        m, k = (15360, 3840) if args.case == "geglu" else (262144, 3840)
+        w0, w1 = packed(m, k), (packed(m, k) if args.case == "geglu" else None)
+        x = torch.randn(k, device="cuda", generator=g)
+        y = torch.empty(m, device="cuda")
+        for _ in range(args.launches):
+            if args.case == "geglu":
+                eng.gate_up(w0, w1, x, y, m, k, 1)
+            else:
+                eng.gemv(sx.QUANT_Q4, w0, x, y, m, k, 1)
+    eng.sync()
+    eng.close()
 
 
 def model_cfg_dict(layers=48):
@@ -228,6 +277,9 @@ def main():
     local = int(os.environ.get("LOCAL_RANK", "0"))
     if args.impl == "reference":
         run_reference(args, rank, world)
+        return
+    if args.case:
+        run_case(args)
         return
 
     import torch
