@@ -21,6 +21,7 @@ enum DeviceError : uint32_t {
   kDevWaitTimeout = 1,
   kDevBadParams = 2,
   kDevBadSlot = 3,
+  kDevBarrierTimeout = 4,
 };
 
 SX_DEV void raise_error(uint32_t *err, uint32_t code) {

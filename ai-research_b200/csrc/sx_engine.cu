@@ -269,6 +269,14 @@ sx_status run_op(sx_engine *e, cudaStream_t s, const Op &op, uint32_t *kernels) 
       if (!a.inv_freq) return fst;
       return cuda_status(sx::launch_attn_fused(a, s, true), "fused attention launch");
     }
+    case OP_PERSIST: {
+      *kernels += 1;
+      SX_TRY_CUDA(cudaMemsetAsync(e->persist_bar, 0, 8, s), "barrier reset");
+      return cuda_status(sx::launch_persist(static_cast<const sx::Phase *>(op.dev), op.u[0],
+                                            e->persist_bar, e->err_dev,
+                                            e->num_sms, s),
+                         "persistent decode launch");
+    }
     case OP_H2D:
       return cuda_status(cudaMemcpyAsync(op.dev, op.host, op.bytes, cudaMemcpyHostToDevice, s),
                          "h2d copy");
@@ -536,6 +544,7 @@ SX_API sx_status sx_engine_create(int device, sx_quant_mode mode, uint32_t flags
       size_t o_bi = take(nw_max * 8 * 4);
       size_t o_done = take(256);
       size_t o_amax = take(sx::argmax_scratch_bytes());
+      size_t o_pbar = take(256);
       e->scratch_bytes = off;
       st = cuda_status(cudaMalloc(&e->scratch, e->scratch_bytes), "engine scratch");
       if (st) break;
@@ -548,12 +557,15 @@ SX_API sx_status sx_engine_create(int device, sx_quant_mode mode, uint32_t flags
       e->best_i = reinterpret_cast<uint32_t *>(b + o_bi);
       e->done_cnt = reinterpret_cast<uint32_t *>(b + o_done);
       e->argmax_part = b + o_amax;
+      e->persist_bar = reinterpret_cast<uint32_t *>(b + o_pbar);
       st = cuda_status(cudaMemset(e->scratch, 0, e->scratch_bytes), "engine scratch zero");
       if (st) break;
     }
     st = cuda_status(sx::prepare_gemv_kernels(), "gemv kernel attributes");
     if (st) break;
     st = cuda_status(sx::prepare_ops_kernels(), "attention kernel attributes");
+    if (st) break;
+    st = cuda_status(sx::prepare_persist_kernel(), "persistent kernel attributes");
   } while (0);
   if (st != SX_OK) {
     sx_engine_destroy(e);
@@ -713,8 +725,84 @@ SX_API sx_status sx_cmd_create(sx_engine *e, sx_cmd **out) {
 static void cmd_release_graph(sx_cmd *c) {
   if (c->exec) cudaGraphExecDestroy(c->exec);
   if (c->graph) cudaGraphDestroy(c->graph);
+  if (c->d_phases) cudaFree(c->d_phases);
   c->exec = nullptr;
   c->graph = nullptr;
+  c->d_phases = nullptr;
+}
+
+// Persistent command buffer: the recorded H2D copies, then the GEMV_FUSED / ATTN_FUSED
+// kernels as the phase table of one persistent launch, then the D2H copies.  Phase q (a GEMV)
+// issues its first weight copies after phase q - 1, or after q - 2 when q - 1 is attention
+// and q's shared-memory layout ends below the attention work items (the o projection).
+static sx_status build_persistent(sx_cmd *c) {
+  sx_engine *e = c->e;
+  std::vector<Op> head, tail;
+  std::vector<sx::Phase> ph;
+  for (const Op &op : c->ops) {
+    if (op.kind == OP_H2D) {
+      if (!ph.empty() || !tail.empty()) {
+        set_error("persistent graph: host-to-device copies must precede the kernels");
+        return SX_ERR_UNSUPPORTED;
+      }
+      head.push_back(op);
+    } else if (op.kind == OP_D2H) {
+      tail.push_back(op);
+    } else if ((op.kind == OP_GEMV_FUSED || op.kind == OP_ATTN_FUSED) && tail.empty()) {
+      sx::Phase p{};
+      if (op.kind == OP_GEMV_FUSED) {
+        if (!sx::gemv_segments_contiguous(op.gemv, op.qt, op.geglu ? 2 : 1)) {
+          set_error("persistent graph: the segments of a multi-segment GEMV must lie back to back");
+          return SX_ERR_UNSUPPORTED;
+        }
+        p.kind = sx::kPhaseGemv;
+        p.g = op.gemv;
+        if (!sx::persist_gemv_variant(op.qt, op.geglu, op.gemv, sx::persist_smem_bytes(),
+                                      &p.variant, &p.smem_off)) {
+          set_error("persistent graph: GEMV k=%u batch=%u has no persistent instantiation",
+                    op.gemv.k, op.gemv.batch);
+          return SX_ERR_UNSUPPORTED;
+        }
+        const uint32_t q = (uint32_t)ph.size();
+        bool first = true;
+        for (const sx::Phase &x : ph) first = first && x.kind != sx::kPhaseGemv;
+        p.prefetch_after = first ? sx::kNoPhase : q - 1;
+        if (!first && q >= 2 && ph[q - 1].kind == sx::kPhaseAttn &&
+            ph[q - 2].kind == sx::kPhaseGemv && p.smem_off <= ph[q - 1].smem_off)
+          p.prefetch_after = q - 2;
+      } else {
+        p.kind = sx::kPhaseAttn;
+        p.at = op.attnf;
+        sx_status fst = SX_OK;
+        p.at.inv_freq = engine_inv_freq(e, op.attn_rot, op.attn_theta, &fst);
+        if (!p.at.inv_freq) return fst;
+        if (!sx::persist_attn_variant(p.at, &p.variant)) {
+          set_error("persistent graph: attention head_dim=%u gqa=%u has no persistent "
+                    "instantiation", p.at.head_dim, p.at.num_q / (p.at.num_kv ? p.at.num_kv : 1));
+          return SX_ERR_UNSUPPORTED;
+        }
+        p.smem_off = sx::persist_attn_offset(p.at);
+      }
+      ph.push_back(p);
+    } else {
+      set_error("persistent graph: op %d cannot run as a phase", (int)op.kind);
+      return SX_ERR_UNSUPPORTED;
+    }
+  }
+  if (ph.empty()) {
+    set_error("persistent graph: no kernels recorded");
+    return SX_ERR_UNSUPPORTED;
+  }
+  const size_t bytes = sizeof(sx::Phase) * ph.size();
+  SX_TRY_CUDA(cudaMalloc(&c->d_phases, bytes), "phase table");
+  SX_TRY_CUDA(cudaMemcpy(c->d_phases, ph.data(), bytes, cudaMemcpyHostToDevice), "phase table");
+  Op run{OP_PERSIST};
+  run.u[0] = (uint32_t)ph.size();
+  run.dev = c->d_phases;
+  c->ops = head;
+  c->ops.push_back(run);
+  c->ops.insert(c->ops.end(), tail.begin(), tail.end());
+  return SX_OK;
 }
 
 SX_API void sx_cmd_destroy(sx_cmd *c) {
@@ -732,6 +820,7 @@ SX_API sx_status sx_cmd_begin(sx_cmd *c) {
   c->poison_msg.clear();
   c->recording = true;
   c->kernels = 0;
+  c->persistent = false;
   return SX_OK;
 }
 
@@ -745,6 +834,10 @@ SX_API sx_status sx_cmd_end(sx_cmd *c) {
   }
   sx_engine *e = c->e;
   SX_TRY_CUDA(cudaSetDevice(e->device), "cudaSetDevice");
+  if (c->persistent) {
+    sx_status pst = build_persistent(c);
+    if (pst != SX_OK) return pst;
+  }
   // device-side tables are created before capture (no allocation inside a capture)
   for (const Op &op : c->ops) {
     sx_status fst = SX_OK;

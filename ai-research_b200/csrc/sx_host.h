@@ -36,6 +36,7 @@ struct sx_engine {
   uint32_t *best_i = nullptr;
   uint32_t *done_cnt = nullptr;
   void *argmax_part = nullptr;
+  uint32_t *persist_bar = nullptr;  // grid-barrier arrival word of the persistent kernel
   int num_sms = 148;
   std::mutex freq_mu;
   std::map<std::pair<uint32_t, uint32_t>, float *> inv_freq;  // (rot, theta bits)
@@ -65,6 +66,7 @@ enum OpKind {
   OP_D2H,
   OP_GEMV_FUSED,  // multi-segment GEMV with fused prologue / epilogue (model graph)
   OP_ATTN_FUSED,  // qkv_rope + decode attention + combine (model graph)
+  OP_PERSIST,     // the GEMV_FUSED / ATTN_FUSED run of a persistent command buffer
 };
 
 struct Op {
@@ -95,11 +97,16 @@ struct sx_cmd {
   cudaGraph_t graph = nullptr;
   cudaGraphExec_t exec = nullptr;
   uint32_t kernels = 0;
+  // persistent: the fused kernels run as phases of one cooperative launch (sx_persist.cu)
+  bool persistent = false;
+  sx::Phase *d_phases = nullptr;
 };
 
 
 // Append an op (including the internal host<->device copy ops) to a recording command buffer.
 void sx_host_push_op(sx_cmd *c, const Op &op);
+// record the command buffer's fused kernels as one persistent launch (sx_persist.cu)
+inline void sx_host_set_persistent(sx_cmd *c, bool on) { c->persistent = on; }
 void sx_host_set_error(const char *msg);
 // Shape / shared-memory validation of a GEMV launch (sets the error message).
 sx_status sx_host_check_gemv(int qt, bool geglu, bool pro, uint32_t m, uint32_t k,

@@ -121,6 +121,32 @@ struct AttnFusedArgs {
 };
 cudaError_t launch_attn_fused(const AttnFusedArgs &a, cudaStream_t s, bool pdl);
 
+// ---------------------------------------------------------------------------------------
+// Persistent decode kernel (sx_persist.cu): one cooperative launch runs a table of phases on
+// one CTA per SM with grid barriers between consecutive phases.
+enum PhaseKind : uint32_t { kPhaseGemv = 0, kPhaseAttn = 1 };
+struct Phase {
+  uint32_t kind;
+  uint32_t variant;         // kernel instantiation (persist_gemv_variant / persist_attn_variant)
+  uint32_t prefetch_after;  // GEMV: first chunks issued after this phase (kNoPhase: at start)
+  uint32_t smem_off;        // GEMV: end of its shared-memory layout; attention: start of
+                            // the two work items' shared memory
+  GemvArgs g;
+  AttnFusedArgs at;
+};
+constexpr uint32_t kNoPhase = 0xFFFFFFFFu;
+// Shared memory of the persistent kernel and where its two attention work items start.
+uint32_t persist_smem_bytes();
+uint32_t persist_attn_offset(const AttnFusedArgs &a);
+// false when the call has no instantiation in the persistent kernel (batch > 4, no ring fits)
+bool persist_gemv_variant(int qt, bool geglu, const GemvArgs &a, uint32_t smem_limit,
+                          uint32_t *variant, uint32_t *smem_end);
+bool persist_attn_variant(const AttnFusedArgs &a, uint32_t *variant);
+cudaError_t prepare_persist_kernel();
+// bar: two words (arrival count, abort), cleared by the caller before every launch
+cudaError_t launch_persist(const Phase *phases, uint32_t n, uint32_t *bar, uint32_t *err,
+                           int num_sms, cudaStream_t s);
+
 cudaError_t launch_argmax(const float *logits, uint32_t n, uint32_t *out, void *scratch,
                           size_t scratch_bytes, cudaStream_t s);
 size_t argmax_scratch_bytes();

@@ -290,11 +290,13 @@ sx::GemvArgs gemv1(const sx_buffer *w, const sx_buffer *x, sx_buffer *y, uint32_
   return a;
 }
 
-sx_status record_forward_fused(sx_model *m, sx_cmd *cmd, bool logits, bool io) {
+sx_status record_forward_fused(sx_model *m, sx_cmd *cmd, bool logits, bool io,
+                               bool persistent) {
   const sx_model_config &c = m->c;
   const uint32_t H = c.hidden_size, I = c.intermediate_size, L = c.num_layers;
   const float eps = c.rms_norm_eps;
   M_TRY(sx_cmd_begin(cmd));
+  sx_host_set_persistent(cmd, persistent);
   if (io) {
     Op a{OP_H2D};
     a.host = m->h_x; a.dev = m->x->d; a.bytes = 4ull * H;
@@ -422,8 +424,8 @@ sx_status record_forward_fused(sx_model *m, sx_cmd *cmd, bool logits, bool io) {
 }
 
 sx_status record_graph(sx_model *m, sx_cmd *cmd, bool logits, bool io) {
-  return m->c.reference_graph ? record_forward(m, cmd, logits, io)
-                              : record_forward_fused(m, cmd, logits, io);
+  if (m->c.reference_graph == 1) return record_forward(m, cmd, logits, io);
+  return record_forward_fused(m, cmd, logits, io, m->c.reference_graph == 2);
 }
 
 sx_status synth_matrix(sx_model *m, sx_buffer *dst, uint32_t rows, uint32_t cols,
@@ -463,7 +465,7 @@ SX_API sx_status sx_model_create(sx_engine *e, const sx_model_config *cfg, sx_mo
   bool ok = c.vocab_size > 0 && c.hidden_size % 32 == 0 && c.intermediate_size % 32 == 0 &&
             c.num_layers > 0 && c.num_q_heads > 0 && c.num_kv_heads > 0 &&
             c.num_q_heads % c.num_kv_heads == 0 && c.window_size > 0 && c.head_dim > 0 &&
-            (c.num_q_heads * c.head_dim) % 32 == 0;
+            (c.num_q_heads * c.head_dim) % 32 == 0 && c.reference_graph <= 2;
   if (c.full_every)
     ok = ok && c.num_global_kv_heads > 0 && c.num_q_heads % c.num_global_kv_heads == 0 &&
          c.global_head_dim > 0;

@@ -1,5 +1,6 @@
 // sx_ops.cu -- RMSNorm / add+RMSNorm, QKV norm + partial RoPE + cache write, GQA decode
 // attention over the ring's active-slot list, and the vocabulary argmax (sm_100a).
+#include "sx_attn_dev.cuh"
 #include "sx_common.cuh"
 #include "sx_internal.h"
 
@@ -141,7 +142,6 @@ __global__ void __launch_bounds__(128) qkv_rope_kernel(QkvRopeArgs a) {
 // over the host-built active-slot list.  Split over slots (flash-decoding): CTA (kv head,
 // chunk) runs an online softmax for the whole GQA group of q heads over 32 slots and writes
 // an unnormalised partial (m, l, o[D]) to scratch; a combine kernel merges the chunks.
-constexpr int kAttnChunk = 32;
 constexpr int kAttnWarps = 4;
 
 // Lane `lane` owns elements [lane*DPL, lane*DPL + DPL) of a head row; the load width matches
@@ -299,284 +299,49 @@ __global__ void attn_combine_kernel(AttnArgs a, uint32_t nchunks) {
 }
 
 // ---------------------------------------------------------------------------
-// Fused decode attention for the model graph: qkv_rope + decode_attn (+ the combine) in one
-// launch.  CTA (kv head h, 32-slot chunk), 8 warps of 4 slots each:
-//   1. before waiting on the QKV projection (programmatic dependent launch), every warp reads
-//      its 4 slot indices and fetches their K/V rows into registers.  The step word, the slot
-//      list and every cache row but the current slot's were written before the graph's first
-//      kernel (host copies, earlier tokens), so this overlaps the fetch with the GEMV's tail;
-//   2. one warp per vector normalises and rotates the GQA group's q heads and the new k, v of
-//      head h (qkv_rope.wgsl semantics, identical rounding to the cache); chunk 0 stores the
-//      new K/V at the current slot, whose row every CTA takes from shared memory;
-//   3. each warp folds its 4 slots into an online softmax in one step, the CTA merges its
-//      warps, and the last CTA of the head merges the chunk partials in chunk order.
-constexpr int kFusedWarps = 8;
-constexpr int kFusedPerWarp = 4;
-static_assert(kFusedWarps * kFusedPerWarp == kAttnChunk, "fused chunk must match the scratch");
-
-// One cache row slice of a lane in its storage format (bf16 pairs or f32 words).
-template <int DPL, bool BF16>
-struct RawRow {
-  static constexpr int kWords = BF16 ? DPL / 2 : DPL;
-  uint32_t w[kWords];
-};
-
-template <int DPL, bool BF16>
-SX_DEV void load_raw(const void *cache, size_t off, int lane, RawRow<DPL, BF16> &r) {
-  constexpr int kBytes = RawRow<DPL, BF16>::kWords * 4;
-  const char *p = reinterpret_cast<const char *>(cache) + (off + (size_t)lane * DPL) * (BF16 ? 2 : 4);
-  if constexpr (kBytes % 16 == 0) {
-#pragma unroll
-    for (int i = 0; i < kBytes / 16; ++i) {
-      uint4 u = __ldcg(reinterpret_cast<const uint4 *>(p) + i);
-      r.w[4 * i] = u.x; r.w[4 * i + 1] = u.y; r.w[4 * i + 2] = u.z; r.w[4 * i + 3] = u.w;
-    }
-  } else if constexpr (kBytes == 8) {
-    uint2 u = __ldcg(reinterpret_cast<const uint2 *>(p));
-    r.w[0] = u.x; r.w[1] = u.y;
-  } else {
-    static_assert(kBytes == 4, "head_dim must be 64, 128, 256 or 512");
-    r.w[0] = __ldcg(reinterpret_cast<const uint32_t *>(p));
-  }
-}
-
-template <int DPL, bool BF16>
-SX_DEV float raw_at(const RawRow<DPL, BF16> &r, int i) {
-  if (BF16) return u2f((i & 1) ? (r.w[i >> 1] & 0xFFFF0000u) : (r.w[i >> 1] << 16));
-  return u2f(r.w[i]);
-}
-
+// Fused decode attention as a kernel of its own: CTA (kv head, chunk) runs one work item
+// (sx_attn_dev.cuh); the dependency wait is griddepcontrol.wait.
 template <int DPL, int G, bool BF16>
 __global__ void __launch_bounds__(kFusedWarps * 32) attn_fused_kernel(AttnFusedArgs a) {
   extern __shared__ float sh[];
-  constexpr int W = kFusedWarps, P = kFusedPerWarp;
-  constexpr uint32_t D = 32 * DPL;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const uint32_t kvh = blockIdx.x, chunk = blockIdx.y, nchunks = gridDim.y;
-  float *qs = sh;                  // [G][D] normalised, rotated q
-  float *kn = qs + G * D;          // [D] new K (cache precision)
-  float *vn = kn + D;              // [D] new V (cache precision)
-  float *wm = vn + D;              // [W][G]
-  float *wl = wm + W * G;          // [W][G]
-  float *wo = wl + W * G;          // [W][G][D]
-  float *cf = wo + W * G * D;      // [G][nchunks] combine weights, then [G] sums
   __shared__ uint32_t last_flag;
-
   pdl_launch_dependents();
-  const uint32_t clock = a.step[0], slot = a.step[1];
-  uint32_t S = a.step[2];
-  const bool bad_step = S > a.total_slots || slot >= a.total_slots;
-  S = S > a.total_slots ? a.total_slots : S;
-  const bool slot_ok = slot < a.total_slots;
+  attn_item<DPL, G, BF16>(a, blockIdx.x, blockIdx.y, gridDim.y, sh, &last_flag,
+                          (int)threadIdx.x, 0, true, [] { pdl_wait(); });
+}
 
-  // 1. slot indices and their cache rows (all but the current slot's)
-  const uint32_t s0 = chunk * kAttnChunk, s1 = min(S, s0 + kAttnChunk);
-  uint32_t sl[P];
-  RawRow<DPL, BF16> kr[P], vr[P];
-#pragma unroll
-  for (int j = 0; j < P; ++j) {
-    const uint32_t si = s0 + warp + j * W;
-    sl[j] = si < s1 ? __ldcg(a.slots + si) : 0xFFFFFFFFu;
-  }
-#pragma unroll
-  for (int j = 0; j < P; ++j) {
-    if (sl[j] < a.total_slots && sl[j] != slot) {
-      const size_t off = (size_t)sl[j] * a.kv_dim + (size_t)kvh * D;
-      load_raw<DPL, BF16>(a.k_cache, off, lane, kr[j]);
-      load_raw<DPL, BF16>(a.v_cache, off, lane, vr[j]);
-    } else {
-#pragma unroll
-      for (int i = 0; i < RawRow<DPL, BF16>::kWords; ++i) kr[j].w[i] = vr[j].w[i] = 0u;
-    }
-  }
-
-  pdl_wait();
-  if (bad_step && threadIdx.x == 0 && chunk == 0 && kvh == 0) raise_error(a.err, kDevBadParams);
-
-  // 2. per-warp norm + rope of the G q heads, k and v
-  const uint32_t half = a.rotary_dim / 2;
-  const float fclock = (float)clock;
-  for (int vi = warp; vi < G + 2; vi += W) {
-    const float *src = vi < G ? a.q + (size_t)(kvh * G + vi) * D
-                              : (vi == G || a.k_eq_v ? a.k : a.v) + (size_t)kvh * D;
-    const float *gain = vi < G ? a.q_norm_w : (vi == G ? a.k_norm_w : nullptr);
-    float *buf = vi < G ? qs + vi * D : (vi == G ? kn : vn);
-    float x[DPL];
-    float ss = 0.0f;
-#pragma unroll
-    for (int i = 0; i < DPL; ++i) {
-      x[i] = __ldcg(src + lane * DPL + i);
-      ss = fmaf(x[i], x[i], ss);
-    }
-    ss = warp_sum(ss);
-    const float rs = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)D), a.eps)));
-#pragma unroll
-    for (int i = 0; i < DPL; ++i) {
-      const uint32_t d = lane * DPL + i;
-      buf[d] = gain ? __fmul_rn(__fmul_rn(x[i], rs), gain[d]) : __fmul_rn(x[i], rs);
-    }
-    __syncwarp();
-    if (vi <= G) {
-      for (uint32_t i = lane; i < half; i += 32) {
-        float ang = __fmul_rn(fclock, a.inv_freq[i]);
-        float sn, cs;
-        sincosf(ang, &sn, &cs);
-        float v0 = buf[i], v1 = buf[i + half];
-        buf[i] = __fsub_rn(__fmul_rn(v0, cs), __fmul_rn(v1, sn));
-        buf[i + half] = __fadd_rn(__fmul_rn(v0, sn), __fmul_rn(v1, cs));
-      }
-      __syncwarp();
-    }
-    if (vi >= G) {
-      void *cache = vi == G ? a.k_cache : a.v_cache;
-      const size_t new_off = ((size_t)slot * a.num_kv + kvh) * D;
-      for (uint32_t d = lane; d < D; d += 32) {
-        if (BF16) {
-          const uint16_t b = bf16_bits_rne(buf[d]);
-          buf[d] = bf16_bits_to_f32(b);
-          if (chunk == 0 && slot_ok) reinterpret_cast<uint16_t *>(cache)[new_off + d] = b;
-        } else if (chunk == 0 && slot_ok) {
-          reinterpret_cast<float *>(cache)[new_off + d] = buf[d];
-        }
-      }
-    }
-  }
-  __syncthreads();
-
-  // 3. online softmax over this warp's slots, all four folded in one step
-  float m[G], l[G], o[G][DPL];
-#pragma unroll
-  for (int h = 0; h < G; ++h) {
-    m[h] = -INFINITY;
-    l[h] = 0.0f;
-#pragma unroll
-    for (int i = 0; i < DPL; ++i) o[h][i] = 0.0f;
-  }
-  bool live[P];
-  float sc[P][G];
-#pragma unroll
-  for (int j = 0; j < P; ++j) {
-    live[j] = sl[j] < a.total_slots;
-    if (!live[j] && sl[j] != 0xFFFFFFFFu && lane == 0) raise_error(a.err, kDevBadSlot);
-    const bool cur = sl[j] == slot;
-#pragma unroll
-    for (int h = 0; h < G; ++h) sc[j][h] = 0.0f;
-#pragma unroll
-    for (int i = 0; i < DPL; ++i) {
-      const float kv = cur ? kn[lane * DPL + i] : raw_at<DPL, BF16>(kr[j], i);
-#pragma unroll
-      for (int h = 0; h < G; ++h) sc[j][h] = fmaf(qs[h * D + lane * DPL + i], kv, sc[j][h]);
-    }
-  }
-#pragma unroll
-  for (int off = 16; off > 0; off >>= 1)
-#pragma unroll
-    for (int j = 0; j < P; ++j)
-#pragma unroll
-      for (int h = 0; h < G; ++h) sc[j][h] += __shfl_xor_sync(0xffffffffu, sc[j][h], off);
-#pragma unroll
-  for (int h = 0; h < G; ++h) {
-    float mn = m[h];
-#pragma unroll
-    for (int j = 0; j < P; ++j) {
-      sc[j][h] = live[j] ? sc[j][h] * a.scale : -INFINITY;
-      mn = fmaxf(mn, sc[j][h]);
-    }
-    if (mn == -INFINITY) continue;
-    const float corr = expf(m[h] - mn);
-    float p[P];
-    float ps = 0.0f;
-#pragma unroll
-    for (int j = 0; j < P; ++j) {
-      p[j] = live[j] ? expf(sc[j][h] - mn) : 0.0f;
-      ps += p[j];
-    }
-    l[h] = fmaf(l[h], corr, ps);
-#pragma unroll
-    for (int i = 0; i < DPL; ++i) {
-      float acc = o[h][i] * corr;
-#pragma unroll
-      for (int j = 0; j < P; ++j) {
-        const float vv = sl[j] == slot ? vn[lane * DPL + i] : raw_at<DPL, BF16>(vr[j], i);
-        acc = fmaf(p[j], vv, acc);
-      }
-      o[h][i] = acc;
-    }
-    m[h] = mn;
-  }
-#pragma unroll
-  for (int h = 0; h < G; ++h) {
-    if (lane == 0) {
-      wm[warp * G + h] = m[h];
-      wl[warp * G + h] = l[h];
-    }
-#pragma unroll
-    for (int i = 0; i < DPL; ++i) wo[(warp * G + h) * D + lane * DPL + i] = o[h][i];
-  }
-  __syncthreads();
-  for (uint32_t idx = threadIdx.x; idx < G * D; idx += blockDim.x) {
-    const uint32_t h = idx / D, d = idx % D;
-    float M = -INFINITY;
-#pragma unroll
-    for (int w = 0; w < W; ++w) M = fmaxf(M, wm[w * G + h]);
-    float Lsum = 0.0f, O = 0.0f;
-#pragma unroll
-    for (int w = 0; w < W; ++w) {
-      const float f = M == -INFINITY ? 0.0f : expf(wm[w * G + h] - M);
-      Lsum = fmaf(wl[w * G + h], f, Lsum);
-      O = fmaf(wo[(w * G + h) * D + d], f, O);
-    }
-    float *rec = a.part + ((size_t)(kvh * G + h) * nchunks + chunk) * (D + 2);
-    rec[2 + d] = O;
-    if (d == 0) {
-      rec[0] = M;
-      rec[1] = Lsum;
-    }
-  }
-
-  // last CTA of this kv head merges the chunks
-  __threadfence();
-  __syncthreads();
-  if (threadIdx.x == 0) last_flag = (atomicAdd(&a.cnt[kvh], 1u) + 1 == nchunks) ? 1u : 0u;
-  __syncthreads();
-  if (!last_flag) return;
-  __threadfence();
-  float *csum = cf + G * nchunks;
-  for (int h = warp; h < G; h += W) {
-    const float *base = a.part + (size_t)(kvh * G + h) * nchunks * (D + 2);
-    float M = -INFINITY;
-    for (uint32_t c = lane; c < nchunks; c += 32) M = fmaxf(M, __ldcg(base + (size_t)c * (D + 2)));
-    M = warp_max(M);
-    float L = 0.0f;
-    for (uint32_t c = lane; c < nchunks; c += 32) {
-      const float *rec = base + (size_t)c * (D + 2);
-      const float f = M == -INFINITY ? 0.0f : expf(__ldcg(rec) - M);
-      cf[h * nchunks + c] = f;
-      L = fmaf(__ldcg(rec + 1), f, L);
-    }
-    L = warp_sum(L);
-    if (lane == 0) csum[h] = L;
-  }
-  __syncthreads();
-  for (uint32_t idx = threadIdx.x; idx < G * D; idx += blockDim.x) {
-    const uint32_t h = idx / D, d = idx % D;
-    const float *base = a.part + (size_t)(kvh * G + h) * nchunks * (D + 2) + 2 + d;
-    const float *f = cf + h * nchunks;
-    float O = 0.0f;
-#pragma unroll 8
-    for (uint32_t c = 0; c < nchunks; ++c) O = fmaf(__ldcg(base + (size_t)c * (D + 2)), f[c], O);
-    const float L = csum[h];
-    a.out[(size_t)(kvh * G + h) * D + d] = L > 0.0f ? O / L : 0.0f;
-  }
-  if (threadIdx.x == 0) a.cnt[kvh] = 0;
+// Cluster form (rings of up to 16 x 64 slots): one cluster of CL CTAs per kv head.
+template <int DPL, int G, bool BF16>
+__global__ void __launch_bounds__(kFusedWarps * 32) attn_cluster_kernel(AttnFusedArgs a) {
+  extern __shared__ float sh[];
+  pdl_launch_dependents();
+  attn_cluster_item<DPL, G, BF16>(a, blockIdx.x, sh, [] { pdl_wait(); });
 }
 
 template <int DPL, int G>
 cudaError_t launch_attn_fused_t(const AttnFusedArgs &a, cudaStream_t s, bool pdl) {
+  const uint32_t ncl = (a.total_slots + kClusterSlots - 1) / kClusterSlots;
+  if (ncl <= (uint32_t)kClusterMax) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(a.num_kv, ncl);
+    cfg.blockDim = dim3(kFusedWarps * 32);
+    cfg.dynamicSmemBytes = sizeof(float) * attn_cluster_floats(G, 32 * DPL, ncl);
+    cfg.stream = s;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 1;
+    attr[0].val.clusterDim.y = ncl;
+    attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 2 : 1;
+    if (a.kv_bf16) return cudaLaunchKernelEx(&cfg, attn_cluster_kernel<DPL, G, true>, a);
+    return cudaLaunchKernelEx(&cfg, attn_cluster_kernel<DPL, G, false>, a);
+  }
   uint32_t nchunks = (a.total_slots + kAttnChunk - 1) / kAttnChunk;
   size_t D = 32 * DPL;
-  size_t smem = sizeof(float) * (G * D + 2 * D + 2 * kFusedWarps * G + kFusedWarps * G * D +
-                                 (size_t)G * nchunks + G);
+  size_t smem = sizeof(float) * attn_item_floats(G, D, nchunks);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(a.num_kv, nchunks);
   cfg.blockDim = dim3(kFusedWarps * 32);
@@ -604,6 +369,11 @@ cudaError_t launch_attn_fused_d(const AttnFusedArgs &a, cudaStream_t s, bool pdl
 
 template <int DPL, int G>
 cudaError_t prepare_attn_fused_t() {
+  for (auto k : {attn_cluster_kernel<DPL, G, true>, attn_cluster_kernel<DPL, G, false>}) {
+    cudaError_t e = allow_max_dynamic_smem(k);
+    if (e == cudaSuccess) e = cudaFuncSetAttribute(k, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+    if (e != cudaSuccess) return e;
+  }
   cudaError_t a = allow_max_dynamic_smem(attn_fused_kernel<DPL, G, true>);
   cudaError_t b = allow_max_dynamic_smem(attn_fused_kernel<DPL, G, false>);
   return a != cudaSuccess ? a : b;

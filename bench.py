@@ -48,6 +48,9 @@ def parse():
     ap.add_argument("--impl", default="sx", choices=["sx", "reference"])
     ap.add_argument("--layers", type=int, default=48)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--graph", choices=["persistent", "fused"], default="fused",
+                    help="persistent: one cooperative launch per token; fused: 5 kernels per "
+                         "layer chained with programmatic dependent launch")
     ap.add_argument("--case", choices=["geglu", "q4_head", "attn"],
                     help="profiling case: launch one kernel of the step standalone "
                          "(--launches times) on synthetic data and exit; prints no JSON line")
@@ -295,6 +298,7 @@ def main():
     import sx
 
     cfgd = model_cfg_dict(args.layers)
+    cfgd["reference_graph"] = 2 if args.graph == "persistent" else 0
     eng = sx.Engine(local)
     stream = torch.cuda.ExternalStream(eng.stream)
     model = sx.Model(eng, sx.model_config(**cfgd))
@@ -438,6 +442,8 @@ def main():
                         "16q/8kv x 256, I 15360, vocab 262144 (Q8_0 head), 640 live ring slots",
             "global_batch": world, "seq_len": total_slots,
             "parallelism": "replicas" if world > 1 else "single",
+            "graph": ("one persistent cooperative launch per token" if args.graph == "persistent"
+                      else "5 kernels per layer + LM head, programmatic dependent launch"),
             "l2": "inputs larger than L2 (8.1 GB of weights+KV read per step)",
             "algorithmic_bytes_per_token": alg["total"],
             "hbm_gbs_per_token_rate": alg["total"] * value / world / 1e9,

@@ -252,8 +252,10 @@ typedef struct {
   uint32_t full_every;       /* layer l is full attention when (l+1) % full_every == 0  */
   uint32_t attention_k_eq_v; /* types.zig:58                                            */
   float rms_norm_eps, rope_theta, rope_theta_full, attn_scale;
-  uint32_t reference_graph;  /* 1: record the reference's op-by-op graph through the record
-                                API (14 launches per layer); 0: the fused graph (5 per layer) */
+  uint32_t reference_graph;  /* graph of one token: 1 = the reference's op-by-op graph through
+                                the record API (14 launches per layer); 0 = the fused graph (5
+                                launches per layer); 2 = the fused graph's kernels as phases of
+                                one persistent cooperative launch per token */
 } sx_model_config;
 
 typedef struct sx_model sx_model;

@@ -69,7 +69,10 @@ def run_decode(engine, cfg, seed, steps, start_clock, n_recall=0):
     return results
 
 
-@pytest.mark.parametrize("reference_graph", [0, 1])
+GRAPHS = [0, 1, 2]  # fused kernels, the reference's op-by-op graph, one persistent launch
+
+
+@pytest.mark.parametrize("reference_graph", GRAPHS)
 @pytest.mark.parametrize("kv_f32", [False, True])
 def test_greedy_decode_matches_checker(engine, engine_f32kv, kv_f32, reference_graph):
     eng = engine_f32kv if kv_f32 else engine
@@ -81,7 +84,7 @@ def test_greedy_decode_matches_checker(engine, engine_f32kv, kv_f32, reference_g
             assert margin_top2(rlg) < 1e-3, f"step {i}: token {tok} vs {rtok}"
 
 
-@pytest.mark.parametrize("reference_graph", [0, 1])
+@pytest.mark.parametrize("reference_graph", GRAPHS)
 def test_greedy_decode_with_recall_and_large_clock(engine, reference_graph):
     cfg = tiny_cfg(reference_graph=reference_graph)
     res = run_decode(engine, cfg, seed=9, steps=6, start_clock=90000, n_recall=3)
@@ -91,12 +94,24 @@ def test_greedy_decode_with_recall_and_large_clock(engine, reference_graph):
             assert margin_top2(rlg) < 1e-3
 
 
-def test_12b_width_two_layers_full_vocab(engine):
+def test_long_ring_uses_global_merge(engine):
+    # 1108 live slots: more than 16 clusters of 64 slots, so the fused graph's attention
+    # takes the global-merge form (one record per 32-slot chunk, last CTA merges)
+    cfg = tiny_cfg(num_anchors=4, window_size=1100, num_recall=4, num_layers=2)
+    res = run_decode(engine, cfg, seed=13, steps=3, start_clock=3000, n_recall=2)
+    for i, (tok, rtok, lg, rlg) in enumerate(res):
+        assert_close(lg, rlg, what=f"logits step {i}")
+        if tok != rtok:
+            assert margin_top2(rlg) < 1e-3
+
+
+@pytest.mark.parametrize("reference_graph", [0, 2])
+def test_12b_width_two_layers_full_vocab(engine, reference_graph):
     # 12B layer shapes and full vocabulary with two layers (one sliding, one full attention)
     cfg = tiny_cfg(vocab_size=262144, hidden_size=3840, intermediate_size=15360, num_layers=2,
                    num_q_heads=16, num_kv_heads=8, num_global_kv_heads=8, head_dim=256,
                    global_head_dim=256, num_anchors=32, window_size=512, num_recall=96,
-                   full_every=2)
+                   full_every=2, reference_graph=reference_graph)
     res = run_decode(engine, cfg, seed=5, steps=2, start_clock=5000, n_recall=96)
     for i, (tok, rtok, lg, rlg) in enumerate(res):
         assert_close(lg, rlg, what=f"logits step {i}")
@@ -104,7 +119,7 @@ def test_12b_width_two_layers_full_vocab(engine):
             assert margin_top2(rlg) < 1e-3
 
 
-@pytest.mark.parametrize("reference_graph", [0, 1])
+@pytest.mark.parametrize("reference_graph", GRAPHS)
 def test_prefill_graph_skips_logits(engine, reference_graph):
     cfg = tiny_cfg(reference_graph=reference_graph)
     model = sx.Model(engine, sx.model_config(**cfg))
@@ -114,9 +129,12 @@ def test_prefill_graph_skips_logits(engine, reference_graph):
     slot = ring.activate_slot(0, 0)
     tok = model.forward_token(x, 0, slot, ring.get_active_slots(0, 0), want_logits=False)
     assert tok == 0
-    assert model.kernels_per_token(False) < model.kernels_per_token(True)
-    per_layer = 14 if reference_graph else 5
-    assert model.kernels_per_token(False) == per_layer * cfg["num_layers"]
+    if reference_graph == 2:  # every phase, LM head included, is one launch
+        assert model.kernels_per_token(False) == model.kernels_per_token(True) == 1
+    else:
+        assert model.kernels_per_token(False) < model.kernels_per_token(True)
+        per_layer = 14 if reference_graph else 5
+        assert model.kernels_per_token(False) == per_layer * cfg["num_layers"]
 
 
 def test_forward_token_rejects_oversized_slot_list(engine):
