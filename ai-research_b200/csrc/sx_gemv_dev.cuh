@@ -343,7 +343,6 @@ SX_DEV void gemv_body(const GemvArgs &a, uint8_t *smem, bool prefetch, bool run,
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, c = lane & 3;
   const uint32_t P = pairs_of(a.k), nv = nv_of(a.batch), batch = a.batch;
   const uint32_t T = a.tiles[0] + a.tiles[1] + a.tiles[2];
-  const uint32_t NW = gridDim.x * kWarps, wid = blockIdx.x * kWarps + warp;
   // CTA b owns whole tiles [ct0, ct1) (counts balanced to within one); its warps split the
   // run's chunks evenly, warp w taking [cbase + ncta w / 16, cbase + ncta (w + 1) / 16)
   const uint32_t ct0 = (uint32_t)((uint64_t)T * blockIdx.x / gridDim.x);
@@ -643,51 +642,67 @@ SX_DEV void gemv_body(const GemvArgs &a, uint8_t *smem, bool prefetch, bool run,
 
   if (a.epi == kEpiArgmax) {
     // Per batch row j: lane (g, c) tracked rows of batch row 4s + c in best[s].  Reduce over
-    // the warp, publish per worker, and let the last worker to arrive merge all workers.
+    // the warp, then over the CTA's warps in shared memory (the rings are free now), publish
+    // one candidate per CTA and let the last CTA to arrive merge the CTAs' candidates.
+    // better() is a total order (value, then lower index), so the merge order is immaterial.
+    float *cv = reinterpret_cast<float *>(smem + L.ring);  // [warp][8]
+    uint32_t *ci = reinterpret_cast<uint32_t *>(cv + kWarps * 8);
+    auto merge = [](Best &b, float v, uint32_t ix) {
+      if (ix != 0xFFFFFFFFu && (b.i == 0xFFFFFFFFu || better(v, ix, b.v, b.i))) b = {v, ix};
+    };
+    auto warp_merge = [&](Best &b) {
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, b.v, o);
+        const uint32_t oi = __shfl_xor_sync(0xffffffffu, b.i, o);
+        merge(b, ov, oi);
+      }
+    };
+    __syncthreads();  // every warp is done with the split-tile records in the rings
     for (uint32_t j = 0; j < batch; ++j) {
       Best b = {-INFINITY, 0xFFFFFFFFu};
 #pragma unroll
       for (int s = 0; s < NSETS; ++s)
         if ((uint32_t)(4 * s + c) == j) b = best[s];
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) {
-        float ov = __shfl_xor_sync(0xffffffffu, b.v, o);
-        uint32_t oi = __shfl_xor_sync(0xffffffffu, b.i, o);
-        if (oi != 0xFFFFFFFFu && (b.i == 0xFFFFFFFFu || better(ov, oi, b.v, b.i))) b = {ov, oi};
-      }
+      warp_merge(b);
       if (lane == 0) {
-        a.best_v[(size_t)wid * 8 + j] = b.v;
-        a.best_i[(size_t)wid * 8 + j] = b.i;
+        cv[warp * 8 + j] = b.v;
+        ci[warp * 8 + j] = b.i;
       }
     }
-    __threadfence();
-    __syncwarp();
-    uint32_t old = 0;
-    if (lane == 0) old = atomicAdd(a.done_cnt, 1u);
-    old = __shfl_sync(0xffffffffu, old, 0);
-    if (old + 1 == NW) {
-      __threadfence();
+    __syncthreads();
+    if (warp == 0) {
       for (uint32_t j = 0; j < batch; ++j) {
-        Best r = {-INFINITY, 0xFFFFFFFFu};
-        for (uint32_t w = lane; w < NW; w += 32) {
-          float v = __ldcg(a.best_v + (size_t)w * 8 + j);
-          uint32_t ix = __ldcg(a.best_i + (size_t)w * 8 + j);
-          if (ix != 0xFFFFFFFFu && (r.i == 0xFFFFFFFFu || better(v, ix, r.v, r.i))) r = {v, ix};
-        }
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
-          float ov = __shfl_xor_sync(0xffffffffu, r.v, o);
-          uint32_t oi = __shfl_xor_sync(0xffffffffu, r.i, o);
-          if (oi != 0xFFFFFFFFu && (r.i == 0xFFFFFFFFu || better(ov, oi, r.v, r.i))) r = {ov, oi};
-        }
+        Best b = {-INFINITY, 0xFFFFFFFFu};
+        if (lane < kWarps) b = {cv[lane * 8 + j], ci[lane * 8 + j]};
+        warp_merge(b);
         if (lane == 0) {
-          uint32_t tok = r.i == 0xFFFFFFFFu ? 0u : r.i;
-          // the CPU rule starts from logits[0]: a NaN there is never beaten
-          if (isnan(__ldcg(a.y[0] + (size_t)j * a.ldy))) tok = 0;
-          a.token[j] = tok;
+          a.best_v[(size_t)blockIdx.x * 8 + j] = b.v;
+          a.best_i[(size_t)blockIdx.x * 8 + j] = b.i;
         }
       }
-      if (lane == 0) *a.done_cnt = 0;
+      __threadfence();
+      __syncwarp();
+      uint32_t old = 0;
+      if (lane == 0) old = atomicAdd(a.done_cnt, 1u);
+      old = __shfl_sync(0xffffffffu, old, 0);
+      if (old + 1 == gridDim.x) {
+        __threadfence();
+        for (uint32_t j = 0; j < batch; ++j) {
+          Best r = {-INFINITY, 0xFFFFFFFFu};
+#pragma unroll 8
+          for (uint32_t w = lane; w < gridDim.x; w += 32)
+            merge(r, __ldcg(a.best_v + (size_t)w * 8 + j), __ldcg(a.best_i + (size_t)w * 8 + j));
+          warp_merge(r);
+          if (lane == 0) {
+            uint32_t tok = r.i == 0xFFFFFFFFu ? 0u : r.i;
+            // the CPU rule starts from logits[0]: a NaN there is never beaten
+            if (isnan(__ldcg(a.y[0] + (size_t)j * a.ldy))) tok = 0;
+            a.token[j] = tok;
+          }
+        }
+        if (lane == 0) *a.done_cnt = 0;
+      }
     }
   }
 }
