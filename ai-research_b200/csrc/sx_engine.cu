@@ -61,7 +61,14 @@ sx_status cuda_status(cudaError_t e, const char *what) {
 
 }  // namespace
 
-void sx_host_set_error(const char *msg) { g_last_error = msg; }
+void sx_host_set_error(const char *fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+}
 
 void sx_host_bind_scratch(sx_engine *e, sx::GemvArgs &a) {
   a.part = e->gemv_part;
@@ -269,6 +276,15 @@ sx_status run_op(sx_engine *e, cudaStream_t s, const Op &op, uint32_t *kernels) 
       if (!a.inv_freq) return fst;
       return cuda_status(sx::launch_attn_fused(a, s, true), "fused attention launch");
     }
+    case OP_ALLREDUCE:
+      return sx_host_allreduce(op.comm, static_cast<float *>(op.dev), op.u[0], s);
+    case OP_ALLGATHER:
+      return sx_host_allgather(op.comm, static_cast<const uint32_t *>(op.bind.at(0)),
+                               static_cast<uint32_t *>(op.bind.at(1)), op.u[0], s);
+    case OP_TP_ARGMAX:
+      *kernels += 1;
+      return sx_host_tp_argmax(static_cast<const uint32_t *>(op.bind.at(0)), op.u[0],
+                               static_cast<uint32_t *>(op.bind.at(1)), s);
     case OP_PERSIST: {
       *kernels += 1;
       SX_TRY_CUDA(cudaMemsetAsync(e->persist_bar, 0, 8, s), "barrier reset");

@@ -697,8 +697,15 @@ SX_DEV void gemv_body(const GemvArgs &a, uint8_t *smem, bool prefetch, bool run,
           if (lane == 0) {
             uint32_t tok = r.i == 0xFFFFFFFFu ? 0u : r.i;
             // the CPU rule starts from logits[0]: a NaN there is never beaten
-            if (isnan(__ldcg(a.y[0] + (size_t)j * a.ldy))) tok = 0;
+            const bool nan0 = a.row_base[0] == 0 && isnan(__ldcg(a.y[0] + (size_t)j * a.ldy));
+            if (nan0) tok = 0;
             a.token[j] = tok;
+            if (a.cand) {
+              a.cand[j * 4 + 0] = __float_as_uint(r.v);
+              a.cand[j * 4 + 1] = r.i;
+              a.cand[j * 4 + 2] = nan0 ? 1u : 0u;
+              a.cand[j * 4 + 3] = 0u;
+            }
           }
         }
         if (lane == 0) *a.done_cnt = 0;

@@ -67,6 +67,9 @@ enum OpKind {
   OP_GEMV_FUSED,  // multi-segment GEMV with fused prologue / epilogue (model graph)
   OP_ATTN_FUSED,  // qkv_rope + decode attention + combine (model graph)
   OP_PERSIST,     // the GEMV_FUSED / ATTN_FUSED run of a persistent command buffer
+  OP_ALLREDUCE,   // tensor parallel: in-place sum all-reduce of u[0] floats at dev
+  OP_ALLGATHER,   // tensor parallel: bind[0] (u[0] u32 words per rank) -> bind[1]
+  OP_TP_ARGMAX,   // tensor parallel: merge u[0] ranks' argmax candidates bind[0] -> bind[1]
 };
 
 struct Op {
@@ -86,6 +89,7 @@ struct Op {
   sx::AttnFusedArgs attnf{};
   uint32_t attn_rot = 0;
   float attn_theta = 0.0f;
+  sx_comm *comm = nullptr;  // OP_ALLREDUCE / OP_ALLGATHER
 };
 
 struct sx_cmd {
@@ -107,7 +111,14 @@ struct sx_cmd {
 void sx_host_push_op(sx_cmd *c, const Op &op);
 // record the command buffer's fused kernels as one persistent launch (sx_persist.cu)
 inline void sx_host_set_persistent(sx_cmd *c, bool on) { c->persistent = on; }
-void sx_host_set_error(const char *msg);
+void sx_host_set_error(const char *fmt, ...);  // printf-style
+// tensor parallel (sx_tp.cu): collectives and the argmax-candidate merge on stream s
+sx_status sx_host_allreduce(sx_comm *c, float *buf, size_t count, cudaStream_t s);
+sx_status sx_host_allgather(sx_comm *c, const uint32_t *src, uint32_t *dst, size_t words,
+                            cudaStream_t s);
+sx_status sx_host_tp_argmax(const uint32_t *cand, uint32_t n, uint32_t *token, cudaStream_t s);
+uint32_t sx_host_comm_ranks(const sx_comm *c);
+uint32_t sx_host_comm_rank(const sx_comm *c);
 // Shape / shared-memory validation of a GEMV launch (sets the error message).
 sx_status sx_host_check_gemv(int qt, bool geglu, bool pro, uint32_t m, uint32_t k,
                              uint32_t batch);

@@ -30,6 +30,8 @@ struct GemvArgs {
   float eps;
   int epi;
   uint32_t *token;          // kEpiArgmax: [batch] greedy ids
+  uint32_t *cand;           // kEpiArgmax, optional: [batch][4] {value bits, global index,
+                            // 1 if this call holds logits row 0 and it is NaN, 0}
   // scratch (engine-owned): split-tile records, per-tile arrival counters (zero at rest),
   // per-worker argmax candidates, the argmax arrival counter (zero at rest)
   float *part;
@@ -62,13 +64,19 @@ cudaError_t launch_repack(int qt, const uint32_t *ref, void *packed, uint32_t m,
                           cudaStream_t s);
 cudaError_t launch_unpack_q4(const void *packed, float *out, uint32_t m, uint32_t k,
                              cudaStream_t s);
+// Synthetic reference-layout rows [row0, row0 + rows) x 32-column blocks [blk0, blk0 + k / 32)
+// of a matrix with nb_global blocks per row (nb_global = 0: k / 32, the whole row).
 cudaError_t launch_synth_ref(int qt, uint32_t *ref, uint32_t row0, uint32_t rows, uint32_t k,
-                             uint64_t seed, uint64_t stream_id, cudaStream_t s);
+                             uint64_t seed, uint64_t stream_id, cudaStream_t s,
+                             uint32_t blk0 = 0, uint32_t nb_global = 0);
 cudaError_t launch_synth_gain(float *dst, uint32_t n, uint64_t seed, uint64_t stream_id,
                               cudaStream_t s);
+// Synthetic past K/V: rows [slot][local kv head] of a cache holding heads
+// [head0, head0 + heads) of heads_global (the values of the one-GPU model's heads).
 cudaError_t launch_fill_kv(void *k_cache, void *v_cache, int kv_bf16, uint32_t rows,
                            uint32_t head_dim, float eps, uint64_t seed, uint32_t layer,
-                           cudaStream_t s);
+                           cudaStream_t s, uint32_t heads = 1, uint32_t head0 = 0,
+                           uint32_t heads_global = 1);
 
 struct NormArgs {
   float *x;           // residual stream (add variant: updated in place)

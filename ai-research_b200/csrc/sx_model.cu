@@ -17,6 +17,7 @@ namespace {
 
 struct LayerBufs {
   uint32_t head_dim = 0, rot = 0, num_kv = 0, q_dim = 0, kv_dim = 0, k_eq_v = 0;
+  uint32_t kv_head0 = 0, num_kv_global = 0;  // this rank's kv heads within the layer's
   float theta = 0.0f, layer_scalar = 1.0f;
   sx_buffer *in_norm = nullptr, *q_norm = nullptr, *k_norm = nullptr;
   sx_buffer *wq = nullptr, *wk = nullptr, *wv = nullptr, *wo = nullptr;
@@ -41,6 +42,11 @@ uint64_t stream_of(uint32_t layer, uint32_t kind) { return (uint64_t)(layer + 1)
 struct sx_model {
   sx_engine *e = nullptr;
   sx_model_config c{};
+  // tensor parallelism: this rank's shard (the whole model when comm == nullptr)
+  sx_comm *comm = nullptr;
+  sx_tp_shard tp{};
+  uint32_t nq = 0, I = 0, V = 0;  // local q heads, intermediate rows, vocabulary rows
+  sx_buffer *cand = nullptr, *cand_all = nullptr;  // LM-head argmax candidates (local / all)
   uint32_t total_slots = 0, max_q = 0, max_kv = 0;
   std::vector<LayerBufs> L;
   sx_buffer *x = nullptr, *x2 = nullptr, *normed = nullptr, *q = nullptr, *k = nullptr, *v = nullptr;
@@ -85,7 +91,11 @@ sx_status mk_set(sx_model *m, std::vector<sx_buffer *> bufs, sx_set **out) {
 
 sx_status alloc_model(sx_model *m) {
   const sx_model_config &c = m->c;
-  const uint32_t H = c.hidden_size, I = c.intermediate_size, V = c.vocab_size;
+  M_TRY(sx_tp_shard_plan(&c, &m->tp));
+  m->nq = m->tp.q_heads;
+  m->I = m->tp.inter;
+  m->V = m->tp.vocab;
+  const uint32_t H = c.hidden_size, I = m->I, V = m->V;
   m->total_slots = c.num_anchors + c.window_size + c.num_recall;
   m->L.resize(c.num_layers);
   for (uint32_t l = 0; l < c.num_layers; ++l) {
@@ -94,8 +104,10 @@ sx_status alloc_model(sx_model *m) {
     bool full = c.full_every && ((l + 1) % c.full_every == 0);
     B.head_dim = full ? c.global_head_dim : c.head_dim;
     B.rot = full ? B.head_dim / 4 : B.head_dim;
-    B.num_kv = full ? c.num_global_kv_heads : c.num_kv_heads;
-    B.q_dim = c.num_q_heads * B.head_dim;
+    B.num_kv = full ? m->tp.global_kv_heads : m->tp.kv_heads;
+    B.kv_head0 = full ? m->tp.global_kv_head0 : m->tp.kv_head0;
+    B.num_kv_global = full ? c.num_global_kv_heads : c.num_kv_heads;
+    B.q_dim = m->nq * B.head_dim;
     B.kv_dim = B.num_kv * B.head_dim;
     B.k_eq_v = (full && c.attention_k_eq_v) ? 1u : 0u;
     B.theta = full ? c.rope_theta_full : c.rope_theta;
@@ -114,6 +126,8 @@ sx_status alloc_model(sx_model *m) {
   M_TRY(mk_buf(m, 4ull * H, &m->mlp_out));
   M_TRY(mk_buf(m, 4ull * V, &m->logits));
   M_TRY(mk_buf(m, 4, &m->token));
+  M_TRY(mk_buf(m, 16, &m->cand));
+  M_TRY(mk_buf(m, 16ull * (c.tp_size > 1 ? c.tp_size : 1), &m->cand_all));
   M_TRY(mk_buf(m, 64, &m->step));
   const size_t kvb = c.kv_bf16 ? 2 : 4;
   for (uint32_t l = 0; l < c.num_layers; ++l) {
@@ -188,19 +202,19 @@ void record_layer(sx_model *m, sx_cmd *cmd, uint32_t l) {
   sx_engine *e = m->e;
   const sx_model_config &c = m->c;
   LayerBufs &B = m->L[l];
-  const uint32_t H = c.hidden_size, I = c.intermediate_size;
+  const uint32_t H = c.hidden_size, I = m->I;
   const float eps = c.rms_norm_eps;
-  const uint32_t gqa = c.num_q_heads / B.num_kv;
+  const uint32_t gqa = m->nq / B.num_kv;
   sx_record_rmsnorm(e, cmd, B.s_input_norm, H, eps);
   sx_record_barrier(e, cmd);
   sx_record_gemv(e, cmd, B.s_q, B.q_dim, H);
   sx_record_gemv(e, cmd, B.s_k, B.kv_dim, H);
   sx_record_gemv(e, cmd, B.s_v, B.kv_dim, H);
   sx_record_barrier(e, cmd);
-  sx_record_qkv_rope(e, cmd, B.s_qkv_rope, c.num_q_heads, B.num_kv, B.head_dim, B.rot, B.k_eq_v,
+  sx_record_qkv_rope(e, cmd, B.s_qkv_rope, m->nq, B.num_kv, B.head_dim, B.rot, B.k_eq_v,
                      B.theta, eps, m->total_slots);
   sx_record_barrier(e, cmd);
-  sx_record_decode_attn(e, cmd, B.s_attn, B.head_dim, B.kv_dim, gqa, c.attn_scale, c.num_q_heads,
+  sx_record_decode_attn(e, cmd, B.s_attn, B.head_dim, B.kv_dim, gqa, c.attn_scale, m->nq,
                         m->total_slots);
   sx_record_barrier(e, cmd);
   sx_record_gemv(e, cmd, B.s_o, H, B.q_dim);
@@ -245,9 +259,9 @@ sx_status record_forward(sx_model *m, sx_cmd *cmd, bool logits, bool io) {
   if (logits) {
     sx_record_rmsnorm(e, cmd, m->s_final_norm, c.hidden_size, c.rms_norm_eps);
     sx_record_barrier(e, cmd);
-    sx_record_gemv_logits(e, cmd, m->s_logits, c.vocab_size, c.hidden_size);
+    sx_record_gemv_logits(e, cmd, m->s_logits, m->V, c.hidden_size);
     sx_record_barrier(e, cmd);
-    sx_record_argmax(e, cmd, m->s_argmax, c.vocab_size);
+    sx_record_argmax(e, cmd, m->s_argmax, m->V);
     if (io) {
       Op t{OP_D2H};
       t.host = m->h_token; t.dev = m->token->d; t.bytes = 4;
@@ -273,6 +287,14 @@ void push_gemv(sx_model *m, sx_cmd *cmd, const sx::GemvArgs &a, int qt, bool geg
   sx_host_push_op(cmd, op);
 }
 
+void push_allreduce(sx_model *m, sx_cmd *cmd, sx_buffer *buf, uint32_t count) {
+  Op op{OP_ALLREDUCE};
+  op.dev = buf->d;
+  op.u[0] = count;
+  op.comm = m->comm;
+  sx_host_push_op(cmd, op);
+}
+
 sx::GemvArgs gemv1(const sx_buffer *w, const sx_buffer *x, sx_buffer *y, uint32_t rows,
                    uint32_t k) {
   sx::GemvArgs a{};
@@ -293,7 +315,8 @@ sx::GemvArgs gemv1(const sx_buffer *w, const sx_buffer *x, sx_buffer *y, uint32_
 sx_status record_forward_fused(sx_model *m, sx_cmd *cmd, bool logits, bool io,
                                bool persistent) {
   const sx_model_config &c = m->c;
-  const uint32_t H = c.hidden_size, I = c.intermediate_size, L = c.num_layers;
+  const uint32_t H = c.hidden_size, I = m->I, L = c.num_layers;
+  const bool tp = m->comm != nullptr;
   const float eps = c.rms_norm_eps;
   M_TRY(sx_cmd_begin(cmd));
   sx_host_set_persistent(cmd, persistent);
@@ -361,7 +384,7 @@ sx_status record_forward_fused(sx_model *m, sx_cmd *cmd, bool logits, bool io,
     A.out = (float *)m->attn_out->d;
     A.head_dim = B.head_dim;
     A.kv_dim = B.kv_dim;
-    A.num_q = c.num_q_heads;
+    A.num_q = m->nq;
     A.num_kv = B.num_kv;
     A.rotary_dim = B.rot;
     A.k_eq_v = B.k_eq_v;
@@ -372,7 +395,7 @@ sx_status record_forward_fused(sx_model *m, sx_cmd *cmd, bool logits, bool io,
     at.attn_rot = B.rot;
     at.attn_theta = B.theta;
     sx_host_bind_scratch(m->e, A);
-    if (sx::attn_scratch_bytes(c.num_q_heads, m->total_slots, B.head_dim) > m->e->attn_part_bytes ||
+    if (sx::attn_scratch_bytes(m->nq, m->total_slots, B.head_dim) > m->e->attn_part_bytes ||
         B.num_kv > 4096) {
       sx_host_set_error("model: attention scratch too small for this ring / head count");
       return SX_ERR_UNSUPPORTED;
@@ -382,6 +405,7 @@ sx_status record_forward_fused(sx_model *m, sx_cmd *cmd, bool logits, bool io,
     // o projection
     M_TRY(sx_host_check_gemv(4, false, false, H, B.q_dim, 1));
     push_gemv(m, cmd, gemv1(B.wo, m->attn_out, m->mlp_out, H, B.q_dim), 4, false);
+    if (tp) push_allreduce(m, cmd, m->mlp_out, H);  // row-parallel o: sum of the ranks' parts
 
     // gate+up GeGLU with the post-attention residual and pre-FFN norm
     sx::GemvArgs g = gemv1(B.wg, m->x, m->act, I, H);
@@ -399,10 +423,12 @@ sx_status record_forward_fused(sx_model *m, sx_cmd *cmd, bool logits, bool io,
     // down projection
     M_TRY(sx_host_check_gemv(4, false, false, H, I, 1));
     push_gemv(m, cmd, gemv1(B.wd, m->act, m->mlp_out, H, I), 4, false);
+    if (tp) push_allreduce(m, cmd, m->mlp_out, H);  // row-parallel down
   }
   if (logits) {
     LayerBufs &P = m->L[L - 1];
-    sx::GemvArgs h = gemv1(m->lm_head, m->x2, m->logits, c.vocab_size, H);
+    sx::GemvArgs h = gemv1(m->lm_head, m->x2, m->logits, m->V, H);
+    h.row_base[0] = m->tp.vocab0;  // global vocabulary index of local row 0
     h.pro = sx::kProResid;
     h.pro_mlp = (const float *)m->mlp_out->d;
     h.pro_post_w = c.has_post_norms ? (const float *)P.post_ffn->d : nullptr;
@@ -412,8 +438,21 @@ sx_status record_forward_fused(sx_model *m, sx_cmd *cmd, bool logits, bool io,
     h.eps = eps;
     h.epi = sx::kEpiArgmax;
     h.token = (uint32_t *)m->token->d;
-    M_TRY(sx_host_check_gemv(8, false, true, c.vocab_size, H, 1));
+    if (tp) h.cand = (uint32_t *)m->cand->d;
+    M_TRY(sx_host_check_gemv(8, false, true, m->V, H, 1));
     push_gemv(m, cmd, h, 8, false);
+    if (tp) {
+      // vocabulary-parallel argmax: all ranks' candidates, merged on device
+      Op g{OP_ALLGATHER};
+      g.bind = {m->cand->d, m->cand_all->d};
+      g.u[0] = 4;  // u32 words per rank
+      g.comm = m->comm;
+      sx_host_push_op(cmd, g);
+      Op mg{OP_TP_ARGMAX};
+      mg.bind = {m->cand_all->d, m->token->d};
+      mg.u[0] = m->c.tp_size;
+      sx_host_push_op(cmd, mg);
+    }
     if (io) {
       Op t{OP_D2H};
       t.host = m->h_token; t.dev = m->token->d; t.bytes = 4;
@@ -428,9 +467,12 @@ sx_status record_graph(sx_model *m, sx_cmd *cmd, bool logits, bool io) {
   return record_forward_fused(m, cmd, logits, io, m->c.reference_graph == 2);
 }
 
+// rows x cols of the synthetic matrix (seed, stream), starting at global row `grow0` and
+// 32-column block `gblk0` of a matrix with `gnb` blocks per row (gnb = 0: cols / 32)
 sx_status synth_matrix(sx_model *m, sx_buffer *dst, uint32_t rows, uint32_t cols,
                        sx_quant_mode mode, uint64_t seed, uint64_t stream, void *tmp,
-                       uint64_t tmp_bytes) {
+                       uint64_t tmp_bytes, uint32_t grow0 = 0, uint32_t gblk0 = 0,
+                       uint32_t gnb = 0) {
   const uint64_t row_bytes = sx_quantized_row_words(cols, mode) * 4;
   uint64_t chunk = tmp_bytes / row_bytes;
   chunk = (chunk / 16) * 16;
@@ -442,8 +484,8 @@ sx_status synth_matrix(sx_model *m, sx_buffer *dst, uint32_t rows, uint32_t cols
   const uint64_t chunk_bytes = qt == 4 ? sx::kQ4ChunkBytes : sx::kQ8ChunkBytes;
   for (uint64_t r0 = 0; r0 < rows; r0 += chunk) {
     uint32_t n = (uint32_t)((rows - r0) < chunk ? (rows - r0) : chunk);
-    M_TRY(sx_host_cuda_status(sx::launch_synth_ref(qt, (uint32_t *)tmp, (uint32_t)r0, n, cols,
-                                                   seed, stream, m->e->stream),
+    M_TRY(sx_host_cuda_status(sx::launch_synth_ref(qt, (uint32_t *)tmp, grow0 + (uint32_t)r0, n,
+                                                   cols, seed, stream, m->e->stream, gblk0, gnb),
                               "synth launch"));
     uint8_t *out = (uint8_t *)dst->d + (r0 / 16) * sx::pairs_of(cols) * chunk_bytes;
     M_TRY(sx_host_cuda_status(
@@ -456,7 +498,9 @@ sx_status synth_matrix(sx_model *m, sx_buffer *dst, uint32_t rows, uint32_t cols
 
 extern "C" {
 
-SX_API sx_status sx_model_create(sx_engine *e, const sx_model_config *cfg, sx_model **out) {
+namespace {
+
+sx_status create_model(sx_engine *e, const sx_model_config *cfg, sx_comm *comm, sx_model **out) {
   if (!e || !cfg || !out) {
     sx_host_set_error("model_create: null argument");
     return SX_ERR_INVALID;
@@ -485,6 +529,7 @@ SX_API sx_status sx_model_create(sx_engine *e, const sx_model_config *cfg, sx_mo
   sx_model *m = new sx_model();
   m->e = e;
   m->c = c;
+  m->comm = comm;
   sx_status st = alloc_model(m);
   for (int lg = 0; lg < 2 && st == SX_OK; ++lg)
     for (int io = 0; io < 2 && st == SX_OK; ++io) {
@@ -494,11 +539,42 @@ SX_API sx_status sx_model_create(sx_engine *e, const sx_model_config *cfg, sx_mo
   if (st != SX_OK) {
     std::string msg = sx_last_error();
     sx_model_destroy(m);
-    sx_host_set_error(msg.c_str());
+    sx_host_set_error("%s", msg.c_str());
     return st;
   }
   *out = m;
   return SX_OK;
+}
+
+}  // namespace
+
+SX_API sx_status sx_model_create(sx_engine *e, const sx_model_config *cfg, sx_model **out) {
+  if (cfg && cfg->tp_size > 1) {
+    sx_host_set_error("model_create: tp_size > 1 needs a communicator (sx_model_create_tp)");
+    return SX_ERR_INVALID;
+  }
+  return create_model(e, cfg, nullptr, out);
+}
+
+SX_API sx_status sx_model_create_tp(sx_engine *e, const sx_model_config *cfg, sx_comm *comm,
+                                    sx_model **out) {
+  if (!cfg || !comm) {
+    sx_host_set_error("model_create_tp: null argument");
+    return SX_ERR_INVALID;
+  }
+  const uint32_t n = cfg->tp_size > 1 ? cfg->tp_size : 1;
+  if (n != sx_host_comm_ranks(comm) || (n > 1 ? cfg->tp_rank : 0) != sx_host_comm_rank(comm)) {
+    sx_host_set_error("model_create_tp: tp_size %u / tp_rank %u do not match the communicator "
+                      "(%u ranks, rank %u)", cfg->tp_size, cfg->tp_rank,
+                      sx_host_comm_ranks(comm), sx_host_comm_rank(comm));
+    return SX_ERR_INVALID;
+  }
+  if (cfg->reference_graph != 0) {
+    sx_host_set_error("model_create_tp: tensor parallelism runs the fused graph (reference_graph "
+                      "0); the persistent kernel and the record-API graph have no collectives");
+    return SX_ERR_UNSUPPORTED;
+  }
+  return create_model(e, cfg, comm, out);
 }
 
 SX_API void sx_model_destroy(sx_model *m) {
@@ -523,7 +599,8 @@ SX_API sx_status sx_model_synth_weights(sx_model *m, uint64_t seed) {
   }
   sx_engine *e = m->e;
   const sx_model_config &c = m->c;
-  const uint32_t H = c.hidden_size, I = c.intermediate_size;
+  const uint32_t H = c.hidden_size, I = m->I;
+  const sx_tp_shard &tp = m->tp;
   cudaSetDevice(e->device);
   const uint64_t tmp_bytes = 64ull << 20;
   void *tmp = nullptr;
@@ -542,21 +619,28 @@ SX_API sx_status sx_model_synth_weights(sx_model *m, uint64_t seed) {
     if (st == SX_OK) st = gain(B.post_ffn, H, T_POST_FFN);
     if (st == SX_OK) st = gain(B.q_norm, B.head_dim, T_QNORM);
     if (st == SX_OK) st = gain(B.k_norm, B.head_dim, T_KNORM);
-    auto mat = [&](sx_buffer *b, uint32_t rows, uint32_t cols, uint32_t kind) {
-      return synth_matrix(m, b, rows, cols, SX_QUANT_Q4, seed, stream_of(l, kind), tmp, tmp_bytes);
+    // this rank's slices of the one-GPU model's matrices: rows of q/k/v/gate/up (its heads
+    // and intermediate rows), 32-column blocks of o/down (the same split of their K)
+    auto mat = [&](sx_buffer *b, uint32_t rows, uint32_t cols, uint32_t kind, uint32_t grow0,
+                   uint32_t gblk0, uint32_t gnb) {
+      return synth_matrix(m, b, rows, cols, SX_QUANT_Q4, seed, stream_of(l, kind), tmp, tmp_bytes,
+                          grow0, gblk0, gnb);
     };
-    if (st == SX_OK) st = mat(B.wq, B.q_dim, H, T_Q);
-    if (st == SX_OK) st = mat(B.wk, B.kv_dim, H, T_K);
-    if (st == SX_OK) st = mat(B.wv, B.kv_dim, H, B.k_eq_v ? T_K : T_V);
-    if (st == SX_OK) st = mat(B.wo, H, B.q_dim, T_O);
-    if (st == SX_OK) st = mat(B.wg, I, H, T_GATE);
-    if (st == SX_OK) st = mat(B.wu, I, H, T_UP);
-    if (st == SX_OK) st = mat(B.wd, H, I, T_DOWN);
+    const uint32_t hd = B.head_dim, q_glob = c.num_q_heads * hd;
+    if (st == SX_OK) st = mat(B.wq, B.q_dim, H, T_Q, tp.q_head0 * hd, 0, 0);
+    if (st == SX_OK) st = mat(B.wk, B.kv_dim, H, T_K, B.kv_head0 * hd, 0, 0);
+    if (st == SX_OK)
+      st = mat(B.wv, B.kv_dim, H, B.k_eq_v ? T_K : T_V, B.kv_head0 * hd, 0, 0);
+    if (st == SX_OK) st = mat(B.wo, H, B.q_dim, T_O, 0, tp.q_head0 * hd / 32, q_glob / 32);
+    if (st == SX_OK) st = mat(B.wg, I, H, T_GATE, tp.inter0, 0, 0);
+    if (st == SX_OK) st = mat(B.wu, I, H, T_UP, tp.inter0, 0, 0);
+    if (st == SX_OK)
+      st = mat(B.wd, H, I, T_DOWN, 0, tp.inter0 / 32, c.intermediate_size / 32);
     float z = sx::synth_normal(seed, stream_of(l, T_SCALAR), 0);
     B.layer_scalar = sx::bf16_bits_to_f32(sx::bf16_bits_rne(fmaf(0.05f, z, 1.0f)));
   }
   if (st == SX_OK)
-    st = synth_matrix(m, m->lm_head, c.vocab_size, H, SX_QUANT_Q8, seed, 2, tmp, tmp_bytes);
+    st = synth_matrix(m, m->lm_head, m->V, H, SX_QUANT_Q8, seed, 2, tmp, tmp_bytes, tp.vocab0);
   if (st == SX_OK)
     st = sx_host_cuda_status(
         sx::launch_synth_gain((float *)m->final_norm->d, H, seed, 3, e->stream), "synth gain");
@@ -580,7 +664,8 @@ SX_API sx_status sx_model_fill_kv(sx_model *m, uint64_t seed) {
     LayerBufs &B = m->L[l];
     M_TRY(sx_host_cuda_status(
         sx::launch_fill_kv(B.kc->d, B.vc->d, m->c.kv_bf16 ? 1 : 0, m->total_slots * B.num_kv,
-                           B.head_dim, m->c.rms_norm_eps, seed, l, m->e->stream),
+                           B.head_dim, m->c.rms_norm_eps, seed, l, m->e->stream, B.num_kv,
+                           B.kv_head0, B.num_kv_global),
         "fill kv"));
   }
   return sx_host_cuda_status(cudaStreamSynchronize(m->e->stream), "fill kv sync");
@@ -606,7 +691,7 @@ SX_API sx_status sx_forward_token(sx_model *m, const float *x, uint32_t clock, u
   sx_status st = sx_submit(m->e, m->cmd[want_logits ? 1 : 0][1], 0);
   if (token_out) *token_out = (st == SX_OK && want_logits) ? m->h_token[0] : 0u;
   if (st == SX_OK && want_logits && logits_out)
-    st = sx_buffer_read(m->logits, 0, logits_out, 4ull * m->c.vocab_size);
+    st = sx_buffer_read(m->logits, 0, logits_out, 4ull * m->V);
   return st;
 }
 

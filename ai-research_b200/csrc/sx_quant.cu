@@ -118,14 +118,15 @@ __global__ void unpack_q4_kernel(const uint8_t *packed, float *out, uint32_t m, 
 // checker's generator).
 template <int QT>
 __global__ void synth_ref_kernel(uint32_t *ref, uint32_t row0, uint32_t rows, uint32_t k,
-                                 uint64_t seed, uint64_t stream) {
+                                 uint64_t seed, uint64_t stream, uint32_t blk0, uint32_t nbg) {
   const uint32_t nb = k / 32;
   constexpr uint32_t WPB = QT == 4 ? 5 : 9;
   constexpr uint32_t STRIDE = QT == 4 ? 8 : 16;
   const uint64_t total = (uint64_t)rows * nb;
   for (uint64_t it = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; it < total;
        it += (uint64_t)gridDim.x * blockDim.x) {
-    uint64_t idx = (uint64_t)row0 * nb + it;
+    const uint64_t r = it / nb, b = it % nb;
+    uint64_t idx = (row0 + r) * nbg + blk0 + b;
     uint32_t *blk = ref + it * WPB;
     blk[0] = f2u(synth_scale(seed, stream, idx * STRIDE));
 #pragma unroll
@@ -141,10 +142,13 @@ __global__ void synth_gain_kernel(float *dst, uint32_t n, uint64_t seed, uint64_
 // Synthetic past K/V rows (one thread per [slot][kv_head] row); sequential fmaf chain so the
 // unit-RMS normalisation of V matches the CPU generator bit for bit.
 __global__ void fill_kv_kernel(void *k_cache, void *v_cache, int kv_bf16, uint32_t rows,
-                               uint32_t D, float eps, uint64_t seed, uint32_t layer) {
+                               uint32_t D, float eps, uint64_t seed, uint32_t layer,
+                               uint32_t heads, uint32_t head0, uint32_t heads_global) {
   const uint64_t ks = 0x10000ull + 2ull * layer, vs = ks + 1;
-  for (uint32_t row = blockIdx.x * blockDim.x + threadIdx.x; row < rows;
-       row += gridDim.x * blockDim.x) {
+  for (uint32_t lrow = blockIdx.x * blockDim.x + threadIdx.x; lrow < rows;
+       lrow += gridDim.x * blockDim.x) {
+    // values of row (slot, head0 + h) of the whole cache, stored at local row lrow
+    const uint64_t row = (uint64_t)(lrow / heads) * heads_global + head0 + lrow % heads;
     float ss = 0.0f;
     for (uint32_t d = 0; d < D; ++d) {
       float vz = synth_normal(seed, vs, (uint64_t)row * D + d);
@@ -152,15 +156,15 @@ __global__ void fill_kv_kernel(void *k_cache, void *v_cache, int kv_bf16, uint32
     }
     float r = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)D), eps)));
     for (uint32_t d = 0; d < D; ++d) {
-      uint64_t i = (uint64_t)row * D + d;
+      const uint64_t i = row * D + d, o = (uint64_t)lrow * D + d;
       float kz = bf16_bits_to_f32(bf16_bits_rne(synth_normal(seed, ks, i)));
       float vz = bf16_bits_to_f32(bf16_bits_rne(__fmul_rn(synth_normal(seed, vs, i), r)));
       if (kv_bf16) {
-        reinterpret_cast<uint16_t *>(k_cache)[i] = bf16_bits_rne(kz);
-        reinterpret_cast<uint16_t *>(v_cache)[i] = bf16_bits_rne(vz);
+        reinterpret_cast<uint16_t *>(k_cache)[o] = bf16_bits_rne(kz);
+        reinterpret_cast<uint16_t *>(v_cache)[o] = bf16_bits_rne(vz);
       } else {
-        reinterpret_cast<float *>(k_cache)[i] = kz;
-        reinterpret_cast<float *>(v_cache)[i] = vz;
+        reinterpret_cast<float *>(k_cache)[o] = kz;
+        reinterpret_cast<float *>(v_cache)[o] = vz;
       }
     }
   }
@@ -192,12 +196,16 @@ cudaError_t launch_unpack_q4(const void *packed, float *out, uint32_t m, uint32_
 }
 
 cudaError_t launch_synth_ref(int qt, uint32_t *ref, uint32_t row0, uint32_t rows, uint32_t k,
-                             uint64_t seed, uint64_t stream_id, cudaStream_t s) {
+                             uint64_t seed, uint64_t stream_id, cudaStream_t s, uint32_t blk0,
+                             uint32_t nb_global) {
   uint64_t items = (uint64_t)rows * (k / 32);
+  const uint32_t nbg = nb_global ? nb_global : k / 32;
   if (qt == 4)
-    synth_ref_kernel<4><<<grid_for(items, 256), 256, 0, s>>>(ref, row0, rows, k, seed, stream_id);
+    synth_ref_kernel<4><<<grid_for(items, 256), 256, 0, s>>>(ref, row0, rows, k, seed, stream_id,
+                                                             blk0, nbg);
   else
-    synth_ref_kernel<8><<<grid_for(items, 256), 256, 0, s>>>(ref, row0, rows, k, seed, stream_id);
+    synth_ref_kernel<8><<<grid_for(items, 256), 256, 0, s>>>(ref, row0, rows, k, seed, stream_id,
+                                                             blk0, nbg);
   return cudaGetLastError();
 }
 
@@ -209,9 +217,10 @@ cudaError_t launch_synth_gain(float *dst, uint32_t n, uint64_t seed, uint64_t st
 
 cudaError_t launch_fill_kv(void *k_cache, void *v_cache, int kv_bf16, uint32_t rows,
                            uint32_t head_dim, float eps, uint64_t seed, uint32_t layer,
-                           cudaStream_t s) {
+                           cudaStream_t s, uint32_t heads, uint32_t head0,
+                           uint32_t heads_global) {
   fill_kv_kernel<<<grid_for(rows, 128), 128, 0, s>>>(k_cache, v_cache, kv_bf16, rows, head_dim,
-                                                     eps, seed, layer);
+                                                     eps, seed, layer, heads, head0, heads_global);
   return cudaGetLastError();
 }
 

@@ -66,7 +66,20 @@ class ModelConfig(C.Structure):
         ("rope_theta_full", C.c_float),
         ("attn_scale", C.c_float),
         ("reference_graph", C.c_uint32),
+        ("tp_size", C.c_uint32),
+        ("tp_rank", C.c_uint32),
     ]
+
+    def as_dict(self) -> dict:
+        return {name: getattr(self, name) for name, _ in self._fields_}
+
+
+class TpShard(C.Structure):
+    """sx_tp_shard: one rank's heads, intermediate rows and vocabulary rows."""
+
+    _fields_ = [(n, C.c_uint32) for n in (
+        "q_heads", "q_head0", "kv_heads", "kv_head0", "global_kv_heads", "global_kv_head0",
+        "inter", "inter0", "vocab", "vocab0")]
 
     def as_dict(self) -> dict:
         return {name: getattr(self, name) for name, _ in self._fields_}
@@ -107,6 +120,8 @@ def model_config(**kw) -> ModelConfig:
         rope_theta_full=1000000.0,
         attn_scale=1.0,
         reference_graph=0,
+        tp_size=1,
+        tp_rank=0,
     )
     base.update(kw)
     return ModelConfig(**base)
@@ -214,6 +229,11 @@ _SIGS = {
     "sx_dispatch_unpack_q4": (_S, [_P, _P, _P, _U32, _U32]),
     "sx_dispatch_synth_weights": (_S, [_P, _I, _P, _U32, _U32, _U32, _U64, _U64]),
     "sx_model_create": (_S, [_P, C.POINTER(ModelConfig), C.POINTER(_P)]),
+    "sx_model_create_tp": (_S, [_P, C.POINTER(ModelConfig), _P, C.POINTER(_P)]),
+    "sx_tp_shard_plan": (_S, [C.POINTER(ModelConfig), C.POINTER(TpShard)]),
+    "sx_comm_unique_id": (_S, [C.c_char_p]),
+    "sx_comm_create": (_S, [_P, C.c_char_p, _U32, _U32, C.POINTER(_P)]),
+    "sx_comm_destroy": (None, [_P]),
     "sx_model_destroy": (None, [_P]),
     "sx_model_synth_weights": (_S, [_P, _U64]),
     "sx_model_fill_kv": (_S, [_P, _U64]),
@@ -534,15 +554,51 @@ class CommandBuffer:
         check(lib().sx_cmd_end(self.h))
 
 
+def tp_shard_plan(cfg: ModelConfig) -> TpShard:
+    """sx_tp_shard_plan: the shard of rank cfg.tp_rank of cfg.tp_size (host only)."""
+    out = TpShard()
+    check(lib().sx_tp_shard_plan(C.byref(cfg), C.byref(out)))
+    return out
+
+
+def comm_unique_id() -> bytes:
+    buf = C.create_string_buffer(128)
+    check(lib().sx_comm_unique_id(buf))
+    return buf.raw
+
+
+class Comm:
+    """A tensor-parallel communicator (NCCL) of one rank, on the engine's GPU."""
+
+    def __init__(self, engine: Engine, unique_id: bytes, nranks: int, rank: int):
+        assert len(unique_id) == 128
+        h = C.c_void_p()
+        check(lib().sx_comm_create(engine.h, unique_id, nranks, rank, C.byref(h)))
+        self.h = h
+        self.engine = engine
+        self.nranks, self.rank = nranks, rank
+
+    def close(self):
+        if getattr(self, "h", None):
+            lib().sx_comm_destroy(self.h)
+            self.h = None
+
+    __del__ = _quiet_close
+
+
 class Model:
     """GpuModelContext (src/gpu/model_gpu.zig:35-197) + gpuDispatchForwardToken."""
 
-    def __init__(self, engine: Engine, cfg: ModelConfig):
+    def __init__(self, engine: Engine, cfg: ModelConfig, comm: "Comm | None" = None):
         h = C.c_void_p()
         self.cfg = cfg
-        check(lib().sx_model_create(engine.h, C.byref(cfg), C.byref(h)))
+        if comm is None:
+            check(lib().sx_model_create(engine.h, C.byref(cfg), C.byref(h)))
+        else:
+            check(lib().sx_model_create_tp(engine.h, C.byref(cfg), comm.h, C.byref(h)))
         self.h = h
         self.engine = engine
+        self.comm = comm  # kept alive while the model's graphs reference it
         self.total_slots = cfg.num_anchors + cfg.window_size + cfg.num_recall
 
     def close(self):

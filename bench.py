@@ -12,8 +12,10 @@ e2e   : tokens/s through the public C ABI sx_forward_token (gpuDispatchForwardTo
 roofline : dominant kernel (fused gate+up GeGLU Q4 GEMV) bytes / CUDA-event launch time
 cpu_baseline : the CPU checker (restatement of the reference's CPU path) on the host cores
 
-N > 1: one process per GPU (torchrun), each rank decodes its own replica of the model
-(independent sessions, no collective); value is the sum over ranks.
+N > 1: one process per GPU (torchrun), the model tensor-parallel over the ranks (column-
+parallel q/k/v/gate/up, row-parallel o/down with an NCCL all-reduce of the hidden vector twice
+per layer, vocabulary-parallel LM head with an all-gather of argmax candidates); value is the
+one token stream's tokens/s (strong scaling), timed as the max over ranks.
 """
 from __future__ import annotations
 
@@ -258,8 +260,8 @@ def run_reference(args, rank, world):
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": per_token * 1e3,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-        "data": "synthetic",
+        "higher_is_better": True, "scaling": "strong" if world > 1 else "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
         "config": {"workload": "c4: 12B-shape Q4_0 decode, batch 1, 48 layers, H 3840, "
                                "16q/8kv x 256, I 15360, vocab 262144, 640 live ring slots",
                    "parallelism": "cpu"},
@@ -293,21 +295,28 @@ def main():
         import torch.distributed as dist
         from datetime import timedelta
 
-        dist.init_process_group("nccl", timeout=timedelta(seconds=300),
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120),
                                 device_id=torch.device("cuda", local))
     import sx
 
     cfgd = model_cfg_dict(args.layers)
     cfgd["reference_graph"] = 2 if args.graph == "persistent" else 0
     eng = sx.Engine(local)
+    comm = None
+    if world > 1:
+        # tensor parallel over the ranks: NCCL id made on rank 0, shared through the process group
+        obj = [sx.comm_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(obj, src=0)
+        comm = sx.Comm(eng, obj[0], world, rank)
+        cfgd.update(tp_size=world, tp_rank=rank, reference_graph=0)
     stream = torch.cuda.ExternalStream(eng.stream)
-    model = sx.Model(eng, sx.model_config(**cfgd))
-    model.synth_weights(SEED + rank)
-    model.fill_kv(SEED + rank)
+    model = sx.Model(eng, sx.model_config(**cfgd), comm)
+    model.synth_weights(SEED)
+    model.fill_kv(SEED)
     total_slots = model.total_slots
     ring = sx.Ring(1, 32, 512, 96)
     ring.prefill(0, START_CLOCK)
-    rng = np.random.default_rng(SEED + rank)
+    rng = np.random.default_rng(SEED)
     for r in range(96):  # synthetic recall tier: every slot live (640)
         ring.write_recall(0, r, int(rng.integers(0, START_CLOCK)))
 
@@ -377,7 +386,8 @@ def main():
         t = torch.tensor([ms], device="cuda")
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms_max = float(t.item())
-    value = world * args.steps / (ms_max / 1e3)
+    # one token stream, sharded over the ranks (tensor parallel) or on one GPU
+    value = args.steps / (ms_max / 1e3)
 
     # ---- e2e through the public API (host buffers, copies inside the timed region)
     token = 7
@@ -400,11 +410,11 @@ def main():
         t = torch.tensor([e2e_s], device="cuda")
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         e2e_s = float(t.item())
-    e2e = world * args.steps / e2e_s
+    e2e = args.steps / e2e_s
 
     # ---- roofline of the dominant kernel: fused gate+up GeGLU over the layers' weights
     peak, peak_kind = load_peaks()
-    I = cfgd["intermediate_size"]
+    I = cfgd["intermediate_size"] // world  # this rank's gate/up rows
     gu_bytes = 2 * (I * H // 32 * 20) + H * 4 + I * 4
     roof_layers = min(args.layers, 24)
     wbufs = []
@@ -435,25 +445,27 @@ def main():
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "f32 (Q4_0/Q8_0 weights)",
+        "scaling": "strong" if world > 1 else "weak", "vs_baseline": None, "dtype": "f32 (Q4_0/Q8_0 weights)",
         "data": "synthetic (seeded random-init 12B-shaped weights, BASELINE distributions)",
         "config": {
             "workload": f"c4: 12B-shape Q4_0 greedy decode, batch 1, {args.layers} layers, H 3840, "
                         "16q/8kv x 256, I 15360, vocab 262144 (Q8_0 head), 640 live ring slots",
-            "global_batch": world, "seq_len": total_slots,
-            "parallelism": "replicas" if world > 1 else "single",
-            "graph": ("one persistent cooperative launch per token" if args.graph == "persistent"
+            "global_batch": 1, "seq_len": total_slots,
+            "parallelism": f"tp{world} (NCCL all-reduce x2 per layer, vocab-parallel head)"
+                           if world > 1 else "single",
+            "graph": ("one persistent cooperative launch per token"
+                      if cfgd["reference_graph"] == 2
                       else "5 kernels per layer + LM head, programmatic dependent launch"),
             "l2": "inputs larger than L2 (8.1 GB of weights+KV read per step)",
             "algorithmic_bytes_per_token": alg["total"],
-            "hbm_gbs_per_token_rate": alg["total"] * value / world / 1e9,
+            "hbm_gbs_per_token_rate": alg["total"] * value / 1e9,
         },
         "e2e": {"value": e2e, "unit": UNIT,
                 "h2d_bytes_per_step": 4 * H + 4 * total_slots + 16, "d2h_bytes_per_step": 4},
         "gpu_launches": kernels_per_token * args.steps,
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                      "frac": achieved / peak, "traffic": traffic,
-                     "kernel": "gemv_kernel<4,2,1> fused gate+up GeGLU, 2 x 15360x3840 Q4_0",
+                     "kernel": f"gemv_kernel<4,2,1> fused gate+up GeGLU, 2 x {I}x{H} Q4_0",
                      "algorithmic_bytes_per_launch": gu_bytes, "launch_ms": launch_ms,
                      "peak_kind": peak_kind + " (burst copy)"},
         "clocks": clk,
@@ -462,7 +474,9 @@ def main():
         line["cpu_baseline"] = cpu_baseline()
     if rank == 0:
         print(json.dumps(line), flush=True)
-    model.close()
+    model.close()  # its graphs hold the collectives: released before the communicator
+    if comm is not None:
+        comm.close()
     eng.close()
     if dist is not None:
         dist.barrier()

@@ -256,6 +256,10 @@ typedef struct {
                                 the record API (14 launches per layer); 0 = the fused graph (5
                                 launches per layer); 2 = the fused graph's kernels as phases of
                                 one persistent cooperative launch per token */
+  uint32_t tp_size;          /* tensor-parallel ranks (0 or 1: one GPU); with tp_size > 1 the
+                                model holds rank tp_rank's shard (sx_tp_shard_plan) and must be
+                                created with sx_model_create_tp */
+  uint32_t tp_rank;
 } sx_model_config;
 
 typedef struct sx_model sx_model;
@@ -289,6 +293,39 @@ SX_API void *sx_model_kcache(sx_model *m, uint32_t layer);
 SX_API void *sx_model_vcache(sx_model *m, uint32_t layer);
 SX_API uint64_t sx_model_weight_bytes(sx_model *m);
 SX_API uint32_t sx_model_kernels_per_token(sx_model *m, int want_logits);
+
+/* ---------------------------------------------------------------------------------------
+ * Tensor-parallel decode (new: the reference runs on one GPU).  One engine, communicator and
+ * model per GPU.  Column-parallel q (num_q_heads / N heads), k / v (num_kv_heads / N and
+ * num_global_kv_heads / N heads: the GQA ratio is preserved), gate / up (intermediate / N
+ * rows); row-parallel o and down (their K split the same way) followed by a sum all-reduce
+ * of the hidden vector, twice per layer; vocabulary-parallel LM head (vocab / N rows) whose
+ * local argmax candidates {value, index} are all-gathered and merged on device (lowest index
+ * on ties, logits[0] = NaN -> token 0 as on one GPU).  Norms, residual stream and x are
+ * replicated; the KV cache holds the rank's kv heads.  Collectives: NCCL, captured in the
+ * per-token graph (graph mode 0).
+ * ------------------------------------------------------------------------------------- */
+typedef struct {
+  uint32_t q_heads, q_head0;                 /* this rank's q heads [q_head0, +q_heads)      */
+  uint32_t kv_heads, kv_head0;               /* sliding-layer kv heads                        */
+  uint32_t global_kv_heads, global_kv_head0; /* full-attention-layer kv heads                 */
+  uint32_t inter, inter0;                    /* intermediate rows / down-projection columns   */
+  uint32_t vocab, vocab0;                    /* LM-head rows                                  */
+} sx_tp_shard;
+/* Host only: the shard of rank cfg->tp_rank of cfg->tp_size; SX_ERR_INVALID when the heads,
+ * intermediate size (in 32-column blocks) or vocabulary do not divide evenly. */
+SX_API sx_status sx_tp_shard_plan(const sx_model_config *cfg, sx_tp_shard *out);
+
+typedef struct sx_comm sx_comm;
+/* NCCL unique id (128 bytes) made on one rank and shared with the others by the caller. */
+SX_API sx_status sx_comm_unique_id(uint8_t id[128]);
+SX_API sx_status sx_comm_create(sx_engine *e, const uint8_t id[128], uint32_t nranks,
+                                uint32_t rank, sx_comm **out);
+SX_API void sx_comm_destroy(sx_comm *c);
+/* sx_model_create for a tensor-parallel rank: cfg->tp_size / tp_rank must match the
+ * communicator; cfg->reference_graph must be 0. */
+SX_API sx_status sx_model_create_tp(sx_engine *e, const sx_model_config *cfg, sx_comm *comm,
+                                    sx_model **out);
 
 #ifdef __cplusplus
 }
