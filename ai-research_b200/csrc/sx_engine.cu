@@ -582,6 +582,8 @@ SX_API sx_status sx_engine_create(int device, sx_quant_mode mode, uint32_t flags
     st = cuda_status(sx::prepare_ops_kernels(), "attention kernel attributes");
     if (st) break;
     st = cuda_status(sx::prepare_persist_kernel(), "persistent kernel attributes");
+    if (st) break;
+    st = cuda_status(sx::prepare_prefill_kernel(), "prefill kernel attributes");
   } while (0);
   if (st != SX_OK) {
     sx_engine_destroy(e);
@@ -993,6 +995,19 @@ SX_API sx_status sx_dispatch_gemv(sx_engine *e, sx_quant_mode mode, const void *
   SX_CHECK_ARG(e, "dispatch: null engine");
   SX_TRY_CUDA(cudaSetDevice(e->device), "cudaSetDevice");
   return do_gemv(e, e->stream, qt_of(mode), false, w_packed, nullptr, x, y, m, k, batch);
+}
+SX_API sx_status sx_dispatch_prefill_gemm(sx_engine *e, const void *w_packed, const void *x_bf16,
+                                          float *y, uint32_t t, uint32_t n, uint32_t k) {
+  SX_CHECK_ARG(e, "dispatch: null engine");
+  SX_CHECK_ARG(w_packed && x_bf16 && y, "prefill_gemm: null pointer");
+  SX_CHECK_ARG(t > 0 && n > 0 && k >= 64 && k % 64 == 0 && t < (1u << 31),
+               "prefill_gemm: need t, n > 0 and k a positive multiple of 64 (t=%u n=%u k=%u)", t,
+               n, k);
+  SX_CHECK_ARG(((uintptr_t)w_packed | (uintptr_t)x_bf16 | (uintptr_t)y) % 16 == 0,
+               "prefill_gemm: w, x and y must be 16-byte aligned");
+  SX_TRY_CUDA(cudaSetDevice(e->device), "cudaSetDevice");
+  return cuda_status(sx::launch_prefill_q4(w_packed, x_bf16, y, t, n, k, n, e->err_dev, e->stream),
+                     "prefill gemm launch");
 }
 SX_API sx_status sx_dispatch_gate_up(sx_engine *e, const void *wg_packed, const void *wu_packed,
                                      const float *x, float *y, uint32_t m, uint32_t k,

@@ -151,6 +151,11 @@ bool persist_gemv_variant(int qt, bool geglu, const GemvArgs &a, uint32_t smem_l
                           uint32_t *variant, uint32_t *smem_end);
 bool persist_attn_variant(const AttnFusedArgs &a, uint32_t *variant);
 cudaError_t prepare_persist_kernel();
+
+// Batch-prefill Q4_0 projection GEMM (sx_prefill.cu): y[t][n] = x[t][:] . bf16(deq(w[n][:]))
+cudaError_t prepare_prefill_kernel();
+cudaError_t launch_prefill_q4(const void *w, const void *x, float *y, uint32_t t, uint32_t n,
+                              uint32_t k, uint32_t ldy, uint32_t *err, cudaStream_t s);
 // bar: two words (arrival count, abort), cleared by the caller before every launch
 cudaError_t launch_persist(const Phase *phases, uint32_t n, uint32_t *bar, uint32_t *err,
                            int num_sms, cudaStream_t s);

@@ -229,6 +229,7 @@ _SIGS = {
     "sx_dispatch_unpack_q4": (_S, [_P, _P, _P, _U32, _U32]),
     "sx_dispatch_synth_weights": (_S, [_P, _I, _P, _U32, _U32, _U32, _U64, _U64]),
     "sx_model_create": (_S, [_P, C.POINTER(ModelConfig), C.POINTER(_P)]),
+    "sx_dispatch_prefill_gemm": (_S, [_P, _P, _P, _P, _U32, _U32, _U32]),
     "sx_model_create_tp": (_S, [_P, C.POINTER(ModelConfig), _P, C.POINTER(_P)]),
     "sx_tp_shard_plan": (_S, [C.POINTER(ModelConfig), C.POINTER(TpShard)]),
     "sx_comm_unique_id": (_S, [C.c_char_p]),
@@ -435,6 +436,11 @@ class Engine:
     # --- immediate mode (device pointers: torch tensors or ints)
     def gemv(self, mode, w_packed, x, y, m, k, batch=1):
         check(lib().sx_dispatch_gemv(self.h, mode, _ptr(w_packed), _ptr(x), _ptr(y), m, k, batch))
+
+    def prefill_gemm(self, w_packed, x_bf16, y, t, n, k):
+        """y[t][n] = x[t][:] . bf16(deq(w[n][:])) on the tcgen05 tensor cores (bf16 x, f32 y)."""
+        check(lib().sx_dispatch_prefill_gemm(self.h, _ptr(w_packed), _ptr(x_bf16), _ptr(y), t, n,
+                                             k))
 
     def gate_up(self, wg, wu, x, y, m, k, batch=1):
         check(lib().sx_dispatch_gate_up(self.h, _ptr(wg), _ptr(wu), _ptr(x), _ptr(y), m, k, batch))
