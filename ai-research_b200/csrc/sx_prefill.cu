@@ -7,14 +7,18 @@
 // many sessions turns each projection into one GEMM.  The dequantised weight equals the
 // checker's (f32)(q - 8) * d rounded to bf16 (round to nearest even), bit for bit.
 //
-// CTA tile: 256 tokens x 128 weight rows, K in steps of 64, 4 shared-memory stages.
-//   warp 0, lane 0   loads: one TMA box of X (256 x 64 bf16, 128-byte swizzle) and the 8 raw
-//                    640-byte Q4 chunks of the stage's 128 rows (bulk copies), both completing
-//                    on the stage's `full` barrier;
-//   warps 4..11      dequantise one chunk each into the stage's B tile, written in the UMMA
+// CTA tile: 256 tokens x 256 weight rows, K in steps of 64, 3 shared-memory stages (74 KB
+// each: X 32 KB, dequantised W 32 KB, raw Q4 10 KB); each weight is dequantised once and used
+// by 256 tokens, each X tile by 256 weight rows.
+//   warp 0, lane 0   loads: one TMA box of X (256 x 64 bf16, 128-byte swizzle) and one TMA box
+//                    of the 16 raw 640-byte Q4 chunks of the stage's 256 rows (the packed
+//                    weights seen as a u32 tensor [tiles][pairs x 160]), both completing on the
+//                    stage's `full` barrier;
+//   warps 4..11      dequantise two chunks each into the stage's B tile, written in the UMMA
 //                    K-major 128-byte-swizzle layout, fence the async proxy and arrive on `ready`;
-//   warp 1, lane 0   issues tcgen05.mma (M 128, N 128, K 16, bf16 x bf16 -> f32) for the two
-//                    token halves into two TMEM accumulators and commits each stage to `empty`;
+//   warp 1, lane 0   issues tcgen05.mma (M 128, N 256, K 16, bf16 x bf16 -> f32) for the two
+//                    token halves into two TMEM accumulators (all 512 columns) and commits each
+//                    stage to `empty`;
 //   warps 0..3       read the accumulators back (tcgen05.ld 32x32b) and store Y.
 // Every mbarrier wait is bounded; a wait that runs out records kDevWaitTimeout, the CTA stops
 // issuing, drains what it already issued and frees its TMEM.
@@ -31,14 +35,14 @@ namespace sx {
 
 namespace {
 
-constexpr int kBM = 256, kBN = 128, kBK = 64, kStages = 4;
+constexpr int kBM = 256, kBN = 256, kBK = 64, kStages = 3;
 constexpr int kPThreads = 384;                          // 12 warps
 constexpr uint32_t kATile = kBM * kBK * 2;              // 32 KB of X per stage
-constexpr uint32_t kBTile = kBN * kBK * 2;              // 16 KB of dequantised W per stage
-constexpr uint32_t kRaw = (kBN / 16) * kQ4ChunkBytes;   // 8 raw chunks = 5 KB per stage
+constexpr uint32_t kBTile = kBN * kBK * 2;              // 32 KB of dequantised W per stage
+constexpr uint32_t kRaw = (kBN / 16) * kQ4ChunkBytes;   // 16 raw chunks = 10 KB per stage
 constexpr uint32_t kStageBytes = kATile + kBTile + ((kRaw + 1023) & ~1023u);
 constexpr uint32_t kPrefillSmem = kStages * kStageBytes + 2048;  // + alignment, barriers
-constexpr uint32_t kTmemCols = 256;                     // two 128 x 128 f32 accumulators
+constexpr uint32_t kTmemCols = 512;                     // two 128 x 256 f32 accumulators
 
 // ---- tcgen05 / TMA wrappers (PTX ISA 8.7, sm_100a) ----
 SX_DEV void tmem_alloc(uint32_t dst_smem, uint32_t cols) {
@@ -127,8 +131,11 @@ SX_DEV void dequant_chunk_sw128(const uint8_t *raw, uint32_t btile, uint32_t row
     const float d = s[wi], nd8 = -8.0f * d;
 #pragma unroll
     for (int sl = 0; sl < 4; ++sl) {
-      const float v0 = fmaf((float)((u >> (4 * sl)) & 15u), d, nd8);
-      const float v1 = fmaf((float)((u >> (4 * sl + 16)) & 15u), d, nd8);
+      // 2^23 + q as a float, minus 2^23: the nibble as an exact float without I2F
+      const float q0 = __uint_as_float(0x4B000000u | ((u >> (4 * sl)) & 15u)) - 8388608.0f;
+      const float q1 = __uint_as_float(0x4B000000u | ((u >> (4 * sl + 16)) & 15u)) - 8388608.0f;
+      const float v0 = fmaf(q0, d, nd8);
+      const float v1 = fmaf(q1, d, nd8);
       const __nv_bfloat162 p = __floats2bfloat162_rn(v0, v1);
       const uint32_t j = hb * 4 + sl;
       asm volatile("st.shared.b32 [%0], %1;\n" ::"r"(rbase + ((j ^ rsw) << 4)),
@@ -150,10 +157,11 @@ SX_DEV void mbar_arrive(uint32_t bar) {
 }
 
 __global__ void __launch_bounds__(kPThreads, 1)
-    prefill_q4_kernel(const __grid_constant__ CUtensorMap xmap, PrefillArgs a) {
+    prefill_q4_kernel(const __grid_constant__ CUtensorMap xmap,
+                      const __grid_constant__ CUtensorMap wmap, PrefillArgs a) {
   extern __shared__ uint8_t smem_raw[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  // stage s: [X tile 32 KB | B tile 16 KB | raw chunks 5 KB], 1024-byte aligned (swizzle atoms)
+  // stage s: [X tile 32 KB | B tile 32 KB | raw chunks 10 KB], 1024-byte aligned (swizzle atoms)
   const uint32_t base = (smem_u32(smem_raw) + 1023) & ~1023u;
   uint8_t *const gbase = smem_raw + (base - smem_u32(smem_raw));
   auto a_tile = [&](int s) { return base + s * kStageBytes; };
@@ -168,8 +176,8 @@ __global__ void __launch_bounds__(kPThreads, 1)
   volatile uint32_t *abort_flag = reinterpret_cast<uint32_t *>(gbase + kStages * kStageBytes + 108);
 
   const uint32_t m0 = blockIdx.x * kBM, n0 = blockIdx.y * kBN;
-  const uint32_t nk = a.k / kBK, pairs = a.k / 64, ntiles = tiles_of(a.n), tile0 = n0 / 16;
-  const uint32_t nvalid = min(8u, ntiles - tile0);  // raw chunks that exist for this tile
+  const uint32_t nk = a.k / kBK, ntiles = tiles_of(a.n), tile0 = n0 / 16;
+  const uint32_t nvalid = min((uint32_t)(kBN / 16), ntiles - tile0);  // raw chunks that exist
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
@@ -207,12 +215,10 @@ __global__ void __launch_bounds__(kPThreads, 1)
         fail();
         break;
       }
-      mbar_arrive_expect_tx(full(s), kATile + nvalid * kQ4ChunkBytes);
+      mbar_arrive_expect_tx(full(s), kATile + kRaw);  // out-of-range boxes are zero-filled
       tma_load_2d(a_tile(s), &xmap, (int32_t)(i * kBK), (int32_t)m0, full(s));
-      for (uint32_t rt = 0; rt < nvalid; ++rt)
-        bulk_g2s(base + raw_off(s) + rt * kQ4ChunkBytes,
-                 a.w + ((size_t)(tile0 + rt) * pairs + i) * kQ4ChunkBytes, kQ4ChunkBytes,
-                 full(s));
+      tma_load_2d(base + raw_off(s), &wmap, (int32_t)(i * (kQ4ChunkBytes / 4)), (int32_t)tile0,
+                  full(s));
       last_round[s] = round;
     }
   } else if (warp == 1 && lane == 0) {
@@ -238,16 +244,18 @@ __global__ void __launch_bounds__(kPThreads, 1)
     }
     umma_commit(acc_bar);  // completes once every issued MMA has
   } else if (warp >= 4) {
-    // ---- dequantisation: warp 4 + rt owns the stage's raw chunk rt (rows 16 rt .. 16 rt + 15)
-    const uint32_t rt = warp - 4;
+    // ---- dequantisation: warp 4 + d owns the stage's raw chunks d and d + 8 (16 rows each)
+    const uint32_t dw = warp - 4;
     for (uint32_t i = 0; i < nk && !*abort_flag; ++i) {
       const int s = i % kStages;
       if (!mbar_wait_bounded(full(s), (i / kStages) & 1)) {
         fail();
         break;
       }
-      if (rt < nvalid) dequant_chunk_sw128(gbase + raw_off(s) + rt * kQ4ChunkBytes, b_tile(s),
-                                           rt * 16, lane);
+#pragma unroll
+      for (uint32_t rt = dw; rt < kBN / 16; rt += 8)
+        if (rt < nvalid)
+          dequant_chunk_sw128(gbase + raw_off(s) + rt * kQ4ChunkBytes, b_tile(s), rt * 16, lane);
       fence_proxy_async();  // generic-proxy stores -> the tensor core's async-proxy reads
       __syncwarp();
       if (lane == 0) mbar_arrive(ready(s));
@@ -279,7 +287,9 @@ __global__ void __launch_bounds__(kPThreads, 1)
                     make_float4(__uint_as_float(r[j]), __uint_as_float(r[j + 1]),
                                 __uint_as_float(r[j + 2]), __uint_as_float(r[j + 3]));
             } else {
-              for (uint32_t j = 0; j < cols; ++j) yr[j] = __uint_as_float(r[j]);
+#pragma unroll
+              for (uint32_t j = 0; j < 32; ++j)
+                if (j < cols) yr[j] = __uint_as_float(r[j]);
             }
           }
         }
@@ -337,9 +347,19 @@ cudaError_t launch_prefill_q4(const void *w, const void *x, float *y, uint32_t t
                       CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                       CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return cudaErrorInvalidValue;
+  // packed Q4_0 as u32 [tiles][pairs * 160]: box = the 16 chunks (160 words each) of one pair
+  CUtensorMap wmap;
+  const uint32_t pairs = k / 64;
+  const cuuint64_t wdims[2] = {(cuuint64_t)pairs * (kQ4ChunkBytes / 4), tiles_of(n)};
+  const cuuint64_t wstrides[1] = {(cuuint64_t)pairs * kQ4ChunkBytes};
+  const cuuint32_t wbox[2] = {kQ4ChunkBytes / 4, kBN / 16};
+  r = encode(&wmap, CU_TENSOR_MAP_DATA_TYPE_UINT32, 2, const_cast<void *>(w), wdims, wstrides,
+             wbox, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return cudaErrorInvalidValue;
   PrefillArgs a{static_cast<const uint8_t *>(w), y, t, n, k, ldy, err};
   dim3 grid((t + kBM - 1) / kBM, (n + kBN - 1) / kBN);
-  prefill_q4_kernel<<<grid, kPThreads, kPrefillSmem, s>>>(map, a);
+  prefill_q4_kernel<<<grid, kPThreads, kPrefillSmem, s>>>(map, wmap, a);
   return cudaGetLastError();
 }
 

@@ -53,7 +53,7 @@ def parse():
     ap.add_argument("--graph", choices=["persistent", "fused"], default="fused",
                     help="persistent: one cooperative launch per token; fused: 5 kernels per "
                          "layer chained with programmatic dependent launch")
-    ap.add_argument("--case", choices=["geglu", "q4_head", "attn"],
+    ap.add_argument("--case", choices=["geglu", "q4_head", "attn", "prefill"],
                     help="profiling case: launch one kernel of the step standalone "
                          "(--launches times) on synthetic data and exit; prints no JSON line")
     ap.add_argument("--launches", type=int, default=3)
@@ -76,6 +76,34 @@ def run_case(args):
         n = sx.packed_bytes(m, k, sx.QUANT_Q4)
         return torch.randint(0, 256, (n,), dtype=torch.uint8, device="cuda", generator=g)
 
+    if args.case == "prefill":
+        # config-5 batch-prefill projections: ~16.9k packed tokens x (q|k|v, o, gate|up, down);
+        # prints one JSON line per shape (TFLOP/s of the tcgen05 GEMM vs the measured peak)
+        peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) \
+            if (ROOT / "MEASURED_PEAKS.json").exists() else {"bf16_tflops": 1590.0}
+        t = 66 * 256
+        x = torch.randn((t, 6144), device="cuda", generator=g).to(torch.bfloat16)
+        for n, k in ((2560, 1536), (1536, 2048), (12288, 1536), (1536, 6144)):
+            w = packed(n, k)
+            xs = x[:, :k].contiguous()
+            y = torch.empty((t, n), device="cuda")
+            for _ in range(2):
+                eng.prefill_gemm(w, xs, y, t, n, k)
+            eng.sync()
+            stream = torch.cuda.ExternalStream(eng.stream)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            for _ in range(args.launches):
+                eng.prefill_gemm(w, xs, y, t, n, k)
+            e1.record(stream)
+            eng.sync()
+            ms = e0.elapsed_time(e1) / args.launches
+            tflops = 2.0 * t * n * k / (ms / 1e3) / 1e12
+            print(json.dumps({"case": "prefill_q4_gemm", "t": t, "n": n, "k": k, "ms": ms,
+                              "tflops": tflops, "frac_of_measured_bf16": tflops / peaks["bf16_tflops"]}),
+                  flush=True)
+        eng.close()
+        return
     if args.case == "attn":
         cfg = model_cfg_dict(1)
         cfg["vocab_size"] = 4096
