@@ -1000,9 +1000,10 @@ SX_API sx_status sx_dispatch_prefill_gemm(sx_engine *e, const void *w_packed, co
                                           float *y, uint32_t t, uint32_t n, uint32_t k) {
   SX_CHECK_ARG(e, "dispatch: null engine");
   SX_CHECK_ARG(w_packed && x_bf16 && y, "prefill_gemm: null pointer");
-  SX_CHECK_ARG(t > 0 && n > 0 && k >= 64 && k % 64 == 0 && t < (1u << 31),
-               "prefill_gemm: need t, n > 0 and k a positive multiple of 64 (t=%u n=%u k=%u)", t,
-               n, k);
+  SX_CHECK_ARG(t > 0 && n > 0 && n % 4 == 0 && k >= 64 && k % 64 == 0 && t < (1u << 31),
+               "prefill_gemm: need t > 0, n a positive multiple of 4 (16-byte rows of y) and k a "
+               "positive multiple of 64 (t=%u n=%u k=%u)",
+               t, n, k);
   SX_CHECK_ARG(((uintptr_t)w_packed | (uintptr_t)x_bf16 | (uintptr_t)y) % 16 == 0,
                "prefill_gemm: w, x and y must be 16-byte aligned");
   SX_TRY_CUDA(cudaSetDevice(e->device), "cudaSetDevice");

@@ -14,12 +14,13 @@
 //                    of the 16 raw 640-byte Q4 chunks of the stage's 256 rows (the packed
 //                    weights seen as a u32 tensor [tiles][pairs x 160]), both completing on the
 //                    stage's `full` barrier;
-//   warps 4..11      dequantise two chunks each into the stage's B tile, written in the UMMA
+//   warps 4..19      dequantise one chunk each into the stage's B tile, written in the UMMA
 //                    K-major 128-byte-swizzle layout, fence the async proxy and arrive on `ready`;
 //   warp 1, lane 0   issues tcgen05.mma (M 128, N 256, K 16, bf16 x bf16 -> f32) for the two
 //                    token halves into two TMEM accumulators (all 512 columns) and commits each
 //                    stage to `empty`;
-//   warps 0..3       read the accumulators back (tcgen05.ld 32x32b) and store Y.
+//   warps 4..19      then read the accumulators back (tcgen05.ld 32x32b), stage them in shared
+//                    memory and store Y with TMA.
 // Every mbarrier wait is bounded; a wait that runs out records kDevWaitTimeout, the CTA stops
 // issuing, drains what it already issued and frees its TMEM.
 #include <cuda.h>
@@ -36,13 +37,15 @@ namespace sx {
 namespace {
 
 constexpr int kBM = 256, kBN = 256, kBK = 64, kStages = 3;
-constexpr int kPThreads = 384;                          // 12 warps
+constexpr int kDqWarps = 16;                            // one raw chunk per warp and stage
+constexpr int kPThreads = (4 + kDqWarps) * 32;          // 20 warps
 constexpr uint32_t kATile = kBM * kBK * 2;              // 32 KB of X per stage
 constexpr uint32_t kBTile = kBN * kBK * 2;              // 32 KB of dequantised W per stage
 constexpr uint32_t kRaw = (kBN / 16) * kQ4ChunkBytes;   // 16 raw chunks = 10 KB per stage
 constexpr uint32_t kStageBytes = kATile + kBTile + ((kRaw + 1023) & ~1023u);
 constexpr uint32_t kPrefillSmem = kStages * kStageBytes + 2048;  // + alignment, barriers
 constexpr uint32_t kTmemCols = 512;                     // two 128 x 256 f32 accumulators
+static_assert(kDqWarps * 8192 <= kStages * kStageBytes, "epilogue staging reuses the stages");
 
 // ---- tcgen05 / TMA wrappers (PTX ISA 8.7, sm_100a) ----
 SX_DEV void tmem_alloc(uint32_t dst_smem, uint32_t cols) {
@@ -99,6 +102,23 @@ SX_DEV void tma_load_2d(uint32_t dst, const CUtensorMap *map, int32_t x, int32_t
       : "memory");
 }
 
+// 2-D tiled TMA store of a shared-memory box to global memory (rows/columns past the tensor's
+// extent are not written), tracked by the issuing thread's bulk async-group
+SX_DEV void tma_store_2d(const CUtensorMap *map, int32_t x, int32_t y, uint32_t src) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.global.shared::cta.tile.bulk_group [%0, {%1, %2}], [%3];\n" ::"l"(
+          reinterpret_cast<uint64_t>(map)),
+      "r"(x), "r"(y), "r"(src)
+      : "memory");
+}
+SX_DEV void bulk_commit() { asm volatile("cp.async.bulk.commit_group;\n" ::: "memory"); }
+// the shared-memory source of all but the newest N committed groups has been read
+template <int N>
+SX_DEV void bulk_wait_read() {
+  asm volatile("cp.async.bulk.wait_group.read %0;\n" ::"n"(N) : "memory");
+}
+SX_DEV void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;\n" ::: "memory"); }
+
 // UMMA shared-memory descriptor of a K-major tile in the 128-byte swizzle layout: rows of 128 B
 // (64 bf16), 8-row groups 1024 B apart (stride byte offset), version 1, layout type 2.
 SX_DEV uint64_t umma_desc_sw128(uint32_t saddr) {
@@ -111,12 +131,34 @@ constexpr uint32_t umma_idesc_bf16(int m, int n) {
          ((uint32_t)(m >> 4) << 24);
 }
 
+// fma.rn.f32x2: two independent single-precision FMAs (sm_100), each rounded once
+SX_DEV float2 ffma2(float2 a, float2 b, float2 c) {
+  float2 d;
+  asm("{\n.reg .b64 pa, pb, pc, pd;\n"
+      "mov.b64 pa, {%2, %3};\nmov.b64 pb, {%4, %5};\nmov.b64 pc, {%6, %7};\n"
+      "fma.rn.f32x2 pd, pa, pb, pc;\nmov.b64 {%0, %1}, pd;\n}\n"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+  return d;
+}
+
+// Nibble at bits [p, p + 4) of v -> the float 2^(23 - p) + q: the nibble becomes the top of the
+// mantissa under exponent 23 - p, one LOP3 (p = 8: magic 2^15, p = 12: magic 2^11).
+SX_DEV float nib_p8(uint32_t v) { return __uint_as_float(and_or(v, 0x00000F00u, 0x47000000u)); }
+SX_DEV float nib_p12(uint32_t v) { return __uint_as_float(and_or(v, 0x0000F000u, 0x45000000u)); }
+
 // Dequantise one raw 640-byte chunk (16 weight rows x 64 columns of the packed Q4_0 layout) into
 // rows [row0, row0 + 16) of a K-major 128-byte-swizzled bf16 tile: row n is 128 B long, 8-row
 // groups are 1024 B apart and 16-byte column chunk j of row n sits at chunk j ^ (n mod 8).
 // Lane l = 4 g + c holds the words of rows g and g + 8 for the pair's two 32-column blocks;
 // nibble slot s of a word is column 8 s + 2 c and slot s + 4 column 8 s + 2 c + 1 (sx_quant.cu).
-// fma(q, d, -8 d) rounds the exact (q - 8) d once, like the checker's f32 product.
+//
+// Exactness: with m = 2^(23-p) + q (exact) and C = 2^(23-p) + 8, fma(m, d, -C d) evaluates
+// m d - C d = (q - 8) d exactly and rounds once, so it equals the checker's f32 product
+// (q - 8) * d whenever -C d is itself exact: d is an f16 scale (11 significant bits) and
+// C = 2^15 + 8 = 8 * 4097 (13 bits) or 2^11 + 8 = 8 * 257 (9 bits) keeps C d within 24 bits.
+// Slots 0, 1 and 4, 5 are moved to bit positions 8 and 12 by shifts, slots 2, 3 and 6, 7 are
+// there already (in v and v >> 16), so every value needs one LOP3 and half a paired FMA.
 SX_DEV void dequant_chunk_sw128(const uint8_t *raw, uint32_t btile, uint32_t row0, int lane) {
   const int g = lane >> 2, c = lane & 3;
   const uint4 wq = *reinterpret_cast<const uint4 *>(raw + lane * 16);
@@ -127,16 +169,18 @@ SX_DEV void dequant_chunk_sw128(const uint8_t *raw, uint32_t btile, uint32_t row
   for (int wi = 0; wi < 4; ++wi) {
     const uint32_t row = row0 + g + (wi & 1) * 8, hb = wi >> 1, rsw = row & 7;
     const uint32_t rbase = btile + (row >> 3) * 1024 + rsw * 128 + 4 * c;
-    const uint32_t u = w[wi];
-    const float d = s[wi], nd8 = -8.0f * d;
+    const uint32_t u = w[wi], ua = u << 8, ub = u >> 8, uc = u >> 16;
+    const float2 d2 = make_float2(s[wi], s[wi]);
+    const float c8 = -32776.0f * s[wi], c12 = -2056.0f * s[wi];
+    const float2 n8 = make_float2(c8, c8), n12 = make_float2(c12, c12);
+    // (slot sl, slot sl + 4) = columns (8 sl + 2 c, 8 sl + 2 c + 1)
+    const float2 v[4] = {ffma2(make_float2(nib_p8(ua), nib_p8(ub)), d2, n8),
+                         ffma2(make_float2(nib_p12(ua), nib_p12(ub)), d2, n12),
+                         ffma2(make_float2(nib_p8(u), nib_p8(uc)), d2, n8),
+                         ffma2(make_float2(nib_p12(u), nib_p12(uc)), d2, n12)};
 #pragma unroll
     for (int sl = 0; sl < 4; ++sl) {
-      // 2^23 + q as a float, minus 2^23: the nibble as an exact float without I2F
-      const float q0 = __uint_as_float(0x4B000000u | ((u >> (4 * sl)) & 15u)) - 8388608.0f;
-      const float q1 = __uint_as_float(0x4B000000u | ((u >> (4 * sl + 16)) & 15u)) - 8388608.0f;
-      const float v0 = fmaf(q0, d, nd8);
-      const float v1 = fmaf(q1, d, nd8);
-      const __nv_bfloat162 p = __floats2bfloat162_rn(v0, v1);
+      const __nv_bfloat162 p = __floats2bfloat162_rn(v[sl].x, v[sl].y);
       const uint32_t j = hb * 4 + sl;
       asm volatile("st.shared.b32 [%0], %1;\n" ::"r"(rbase + ((j ^ rsw) << 4)),
                    "r"(*reinterpret_cast<const uint32_t *>(&p))
@@ -158,7 +202,8 @@ SX_DEV void mbar_arrive(uint32_t bar) {
 
 __global__ void __launch_bounds__(kPThreads, 1)
     prefill_q4_kernel(const __grid_constant__ CUtensorMap xmap,
-                      const __grid_constant__ CUtensorMap wmap, PrefillArgs a) {
+                      const __grid_constant__ CUtensorMap wmap,
+                      const __grid_constant__ CUtensorMap ymap, PrefillArgs a) {
   extern __shared__ uint8_t smem_raw[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   // stage s: [X tile 32 KB | B tile 32 KB | raw chunks 10 KB], 1024-byte aligned (swizzle atoms)
@@ -244,7 +289,7 @@ __global__ void __launch_bounds__(kPThreads, 1)
     }
     umma_commit(acc_bar);  // completes once every issued MMA has
   } else if (warp >= 4) {
-    // ---- dequantisation: warp 4 + d owns the stage's raw chunks d and d + 8 (16 rows each)
+    // ---- dequantisation: warp 4 + d owns the stage's raw chunk d (16 weight rows)
     const uint32_t dw = warp - 4;
     for (uint32_t i = 0; i < nk && !*abort_flag; ++i) {
       const int s = i % kStages;
@@ -252,48 +297,52 @@ __global__ void __launch_bounds__(kPThreads, 1)
         fail();
         break;
       }
-#pragma unroll
-      for (uint32_t rt = dw; rt < kBN / 16; rt += 8)
-        if (rt < nvalid)
-          dequant_chunk_sw128(gbase + raw_off(s) + rt * kQ4ChunkBytes, b_tile(s), rt * 16, lane);
+      if (dw < nvalid)
+        dequant_chunk_sw128(gbase + raw_off(s) + dw * kQ4ChunkBytes, b_tile(s), dw * 16, lane);
       fence_proxy_async();  // generic-proxy stores -> the tensor core's async-proxy reads
       __syncwarp();
       if (lane == 0) mbar_arrive(ready(s));
     }
   }
 
-  if (warp < 4) {
-    // ---- epilogue: TMEM lanes 32 w .. 32 w + 31 are rows of both halves
-    __syncwarp();
+  if (warp >= 4) {
+    // ---- epilogue (the dequantisation warps, once the accumulators are final): the pipeline's
+    // shared memory is free by then (every MMA, hence every load and dequantisation, is done),
+    // so each warp stages 32 x 32 f32 boxes in the 128-byte-swizzle layout, two buffers deep,
+    // and stores them with TMA.  Warp 4 + 4 gi + q reads TMEM lanes 32 q .. 32 q + 31 (its
+    // lane quarter) and owns boxes (half h, column block cb) = item gi, gi + 4, gi + 8, gi + 12.
+    const uint32_t q = warp & 3, gi = (warp - 4) >> 2;
     const bool ok = mbar_wait_bounded(acc_bar, 0);
     tc_fence_after();
     if (!ok) fail();
     if (ok && !*abort_flag) {
+      const uint32_t stage_buf = base + (warp - 4) * 8192;
 #pragma unroll 1
-      for (int h = 0; h < 2; ++h) {
-        const uint32_t row = m0 + h * 128 + warp * 32 + lane;
-#pragma unroll 1
-        for (int cb = 0; cb < kBN / 32; ++cb) {
-          uint32_t r[32];
-          tmem_ld32(tmem + ((uint32_t)(warp * 32) << 16) + h * kBN + cb * 32, r);
-          tmem_wait_ld();
-          if (row < a.t) {
-            float *yr = a.y + (size_t)row * a.ldy + n0 + cb * 32;
-            const uint32_t cols = min(32u, a.n > n0 + cb * 32 ? a.n - n0 - cb * 32 : 0u);
-            if (cols == 32 && (a.ldy & 3) == 0) {
+      for (uint32_t m = 0; m < 4; ++m) {
+        const uint32_t item = gi + 4 * m, h = item >> 3, cb = item & 7;
+        const uint32_t buf = stage_buf + (m & 1) * 4096;
+        if (m >= 2) {
+          if (lane == 0) bulk_wait_read<1>();  // the store issued from this buffer has read it
+          __syncwarp();
+        }
+        uint32_t r[32];
+        tmem_ld32(tmem + ((32 * q) << 16) + h * kBN + cb * 32, r);
+        tmem_wait_ld();
+        const uint32_t row = buf + lane * 128, sw = lane & 7;
 #pragma unroll
-              for (int j = 0; j < 32; j += 4)
-                *reinterpret_cast<float4 *>(yr + j) =
-                    make_float4(__uint_as_float(r[j]), __uint_as_float(r[j + 1]),
-                                __uint_as_float(r[j + 2]), __uint_as_float(r[j + 3]));
-            } else {
-#pragma unroll
-              for (uint32_t j = 0; j < 32; ++j)
-                if (j < cols) yr[j] = __uint_as_float(r[j]);
-            }
-          }
+        for (uint32_t c = 0; c < 8; ++c)
+          asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};\n" ::"r"(row + ((c ^ sw) << 4)),
+                       "r"(r[4 * c]), "r"(r[4 * c + 1]), "r"(r[4 * c + 2]), "r"(r[4 * c + 3])
+                       : "memory");
+        fence_proxy_async();  // generic-proxy writes -> the TMA engine's reads
+        __syncwarp();
+        if (lane == 0) {
+          tma_store_2d(&ymap, (int32_t)(n0 + cb * 32), (int32_t)(m0 + h * 128 + 32 * q), buf);
+          bulk_commit();
         }
       }
+      if (lane == 0) bulk_wait_all();
+      __syncwarp();
     }
   }
 
@@ -357,9 +406,18 @@ cudaError_t launch_prefill_q4(const void *w, const void *x, float *y, uint32_t t
              wbox, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return cudaErrorInvalidValue;
+  // Y as f32 [t][ldy], stored in 32 x 32 boxes from the 128-byte-swizzled staging buffers
+  CUtensorMap ymap;
+  const cuuint64_t ydims[2] = {n, t};
+  const cuuint64_t ystrides[1] = {(cuuint64_t)ldy * 4};
+  const cuuint32_t ybox[2] = {32, 32};
+  r = encode(&ymap, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, y, ydims, ystrides, ybox, estr,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+             CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return cudaErrorInvalidValue;
   PrefillArgs a{static_cast<const uint8_t *>(w), y, t, n, k, ldy, err};
   dim3 grid((t + kBM - 1) / kBM, (n + kBN - 1) / kBN);
-  prefill_q4_kernel<<<grid, kPThreads, kPrefillSmem, s>>>(map, wmap, a);
+  prefill_q4_kernel<<<grid, kPThreads, kPrefillSmem, s>>>(map, wmap, ymap, a);
   return cudaGetLastError();
 }
 

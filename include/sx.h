@@ -192,8 +192,8 @@ SX_API sx_status sx_dispatch_gemv(sx_engine *e, sx_quant_mode mode, const void *
                                   uint32_t batch);
 /* Batch-prefill projection (new: the reference prefills token by token through gemv_q4):
  * y[t][n] (f32, row stride n) = sum_k x[t][k] (bf16) * bf16_rne((q[n][k] - 8) * d[n][k / 32])
- * on the tcgen05 tensor cores, for all T tokens at once.  w_packed: packed Q4_0 (n x k);
- * k % 64 == 0; x and y 16-byte aligned. */
+ * on the tcgen05 tensor cores, for all T tokens at once.  w_packed: packed Q4_0 (n x k) with
+ * finite scales; k % 64 == 0; n % 4 == 0; x and y 16-byte aligned. */
 SX_API sx_status sx_dispatch_prefill_gemm(sx_engine *e, const void *w_packed, const void *x_bf16,
                                           float *y, uint32_t t, uint32_t n, uint32_t k);
 SX_API sx_status sx_dispatch_gate_up(sx_engine *e, const void *wg_packed, const void *wu_packed,

@@ -59,3 +59,8 @@ def test_gemm_rejects_bad_shapes(engine):
     y = torch.zeros((4, 128), dtype=torch.float32, device="cuda")
     with pytest.raises(sx.SxError):
         engine.prefill_gemm(buf.ptr, x, y, 4, 128, 96)  # k not a multiple of 64
+    buf2 = engine.buffer(sx.packed_bytes(130, 128, sx.QUANT_Q4))
+    x2 = torch.zeros((4, 128), dtype=torch.bfloat16, device="cuda")
+    y2 = torch.zeros((4, 130), dtype=torch.float32, device="cuda")
+    with pytest.raises(sx.SxError):
+        engine.prefill_gemm(buf2.ptr, x2, y2, 4, 130, 128)  # rows of y not 16-byte multiples
