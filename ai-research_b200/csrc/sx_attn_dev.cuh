@@ -385,8 +385,9 @@ constexpr int kClusterSlots = kFusedWarps * kClusterPerWarp;  // 64
 constexpr int kClusterMax = 16;                               // non-portable cluster size
 
 SX_HD uint32_t attn_cluster_floats(int g, uint32_t d, uint32_t cl) {
-  // qs, kn, vn, wm, wl, wo, rec [G][D + 2], weights [G][CL], sums [G]
-  return g * d + 2 * d + 2 * kFusedWarps * g + kFusedWarps * g * d + g * (d + 2) + g * cl + g;
+  // qs, kn, vn, wm, wl, wo, rec [G][D + 2], weights [G][CL], sums [G], record sums [G][CL]
+  return g * d + 2 * d + 2 * kFusedWarps * g + kFusedWarps * g * d + g * (d + 2) + g * cl + g +
+         g * cl;
 }
 
 template <int DPL, int G, bool BF16, typename Wait>
@@ -406,6 +407,7 @@ SX_DEV void attn_cluster_item(const AttnFusedArgs &a, uint32_t kvh, float *sh, W
   float *rec = wo + W * G * D;      // [G][D + 2]: M, L, O[D]
   float *fw = rec + G * (D + 2);    // [G][CL]
   float *ls = fw + G * ncl;         // [G]
+  float *fl = ls + G;               // [G][CL]: the records' L
 
   const uint32_t slot = a.step[1];
   uint32_t S = a.step[2];
@@ -429,10 +431,13 @@ SX_DEV void attn_cluster_item(const AttnFusedArgs &a, uint32_t kvh, float *sh, W
     }
   });
   cl.sync();
-  // weights of the CL records per head (every CTA computes them; CL x G remote reads)
+  // weights of the CL records per head: every CTA reads all CL x G (M, L) pairs at once
+  // (independent remote reads), then one thread per head folds them locally in record order
   for (uint32_t i = t; i < G * ncl; i += W * 32) {
     const uint32_t h = i / ncl, r = i % ncl;
-    fw[i] = cl.map_shared_rank(rec, r)[h * (D + 2)];
+    const float *rr = cl.map_shared_rank(rec, r) + h * (D + 2);
+    fw[i] = rr[0];
+    fl[i] = rr[1];
   }
   __syncthreads();
   if (t < G) {
@@ -441,19 +446,25 @@ SX_DEV void attn_cluster_item(const AttnFusedArgs &a, uint32_t kvh, float *sh, W
     float L = 0.0f;
     for (uint32_t r = 0; r < ncl; ++r) {
       const float f = M == -INFINITY ? 0.0f : expf(fw[t * ncl + r] - M);
-      L = fmaf(cl.map_shared_rank(rec, r)[t * (D + 2) + 1], f, L);
+      L = fmaf(fl[t * ncl + r], f, L);
       fw[t * ncl + r] = f;
     }
     ls[t] = L;
   }
   __syncthreads();
-  // this CTA's slice of the G x D outputs
+  // this CTA's slice of the G x D outputs: the CL remote values of an output are loaded
+  // together, then summed in record order
   const uint32_t per = (G * D + ncl - 1) / ncl, lo = rank * per, hi = min(G * D, lo + per);
   for (uint32_t idx = lo + t; idx < hi; idx += W * 32) {
     const uint32_t h = idx / D, d = idx % D;
+    float v[kClusterMax];
+#pragma unroll
+    for (uint32_t r = 0; r < (uint32_t)kClusterMax; ++r)
+      v[r] = r < ncl ? cl.map_shared_rank(rec, r)[h * (D + 2) + 2 + d] : 0.0f;
     float O = 0.0f;
-    for (uint32_t r = 0; r < ncl; ++r)
-      O = fmaf(cl.map_shared_rank(rec, r)[h * (D + 2) + 2 + d], fw[h * ncl + r], O);
+#pragma unroll
+    for (uint32_t r = 0; r < (uint32_t)kClusterMax; ++r)
+      if (r < ncl) O = fmaf(v[r], fw[h * ncl + r], O);
     const float L = ls[h];
     a.out[(size_t)(kvh * G + h) * D + d] = L > 0.0f ? O / L : 0.0f;
   }

@@ -406,6 +406,20 @@ SX_DEV void gemv_body(const GemvArgs &a, uint8_t *smem, bool prefetch, bool run,
   }
   if (!run) return;
   if (standalone) {
+    if (a.pf_slots != nullptr) {
+      // the following attention's K/V rows, spread over the CTAs (slot j: thread j / grid of
+      // CTA j % grid); the slot list and count are graph inputs, ready before this launch
+      const uint32_t S = min(a.pf_step[2], a.pf_max);
+      for (uint32_t j = tid * gridDim.x + blockIdx.x; j < S; j += blockDim.x * gridDim.x) {
+        const uint32_t sl = a.pf_slots[j];
+        if (sl < a.pf_max)
+#pragma unroll
+          for (int b = 0; b < 2; ++b)
+            if (a.pf_base[b] != nullptr)
+              prefetch_l2_bulk(static_cast<const uint8_t *>(a.pf_base[b]) + (size_t)sl * a.pf_row_bytes,
+                               a.pf_row_bytes);
+      }
+    }
     pdl_launch_dependents();
     // 2. wait for the producer of x, bring x into shared memory and build the B fragments
     pdl_wait();
@@ -418,14 +432,23 @@ SX_DEV void gemv_body(const GemvArgs &a, uint8_t *smem, bool prefetch, bool run,
     xsrc = xin;
     xld = a.k;
   } else if (have_xin) {
-    // one batch of independent 16-byte copies instead of a dependent round trip per element
-    const uint32_t per_row = a.k / 4;
-    for (uint32_t q = tid; q < batch * per_row; q += blockDim.x) {
-      uint32_t j = q / per_row, i = q % per_row;
-      cp_async16(smem_u32(xin + (size_t)j * a.k + 4 * i), a.x + (size_t)j * a.ldx + 4 * i);
+    // independent 16-byte loads, four in flight per thread, through registers: a cp.async
+    // group here would also wait for the weight chunks already in flight
+    const uint32_t per_row = a.k / 4, total = batch * per_row;
+    constexpr uint32_t U = 4;
+    for (uint32_t q0 = tid; q0 < total; q0 += U * blockDim.x) {
+      float4 v[U];
+#pragma unroll
+      for (uint32_t u = 0; u < U; ++u) {
+        const uint32_t q = q0 + u * blockDim.x, j = q / per_row, i = q % per_row;
+        if (q < total) v[u] = __ldcg(reinterpret_cast<const float4 *>(a.x + (size_t)j * a.ldx) + i);
+      }
+#pragma unroll
+      for (uint32_t u = 0; u < U; ++u) {
+        const uint32_t q = q0 + u * blockDim.x, j = q / per_row, i = q % per_row;
+        if (q < total) *reinterpret_cast<float4 *>(xin + (size_t)j * a.k + 4 * i) = v[u];
+      }
     }
-    cp_async_commit();
-    cp_async_wait<0>();
     __syncthreads();
     xsrc = xin;
     xld = a.k;

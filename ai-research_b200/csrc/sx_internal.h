@@ -40,6 +40,12 @@ struct GemvArgs {
   uint32_t *best_i;
   uint32_t *done_cnt;
   uint32_t *err;
+  // optional L2 prefetch issued before the dependency wait (standalone launches): the rows
+  // pf_slots[0 .. min(pf_step[2], pf_max)) of pf_base[0] and pf_base[1] (pf_row_bytes each,
+  // a multiple of 16), i.e. the live K/V cache rows the following attention reads
+  const uint32_t *pf_slots, *pf_step;
+  const void *pf_base[2];
+  uint32_t pf_row_bytes, pf_max;
 };
 
 // Per-device kernel attributes (dynamic shared memory limits); called at engine creation,
@@ -126,8 +132,58 @@ struct AttnFusedArgs {
   uint32_t head_dim, kv_dim, num_q, num_kv, rotary_dim, k_eq_v, kv_bf16, total_slots;
   float scale, eps;
   uint32_t *err;
+  // independent sessions (cluster form only): session z < sessions reads q/k/v at + z qkv_ld
+  // floats, its caches at + z cache_ld elements, slots at + z total_slots, step at + 4 z, and
+  // writes out at + z out_ld floats
+  uint32_t sessions, qkv_ld, out_ld;
+  uint64_t cache_ld;
 };
 cudaError_t launch_attn_fused(const AttnFusedArgs &a, cudaStream_t s, bool pdl);
+// rings up to this many live slots run the cluster form (16 CTAs x 64 slots per kv head)
+constexpr uint32_t kAttnClusterMaxSlots = 1024;
+
+// ---------------------------------------------------------------------------------------
+// Batched prefill (sx_prefill_model.cu): per-token kernels around the tcgen05 GEMMs.
+struct PfNormArgs {
+  const float *x;        // [rows][n] residual stream (input)
+  const float *mlp;      // optional sublayer output: x = (x + post?(mlp)) * scalar first
+  const float *post_w;   // optional post-norm gain of mlp
+  float scalar;
+  float *x_out;          // updated residual stream (may equal x), when mlp is set
+  const float *w;        // norm gain
+  void *out;             // [rows][n] bf16 or f32
+  const uint32_t *rows;  // optional: input row of each output row
+  uint32_t n;
+  float eps;
+};
+cudaError_t launch_pf_norm(const PfNormArgs &a, uint32_t rows, bool out_bf16, cudaStream_t s);
+
+struct PfQkvArgs {
+  const float *y;  // [tokens][ldy]: q (num_q heads) | k (num_kv) | v (num_kv) projections
+  uint32_t ldy;
+  const float *q_norm_w, *k_norm_w, *inv_freq;
+  float *q_out;    // [tokens][num_q * head_dim]
+  void *k_cache, *v_cache;  // [sessions][total_slots][num_kv][head_dim]
+  uint64_t cache_ld;        // elements per session
+  const uint32_t *sess, *clock, *slot;  // per token
+  uint32_t sessions, total_slots, num_q, num_kv, head_dim, rotary_dim, k_eq_v, kv_bf16;
+  float eps;
+  uint32_t *err;
+};
+cudaError_t launch_pf_qkv_rope(const PfQkvArgs &a, uint32_t tokens, cudaStream_t s);
+
+struct PfAttnArgs {
+  const float *q;           // [tokens][num_q * head_dim]
+  const void *k_cache, *v_cache;
+  uint64_t cache_ld;
+  const uint32_t *sess, *slots, *count;  // per token: session, active list [total_slots], n
+  void *out;                // [tokens][num_q * head_dim] bf16
+  uint32_t tokens, sessions, total_slots, num_q, num_kv, head_dim, kv_bf16;
+  float scale;
+  uint32_t *err;
+};
+cudaError_t launch_pf_attn(const PfAttnArgs &a, cudaStream_t s);
+cudaError_t launch_pf_geglu(const float *g, const float *u, void *h, size_t count, cudaStream_t s);
 
 // ---------------------------------------------------------------------------------------
 // Persistent decode kernel (sx_persist.cu): one cooperative launch runs a table of phases on

@@ -55,6 +55,15 @@ struct sx_model {
   sx_buffer *lm_head = nullptr, *final_norm = nullptr;
   sx_set *s_final_norm = nullptr, *s_logits = nullptr, *s_argmax = nullptr;
   sx_cmd *cmd[2][2] = {{nullptr, nullptr}, {nullptr, nullptr}};  // [want_logits][io]
+  // independent sessions: activation rows [S][...], KV caches [S][slots][kv_dim] (session 0
+  // first, so the one-session graphs see exactly session 0), q | k | v rows packed per
+  // session with the layer's stride; batched graphs [sessions in the step][want_logits]
+  uint32_t S = 1, max_base = 0;
+  sx_buffer *qkv = nullptr;
+  sx_cmd *bcmd[9][2] = {};
+  // batched-prefill scratch, grown to the largest call (sx_prefill_batch)
+  uint64_t pf_T = 0;
+  std::vector<void *> pf;
   float *h_x = nullptr;
   uint32_t *h_slots = nullptr, *h_step = nullptr, *h_token = nullptr;
   std::vector<sx_buffer *> buffers;
@@ -113,22 +122,25 @@ sx_status alloc_model(sx_model *m) {
     B.theta = full ? c.rope_theta_full : c.rope_theta;
     if (B.q_dim > m->max_q) m->max_q = B.q_dim;
     if (B.kv_dim > m->max_kv) m->max_kv = B.kv_dim;
+    if (B.q_dim + 2 * B.kv_dim > m->max_base) m->max_base = B.q_dim + 2 * B.kv_dim;
   }
-  M_TRY(mk_buf(m, 4ull * H, &m->x));
-  M_TRY(mk_buf(m, 4ull * H, &m->x2));
-  M_TRY(mk_buf(m, 4ull * H, &m->normed));
+  const uint64_t S = m->S = c.num_sessions > 1 ? c.num_sessions : 1;
+  M_TRY(mk_buf(m, 4ull * H * S, &m->x));
+  M_TRY(mk_buf(m, 4ull * H * S, &m->x2));
+  M_TRY(mk_buf(m, 4ull * H * S, &m->normed));
   M_TRY(mk_buf(m, 4ull * m->max_q, &m->q));
   M_TRY(mk_buf(m, 4ull * m->max_kv, &m->k));
   M_TRY(mk_buf(m, 4ull * m->max_kv, &m->v));
-  M_TRY(mk_buf(m, 4ull * m->max_q, &m->attn_out));
-  M_TRY(mk_buf(m, 4ull * m->total_slots, &m->slots));
-  M_TRY(mk_buf(m, 4ull * I, &m->act));
-  M_TRY(mk_buf(m, 4ull * H, &m->mlp_out));
-  M_TRY(mk_buf(m, 4ull * V, &m->logits));
-  M_TRY(mk_buf(m, 4, &m->token));
+  M_TRY(mk_buf(m, 4ull * m->max_base * S, &m->qkv));
+  M_TRY(mk_buf(m, 4ull * m->max_q * S, &m->attn_out));
+  M_TRY(mk_buf(m, 4ull * m->total_slots * S, &m->slots));
+  M_TRY(mk_buf(m, 4ull * I * S, &m->act));
+  M_TRY(mk_buf(m, 4ull * H * S, &m->mlp_out));
+  M_TRY(mk_buf(m, 4ull * V * S, &m->logits));
+  M_TRY(mk_buf(m, 64, &m->token));
   M_TRY(mk_buf(m, 16, &m->cand));
   M_TRY(mk_buf(m, 16ull * (c.tp_size > 1 ? c.tp_size : 1), &m->cand_all));
-  M_TRY(mk_buf(m, 64, &m->step));
+  M_TRY(mk_buf(m, 16 * S < 64 ? 64 : 16 * S, &m->step));
   const size_t kvb = c.kv_bf16 ? 2 : 4;
   for (uint32_t l = 0; l < c.num_layers; ++l) {
     LayerBufs &B = m->L[l];
@@ -150,8 +162,8 @@ sx_status alloc_model(sx_model *m) {
     M_TRY(mk_buf(m, sx_packed_bytes(I, H, SX_QUANT_Q4), &B.wg));
     M_TRY(mk_buf(m, sx_packed_bytes(I, H, SX_QUANT_Q4), &B.wu));
     M_TRY(mk_buf(m, sx_packed_bytes(H, I, SX_QUANT_Q4), &B.wd));
-    M_TRY(mk_buf(m, (uint64_t)m->total_slots * B.kv_dim * kvb, &B.kc));
-    M_TRY(mk_buf(m, (uint64_t)m->total_slots * B.kv_dim * kvb, &B.vc));
+    M_TRY(mk_buf(m, (uint64_t)m->total_slots * B.kv_dim * kvb * S, &B.kc));
+    M_TRY(mk_buf(m, (uint64_t)m->total_slots * B.kv_dim * kvb * S, &B.vc));
     m->weight_bytes += B.wq->bytes + B.wk->bytes + B.wv->bytes + B.wo->bytes + B.wg->bytes +
                        B.wu->bytes + B.wd->bytes;
   }
@@ -181,18 +193,19 @@ sx_status alloc_model(sx_model *m) {
   M_TRY(mk_set(m, {m->lm_head, m->normed, m->logits}, &m->s_logits));
   M_TRY(mk_set(m, {m->logits, m->token}, &m->s_argmax));
 
-  M_TRY(sx_host_cuda_status(cudaHostAlloc((void **)&m->h_x, 4ull * H, cudaHostAllocDefault),
-                            "pinned x"));
+  const uint64_t step_bytes = 16 * S < 64 ? 64 : 16 * S;
   M_TRY(sx_host_cuda_status(
-      cudaHostAlloc((void **)&m->h_slots, 4ull * m->total_slots, cudaHostAllocDefault),
+      cudaHostAlloc((void **)&m->h_x, 4ull * H * S, cudaHostAllocDefault), "pinned x"));
+  M_TRY(sx_host_cuda_status(
+      cudaHostAlloc((void **)&m->h_slots, 4ull * m->total_slots * S, cudaHostAllocDefault),
       "pinned slots"));
-  M_TRY(sx_host_cuda_status(cudaHostAlloc((void **)&m->h_step, 64, cudaHostAllocDefault),
-                            "pinned step"));
+  M_TRY(sx_host_cuda_status(
+      cudaHostAlloc((void **)&m->h_step, step_bytes, cudaHostAllocDefault), "pinned step"));
   M_TRY(sx_host_cuda_status(cudaHostAlloc((void **)&m->h_token, 64, cudaHostAllocDefault),
                             "pinned token"));
-  memset(m->h_x, 0, 4ull * H);
-  memset(m->h_slots, 0, 4ull * m->total_slots);
-  memset(m->h_step, 0, 64);
+  memset(m->h_x, 0, 4ull * H * S);
+  memset(m->h_slots, 0, 4ull * m->total_slots * S);
+  memset(m->h_step, 0, step_bytes);
   memset(m->h_token, 0, 64);
   return SX_OK;
 }
@@ -312,8 +325,10 @@ sx::GemvArgs gemv1(const sx_buffer *w, const sx_buffer *x, sx_buffer *y, uint32_
   return a;
 }
 
+// nb: sessions stepped together (1 for the one-session graphs); every GEMV runs with batch nb
+// (row j = session j) and the attention with one grid layer per session.
 sx_status record_forward_fused(sx_model *m, sx_cmd *cmd, bool logits, bool io,
-                               bool persistent) {
+                               bool persistent, uint32_t nb = 1) {
   const sx_model_config &c = m->c;
   const uint32_t H = c.hidden_size, I = m->I, L = c.num_layers;
   const bool tp = m->comm != nullptr;
@@ -322,33 +337,34 @@ sx_status record_forward_fused(sx_model *m, sx_cmd *cmd, bool logits, bool io,
   sx_host_set_persistent(cmd, persistent);
   if (io) {
     Op a{OP_H2D};
-    a.host = m->h_x; a.dev = m->x->d; a.bytes = 4ull * H;
+    a.host = m->h_x; a.dev = m->x->d; a.bytes = 4ull * H * nb;
     sx_host_push_op(cmd, a);
     Op b{OP_H2D};
-    b.host = m->h_slots; b.dev = m->slots->d; b.bytes = 4ull * m->total_slots;
+    b.host = m->h_slots; b.dev = m->slots->d; b.bytes = 4ull * m->total_slots * nb;
     sx_host_push_op(cmd, b);
     Op s{OP_H2D};
-    s.host = m->h_step; s.dev = m->step->d; s.bytes = 16;
+    s.host = m->h_step; s.dev = m->step->d; s.bytes = 16ull * nb;
     sx_host_push_op(cmd, s);
   }
   for (uint32_t l = 0; l < L; ++l) {
     LayerBufs &B = m->L[l];
     // q | k | v with the input norm (and, after layer 0, the previous layer's residual)
+    // q | k | v rows of session j at qkv + j * base (base = q_dim + 2 kv_dim of this layer)
     sx::GemvArgs q{};
     const sx_buffer *w3[3] = {B.wq, B.wk, B.wv};
-    sx_buffer *y3[3] = {m->q, m->k, m->v};
     uint32_t r3[3] = {B.q_dim, B.kv_dim, B.kv_dim};
     uint32_t base = 0;
     for (int s = 0; s < 3; ++s) {
       q.w[s][0] = q.w[s][1] = w3[s]->d;
-      q.y[s] = (float *)y3[s]->d;
+      q.y[s] = (float *)m->qkv->d + base;
       q.rows[s] = r3[s];
       q.tiles[s] = sx::tiles_of(r3[s]);
       q.row_base[s] = base;
       base += r3[s];
     }
+    float *const qp = (float *)m->qkv->d, *const kp = qp + B.q_dim, *const vp = kp + B.kv_dim;
     q.k = H;
-    q.batch = 1;
+    q.batch = nb;
     q.ldy = base;
     q.ldx = H;
     q.eps = eps;
@@ -366,15 +382,24 @@ sx_status record_forward_fused(sx_model *m, sx_cmd *cmd, bool logits, bool io,
       q.pro_x_out = (float *)m->x->d;
     }
     q.epi = sx::kEpiPlain;
-    M_TRY(sx_host_check_gemv(4, false, true, B.q_dim + 2 * B.kv_dim, H, 1));
+    // the attention below reads the live K/V rows of this layer's cache, last touched one
+    // token ago: start pulling them into L2 while this GEMV runs
+    if (B.kv_dim * (c.kv_bf16 ? 2u : 4u) % 16 == 0 && nb == 1)  // bulk: 16-byte multiples
+      q.pf_slots = (const uint32_t *)m->slots->d;
+    q.pf_step = (const uint32_t *)m->step->d;
+    q.pf_base[0] = B.kc->d;
+    q.pf_base[1] = B.k_eq_v ? nullptr : B.vc->d;
+    q.pf_row_bytes = B.kv_dim * (c.kv_bf16 ? 2u : 4u);
+    q.pf_max = m->total_slots;
+    M_TRY(sx_host_check_gemv(4, false, true, B.q_dim + 2 * B.kv_dim, H, nb));
     push_gemv(m, cmd, q, 4, false);
 
     // fused qkv_rope + attention
     Op at{OP_ATTN_FUSED};
     sx::AttnFusedArgs &A = at.attnf;
-    A.q = (const float *)m->q->d;
-    A.k = (const float *)m->k->d;
-    A.v = (const float *)m->v->d;
+    A.q = qp;
+    A.k = kp;
+    A.v = vp;
     A.q_norm_w = (const float *)B.q_norm->d;
     A.k_norm_w = (const float *)B.k_norm->d;
     A.k_cache = B.kc->d;
@@ -392,6 +417,10 @@ sx_status record_forward_fused(sx_model *m, sx_cmd *cmd, bool logits, bool io,
     A.total_slots = m->total_slots;
     A.scale = c.attn_scale;
     A.eps = eps;
+    A.sessions = nb;
+    A.qkv_ld = base;
+    A.out_ld = B.q_dim;
+    A.cache_ld = (uint64_t)m->total_slots * B.kv_dim;
     at.attn_rot = B.rot;
     at.attn_theta = B.theta;
     sx_host_bind_scratch(m->e, A);
@@ -403,8 +432,10 @@ sx_status record_forward_fused(sx_model *m, sx_cmd *cmd, bool logits, bool io,
     sx_host_push_op(cmd, at);
 
     // o projection
-    M_TRY(sx_host_check_gemv(4, false, false, H, B.q_dim, 1));
-    push_gemv(m, cmd, gemv1(B.wo, m->attn_out, m->mlp_out, H, B.q_dim), 4, false);
+    M_TRY(sx_host_check_gemv(4, false, false, H, B.q_dim, nb));
+    sx::GemvArgs o = gemv1(B.wo, m->attn_out, m->mlp_out, H, B.q_dim);
+    o.batch = nb;
+    push_gemv(m, cmd, o, 4, false);
     if (tp) push_allreduce(m, cmd, m->mlp_out, H);  // row-parallel o: sum of the ranks' parts
 
     // gate+up GeGLU with the post-attention residual and pre-FFN norm
@@ -417,12 +448,15 @@ sx_status record_forward_fused(sx_model *m, sx_cmd *cmd, bool logits, bool io,
     g.pro_w = (const float *)B.pre_ffn->d;
     g.pro_x_out = (float *)m->x2->d;
     g.eps = eps;
-    M_TRY(sx_host_check_gemv(4, true, true, I, H, 1));
+    g.batch = nb;
+    M_TRY(sx_host_check_gemv(4, true, true, I, H, nb));
     push_gemv(m, cmd, g, 4, true);
 
     // down projection
-    M_TRY(sx_host_check_gemv(4, false, false, H, I, 1));
-    push_gemv(m, cmd, gemv1(B.wd, m->act, m->mlp_out, H, I), 4, false);
+    M_TRY(sx_host_check_gemv(4, false, false, H, I, nb));
+    sx::GemvArgs d = gemv1(B.wd, m->act, m->mlp_out, H, I);
+    d.batch = nb;
+    push_gemv(m, cmd, d, 4, false);
     if (tp) push_allreduce(m, cmd, m->mlp_out, H);  // row-parallel down
   }
   if (logits) {
@@ -438,8 +472,9 @@ sx_status record_forward_fused(sx_model *m, sx_cmd *cmd, bool logits, bool io,
     h.eps = eps;
     h.epi = sx::kEpiArgmax;
     h.token = (uint32_t *)m->token->d;
+    h.batch = nb;
     if (tp) h.cand = (uint32_t *)m->cand->d;
-    M_TRY(sx_host_check_gemv(8, false, true, m->V, H, 1));
+    M_TRY(sx_host_check_gemv(8, false, true, m->V, H, nb));
     push_gemv(m, cmd, h, 8, false);
     if (tp) {
       // vocabulary-parallel argmax: all ranks' candidates, merged on device
@@ -455,7 +490,7 @@ sx_status record_forward_fused(sx_model *m, sx_cmd *cmd, bool logits, bool io,
     }
     if (io) {
       Op t{OP_D2H};
-      t.host = m->h_token; t.dev = m->token->d; t.bytes = 4;
+      t.host = m->h_token; t.dev = m->token->d; t.bytes = 4ull * nb;
       sx_host_push_op(cmd, t);
     }
   }
@@ -517,6 +552,16 @@ sx_status create_model(sx_engine *e, const sx_model_config *cfg, sx_comm *comm, 
     sx_host_set_error("model_create: inconsistent config");
     return SX_ERR_INVALID;
   }
+  if (c.num_sessions > 1) {
+    const uint32_t slots = c.num_anchors + c.window_size + c.num_recall;
+    if (c.num_sessions > 8 || c.reference_graph != 0 || c.tp_size > 1 ||
+        slots > sx::kAttnClusterMaxSlots) {
+      sx_host_set_error("model_create: num_sessions %u needs <= 8 sessions, the fused graph "
+                        "(reference_graph 0), one GPU and a ring of at most %u slots",
+                        c.num_sessions, sx::kAttnClusterMaxSlots);
+      return SX_ERR_UNSUPPORTED;
+    }
+  }
   if ((c.kv_bf16 != 0) != e->kv_bf16) {
     sx_host_set_error("model_create: config.kv_bf16 must match the engine's KV precision flag");
     return SX_ERR_INVALID;
@@ -547,6 +592,8 @@ sx_status create_model(sx_engine *e, const sx_model_config *cfg, sx_comm *comm, 
 }
 
 }  // namespace
+
+SX_API uint32_t sx_model_config_bytes(void) { return (uint32_t)sizeof(sx_model_config); }
 
 SX_API sx_status sx_model_create(sx_engine *e, const sx_model_config *cfg, sx_model **out) {
   if (cfg && cfg->tp_size > 1) {
@@ -583,8 +630,11 @@ SX_API void sx_model_destroy(sx_model *m) {
   cudaStreamSynchronize(m->e->stream);
   for (auto &row : m->cmd)
     for (sx_cmd *c : row) sx_cmd_destroy(c);
+  for (auto &row : m->bcmd)
+    for (sx_cmd *c : row) sx_cmd_destroy(c);
   for (sx_set *s : m->sets) sx_set_destroy(s);
   for (sx_buffer *b : m->buffers) sx_buffer_destroy(b);
+  for (void *p : m->pf) cudaFree(p);
   if (m->h_x) cudaFreeHost(m->h_x);
   if (m->h_slots) cudaFreeHost(m->h_slots);
   if (m->h_step) cudaFreeHost(m->h_step);
@@ -651,19 +701,33 @@ SX_API sx_status sx_model_synth_weights(sx_model *m, uint64_t seed) {
   for (int lg = 0; lg < 2 && st == SX_OK; ++lg)
     for (int io = 0; io < 2 && st == SX_OK; ++io)
       st = record_graph(m, m->cmd[lg][io], lg != 0, io != 0);
+  for (uint32_t n = 2; n <= 8 && st == SX_OK; ++n)
+    for (int lg = 0; lg < 2 && st == SX_OK; ++lg)
+      if (m->bcmd[n][lg]) st = record_forward_fused(m, m->bcmd[n][lg], lg != 0, true, false, n);
   return st;
 }
 
 SX_API sx_status sx_model_fill_kv(sx_model *m, uint64_t seed) {
+  return sx_model_fill_kv_session(m, 0, seed);
+}
+
+SX_API sx_status sx_model_fill_kv_session(sx_model *m, uint32_t session, uint64_t seed) {
   if (!m) {
     sx_host_set_error("model: null");
     return SX_ERR_INVALID;
   }
+  if (session >= m->S) {
+    sx_host_set_error("fill_kv: session %u of a model with %u sessions", session, m->S);
+    return SX_ERR_INVALID;
+  }
   cudaSetDevice(m->e->device);
+  const uint64_t eb = m->c.kv_bf16 ? 2 : 4;
   for (uint32_t l = 0; l < m->c.num_layers; ++l) {
     LayerBufs &B = m->L[l];
+    const uint64_t off = (uint64_t)session * m->total_slots * B.kv_dim * eb;
     M_TRY(sx_host_cuda_status(
-        sx::launch_fill_kv(B.kc->d, B.vc->d, m->c.kv_bf16 ? 1 : 0, m->total_slots * B.num_kv,
+        sx::launch_fill_kv((uint8_t *)B.kc->d + off, (uint8_t *)B.vc->d + off,
+                           m->c.kv_bf16 ? 1 : 0, m->total_slots * B.num_kv,
                            B.head_dim, m->c.rms_norm_eps, seed, l, m->e->stream, B.num_kv,
                            B.kv_head0, B.num_kv_global),
         "fill kv"));
@@ -692,6 +756,56 @@ SX_API sx_status sx_forward_token(sx_model *m, const float *x, uint32_t clock, u
   if (token_out) *token_out = (st == SX_OK && want_logits) ? m->h_token[0] : 0u;
   if (st == SX_OK && want_logits && logits_out)
     st = sx_buffer_read(m->logits, 0, logits_out, 4ull * m->V);
+  return st;
+}
+
+SX_API sx_status sx_decode_batch(sx_model *m, uint32_t n, const float *x, const uint32_t *clock,
+                                 const uint32_t *slot, const uint32_t *active,
+                                 const uint32_t *n_active, int want_logits, uint32_t *tokens,
+                                 float *logits_out) {
+  if (!m || !x || !clock || !slot || !active || !n_active) {
+    sx_host_set_error("decode_batch: null argument");
+    return SX_ERR_INVALID;
+  }
+  if (n == 0 || n > m->S) {
+    sx_host_set_error("decode_batch: %u sessions requested, the model holds %u", n, m->S);
+    return SX_ERR_INVALID;
+  }
+  const uint32_t H = m->c.hidden_size, TS = m->total_slots;
+  for (uint32_t i = 0; i < n; ++i)
+    if (n_active[i] > TS || slot[i] >= TS) {
+      sx_host_set_error("decode_batch: session %u: slot list larger than the ring or slot out "
+                        "of range", i);
+      return SX_ERR_INVALID;
+    }
+  const int lg = want_logits ? 1 : 0;
+  sx_cmd *cmd = m->cmd[lg][1];
+  if (n > 1) {
+    if (!m->bcmd[n][lg]) {
+      // first step with n sessions: record its graph (outside any capture of the caller's)
+      M_TRY(sx_cmd_create(m->e, &m->bcmd[n][lg]));
+      sx_status st = record_forward_fused(m, m->bcmd[n][lg], lg != 0, true, false, n);
+      if (st != SX_OK) {
+        sx_cmd_destroy(m->bcmd[n][lg]);
+        m->bcmd[n][lg] = nullptr;
+        return st;
+      }
+    }
+    cmd = m->bcmd[n][lg];
+  }
+  memcpy(m->h_x, x, 4ull * H * n);
+  for (uint32_t i = 0; i < n; ++i) {
+    if (n_active[i]) memcpy(m->h_slots + (size_t)i * TS, active + (size_t)i * TS, 4ull * n_active[i]);
+    m->h_step[4 * i + 0] = clock[i];
+    m->h_step[4 * i + 1] = slot[i];
+    m->h_step[4 * i + 2] = n_active[i];
+    m->h_step[4 * i + 3] = 0;
+  }
+  sx_status st = sx_submit(m->e, cmd, 0);
+  if (tokens)
+    for (uint32_t i = 0; i < n; ++i) tokens[i] = (st == SX_OK && want_logits) ? m->h_token[i] : 0u;
+  if (st == SX_OK && want_logits && logits_out)
+    st = sx_buffer_read(m->logits, 0, logits_out, 4ull * m->V * n);
   return st;
 }
 
@@ -730,3 +844,261 @@ SX_API uint32_t sx_model_kernels_per_token(sx_model *m, int want_logits) {
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------------------
+// Batched prefill: every token of the call goes through each layer at once (tcgen05 GEMMs for
+// the projections, per-token kernels in sx_prefill_model.cu); the LM head runs on the
+// requested rows (normally the last prompt token of each session).
+namespace {
+
+enum PfBuf { PF_XA, PF_XB, PF_MLP, PF_XN, PF_Y, PF_Y2, PF_Q, PF_META, PF_LISTS, PF_OUT, PF_NUM };
+
+sx_status pf_ensure(sx_model *m, uint64_t T) {
+  if (T <= m->pf_T) return SX_OK;
+  for (void *p : m->pf) cudaFree(p);
+  m->pf.assign(PF_NUM, nullptr);
+  m->pf_T = 0;
+  const uint64_t H = m->c.hidden_size, I = m->I, ts = m->total_slots;
+  uint64_t wide = H > I ? H : I;
+  if (m->max_q > wide) wide = m->max_q;
+  const uint64_t ywide = m->max_base > I ? m->max_base : I;
+  const uint64_t bytes[PF_NUM] = {
+      4 * T * H, 4 * T * H, 4 * T * H, 2 * T * wide, 4 * T * ywide, 4 * T * I,
+      4 * T * m->max_q, 16 * T, 4 * T * ts,
+      // out: row ids [8], normed rows [8][H], tokens [8], logits [8][V]
+      4 * 8 + 4 * 8 * H + 4 * 8 + 4ull * 8 * m->V};
+  for (int i = 0; i < PF_NUM; ++i)
+    M_TRY(sx_host_cuda_status(cudaMalloc(&m->pf[i], bytes[i]), "prefill scratch"));
+  m->pf_T = T;
+  return SX_OK;
+}
+
+}  // namespace
+
+extern "C" SX_API sx_status sx_prefill_batch(sx_model *m, uint32_t T, const float *x,
+                                             const uint32_t *session, const uint32_t *clock,
+                                             const uint32_t *slot, const uint32_t *active,
+                                             const uint32_t *n_active, uint32_t n_out,
+                                             const uint32_t *out_rows, uint32_t *tokens,
+                                             float *logits_out) {
+  if (!m || !x || !session || !clock || !slot || !active || !n_active || T == 0 ||
+      (n_out && !out_rows)) {
+    sx_host_set_error("prefill_batch: null argument or no tokens");
+    return SX_ERR_INVALID;
+  }
+  const sx_model_config &c = m->c;
+  if (m->comm || c.reference_graph == 1) {
+    sx_host_set_error("prefill_batch: runs on one GPU with the fused kernels (tp_size <= 1, "
+                      "reference_graph != 1)");
+    return SX_ERR_UNSUPPORTED;
+  }
+  const uint32_t H = c.hidden_size, I = m->I, ts = m->total_slots, L = c.num_layers;
+  if (n_out > 8) {
+    sx_host_set_error("prefill_batch: at most 8 output rows per call (%u asked)", n_out);
+    return SX_ERR_INVALID;
+  }
+  for (uint32_t i = 0; i < n_out; ++i)
+    if (out_rows[i] >= T) {
+      sx_host_set_error("prefill_batch: output row %u beyond %u tokens", out_rows[i], T);
+      return SX_ERR_INVALID;
+    }
+  // GEMM shapes: K of every projection a multiple of 64, N a multiple of 4
+  for (uint32_t l = 0; l < L; ++l) {
+    const LayerBufs &B = m->L[l];
+    if (H % 64 || B.q_dim % 64 || I % 64 || (B.q_dim + 2 * B.kv_dim) % 4) {
+      sx_host_set_error("prefill_batch: hidden, q and intermediate sizes must be multiples of "
+                        "64 for the tcgen05 GEMM");
+      return SX_ERR_UNSUPPORTED;
+    }
+  }
+  // per-token checks, and causality of the one-pass layers: no token may read a slot that a
+  // later token of its session rewrites in this call (and no slot is written twice)
+  std::vector<std::vector<uint32_t>> writer(m->S, std::vector<uint32_t>(ts, 0xFFFFFFFFu));
+  for (uint32_t t = 0; t < T; ++t) {
+    if (session[t] >= m->S || slot[t] >= ts || n_active[t] > ts) {
+      sx_host_set_error("prefill_batch: token %u: session %u (of %u), slot %u or %u active "
+                        "slots out of range", t, session[t], m->S, slot[t], n_active[t]);
+      return SX_ERR_INVALID;
+    }
+    uint32_t &w = writer[session[t]][slot[t]];
+    if (w != 0xFFFFFFFFu) {
+      sx_host_set_error("prefill_batch: slot %u of session %u written twice in one call; split "
+                        "the prompt", slot[t], session[t]);
+      return SX_ERR_INVALID;
+    }
+    w = clock[t];
+  }
+  for (uint32_t t = 0; t < T; ++t) {
+    const uint32_t *lst = active + (size_t)t * ts;
+    for (uint32_t j = 0; j < n_active[t]; ++j) {
+      if (lst[j] >= ts) {
+        sx_host_set_error("prefill_batch: token %u lists slot %u of a %u-slot ring", t, lst[j], ts);
+        return SX_ERR_INVALID;
+      }
+      const uint32_t w = writer[session[t]][lst[j]];
+      if (w != 0xFFFFFFFFu && w > clock[t]) {
+        sx_host_set_error("prefill_batch: token %u (clock %u) reads slot %u, which the token at "
+                          "clock %u of the same session rewrites in this call; split the prompt",
+                          t, clock[t], lst[j], w);
+        return SX_ERR_INVALID;
+      }
+    }
+  }
+  sx_engine *e = m->e;
+  cudaSetDevice(e->device);
+  M_TRY(pf_ensure(m, T));
+  cudaStream_t s = e->stream;
+  float *xa = (float *)m->pf[PF_XA], *xb = (float *)m->pf[PF_XB], *mlp = (float *)m->pf[PF_MLP];
+  void *xn = m->pf[PF_XN];
+  float *y = (float *)m->pf[PF_Y], *y2 = (float *)m->pf[PF_Y2], *qo = (float *)m->pf[PF_Q];
+  uint32_t *meta = (uint32_t *)m->pf[PF_META], *lists = (uint32_t *)m->pf[PF_LISTS];
+  uint32_t *d_sess = meta, *d_clock = meta + T, *d_slot = meta + 2 * T, *d_cnt = meta + 3 * T;
+  uint32_t *d_rows = (uint32_t *)m->pf[PF_OUT];
+  float *d_norm = (float *)(d_rows + 8);
+  uint32_t *d_tok = (uint32_t *)(d_norm + 8ull * H);
+  float *d_logits = (float *)(d_tok + 8);
+  auto cp = [&](void *dst, const void *src, size_t bytes) {
+    return sx_host_cuda_status(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyHostToDevice, s),
+                               "prefill upload");
+  };
+  M_TRY(cp(xa, x, 4ull * T * H));
+  M_TRY(cp(d_sess, session, 4ull * T));
+  M_TRY(cp(d_clock, clock, 4ull * T));
+  M_TRY(cp(d_slot, slot, 4ull * T));
+  M_TRY(cp(d_cnt, n_active, 4ull * T));
+  M_TRY(cp(lists, active, 4ull * T * ts));
+  if (n_out) M_TRY(cp(d_rows, out_rows, 4ull * n_out));
+  const float eps = c.rms_norm_eps;
+  auto run = [&](cudaError_t ce, const char *what) { return sx_host_cuda_status(ce, what); };
+  for (uint32_t l = 0; l < L; ++l) {
+    LayerBufs &B = m->L[l];
+    const uint32_t base = B.q_dim + 2 * B.kv_dim;
+    // input norm, after layer 0 with the previous layer's residual update
+    sx::PfNormArgs na{};
+    na.n = H;
+    na.eps = eps;
+    na.w = (const float *)B.in_norm->d;
+    na.out = xn;
+    if (l == 0) {
+      na.x = xa;
+    } else {
+      const LayerBufs &P = m->L[l - 1];
+      na.x = xb;
+      na.mlp = mlp;
+      na.post_w = c.has_post_norms ? (const float *)P.post_ffn->d : nullptr;
+      na.scalar = P.layer_scalar;
+      na.x_out = xa;
+    }
+    M_TRY(run(sx::launch_pf_norm(na, T, true, s), "prefill norm"));
+    M_TRY(run(sx::launch_prefill_q4(B.wq->d, xn, y, T, base, H, base, e->err_dev, s),
+              "prefill qkv gemm"));
+    sx_status fst = SX_OK;
+    const float *freq = sx_host_inv_freq(e, B.rot, B.theta, &fst);
+    if (!freq) return fst;
+    sx::PfQkvArgs qa{};
+    qa.y = y;
+    qa.ldy = base;
+    qa.q_norm_w = (const float *)B.q_norm->d;
+    qa.k_norm_w = (const float *)B.k_norm->d;
+    qa.inv_freq = freq;
+    qa.q_out = qo;
+    qa.k_cache = B.kc->d;
+    qa.v_cache = B.vc->d;
+    qa.cache_ld = (uint64_t)ts * B.kv_dim;
+    qa.sess = d_sess;
+    qa.clock = d_clock;
+    qa.slot = d_slot;
+    qa.sessions = m->S;
+    qa.total_slots = ts;
+    qa.num_q = m->nq;
+    qa.num_kv = B.num_kv;
+    qa.head_dim = B.head_dim;
+    qa.rotary_dim = B.rot;
+    qa.k_eq_v = B.k_eq_v;
+    qa.kv_bf16 = c.kv_bf16 ? 1u : 0u;
+    qa.eps = eps;
+    qa.err = e->err_dev;
+    M_TRY(run(sx::launch_pf_qkv_rope(qa, T, s), "prefill qkv rope"));
+    sx::PfAttnArgs aa{};
+    aa.q = qo;
+    aa.k_cache = B.kc->d;
+    aa.v_cache = B.vc->d;
+    aa.cache_ld = qa.cache_ld;
+    aa.sess = d_sess;
+    aa.slots = lists;
+    aa.count = d_cnt;
+    aa.out = xn;
+    aa.tokens = T;
+    aa.sessions = m->S;
+    aa.total_slots = ts;
+    aa.num_q = m->nq;
+    aa.num_kv = B.num_kv;
+    aa.head_dim = B.head_dim;
+    aa.kv_bf16 = qa.kv_bf16;
+    aa.scale = c.attn_scale;
+    aa.err = e->err_dev;
+    M_TRY(run(sx::launch_pf_attn(aa, s), "prefill attention"));
+    M_TRY(run(sx::launch_prefill_q4(B.wo->d, xn, mlp, T, H, B.q_dim, H, e->err_dev, s),
+              "prefill o gemm"));
+    // post-attention residual and pre-FFN norm
+    sx::PfNormArgs nb{};
+    nb.n = H;
+    nb.eps = eps;
+    nb.x = xa;
+    nb.mlp = mlp;
+    nb.post_w = c.has_post_norms ? (const float *)B.post_attn->d : nullptr;
+    nb.scalar = 1.0f;
+    nb.x_out = xb;
+    nb.w = (const float *)B.pre_ffn->d;
+    nb.out = xn;
+    M_TRY(run(sx::launch_pf_norm(nb, T, true, s), "prefill pre-ffn norm"));
+    M_TRY(run(sx::launch_prefill_q4(B.wg->d, xn, y, T, I, H, I, e->err_dev, s), "prefill gate"));
+    M_TRY(run(sx::launch_prefill_q4(B.wu->d, xn, y2, T, I, H, I, e->err_dev, s), "prefill up"));
+    M_TRY(run(sx::launch_pf_geglu(y, y2, xn, (size_t)T * I, s), "prefill geglu"));
+    M_TRY(run(sx::launch_prefill_q4(B.wd->d, xn, mlp, T, H, I, H, e->err_dev, s),
+              "prefill down gemm"));
+  }
+  if (n_out) {
+    // last residual update and final norm of the output rows, then the Q8 LM head + argmax
+    const LayerBufs &P = m->L[L - 1];
+    sx::PfNormArgs nf{};
+    nf.n = H;
+    nf.eps = eps;
+    nf.x = xb;
+    nf.mlp = mlp;
+    nf.post_w = c.has_post_norms ? (const float *)P.post_ffn->d : nullptr;
+    nf.scalar = P.layer_scalar;
+    nf.x_out = xa;
+    nf.w = (const float *)m->final_norm->d;
+    nf.out = d_norm;
+    nf.rows = d_rows;
+    M_TRY(run(sx::launch_pf_norm(nf, n_out, false, s), "prefill final norm"));
+    sx::GemvArgs h{};
+    h.w[0][0] = h.w[0][1] = m->lm_head->d;
+    h.y[0] = d_logits;
+    h.rows[0] = m->V;
+    h.tiles[0] = sx::tiles_of(m->V);
+    h.k = H;
+    h.batch = n_out;
+    h.ldy = m->V;
+    h.x = d_norm;
+    h.ldx = H;
+    h.pro = sx::kProNone;
+    h.epi = sx::kEpiArgmax;
+    h.token = d_tok;
+    M_TRY(sx_host_check_gemv(8, false, false, m->V, H, n_out));
+    sx_host_bind_scratch(e, h);
+    M_TRY(run(sx::launch_gemv(8, false, h, e->num_sms, s, false), "prefill lm head"));
+    uint32_t tok_h[8];
+    M_TRY(sx_host_cuda_status(
+        cudaMemcpyAsync(tok_h, d_tok, 4ull * n_out, cudaMemcpyDeviceToHost, s), "tokens"));
+    if (logits_out)
+      M_TRY(sx_host_cuda_status(cudaMemcpyAsync(logits_out, d_logits, 4ull * n_out * m->V,
+                                                cudaMemcpyDeviceToHost, s),
+                                "logits"));
+    M_TRY(sx_engine_sync(e));
+    if (tokens) memcpy(tokens, tok_h, 4ull * n_out);
+    return SX_OK;
+  }
+  return sx_engine_sync(e);
+}

@@ -315,15 +315,29 @@ template <int DPL, int G, bool BF16>
 __global__ void __launch_bounds__(kFusedWarps * 32) attn_cluster_kernel(AttnFusedArgs a) {
   extern __shared__ float sh[];
   pdl_launch_dependents();
-  attn_cluster_item<DPL, G, BF16>(a, blockIdx.x, sh, [] { pdl_wait(); });
+  // this CTA's session (grid z): the same item over that session's vectors, caches and ring
+  AttnFusedArgs s = a;
+  const uint32_t z = blockIdx.z;
+  const size_t eb = a.kv_bf16 ? 2 : 4;
+  s.q += (size_t)z * a.qkv_ld;
+  s.k += (size_t)z * a.qkv_ld;
+  s.v += (size_t)z * a.qkv_ld;
+  s.k_cache = static_cast<uint8_t *>(a.k_cache) + z * a.cache_ld * eb;
+  s.v_cache = static_cast<uint8_t *>(a.v_cache) + z * a.cache_ld * eb;
+  s.slots += (size_t)z * a.total_slots;
+  s.step += 4 * z;
+  s.out += (size_t)z * a.out_ld;
+  attn_cluster_item<DPL, G, BF16>(s, blockIdx.x, sh, [] { pdl_wait(); });
 }
+
+static_assert(kClusterSlots * kClusterMax == (int)kAttnClusterMaxSlots, "cluster ring limit");
 
 template <int DPL, int G>
 cudaError_t launch_attn_fused_t(const AttnFusedArgs &a, cudaStream_t s, bool pdl) {
   const uint32_t ncl = (a.total_slots + kClusterSlots - 1) / kClusterSlots;
   if (ncl <= (uint32_t)kClusterMax) {
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(a.num_kv, ncl);
+    cfg.gridDim = dim3(a.num_kv, ncl, a.sessions > 1 ? a.sessions : 1);
     cfg.blockDim = dim3(kFusedWarps * 32);
     cfg.dynamicSmemBytes = sizeof(float) * attn_cluster_floats(G, 32 * DPL, ncl);
     cfg.stream = s;
@@ -339,6 +353,7 @@ cudaError_t launch_attn_fused_t(const AttnFusedArgs &a, cudaStream_t s, bool pdl
     if (a.kv_bf16) return cudaLaunchKernelEx(&cfg, attn_cluster_kernel<DPL, G, true>, a);
     return cudaLaunchKernelEx(&cfg, attn_cluster_kernel<DPL, G, false>, a);
   }
+  if (a.sessions > 1) return cudaErrorInvalidValue;  // sessions: cluster form only
   uint32_t nchunks = (a.total_slots + kAttnChunk - 1) / kAttnChunk;
   size_t D = 32 * DPL;
   size_t smem = sizeof(float) * attn_item_floats(G, D, nchunks);

@@ -10,6 +10,7 @@ from __future__ import annotations
 
 import ctypes as C
 import os
+import weakref
 from pathlib import Path
 
 import numpy as np
@@ -68,6 +69,7 @@ class ModelConfig(C.Structure):
         ("reference_graph", C.c_uint32),
         ("tp_size", C.c_uint32),
         ("tp_rank", C.c_uint32),
+        ("num_sessions", C.c_uint32),
     ]
 
     def as_dict(self) -> dict:
@@ -122,6 +124,7 @@ def model_config(**kw) -> ModelConfig:
         reference_graph=0,
         tp_size=1,
         tp_rank=0,
+        num_sessions=1,
     )
     base.update(kw)
     return ModelConfig(**base)
@@ -238,6 +241,10 @@ _SIGS = {
     "sx_model_destroy": (None, [_P]),
     "sx_model_synth_weights": (_S, [_P, _U64]),
     "sx_model_fill_kv": (_S, [_P, _U64]),
+    "sx_model_fill_kv_session": (_S, [_P, _U32, _U64]),
+    "sx_model_config_bytes": (_U32, []),
+    "sx_decode_batch": (_S, [_P, _U32, _P, _P, _P, _P, _P, _I, _P, _P]),
+    "sx_prefill_batch": (_S, [_P, _U32, _P, _P, _P, _P, _P, _P, _U32, _P, _P, _P]),
     "sx_forward_token": (_S, [_P, _P, _U32, _U32, _P, _U32, _I, _P, _P]),
     "sx_model_launch": (_S, [_P, _I]),
     "sx_model_get_io": (_S, [_P, C.POINTER(ModelIO)]),
@@ -264,6 +271,9 @@ def lib():
         fn = getattr(L, name)
         fn.restype = res
         fn.argtypes = args
+    if L.sx_model_config_bytes() != C.sizeof(ModelConfig):
+        raise ImportError(f"{path}: sx_model_config is {L.sx_model_config_bytes()} bytes, this "
+                          f"binding's mirror {C.sizeof(ModelConfig)}: rebuild the library")
     _lib = L
     return L
 
@@ -365,9 +375,12 @@ class Engine:
         self.h = h
         self.mode = mode
         self.kv_bf16 = not kv_f32
+        self._models = weakref.WeakSet()  # closed before the engine they were made on
 
     def close(self):
         if getattr(self, "h", None):
+            for m in list(getattr(self, "_models", ())):
+                m.close()
             lib().sx_engine_destroy(self.h)
             self.h = None
 
@@ -606,6 +619,8 @@ class Model:
         self.engine = engine
         self.comm = comm  # kept alive while the model's graphs reference it
         self.total_slots = cfg.num_anchors + cfg.window_size + cfg.num_recall
+        self.sessions = max(1, cfg.num_sessions)
+        engine._models.add(self)
 
     def close(self):
         if getattr(self, "h", None):
@@ -620,6 +635,30 @@ class Model:
     def fill_kv(self, seed: int) -> None:
         check(lib().sx_model_fill_kv(self.h, seed))
 
+    def fill_kv_session(self, session: int, seed: int) -> None:
+        check(lib().sx_model_fill_kv_session(self.h, session, seed))
+
+    def decode_batch(self, xs: np.ndarray, clocks, slots, active_lists, want_logits: bool = True,
+                     logits_out: np.ndarray | None = None) -> np.ndarray:
+        """One token for each of sessions 0..n-1 (sx_decode_batch): xs [n][hidden], per-session
+        clock, slot and active-slot list; returns the n greedy tokens."""
+        x = np.ascontiguousarray(xs, np.float32)
+        n = x.shape[0]
+        act = np.zeros((n, self.total_slots), np.uint32)
+        cnt = np.zeros(n, np.uint32)
+        for i, a in enumerate(active_lists):
+            a = np.asarray(a, np.uint32)
+            act[i, : len(a)] = a
+            cnt[i] = len(a)
+        clk = np.ascontiguousarray(clocks, np.uint32)
+        sl = np.ascontiguousarray(slots, np.uint32)
+        toks = np.zeros(n, np.uint32)
+        check(lib().sx_decode_batch(self.h, n, x.ctypes.data, clk.ctypes.data, sl.ctypes.data,
+                                    act.ctypes.data, cnt.ctypes.data, int(want_logits),
+                                    toks.ctypes.data,
+                                    None if logits_out is None else logits_out.ctypes.data))
+        return toks
+
     def forward_token(self, x: np.ndarray, clock: int, slot: int, active_slots: np.ndarray,
                       want_logits: bool = True, logits_out: np.ndarray | None = None) -> int:
         xs = np.ascontiguousarray(x, np.float32)
@@ -629,6 +668,43 @@ class Model:
                                      len(sl), int(want_logits), C.byref(tok),
                                      None if logits_out is None else logits_out.ctypes.data))
         return int(tok.value)
+
+    def prefill_batch(self, prompts, rings, start_clocks, sessions=None,
+                      logits_out: np.ndarray | None = None) -> np.ndarray:
+        """Prefill the prompts of several sessions in one pass (sx_prefill_batch).
+
+        prompts[i]: embedding rows [L_i][hidden] of session sessions[i] (default i), whose
+        ring (sx.Ring, updated here) is at start_clocks[i]; token j gets clock
+        start_clocks[i] + j, its slot and active list from the ring.  Returns the greedy
+        token after each prompt (logits_out, optional: [len(prompts)][vocab])."""
+        sessions = list(range(len(prompts))) if sessions is None else list(sessions)
+        ts = self.total_slots
+        rows, sess, clk, slt, lists, cnt, out_rows = [], [], [], [], [], [], []
+        for i, (xs, ring, c0) in enumerate(zip(prompts, rings, start_clocks)):
+            for j in range(len(xs)):
+                c = c0 + j
+                sl = ring.activate_slot(0, c)
+                a = ring.get_active_slots(0, c)
+                row = np.zeros(ts, np.uint32)
+                row[: len(a)] = a
+                rows.append(xs[j])
+                sess.append(sessions[i])
+                clk.append(c)
+                slt.append(sl)
+                lists.append(row)
+                cnt.append(len(a))
+            out_rows.append(len(rows) - 1)
+        T = len(rows)
+        x = np.ascontiguousarray(np.stack(rows), np.float32)
+        u = lambda v: np.ascontiguousarray(v, np.uint32)
+        sess, clk, slt, cnt, orow = u(sess), u(clk), u(slt), u(cnt), u(out_rows)
+        act = u(np.stack(lists))
+        toks = np.zeros(len(out_rows), np.uint32)
+        check(lib().sx_prefill_batch(self.h, T, x.ctypes.data, sess.ctypes.data, clk.ctypes.data,
+                                     slt.ctypes.data, act.ctypes.data, cnt.ctypes.data,
+                                     len(orow), orow.ctypes.data, toks.ctypes.data,
+                                     None if logits_out is None else logits_out.ctypes.data))
+        return toks
 
     def launch(self, want_logits: bool = True) -> None:
         check(lib().sx_model_launch(self.h, int(want_logits)))

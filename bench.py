@@ -53,11 +53,79 @@ def parse():
     ap.add_argument("--graph", choices=["persistent", "fused"], default="fused",
                     help="persistent: one cooperative launch per token; fused: 5 kernels per "
                          "layer chained with programmatic dependent launch")
-    ap.add_argument("--case", choices=["geglu", "q4_head", "attn", "prefill"],
+    ap.add_argument("--case", choices=["geglu", "q4_head", "attn", "prefill", "sessions"],
                     help="profiling case: launch one kernel of the step standalone "
                          "(--launches times) on synthetic data and exit; prints no JSON line")
     ap.add_argument("--launches", type=int, default=3)
     return ap.parse_args()
+
+
+def c5_config(**kw):
+    import sx
+
+    # config 5: H 1536, 35 layers, 8 q / 1 kv heads x 256, I 6144, Q4_0 layers, Q8_0 head
+    d = dict(hidden_size=1536, intermediate_size=6144, num_layers=35, num_q_heads=8,
+             num_kv_heads=1, num_global_kv_heads=1, head_dim=256, global_head_dim=256,
+             num_sessions=8)
+    d.update(kw)
+    return sx.model_config(**d)
+
+
+def run_sessions(eng, args, rank=0):
+    import torch
+    import sx
+
+    cfg = c5_config()
+    model = sx.Model(eng, cfg)
+    model.synth_weights(SEED + 1)
+    H, V = cfg.hidden_size, cfg.vocab_size
+    rng = np.random.default_rng(SEED + 1)
+    lens = rng.integers(16, 513, 64)[8 * rank: 8 * rank + 8]
+    prompts = [np.stack([sx.synth_embed_row(H, int(t), SEED + 1)
+                         for t in rng.integers(0, V, n)]) for n in lens]
+    stream = torch.cuda.ExternalStream(eng.stream)
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+    rings = [sx.Ring(1, cfg.num_anchors, cfg.window_size, cfg.num_recall) for _ in lens]
+    # warm-up prefill on scratch rings (allocates the prefill scratch), then the timed one
+    model.prefill_batch([p[:16] for p in prompts], [sx.Ring(1, cfg.num_anchors, cfg.window_size,
+                                                            cfg.num_recall) for _ in lens],
+                        [0] * 8)
+    eng.sync()
+    ev[0].record(stream)
+    toks = model.prefill_batch(prompts, rings, [0] * 8)
+    ev[1].record(stream)
+    eng.sync()
+    T = int(lens.sum())
+    ms_p = ev[0].elapsed_time(ev[1])
+    flops = T * cfg.num_layers * 2.0 * H * (cfg.num_q_heads * 256 + 2 * 256 + 8 * 256 + 3 * 6144)
+    print(json.dumps({"case": "c5_prefill", "sessions": 8, "tokens": T, "ms": ms_p,
+                      "tok_s": T / (ms_p / 1e3), "gemm_tflops": flops / (ms_p / 1e3) / 1e12}),
+          flush=True)
+    clocks = [int(n) for n in lens]
+    tokens = [int(t) for t in toks]
+    steps = 128
+
+    def step():
+        nonlocal clocks, tokens
+        xs = np.stack([sx.synth_embed_row(H, tokens[s], SEED + 1) for s in range(8)])
+        slots = [rings[s].activate_slot(0, clocks[s]) for s in range(8)]
+        lists = [rings[s].get_active_slots(0, clocks[s]) for s in range(8)]
+        got = model.decode_batch(xs, clocks, slots, lists, True)
+        tokens = [int(t) for t in got]
+        clocks = [c + 1 for c in clocks]
+
+    for _ in range(3):
+        step()
+    eng.sync()
+    ev[2].record(stream)
+    for _ in range(steps - 3):
+        step()
+    ev[3].record(stream)
+    eng.sync()
+    ms_d = ev[2].elapsed_time(ev[3]) / (steps - 3)
+    print(json.dumps({"case": "c5_decode_batch8", "sessions": 8, "steps": steps,
+                      "ms_per_step": ms_d, "tok_s": 8 / (ms_d / 1e3)}), flush=True)
+    model.close()
 
 
 def run_case(args):
@@ -65,7 +133,11 @@ def run_case(args):
     geglu   -- the fused gate+up GeGLU GEMV of one 12B layer (2 x 15360 x 3840 Q4_0, 73.8 MB)
     q4_head -- a 262144 x 3840 Q4_0 GEMV (629 MB), the steady-state streaming case
     attn    -- one 12B-width layer token (16 q / 8 kv heads x 256, 640 live slots), whose
-               second kernel is the fused attention"""
+               second kernel is the fused attention
+    prefill -- the tcgen05 Q4_0 GEMM on config 5's projection shapes (TFLOP/s per shape)
+    sessions -- config 5 on one GPU: this GPU's 8 of the 64 seeded prompts prefilled with
+               sx_prefill_batch, then 128 greedy tokens x 8 sessions with sx_decode_batch
+               (host buffers in and out, timed with CUDA events on the engine stream)"""
     import torch
     import sx
 
@@ -102,6 +174,10 @@ def run_case(args):
             print(json.dumps({"case": "prefill_q4_gemm", "t": t, "n": n, "k": k, "ms": ms,
                               "tflops": tflops, "frac_of_measured_bf16": tflops / peaks["bf16_tflops"]}),
                   flush=True)
+        eng.close()
+        return
+    if args.case == "sessions":
+        run_sessions(eng, args)
         eng.close()
         return
     if args.case == "attn":

@@ -266,7 +266,16 @@ typedef struct {
                                 model holds rank tp_rank's shard (sx_tp_shard_plan) and must be
                                 created with sx_model_create_tp */
   uint32_t tp_rank;
+  uint32_t num_sessions;     /* independent decode sessions held by the model (0 or 1: one);
+                                each has its own KV cache, ring and clock and they share the
+                                weights: sx_decode_batch steps n <= num_sessions of them with
+                                one batched pass (config 2 batch 8, config 5 sessions).  At
+                                most 8; needs the fused graph (reference_graph 0), tp_size <= 1
+                                and a ring of at most 1024 slots. */
 } sx_model_config;
+
+/* sizeof(sx_model_config): bindings check their mirror of the struct against it. */
+SX_API uint32_t sx_model_config_bytes(void);
 
 typedef struct sx_model sx_model;
 /* GpuModelContext.init without weights: allocates every device buffer and records the
@@ -275,14 +284,43 @@ SX_API sx_status sx_model_create(sx_engine *e, const sx_model_config *cfg, sx_mo
 SX_API void sx_model_destroy(sx_model *m);
 /* Fill all weights with the synthetic checkpoint (seeded, BASELINE distributions). */
 SX_API sx_status sx_model_synth_weights(sx_model *m, uint64_t seed);
-/* Fill every KV slot with a synthetic past (K = bf16 N(0,1), V unit-RMS). */
+/* Fill every KV slot with a synthetic past (K = bf16 N(0,1), V unit-RMS): session 0. */
 SX_API sx_status sx_model_fill_kv(sx_model *m, uint64_t seed);
+/* The same for the KV cache of session `session` (< num_sessions). */
+SX_API sx_status sx_model_fill_kv_session(sx_model *m, uint32_t session, uint64_t seed);
 /* gpuDispatchForwardToken (model_dispatch.zig:131-147): host x[hidden], clock, slot and the
  * active-slot list in; greedy token out (and the logits when logits_out != NULL).
  * want_logits == 0 runs the prefill graph (no LM head).  Host<->device copies included. */
 SX_API sx_status sx_forward_token(sx_model *m, const float *x, uint32_t clock, uint32_t slot,
                                   const uint32_t *active_slots, uint32_t n_active,
                                   int want_logits, uint32_t *token_out, float *logits_out);
+/* Batch-8 decode (new; the reference runs one session per forwardToken): one token for each
+ * of sessions 0..n-1 (n <= num_sessions) in one pass that streams the weights once.  Row i of
+ * x[n][hidden], clock[i], slot[i], the active list active[i * total_slots ..][0, n_active[i])
+ * and the greedy token tokens[i] belong to session i; logits_out (optional) is [n][vocab].
+ * Equal to n calls of sx_forward_token on n single-session models with those caches. */
+SX_API sx_status sx_decode_batch(sx_model *m, uint32_t n, const float *x, const uint32_t *clock,
+                                 const uint32_t *slot, const uint32_t *active,
+                                 const uint32_t *n_active, int want_logits, uint32_t *tokens,
+                                 float *logits_out);
+/* Batched prefill (new; the reference prefills with one forwardToken per prompt token,
+ * forward.zig:19-75): T tokens of any of the model's sessions in one pass per layer, the
+ * projections on the tcgen05 Q4_0 GEMM (sx_dispatch_prefill_gemm).  Token t: embedding row
+ * x[t][hidden], session[t] (< num_sessions), clock[t], slot[t] and its ring's active list
+ * active[t * total_slots ..][0, n_active[t]) -- exactly what sx_forward_token would take for
+ * it.  Every token's K/V is written to its session's cache.  The greedy next token (and,
+ * with logits_out, the [n_out][vocab] logits) is returned for the n_out <= 8 token rows
+ * out_rows (normally the last prompt token of each session).  Equal to calling
+ * sx_forward_token token by token, with the activations entering each projection rounded to
+ * bf16.  Rejected (SX_ERR_INVALID) when a slot is written twice in the call or a token lists
+ * a slot that a later token of its session rewrites: prompts up to anchors + window tokens
+ * from a fresh ring go in one call; once a session's window has wrapped, each call holds one
+ * token of it.  Hidden, q and intermediate sizes must be multiples of 64. */
+SX_API sx_status sx_prefill_batch(sx_model *m, uint32_t T, const float *x,
+                                  const uint32_t *session, const uint32_t *clock,
+                                  const uint32_t *slot, const uint32_t *active,
+                                  const uint32_t *n_active, uint32_t n_out,
+                                  const uint32_t *out_rows, uint32_t *tokens, float *logits_out);
 /* Device-resident replay: inputs already in the model's device buffers (sx_model_io). */
 SX_API sx_status sx_model_launch(sx_model *m, int want_logits);
 typedef struct {

@@ -85,6 +85,7 @@ _SIGS = {
     "orc_model_destroy": (None, [_P]),
     "orc_model_ring": (_P, [_P]),
     "orc_model_forward": (_U32, [_P, _P, _U64, _I, _P, _P]),
+    "orc_model_set_act_bf16": (None, [_P, _I]),
     "orc_model_fill_kv": (None, [_P, _U64]),
     "orc_model_synth_recall": (None, [_P, _U64, _U32, _U64]),
     "orc_model_kcache": (C.POINTER(_F), [_P, _U32]),
@@ -355,6 +356,10 @@ class Model:
 
     def fill_kv(self, seed):
         lib().orc_model_fill_kv(self.h, seed)
+
+    def set_act_bf16(self, on=True):
+        """Round each projection's input to bf16 (the batched-prefill GEMM path)."""
+        lib().orc_model_set_act_bf16(self.h, int(on))
 
     def synth_recall(self, clock, n_recall, seed):
         lib().orc_model_synth_recall(self.h, clock, n_recall, seed)

@@ -226,10 +226,12 @@ typedef struct {
   const uint32_t *w, *w2;
   const float *x;
   size_t cols;
+  int wbf16; /* Q4 weights rounded to bf16 after the dequant (the prefill GEMM's operand) */
 } orc_gemv_ctx;
 
-/* test_q4_exec.zig:56-74: row_sum += ((nib - 8) * d) * x[elem], sequential over b, w, n */
-static float orc_row_q4(const uint32_t *row, const float *x, size_t cols) {
+/* test_q4_exec.zig:56-74: row_sum += ((nib - 8) * d) * x[elem], sequential over b, w, n;
+ * wbf16: the dequantised weight is rounded to bf16 (RNE) first */
+static float orc_row_q4(const uint32_t *row, const float *x, size_t cols, int wbf16) {
   size_t nb = cols / 32;
   float sum = 0.0f;
   for (size_t b = 0; b < nb; ++b) {
@@ -239,6 +241,7 @@ static float orc_row_q4(const uint32_t *row, const float *x, size_t cols) {
       uint32_t pk = blk[1 + wi];
       for (int n = 0; n < 8; ++n) {
         float wt = ((float)((pk >> (n * 4)) & 0xFu) - 8.0f) * d;
+        if (wbf16) wt = orc_bf16_to_f32(orc_bf16_from_f32(wt));
         sum += wt * x[b * 32 + wi * 8 + n];
       }
     }
@@ -266,7 +269,7 @@ static float orc_row_q8(const uint32_t *row, const float *x, size_t cols) {
 static void orc_gemv_q4_range(void *p, size_t b, size_t e) {
   orc_gemv_ctx *c = (orc_gemv_ctx *)p;
   size_t rw = (c->cols / 32) * 5;
-  for (size_t r = b; r < e; ++r) c->y[r] = orc_row_q4(c->w + r * rw, c->x, c->cols);
+  for (size_t r = b; r < e; ++r) c->y[r] = orc_row_q4(c->w + r * rw, c->x, c->cols, c->wbf16);
 }
 static void orc_gemv_q8_range(void *p, size_t b, size_t e) {
   orc_gemv_ctx *c = (orc_gemv_ctx *)p;
@@ -275,12 +278,17 @@ static void orc_gemv_q8_range(void *p, size_t b, size_t e) {
 }
 void orc_gemv_q4(float *y, const uint32_t *w, const float *x, size_t rows, size_t cols,
                  int threads) {
-  orc_gemv_ctx c = {y, w, NULL, x, cols};
+  orc_gemv_ctx c = {y, w, NULL, x, cols, 0};
+  orc_parallel_for(rows, threads, orc_gemv_q4_range, &c);
+}
+static void orc_gemv_q4_w(float *y, const uint32_t *w, const float *x, size_t rows, size_t cols,
+                          int threads, int wbf16) {
+  orc_gemv_ctx c = {y, w, NULL, x, cols, wbf16};
   orc_parallel_for(rows, threads, orc_gemv_q4_range, &c);
 }
 void orc_gemv_q8(float *y, const uint32_t *w, const float *x, size_t rows, size_t cols,
                  int threads) {
-  orc_gemv_ctx c = {y, w, NULL, x, cols};
+  orc_gemv_ctx c = {y, w, NULL, x, cols, 0};
   orc_parallel_for(rows, threads, orc_gemv_q8_range, &c);
 }
 
@@ -295,14 +303,19 @@ static void orc_geglu_range(void *p, size_t b, size_t e) {
   orc_gemv_ctx *c = (orc_gemv_ctx *)p;
   size_t rw = (c->cols / 32) * 5;
   for (size_t r = b; r < e; ++r) {
-    float g = orc_row_q4(c->w + r * rw, c->x, c->cols);
-    float u = orc_row_q4(c->w2 + r * rw, c->x, c->cols);
+    float g = orc_row_q4(c->w + r * rw, c->x, c->cols, c->wbf16);
+    float u = orc_row_q4(c->w2 + r * rw, c->x, c->cols, c->wbf16);
     c->y[r] = orc_gelu_tanh(g) * u;
   }
 }
 void orc_gate_up_geglu_q4(float *y, const uint32_t *wg, const uint32_t *wu, const float *x,
                           size_t rows, size_t cols, int threads) {
-  orc_gemv_ctx c = {y, wg, wu, x, cols};
+  orc_gemv_ctx c = {y, wg, wu, x, cols, 0};
+  orc_parallel_for(rows, threads, orc_geglu_range, &c);
+}
+static void orc_geglu_w(float *y, const uint32_t *wg, const uint32_t *wu, const float *x,
+                        size_t rows, size_t cols, int threads, int wbf16) {
+  orc_gemv_ctx c = {y, wg, wu, x, cols, wbf16};
   orc_parallel_for(rows, threads, orc_geglu_range, &c);
 }
 
@@ -674,6 +687,7 @@ struct orc_model {
   orc_ring *ring;
   float *x, *normed, *q, *k, *v, *attn, *mlp, *act, *logits;
   uint32_t *slots;
+  int act_bf16; /* round every projection input to bf16 (the batched-prefill GEMM path) */
 };
 
 static uint32_t *orc_alloc_q(size_t rows, size_t cols, int mode) {
@@ -813,6 +827,18 @@ void orc_model_synth_recall(orc_model *m, uint64_t clock, uint32_t n_recall, uin
   }
 }
 
+/* The tcgen05 prefill path multiplies bf16 operands: each layer projection gets a bf16 copy
+ * of its f32 input (the normed residual, the attention output, the GeGLU product) and the
+ * dequantised weight (f32)(nib - 8) * d rounded to bf16.  This mode rounds the same values
+ * (round to nearest even, tensor.zig:7-18) so that path can be held to the f32 tolerance.
+ * The LM head (Q8, f32 input) is unchanged. */
+void orc_model_set_act_bf16(orc_model *m, int on) { m->act_bf16 = on; }
+
+static void orc_round_bf16(orc_model *m, float *v, size_t n) {
+  if (!m->act_bf16) return;
+  for (size_t i = 0; i < n; ++i) v[i] = orc_bf16_to_f32(orc_bf16_from_f32(v[i]));
+}
+
 uint32_t orc_model_forward(orc_model *m, const float *x_in, uint64_t clock, int want_logits,
                            float *logits_out, float *x_out) {
   const orc_model_config *c = &m->c;
@@ -825,19 +851,23 @@ uint32_t orc_model_forward(orc_model *m, const float *x_in, uint64_t clock, int 
   for (uint32_t l = 0; l < c->num_layers; ++l) {
     orc_layer *L = &m->layers[l];
     orc_rmsnorm(m->normed, m->x, L->in_norm, H, eps);
-    orc_gemv_q4(m->q, L->wq, m->normed, L->q_dim, H, m->threads);
-    orc_gemv_q4(m->k, L->wk, m->normed, L->kv_dim, H, m->threads);
-    orc_gemv_q4(m->v, L->wv, m->normed, L->kv_dim, H, m->threads);
+    orc_round_bf16(m, m->normed, H);
+    orc_gemv_q4_w(m->q, L->wq, m->normed, L->q_dim, H, m->threads, m->act_bf16);
+    orc_gemv_q4_w(m->k, L->wk, m->normed, L->kv_dim, H, m->threads, m->act_bf16);
+    orc_gemv_q4_w(m->v, L->wv, m->normed, L->kv_dim, H, m->threads, m->act_bf16);
     orc_qkv_rope(m->q, m->k, m->v, L->q_norm, L->k_norm, L->k_cache, L->v_cache, c->kv_bf16,
                  c->num_q_heads, L->num_kv, L->head_dim, L->rot, L->k_eq_v, L->inv_freq, eps,
                  clock, slot, total_slots);
     orc_decode_attn(m->attn, m->q, L->k_cache, L->v_cache, m->slots, n, c->num_q_heads,
                     L->num_kv, L->head_dim, total_slots, c->attn_scale);
-    orc_gemv_q4(m->mlp, L->wo, m->attn, H, L->q_dim, m->threads);
+    orc_round_bf16(m, m->attn, L->q_dim);
+    orc_gemv_q4_w(m->mlp, L->wo, m->attn, H, L->q_dim, m->threads, m->act_bf16);
     if (c->has_post_norms) orc_rmsnorm(m->mlp, m->mlp, L->post_attn, H, eps);
     orc_add_rmsnorm(m->x, m->mlp, L->pre_ffn, m->normed, H, eps, 1.0f);
-    orc_gate_up_geglu_q4(m->act, L->wg, L->wu, m->normed, I, H, m->threads);
-    orc_gemv_q4(m->mlp, L->wd, m->act, H, I, m->threads);
+    orc_round_bf16(m, m->normed, H);
+    orc_geglu_w(m->act, L->wg, L->wu, m->normed, I, H, m->threads, m->act_bf16);
+    orc_round_bf16(m, m->act, I);
+    orc_gemv_q4_w(m->mlp, L->wd, m->act, H, I, m->threads, m->act_bf16);
     if (c->has_post_norms) orc_rmsnorm(m->mlp, m->mlp, L->post_ffn, H, eps);
     orc_add_rmsnorm(m->x, m->mlp, L->in_norm, m->normed, H, eps, L->layer_scalar);
   }

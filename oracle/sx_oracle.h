@@ -112,6 +112,7 @@ orc_ring *orc_model_ring(orc_model *m);
 uint32_t orc_model_forward(orc_model *m, const float *x_in, uint64_t clock, int want_logits,
                            float *logits_out, float *x_out);
 void orc_model_fill_kv(orc_model *m, uint64_t seed);
+void orc_model_set_act_bf16(orc_model *m, int on);
 void orc_model_synth_recall(orc_model *m, uint64_t clock, uint32_t n_recall, uint64_t seed);
 float *orc_model_kcache(orc_model *m, uint32_t layer);
 float *orc_model_vcache(orc_model *m, uint32_t layer);

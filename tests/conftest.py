@@ -48,3 +48,27 @@ def assert_close(got, want, atol=1e-3, rtol=1e-2, what="values"):
         f"{what}: {len(bad)} elements out of tolerance; worst err {err.max():.3e} "
         f"at {np.unravel_index(np.argmax(err - tol), err.shape)}"
     )
+
+
+def assert_close_bf16_operands(got, want, what="values", frac=1e-2, scale_tol=1e-3):
+    """The f32 tolerance for a path that multiplies bf16 operands (the batched prefill), with
+    an allowance for double rounding: the path and the checker each round their own f32 value
+    to bf16, and where those f32 values straddle a bf16 rounding boundary (a 1-ulp difference
+    before rounding) one operand differs by 2^-8, which attention at scale 1.0 can amplify.
+    A flip in a late layer moves many logits a little (measured on the 3-layer test model:
+    7 of 4096 logits past the elementwise bound, worst 6e-3 at a scale of 110, i.e. 6e-5 of
+    it), while a wrong operand, slot or head moves them by the order of the scale.  So: all
+    but a fraction `frac` of the elements must meet |a - b| <= 1e-3 + 1e-2 |b|, and every
+    element must lie within scale_tol of the vector's scale max |b|."""
+    import numpy as np
+
+    got = np.asarray(got, np.float64)
+    want = np.asarray(want, np.float64)
+    assert got.shape == want.shape, f"{what}: shape {got.shape} != {want.shape}"
+    err = np.abs(got - want)
+    bad = int(np.count_nonzero(err > 1e-3 + 1e-2 * np.abs(want)))
+    scale = float(np.abs(want).max())
+    assert bad <= max(1, int(frac * err.size)), (
+        f"{what}: {bad} of {err.size} elements out of the elementwise tolerance")
+    assert err.max() <= scale_tol * scale, (
+        f"{what}: worst err {err.max():.3e} above {scale_tol} of the scale {scale:.3e}")
