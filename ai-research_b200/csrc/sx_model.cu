@@ -759,6 +759,27 @@ SX_API sx_status sx_forward_token(sx_model *m, const float *x, uint32_t clock, u
   return st;
 }
 
+namespace {
+// the graph stepping sessions 0..n-1 (with host staging); recorded on first use
+sx_status batch_cmd(sx_model *m, uint32_t n, int lg, sx_cmd **out) {
+  if (n == 1) {
+    *out = m->cmd[lg][1];
+    return SX_OK;
+  }
+  if (!m->bcmd[n][lg]) {
+    M_TRY(sx_cmd_create(m->e, &m->bcmd[n][lg]));
+    sx_status st = record_forward_fused(m, m->bcmd[n][lg], lg != 0, true, false, n);
+    if (st != SX_OK) {
+      sx_cmd_destroy(m->bcmd[n][lg]);
+      m->bcmd[n][lg] = nullptr;
+      return st;
+    }
+  }
+  *out = m->bcmd[n][lg];
+  return SX_OK;
+}
+}  // namespace
+
 SX_API sx_status sx_decode_batch(sx_model *m, uint32_t n, const float *x, const uint32_t *clock,
                                  const uint32_t *slot, const uint32_t *active,
                                  const uint32_t *n_active, int want_logits, uint32_t *tokens,
@@ -779,20 +800,8 @@ SX_API sx_status sx_decode_batch(sx_model *m, uint32_t n, const float *x, const 
       return SX_ERR_INVALID;
     }
   const int lg = want_logits ? 1 : 0;
-  sx_cmd *cmd = m->cmd[lg][1];
-  if (n > 1) {
-    if (!m->bcmd[n][lg]) {
-      // first step with n sessions: record its graph (outside any capture of the caller's)
-      M_TRY(sx_cmd_create(m->e, &m->bcmd[n][lg]));
-      sx_status st = record_forward_fused(m, m->bcmd[n][lg], lg != 0, true, false, n);
-      if (st != SX_OK) {
-        sx_cmd_destroy(m->bcmd[n][lg]);
-        m->bcmd[n][lg] = nullptr;
-        return st;
-      }
-    }
-    cmd = m->bcmd[n][lg];
-  }
+  sx_cmd *cmd = nullptr;
+  M_TRY(batch_cmd(m, n, lg, &cmd));
   memcpy(m->h_x, x, 4ull * H * n);
   for (uint32_t i = 0; i < n; ++i) {
     if (n_active[i]) memcpy(m->h_slots + (size_t)i * TS, active + (size_t)i * TS, 4ull * n_active[i]);
@@ -807,6 +816,17 @@ SX_API sx_status sx_decode_batch(sx_model *m, uint32_t n, const float *x, const 
   if (st == SX_OK && want_logits && logits_out)
     st = sx_buffer_read(m->logits, 0, logits_out, 4ull * m->V * n);
   return st;
+}
+
+SX_API sx_status sx_model_launch_batch(sx_model *m, uint32_t n, int want_logits) {
+  if (!m || n == 0 || n > m->S) {
+    sx_host_set_error("model_launch_batch: null model or %u sessions (the model holds %u)", n,
+                      m ? m->S : 0);
+    return SX_ERR_INVALID;
+  }
+  sx_cmd *cmd = nullptr;
+  M_TRY(batch_cmd(m, n, want_logits ? 1 : 0, &cmd));
+  return sx_host_cuda_status(cudaGraphLaunch(cmd->exec, m->e->stream), "graph launch");
 }
 
 SX_API sx_status sx_model_launch(sx_model *m, int want_logits) {

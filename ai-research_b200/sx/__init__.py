@@ -245,6 +245,7 @@ _SIGS = {
     "sx_model_config_bytes": (_U32, []),
     "sx_decode_batch": (_S, [_P, _U32, _P, _P, _P, _P, _P, _I, _P, _P]),
     "sx_prefill_batch": (_S, [_P, _U32, _P, _P, _P, _P, _P, _P, _U32, _P, _P, _P]),
+    "sx_model_launch_batch": (_S, [_P, _U32, _I]),
     "sx_forward_token": (_S, [_P, _P, _U32, _U32, _P, _U32, _I, _P, _P]),
     "sx_model_launch": (_S, [_P, _I]),
     "sx_model_get_io": (_S, [_P, C.POINTER(ModelIO)]),
@@ -669,45 +670,60 @@ class Model:
                                      None if logits_out is None else logits_out.ctypes.data))
         return int(tok.value)
 
-    def prefill_batch(self, prompts, rings, start_clocks, sessions=None,
-                      logits_out: np.ndarray | None = None) -> np.ndarray:
-        """Prefill the prompts of several sessions in one pass (sx_prefill_batch).
-
-        prompts[i]: embedding rows [L_i][hidden] of session sessions[i] (default i), whose
-        ring (sx.Ring, updated here) is at start_clocks[i]; token j gets clock
-        start_clocks[i] + j, its slot and active list from the ring.  Returns the greedy
-        token after each prompt (logits_out, optional: [len(prompts)][vocab])."""
+    def prefill_plan(self, prompts, rings, start_clocks, sessions=None) -> dict:
+        """Per-token inputs of sx_prefill_batch for several sessions' prompts: prompts[i] are
+        the embedding rows [L_i][hidden] of session sessions[i] (default i), whose ring
+        (sx.Ring, advanced here) is at start_clocks[i]; token j gets clock start_clocks[i] + j
+        and its slot and active list from the ring, as forwardToken would."""
         sessions = list(range(len(prompts))) if sessions is None else list(sessions)
         ts = self.total_slots
-        rows, sess, clk, slt, lists, cnt, out_rows = [], [], [], [], [], [], []
+        T = sum(len(p) for p in prompts)
+        x = np.empty((T, self.cfg.hidden_size), np.float32)
+        sess, clk, slt, cnt = (np.empty(T, np.uint32) for _ in range(4))
+        act = np.zeros((T, ts), np.uint32)
+        out_rows = []
+        t = 0
         for i, (xs, ring, c0) in enumerate(zip(prompts, rings, start_clocks)):
             for j in range(len(xs)):
                 c = c0 + j
-                sl = ring.activate_slot(0, c)
+                slt[t] = ring.activate_slot(0, c)
                 a = ring.get_active_slots(0, c)
-                row = np.zeros(ts, np.uint32)
-                row[: len(a)] = a
-                rows.append(xs[j])
-                sess.append(sessions[i])
-                clk.append(c)
-                slt.append(sl)
-                lists.append(row)
-                cnt.append(len(a))
-            out_rows.append(len(rows) - 1)
-        T = len(rows)
-        x = np.ascontiguousarray(np.stack(rows), np.float32)
-        u = lambda v: np.ascontiguousarray(v, np.uint32)
-        sess, clk, slt, cnt, orow = u(sess), u(clk), u(slt), u(cnt), u(out_rows)
-        act = u(np.stack(lists))
-        toks = np.zeros(len(out_rows), np.uint32)
-        check(lib().sx_prefill_batch(self.h, T, x.ctypes.data, sess.ctypes.data, clk.ctypes.data,
-                                     slt.ctypes.data, act.ctypes.data, cnt.ctypes.data,
-                                     len(orow), orow.ctypes.data, toks.ctypes.data,
+                act[t, : len(a)] = a
+                cnt[t] = len(a)
+                x[t] = xs[j]
+                sess[t] = sessions[i]
+                clk[t] = c
+                t += 1
+            out_rows.append(t - 1)
+        return dict(x=x, session=sess, clock=clk, slot=slt, active=act, n_active=cnt,
+                    out_rows=np.asarray(out_rows, np.uint32))
+
+    def prefill_run(self, plan: dict, logits_out: np.ndarray | None = None) -> np.ndarray:
+        """sx_prefill_batch on a plan from prefill_plan; returns the greedy token after each
+        prompt (logits_out, optional: [prompts][vocab])."""
+        p = plan
+        toks = np.zeros(len(p["out_rows"]), np.uint32)
+        check(lib().sx_prefill_batch(self.h, len(p["x"]), p["x"].ctypes.data,
+                                     p["session"].ctypes.data, p["clock"].ctypes.data,
+                                     p["slot"].ctypes.data, p["active"].ctypes.data,
+                                     p["n_active"].ctypes.data, len(p["out_rows"]),
+                                     p["out_rows"].ctypes.data, toks.ctypes.data,
                                      None if logits_out is None else logits_out.ctypes.data))
         return toks
 
+    def prefill_batch(self, prompts, rings, start_clocks, sessions=None,
+                      logits_out: np.ndarray | None = None) -> np.ndarray:
+        """Prefill the prompts of several sessions in one pass (sx_prefill_batch); see
+        prefill_plan for the arguments."""
+        return self.prefill_run(self.prefill_plan(prompts, rings, start_clocks, sessions),
+                                logits_out)
+
     def launch(self, want_logits: bool = True) -> None:
         check(lib().sx_model_launch(self.h, int(want_logits)))
+
+    def launch_batch(self, n: int, want_logits: bool = True) -> None:
+        """Replay the n-session step of the last decode_batch on the engine stream."""
+        check(lib().sx_model_launch_batch(self.h, n, int(want_logits)))
 
     def io(self) -> ModelIO:
         io = ModelIO()

@@ -323,6 +323,10 @@ SX_API sx_status sx_prefill_batch(sx_model *m, uint32_t T, const float *x,
                                   const uint32_t *out_rows, uint32_t *tokens, float *logits_out);
 /* Device-resident replay: inputs already in the model's device buffers (sx_model_io). */
 SX_API sx_status sx_model_launch(sx_model *m, int want_logits);
+/* Asynchronous replay of the n-session step of sx_decode_batch on the engine stream, from
+ * the inputs its last call staged (benchmarks: the device time of a batched step without the
+ * host's per-step work).  The first use of an n records its graph (outside stream capture). */
+SX_API sx_status sx_model_launch_batch(sx_model *m, uint32_t n, int want_logits);
 typedef struct {
   float *x;            /* device f32[hidden]                  */
   uint32_t *slots;     /* device u32[total_slots]             */
