@@ -93,7 +93,7 @@ SX_DEV void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
 }
 SX_DEV void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory"); }
 
-// 2-D tiled TMA load of box (x = k, y = token row) into shared memory, no multicast
+// 2-D tiled TMA load of box (x = k, y = token row) into this CTA's own shared memory
 SX_DEV void tma_load_2d(uint32_t dst, const CUtensorMap *map, int32_t x, int32_t y, uint32_t bar) {
   asm volatile(
       "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], "

@@ -1,5 +1,6 @@
-// sx_tp.cu -- tensor-parallel decode support: the shard plan, the NCCL communicator and the
-// on-device merge of the ranks' LM-head argmax candidates.
+// sx_tp.cu -- tensor-parallel decode support: the shard plan, the communicator (NCCL plus a
+// one-shot peer-to-peer all-reduce over NVLink), and the on-device merge of the ranks' LM-head
+// argmax candidates.
 //
 // NCCL is opened at run time (dlopen "libnccl.so.2"), only when a communicator is made: a
 // process that already loaded torch's NCCL reuses that library, and a single-GPU process never
@@ -9,15 +10,34 @@
 
 #include <cstring>
 #include <mutex>
+#include <vector>
 
 #include "sx_common.cuh"
 #include "sx_host.h"
 #include "sx_internal.h"
 
+namespace sx {
+// One-shot peer all-reduce workspace, one per rank, opened by every peer through CUDA IPC:
+// [flags: 8 u32, padded to 256 B][data: 2 parities x 8 source ranks x kP2pMaxCount f32].
+constexpr uint32_t kP2pMaxRanks = 8;
+constexpr uint32_t kP2pMaxCount = 16384;  // floats per all-reduce (hidden sizes up to 16384)
+constexpr size_t kP2pFlagBytes = 256;
+constexpr size_t kP2pBytes = kP2pFlagBytes + sizeof(float) * 2ull * kP2pMaxRanks * kP2pMaxCount;
+struct P2pArgs {
+  uint8_t *ws[kP2pMaxRanks];  // every rank's workspace, mapped into this process (own: local)
+  uint32_t nranks, rank;
+  uint32_t *gen;              // this rank's call counter (device), equal on all ranks
+  uint32_t *err;
+};
+}  // namespace sx
+
 struct sx_comm {
   sx_engine *e = nullptr;
   ncclComm_t comm = nullptr;
   uint32_t nranks = 1, rank = 0;
+  bool p2p = false;  // all-reduce with the peer kernel (else NCCL)
+  sx::P2pArgs pa{};
+  uint8_t *ws = nullptr;
 };
 
 namespace {
@@ -127,6 +147,139 @@ SX_API sx_status sx_tp_shard_plan(const sx_model_config *cfg, sx_tp_shard *out) 
 }
 
 // ---------------------------------------------------------------------------------------
+namespace {
+
+// One-shot all-reduce over peer memory (one CTA per rank; the vector is a hidden state of at
+// most kP2pMaxCount floats, so the exchange is latency-bound and one CTA keeps every rank's
+// order of operations simple).  Call g (a counter kept on each device; every rank makes the
+// same calls in the same order) uses data parity g & 1:
+//   1. store this rank's vector into data[parity][rank] of every rank's workspace (peer stores
+//      over NVLink), fence system-wide, then release flags[rank] = g on every rank;
+//   2. wait (bounded) until this rank's flags[r] >= g for all r;
+//   3. out = sum over r = 0..n-1 of data[parity][r], in rank order -- the same bits on every rank.
+// Two parities suffice: a rank can only start call g + 2 after every rank has released g + 1,
+// i.e. has finished reading the data of call g.  A wait that runs out records
+// kDevWaitTimeout and the kernel finishes with what it has (no hang).
+SX_DEV void st_release_sys(uint32_t *p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;\n" ::"l"(p), "r"(v) : "memory");
+}
+SX_DEV uint32_t ld_acquire_sys(const uint32_t *p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];\n" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__global__ void __launch_bounds__(512) p2p_allreduce_kernel(float *buf, uint32_t count,
+                                                            sx::P2pArgs a) {
+  __shared__ uint32_t g_s, late;
+  const uint32_t tid = threadIdx.x;
+  if (tid == 0) {
+    g_s = *a.gen + 1;
+    *a.gen = g_s;
+    late = 0;
+  }
+  __syncthreads();
+  const uint32_t g = g_s, par = g & 1;
+  auto data = [&](uint8_t *ws, uint32_t src) {
+    return reinterpret_cast<float *>(ws + sx::kP2pFlagBytes) +
+           ((size_t)par * sx::kP2pMaxRanks + src) * sx::kP2pMaxCount;
+  };
+  auto flags = [&](uint8_t *ws) { return reinterpret_cast<uint32_t *>(ws); };
+  // 1. push
+  const uint32_t n4 = count / 4;
+  for (uint32_t r = 0; r < a.nranks; ++r) {
+    float *dst = data(a.ws[r], a.rank);
+    const float4 *src = reinterpret_cast<const float4 *>(buf);
+    for (uint32_t i = tid; i < n4; i += blockDim.x) reinterpret_cast<float4 *>(dst)[i] = src[i];
+    for (uint32_t i = 4 * n4 + tid; i < count; i += blockDim.x) dst[i] = buf[i];
+  }
+  __threadfence_system();
+  __syncthreads();
+  if (tid < a.nranks) st_release_sys(flags(a.ws[tid]) + a.rank, g);
+  // 2. wait for every rank's data of call g
+  if (tid < a.nranks) {
+    const uint32_t *f = flags(a.ws[a.rank]) + tid;
+    uint32_t spins = 0;
+    while ((int32_t)(ld_acquire_sys(f) - g) < 0) {
+      if (++spins > (1u << 24)) {  // ~1 s of polling: a rank that never came
+        atomicOr(&late, 1u);
+        break;
+      }
+      __nanosleep(32);
+    }
+  }
+  __syncthreads();
+  if (late && tid == 0) raise_error(a.err, sx::kDevWaitTimeout);
+  // 3. sum in rank order
+  const float *mine = data(a.ws[a.rank], 0);
+  for (uint32_t i = tid; i < count; i += blockDim.x) {
+    float s = 0.0f;
+    for (uint32_t r = 0; r < a.nranks; ++r) s += mine[(size_t)r * sx::kP2pMaxCount + i];
+    buf[i] = s;
+  }
+}
+
+// Maps every rank's workspace into this process: handles exchanged with one NCCL all-gather.
+sx_status p2p_setup(const NcclApi &api, sx_comm *c) {
+  if (c->nranks > sx::kP2pMaxRanks) return SX_ERR_UNSUPPORTED;
+  cudaStream_t s = c->e->stream;
+  void *ws = nullptr, *gen = nullptr, *hbuf = nullptr;
+  sx_status st = sx_host_cuda_status(cudaMalloc(&ws, sx::kP2pBytes), "peer workspace");
+  if (st == SX_OK) st = sx_host_cuda_status(cudaMemset(ws, 0, sx::kP2pBytes), "peer workspace");
+  if (st == SX_OK) st = sx_host_cuda_status(cudaMalloc(&gen, 256), "peer counter");
+  if (st == SX_OK) st = sx_host_cuda_status(cudaMemset(gen, 0, 256), "peer counter");
+  if (st == SX_OK)
+    st = sx_host_cuda_status(cudaMalloc(&hbuf, sizeof(cudaIpcMemHandle_t) * c->nranks),
+                             "ipc handle exchange");
+  cudaIpcMemHandle_t mine{};
+  std::vector<cudaIpcMemHandle_t> all(c->nranks);
+  if (st == SX_OK) st = sx_host_cuda_status(cudaIpcGetMemHandle(&mine, ws), "cudaIpcGetMemHandle");
+  if (st == SX_OK)
+    st = sx_host_cuda_status(
+        cudaMemcpy(static_cast<uint8_t *>(hbuf) + sizeof(mine) * c->rank, &mine, sizeof(mine),
+                   cudaMemcpyHostToDevice),
+        "ipc handle upload");
+  if (st == SX_OK)
+    st = nccl_status(api,
+                     api.all_gather(static_cast<uint8_t *>(hbuf) + sizeof(mine) * c->rank, hbuf,
+                                    sizeof(mine), ncclUint8, c->comm, s),
+                     "ncclAllGather (ipc handles)");
+  if (st == SX_OK) st = sx_host_cuda_status(cudaStreamSynchronize(s), "ipc handle exchange");
+  if (st == SX_OK)
+    st = sx_host_cuda_status(cudaMemcpy(all.data(), hbuf, sizeof(mine) * c->nranks,
+                                        cudaMemcpyDeviceToHost),
+                             "ipc handle download");
+  if (hbuf) cudaFree(hbuf);
+  c->ws = static_cast<uint8_t *>(ws);
+  c->pa.gen = static_cast<uint32_t *>(gen);
+  for (uint32_t r = 0; r < c->nranks && st == SX_OK; ++r) {
+    if (r == c->rank) {
+      c->pa.ws[r] = static_cast<uint8_t *>(ws);
+      continue;
+    }
+    void *p = nullptr;
+    st = sx_host_cuda_status(cudaIpcOpenMemHandle(&p, all[r], cudaIpcMemLazyEnablePeerAccess),
+                             "cudaIpcOpenMemHandle");
+    c->pa.ws[r] = static_cast<uint8_t *>(p);
+  }
+  c->pa.nranks = c->nranks;
+  c->pa.rank = c->rank;
+  c->pa.err = c->e->err_dev;
+  return st;
+}
+
+void p2p_teardown(sx_comm *c) {
+  for (uint32_t r = 0; r < c->nranks && r < sx::kP2pMaxRanks; ++r)
+    if (r != c->rank && c->pa.ws[r]) cudaIpcCloseMemHandle(c->pa.ws[r]);
+  if (c->ws) cudaFree(c->ws);
+  if (c->pa.gen) cudaFree(c->pa.gen);
+  c->ws = nullptr;
+  c->pa = sx::P2pArgs{};
+  c->p2p = false;
+}
+
+}  // namespace
+
 // communicator
 SX_API sx_status sx_comm_unique_id(uint8_t id[128]) {
   if (!id) {
@@ -164,17 +317,36 @@ SX_API sx_status sx_comm_create(sx_engine *e, const uint8_t id[128], uint32_t nr
     delete c;
     return st;
   }
+  // map the peer all-reduce's workspaces (collective: every rank does it here); NCCL stays the
+  // all-reduce until sx_comm_set_allreduce(c, 0) selects the peer kernel
+  if (nranks > 1 && p2p_setup(api, c) != SX_OK) p2p_teardown(c);
   *out = c;
   return SX_OK;
 }
 
+SX_API sx_status sx_comm_set_allreduce(sx_comm *c, int use_nccl) {
+  if (!c) {
+    sx_host_set_error("comm: null");
+    return SX_ERR_INVALID;
+  }
+  if (!use_nccl && !c->ws && c->nranks > 1) {
+    sx_host_set_error("comm: the peer all-reduce is unavailable (its workspace could not be "
+                      "mapped on every rank)");
+    return SX_ERR_UNSUPPORTED;
+  }
+  c->p2p = !use_nccl && c->nranks > 1;
+  return SX_OK;
+}
+
+SX_API int sx_comm_allreduce_is_nccl(const sx_comm *c) { return c && c->p2p ? 0 : 1; }
+
 SX_API void sx_comm_destroy(sx_comm *c) {
   if (!c) return;
   NcclApi api;
-  if (c->comm && nccl_api(&api)) {
-    cudaSetDevice(c->e->device);
-    api.comm_destroy(c->comm);
-  }
+  cudaSetDevice(c->e->device);
+  cudaStreamSynchronize(c->e->stream);
+  p2p_teardown(c);
+  if (c->comm && nccl_api(&api)) api.comm_destroy(c->comm);
   delete c;
 }
 
@@ -184,6 +356,10 @@ uint32_t sx_host_comm_ranks(const sx_comm *c) { return c ? c->nranks : 1; }
 uint32_t sx_host_comm_rank(const sx_comm *c) { return c ? c->rank : 0; }
 
 sx_status sx_host_allreduce(sx_comm *c, float *buf, size_t count, cudaStream_t s) {
+  if (c && c->p2p && count <= sx::kP2pMaxCount && ((uintptr_t)buf & 15) == 0) {
+    p2p_allreduce_kernel<<<1, 512, 0, s>>>(buf, (uint32_t)count, c->pa);
+    return sx_host_cuda_status(cudaGetLastError(), "peer all-reduce");
+  }
   NcclApi api;
   if (!c || !nccl_api(&api)) {
     if (!c) sx_host_set_error("all-reduce: no communicator");

@@ -238,6 +238,8 @@ _SIGS = {
     "sx_comm_unique_id": (_S, [C.c_char_p]),
     "sx_comm_create": (_S, [_P, C.c_char_p, _U32, _U32, C.POINTER(_P)]),
     "sx_comm_destroy": (None, [_P]),
+    "sx_comm_set_allreduce": (_S, [_P, _I]),
+    "sx_comm_allreduce_is_nccl": (_I, [_P]),
     "sx_model_destroy": (None, [_P]),
     "sx_model_synth_weights": (_S, [_P, _U64]),
     "sx_model_fill_kv": (_S, [_P, _U64]),
@@ -597,6 +599,14 @@ class Comm:
         self.h = h
         self.engine = engine
         self.nranks, self.rank = nranks, rank
+
+    def set_allreduce(self, use_nccl: bool) -> None:
+        """NCCL or the one-shot peer kernel for the o / down all-reduces (before the model)."""
+        check(lib().sx_comm_set_allreduce(self.h, int(use_nccl)))
+
+    @property
+    def allreduce_is_nccl(self) -> bool:
+        return bool(lib().sx_comm_allreduce_is_nccl(self.h))
 
     def close(self):
         if getattr(self, "h", None):

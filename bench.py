@@ -57,6 +57,8 @@ def parse():
                     help="profiling case: launch one kernel of the step standalone "
                          "(--launches times) on synthetic data and exit; prints no JSON line")
     ap.add_argument("--launches", type=int, default=3)
+    ap.add_argument("--allreduce", choices=["peer", "nccl"], default="nccl",
+                    help="tensor parallel (N > 1): NCCL or the one-shot peer all-reduce")
     return ap.parse_args()
 
 
@@ -423,6 +425,7 @@ def main():
         obj = [sx.comm_unique_id() if rank == 0 else None]
         dist.broadcast_object_list(obj, src=0)
         comm = sx.Comm(eng, obj[0], world, rank)
+        comm.set_allreduce(args.allreduce == "nccl")
         cfgd.update(tp_size=world, tp_rank=rank, reference_graph=0)
     stream = torch.cuda.ExternalStream(eng.stream)
     model = sx.Model(eng, sx.model_config(**cfgd), comm)
@@ -566,7 +569,8 @@ def main():
             "workload": f"c4: 12B-shape Q4_0 greedy decode, batch 1, {args.layers} layers, H 3840, "
                         "16q/8kv x 256, I 15360, vocab 262144 (Q8_0 head), 640 live ring slots",
             "global_batch": 1, "seq_len": total_slots,
-            "parallelism": f"tp{world} (NCCL all-reduce x2 per layer, vocab-parallel head)"
+            "parallelism": f"tp{world} ({'NCCL' if args.allreduce == 'nccl' else 'one-shot peer'} "
+                           f"all-reduce x2 per layer, vocab-parallel head)"
                            if world > 1 else "single",
             "graph": ("one persistent cooperative launch per token"
                       if cfgd["reference_graph"] == 2

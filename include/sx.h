@@ -370,6 +370,13 @@ SX_API sx_status sx_comm_unique_id(uint8_t id[128]);
 SX_API sx_status sx_comm_create(sx_engine *e, const uint8_t id[128], uint32_t nranks,
                                 uint32_t rank, sx_comm **out);
 SX_API void sx_comm_destroy(sx_comm *c);
+/* The all-reduce of the row-parallel o / down outputs: NCCL, or (use_nccl = 0) a one-shot
+ * peer-to-peer kernel over NVLink -- each rank stores its vector into every rank's workspace
+ * (mapped through CUDA IPC when the communicator is made), releases a flag, waits for all the
+ * flags with a bounded poll and sums in rank order.  Choose before creating the model (its
+ * graphs capture the choice).  The reference has no multi-GPU path. */
+SX_API sx_status sx_comm_set_allreduce(sx_comm *c, int use_nccl);
+SX_API int sx_comm_allreduce_is_nccl(const sx_comm *c);
 /* sx_model_create for a tensor-parallel rank: cfg->tp_size / tp_rank must match the
  * communicator; cfg->reference_graph must be 0. */
 SX_API sx_status sx_model_create_tp(sx_engine *e, const sx_model_config *cfg, sx_comm *comm,

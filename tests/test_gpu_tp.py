@@ -1,7 +1,7 @@
 """Tensor-parallel decode on 2 GPUs (skipped with fewer): two ranks, each with its engine,
-NCCL communicator and model shard, decode greedily; both ranks agree on every token, which
+communicator and model shard, decode greedily; both ranks agree on every token, which
 matches the one-process CPU checker, and the concatenated logits shards stay within the
-path's tolerance."""
+path's tolerance.  Run with NCCL and with the one-shot peer all-reduce."""
 import os
 import socket
 
@@ -19,7 +19,7 @@ torch = pytest.importorskip("torch")
 SEED, STEPS, START = 11, 6, 40
 
 
-def _rank(rank, world, port, cfg):
+def _rank(rank, world, port, cfg, allreduce="nccl"):
     import torch.distributed as dist
 
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
@@ -29,6 +29,8 @@ def _rank(rank, world, port, cfg):
     obj = [sx.comm_unique_id() if rank == 0 else None]
     dist.broadcast_object_list(obj, src=0)
     comm = sx.Comm(eng, obj[0], world, rank)
+    comm.set_allreduce(allreduce == "nccl")
+    assert comm.allreduce_is_nccl == (allreduce == "nccl")
     model = sx.Model(eng, sx.model_config(**cfg, tp_size=world, tp_rank=rank), comm)
     try:
         model.synth_weights(SEED)
@@ -75,8 +77,9 @@ def _free_port():
 
 @pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2,
                     reason="tensor parallelism needs 2 GPUs")
+@pytest.mark.parametrize("allreduce", ["nccl", "peer"])
 @pytest.mark.parametrize("shape", ["tiny", "12b_width"])
-def test_tensor_parallel_decode_two_gpus(shape):
+def test_tensor_parallel_decode_two_gpus(shape, allreduce):
     import torch.multiprocessing as mp
 
     if shape == "tiny":
@@ -87,4 +90,4 @@ def test_tensor_parallel_decode_two_gpus(shape):
                        head_dim=256, global_head_dim=256, num_anchors=32, window_size=512,
                        num_recall=96, full_every=2)
     cfg.pop("reference_graph", None)
-    mp.spawn(_rank, args=(2, _free_port(), cfg), nprocs=2, join=True)
+    mp.spawn(_rank, args=(2, _free_port(), cfg, allreduce), nprocs=2, join=True)
