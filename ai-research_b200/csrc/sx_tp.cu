@@ -173,6 +173,10 @@ __global__ void __launch_bounds__(512) p2p_allreduce_kernel(float *buf, uint32_t
                                                             sx::P2pArgs a) {
   __shared__ uint32_t g_s, late;
   const uint32_t tid = threadIdx.x;
+  // programmatic dependent launch: the next kernel may become resident (and stream its first
+  // weight chunks) while this one exchanges; it waits for our completion before reading buf
+  sx::pdl_launch_dependents();
+  sx::pdl_wait();  // the producer of buf is complete
   if (tid == 0) {
     g_s = *a.gen + 1;
     *a.gen = g_s;
@@ -357,8 +361,18 @@ uint32_t sx_host_comm_rank(const sx_comm *c) { return c ? c->rank : 0; }
 
 sx_status sx_host_allreduce(sx_comm *c, float *buf, size_t count, cudaStream_t s) {
   if (c && c->p2p && count <= sx::kP2pMaxCount && ((uintptr_t)buf & 15) == 0) {
-    p2p_allreduce_kernel<<<1, 512, 0, s>>>(buf, (uint32_t)count, c->pa);
-    return sx_host_cuda_status(cudaGetLastError(), "peer all-reduce");
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(1);
+    cfg.blockDim = dim3(512);
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return sx_host_cuda_status(
+        cudaLaunchKernelEx(&cfg, p2p_allreduce_kernel, buf, (uint32_t)count, c->pa),
+        "peer all-reduce");
   }
   NcclApi api;
   if (!c || !nccl_api(&api)) {
