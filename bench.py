@@ -57,8 +57,9 @@ def parse():
                     help="profiling case: launch one kernel of the step standalone "
                          "(--launches times) on synthetic data and exit; prints no JSON line")
     ap.add_argument("--launches", type=int, default=3)
-    ap.add_argument("--allreduce", choices=["peer", "nccl"], default="nccl",
-                    help="tensor parallel (N > 1): NCCL or the one-shot peer all-reduce")
+    ap.add_argument("--allreduce", choices=["peer", "nccl"], default="peer",
+                    help="tensor parallel (N > 1): the one-shot peer all-reduce (NCCL when its "
+                         "workspaces cannot be mapped) or NCCL")
     return ap.parse_args()
 
 
@@ -425,7 +426,10 @@ def main():
         obj = [sx.comm_unique_id() if rank == 0 else None]
         dist.broadcast_object_list(obj, src=0)
         comm = sx.Comm(eng, obj[0], world, rank)
-        comm.set_allreduce(args.allreduce == "nccl")
+        try:
+            comm.set_allreduce(args.allreduce == "nccl")
+        except sx.SxError:
+            args.allreduce = "nccl"  # peer workspaces unavailable: every rank keeps NCCL
         cfgd.update(tp_size=world, tp_rank=rank, reference_graph=0)
     stream = torch.cuda.ExternalStream(eng.stream)
     model = sx.Model(eng, sx.model_config(**cfgd), comm)
