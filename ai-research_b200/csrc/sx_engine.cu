@@ -698,6 +698,41 @@ SX_API sx_status sx_buffer_repack_device(sx_buffer *dst, const void *ref_words_d
   return SX_OK;
 }
 
+SX_API sx_status sx_dispatch_quantize(sx_engine *e, sx_quant_mode mode, const void *bf16_device,
+                                     uint32_t *ref_words_device, uint32_t rows, uint32_t cols) {
+  SX_CHECK_ARG(e && bf16_device && ref_words_device, "quantize: null argument");
+  SX_CHECK_ARG(mode == SX_QUANT_Q4 || mode == SX_QUANT_Q8, "quantize: mode must be Q4 or Q8");
+  SX_CHECK_ARG(rows > 0 && cols > 0 && cols % 32 == 0, "quantize: cols must be a multiple of 32");
+  SX_CHECK_ARG((uintptr_t)bf16_device % 16 == 0, "quantize: the bf16 matrix must be 16-byte aligned");
+  SX_TRY_CUDA(cudaSetDevice(e->device), "cudaSetDevice");
+  SX_TRY_CUDA(sx::launch_quantize(qt_of(mode), bf16_device, ref_words_device,
+                                  (uint64_t)rows * (cols / 32), e->stream),
+              "quantize launch");
+  return SX_OK;
+}
+
+SX_API sx_status sx_buffer_quantize_device(sx_buffer *dst, const void *bf16_device, uint32_t rows,
+                                           uint32_t cols, sx_quant_mode mode) {
+  SX_CHECK_ARG(dst && bf16_device, "quantize_device: null argument");
+  sx_engine *e = dst->e;
+  SX_TRY_CUDA(cudaSetDevice(e->device), "cudaSetDevice");
+  SX_CHECK_ARG(mode == SX_QUANT_Q4 || mode == SX_QUANT_Q8, "quantize_device: mode must be Q4 or Q8");
+  SX_CHECK_ARG(rows > 0 && cols > 0 && cols % 32 == 0,
+               "quantize_device: cols must be a multiple of 32");
+  SX_CHECK_ARG(sx_packed_bytes(rows, cols, mode) <= dst->bytes,
+               "quantize_device: destination holds %llu B, need %llu",
+               (unsigned long long)dst->bytes,
+               (unsigned long long)sx_packed_bytes(rows, cols, mode));
+  const uint64_t bytes = (uint64_t)rows * sx_quantized_row_words(cols, mode) * 4;
+  void *tmp = nullptr;
+  SX_TRY_CUDA(cudaMalloc(&tmp, bytes), "quantize staging");
+  sx_status st = sx_dispatch_quantize(e, mode, bf16_device, (uint32_t *)tmp, rows, cols);
+  if (st == SX_OK) st = sx_buffer_repack_device(dst, tmp, rows, cols, mode);
+  if (st == SX_OK) st = cuda_status(cudaStreamSynchronize(e->stream), "quantize sync");
+  cudaFree(tmp);
+  return st;
+}
+
 SX_API sx_status sx_buffer_upload_weights(sx_buffer *dst, const uint32_t *ref_words,
                                           uint32_t rows, uint32_t cols, sx_quant_mode mode) {
   SX_CHECK_ARG(dst && ref_words, "upload_weights: null argument");

@@ -66,6 +66,9 @@ size_t gemv_workers(int num_sms);
 constexpr uint32_t kGemvPrologueMaxK = 4096;  // fused norm prologues hold K / 512 <= 8 per thread
 constexpr uint32_t kMaxGemvTiles = 262144;
 
+// quantizeMatrix on the device: nblocks 32-value bf16 blocks -> reference block words
+cudaError_t launch_quantize(int qt, const void *bf16, uint32_t *ref, uint64_t nblocks,
+                            cudaStream_t s);
 cudaError_t launch_repack(int qt, const uint32_t *ref, void *packed, uint32_t m, uint32_t k,
                           cudaStream_t s);
 cudaError_t launch_unpack_q4(const void *packed, float *out, uint32_t m, uint32_t k,

@@ -170,6 +170,61 @@ __global__ void fill_kv_kernel(void *k_cache, void *v_cache, int kv_bf16, uint32
   }
 }
 
+// quantizeRowQ4_0 / quantizeRowQ8_0 (quant.zig:18-90) on the device, one thread per 32-value
+// block of a row-major bf16 matrix, the reference block layout out: f32 d = amax / 7 (Q8:
+// amax / 127), then q = round_half_away(v * (7 / amax)) clamped to [-8, 7] and stored as
+// nibble n = q + 8 of word w for element 8 w + n (Q8: clamp [-128, 127], byte k of word w for
+// element 4 w + k).  IEEE-rounded division and product, C roundf: the words equal the CPU
+// quantiser's bit for bit.
+template <int QT>
+__global__ void quantize_kernel(const uint16_t *src, uint32_t *dst, uint64_t nblocks) {
+  constexpr float kMax = QT == 4 ? 7.0f : 127.0f;
+  constexpr int kWords = QT == 4 ? 5 : 9;
+  for (uint64_t b = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; b < nblocks;
+       b += (uint64_t)gridDim.x * blockDim.x) {
+    const uint4 *s4 = reinterpret_cast<const uint4 *>(src + b * 32);
+    float v[32];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const uint4 u = s4[i];
+      const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        v[8 * i + 2 * j] = __uint_as_float(w[j] << 16);
+        v[8 * i + 2 * j + 1] = __uint_as_float(w[j] & 0xFFFF0000u);
+      }
+    }
+    float amax = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+      const float a = fabsf(v[i]);
+      if (a > amax) amax = a;
+    }
+    const float id = amax > 0.0f ? __fdiv_rn(kMax, amax) : 0.0f;
+    uint32_t out[kWords];
+    out[0] = __float_as_uint(__fdiv_rn(amax, kMax));
+#pragma unroll
+    for (int w = 0; w < kWords - 1; ++w) {
+      uint32_t word = 0;
+#pragma unroll
+      for (int k = 0; k < (QT == 4 ? 8 : 4); ++k) {
+        int q = (int)roundf(__fmul_rn(v[w * (QT == 4 ? 8 : 4) + k], id));
+        if (QT == 4) {
+          q = q < -8 ? -8 : (q > 7 ? 7 : q);
+          word |= (uint32_t)(q + 8) << (4 * k);
+        } else {
+          q = q < -128 ? -128 : (q > 127 ? 127 : q);
+          word |= (uint32_t)(uint8_t)(int8_t)q << (8 * k);
+        }
+      }
+      out[1 + w] = word;
+    }
+    uint32_t *o = dst + b * kWords;
+#pragma unroll
+    for (int w = 0; w < kWords; ++w) o[w] = out[w];
+  }
+}
+
 uint32_t grid_for(uint64_t items, uint32_t threads) {
   uint64_t g = (items + threads - 1) / threads;
   if (g > 65535u * 16) g = 65535u * 16;
@@ -221,6 +276,18 @@ cudaError_t launch_fill_kv(void *k_cache, void *v_cache, int kv_bf16, uint32_t r
                            uint32_t heads_global) {
   fill_kv_kernel<<<grid_for(rows, 128), 128, 0, s>>>(k_cache, v_cache, kv_bf16, rows, head_dim,
                                                      eps, seed, layer, heads, head0, heads_global);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_quantize(int qt, const void *bf16, uint32_t *ref, uint64_t nblocks,
+                            cudaStream_t s) {
+  if (nblocks == 0) return cudaSuccess;
+  if (qt == 4)
+    quantize_kernel<4><<<grid_for(nblocks, 256), 256, 0, s>>>(static_cast<const uint16_t *>(bf16),
+                                                               ref, nblocks);
+  else
+    quantize_kernel<8><<<grid_for(nblocks, 256), 256, 0, s>>>(static_cast<const uint16_t *>(bf16),
+                                                               ref, nblocks);
   return cudaGetLastError();
 }
 

@@ -196,6 +196,8 @@ _SIGS = {
     "sx_buffer_read": (_S, [_P, _U64, _P, _U64]),
     "sx_buffer_upload_weights": (_S, [_P, _P, _U32, _U32, _I]),
     "sx_buffer_repack_device": (_S, [_P, _P, _U32, _U32, _I]),
+    "sx_buffer_quantize_device": (_S, [_P, _P, _U32, _U32, _I]),
+    "sx_dispatch_quantize": (_S, [_P, _I, _P, _P, _U32, _U32]),
     "sx_set_create": (_S, [_P, _P, _U32, C.POINTER(_P)]),
     "sx_set_destroy": (None, [_P]),
     "sx_cmd_create": (_S, [_P, C.POINTER(_P)]),
@@ -450,6 +452,10 @@ class Engine:
         check(lib().sx_submit(self.h, cmd.h, timeout_ns))
 
     # --- immediate mode (device pointers: torch tensors or ints)
+    def quantize(self, mode, bf16, ref_out, rows, cols):
+        """sx_dispatch_quantize: reference-layout Q4_0/Q8_0 block words of a device bf16 matrix."""
+        check(lib().sx_dispatch_quantize(self.h, mode, _ptr(bf16), _ptr(ref_out), rows, cols))
+
     def gemv(self, mode, w_packed, x, y, m, k, batch=1):
         check(lib().sx_dispatch_gemv(self.h, mode, _ptr(w_packed), _ptr(x), _ptr(y), m, k, batch))
 
@@ -535,6 +541,10 @@ class Buffer:
     def upload_weights(self, ref_words: np.ndarray, rows: int, cols: int, mode: int) -> None:
         w = np.ascontiguousarray(ref_words, dtype=np.uint32)
         check(lib().sx_buffer_upload_weights(self.h, w.ctypes.data, rows, cols, mode))
+
+    def quantize_device(self, bf16_ptr, rows: int, cols: int, mode: int) -> None:
+        """sx_buffer_quantize_device: quantise a device bf16 matrix into this buffer."""
+        check(lib().sx_buffer_quantize_device(self.h, _ptr(bf16_ptr), rows, cols, mode))
 
     def repack_device(self, ref_ptr, rows: int, cols: int, mode: int) -> None:
         check(lib().sx_buffer_repack_device(self.h, _ptr(ref_ptr), rows, cols, mode))

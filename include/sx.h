@@ -126,6 +126,13 @@ SX_API sx_status sx_buffer_read(sx_buffer *b, uint64_t offset, void *dst, uint64
  * sx_packed_bytes).  mode NONE is rejected. */
 SX_API sx_status sx_buffer_upload_weights(sx_buffer *dst, const uint32_t *ref_words,
                                           uint32_t rows, uint32_t cols, sx_quant_mode mode);
+/* Weight ingest on the device (quantizeMatrix, quant.zig:92-162, which the reference runs on
+ * 16 CPU threads at load): a row-major bf16 matrix already in device memory (16-byte aligned,
+ * cols % 32 == 0) quantised to Q4_0 / Q8_0 blocks bit-identical to the CPU quantiser's, then
+ * stored packed in `dst` like sx_buffer_upload_weights.  Synchronous; allocates a staging
+ * buffer of the reference-layout size for the call. */
+SX_API sx_status sx_buffer_quantize_device(sx_buffer *dst, const void *bf16_device, uint32_t rows,
+                                           uint32_t cols, sx_quant_mode mode);
 /* Same, from reference-layout words already in device memory. */
 SX_API sx_status sx_buffer_repack_device(sx_buffer *dst, const void *ref_words_device,
                                          uint32_t rows, uint32_t cols, sx_quant_mode mode);
@@ -237,6 +244,10 @@ SX_API sx_status sx_decode_attn_noalloc(const float *q, const void *k_cache, con
                                         uint32_t head_dim, uint32_t kv_dim, uint32_t gqa_ratio,
                                         float scale, uint32_t num_q_heads, uint32_t total_slots,
                                         uint32_t kv_bf16, void *cuda_stream);
+/* The quantiser alone: reference-layout block words (Q4 5 / Q8 9 words per 32 values) of a
+ * device bf16 matrix into device memory, asynchronous on the engine stream. */
+SX_API sx_status sx_dispatch_quantize(sx_engine *e, sx_quant_mode mode, const void *bf16_device,
+                                     uint32_t *ref_words_device, uint32_t rows, uint32_t cols);
 /* Dequantise a packed Q4 matrix to f32 (nib - 8) * d in reference element order. */
 SX_API sx_status sx_dispatch_unpack_q4(sx_engine *e, const void *w_packed, float *out,
                                        uint32_t m, uint32_t k);
