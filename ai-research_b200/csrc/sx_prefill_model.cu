@@ -192,10 +192,36 @@ __global__ void __launch_bounds__(kPfThreads, 1) pf_attn_kernel(PfAttnArgs a) {
     m[h] = -INFINITY;
     l[h] = 0.0f;
   }
-  auto row_at = [&](const void *cache, uint32_t sl, int i) -> float {
-    const size_t idx = cache0 + ((size_t)sl * a.num_kv + kvh) * D + lane * DPL + i;
-    return BF16 ? bf16_bits_to_f32(reinterpret_cast<const uint16_t *>(cache)[idx])
-                : reinterpret_cast<const float *>(cache)[idx];
+  // the lane's DPL elements of a cached row with the widest aligned loads (rows start on
+  // D-element boundaries, so lane * DPL elements is 4 * DPL (f32) or 2 * DPL (bf16) aligned)
+  auto load_row = [&](const void *cache, uint32_t sl, float (&out)[DPL]) {
+    const size_t idx = cache0 + ((size_t)sl * a.num_kv + kvh) * D + lane * DPL;
+    if constexpr (BF16) {
+      const uint16_t *p = reinterpret_cast<const uint16_t *>(cache) + idx;
+      uint32_t w[DPL / 2];
+      if constexpr (DPL == 8) {
+        const uint4 u = *reinterpret_cast<const uint4 *>(p);
+        w[0] = u.x; w[1] = u.y; w[2] = u.z; w[3] = u.w;
+      } else if constexpr (DPL == 4) {
+        const uint2 u = *reinterpret_cast<const uint2 *>(p);
+        w[0] = u.x; w[1] = u.y;
+      } else {
+        w[0] = *reinterpret_cast<const uint32_t *>(p);
+      }
+#pragma unroll
+      for (int i = 0; i < DPL / 2; ++i) {
+        out[2 * i] = __uint_as_float(w[i] << 16);
+        out[2 * i + 1] = __uint_as_float(w[i] & 0xFFFF0000u);
+      }
+    } else {
+      const float *p = reinterpret_cast<const float *>(cache) + idx;
+#pragma unroll
+      for (int i = 0; i < DPL; i += 2) {
+        const float2 u = *reinterpret_cast<const float2 *>(p + i);
+        out[i] = u.x;
+        out[i + 1] = u.y;
+      }
+    }
   };
   for (uint32_t j0 = warp; j0 < S; j0 += W * kPfChunk) {
     uint32_t sl[kPfChunk];
@@ -209,12 +235,15 @@ __global__ void __launch_bounds__(kPfThreads, 1) pf_attn_kernel(PfAttnArgs a) {
     }
     float kr[kPfChunk][DPL], vr[kPfChunk][DPL];
 #pragma unroll
-    for (int p = 0; p < kPfChunk; ++p)
+    for (int p = 0; p < kPfChunk; ++p) {
+      if (live[p]) {
+        load_row(a.k_cache, sl[p], kr[p]);
+        load_row(a.v_cache, sl[p], vr[p]);
+      } else {
 #pragma unroll
-      for (int i = 0; i < DPL; ++i) {
-        kr[p][i] = live[p] ? row_at(a.k_cache, sl[p], i) : 0.0f;
-        vr[p][i] = live[p] ? row_at(a.v_cache, sl[p], i) : 0.0f;
+        for (int i = 0; i < DPL; ++i) kr[p][i] = vr[p][i] = 0.0f;
       }
+    }
 #pragma unroll
     for (int h = 0; h < G; ++h) {
       float sc[kPfChunk];
