@@ -1089,6 +1089,74 @@ SX_API sx_status sx_dispatch_decode_attn(sx_engine *e, const float *q, const voi
   return do_attn(e, e->stream, q, k_cache, v_cache, active_slots, step_params, out, head_dim,
                  kv_dim, gqa_ratio, scale, num_q_heads, total_slots);
 }
+SX_API sx_status sx_dispatch_qkv_rope_attn(
+    sx_engine *e, const float *q_in, const float *k_in, const float *v_in, const float *q_norm_w,
+    const float *k_norm_w, void *k_cache, void *v_cache, const uint32_t *active_slots,
+    const uint32_t *step_params, float *out, uint32_t num_q, uint32_t num_kv, uint32_t head_dim,
+    uint32_t rotary_dim, uint32_t k_eq_v, float theta, float eps, float scale,
+    uint32_t total_slots, uint32_t instances, uint32_t qkv_stride) {
+  SX_CHECK_ARG(e, "dispatch: null engine");
+  SX_CHECK_ARG(q_in && k_in && v_in && q_norm_w && k_norm_w && k_cache && v_cache &&
+                   active_slots && step_params && out,
+               "qkv_rope_attn: null pointer");
+  SX_CHECK_ARG(head_dim == 64 || head_dim == 128 || head_dim == 256 || head_dim == 512,
+               "qkv_rope_attn: head_dim must be 64/128/256/512 (got %u)", head_dim);
+  SX_CHECK_ARG(num_kv > 0 && num_q % num_kv == 0, "qkv_rope_attn: num_q must be a multiple of num_kv");
+  const uint32_t g = num_q / num_kv;
+  SX_CHECK_ARG(g == 1 || g == 2 || g == 4 || g == 8,
+               "qkv_rope_attn: q heads per kv head must be 1/2/4/8 (got %u)", g);
+  SX_CHECK_ARG(rotary_dim <= head_dim && rotary_dim % 2 == 0,
+               "qkv_rope_attn: rotary_dim must be even and <= head_dim");
+  SX_CHECK_ARG(total_slots > 0 && instances >= 1 && num_kv <= 4096,
+               "qkv_rope_attn: need total_slots > 0, instances >= 1, num_kv <= 4096");
+  SX_CHECK_ARG(instances == 1 || (total_slots <= sx::kAttnClusterMaxSlots &&
+                                  qkv_stride >= (num_q + 2 * num_kv) * head_dim &&
+                                  qkv_stride % 4 == 0 && instances <= 65535),
+               "qkv_rope_attn: several instances need a ring of at most %u slots and a q|k|v "
+               "stride of at least (num_q + 2 num_kv) head_dim floats, a multiple of 4",
+               sx::kAttnClusterMaxSlots);
+  SX_CHECK_ARG(((uintptr_t)q_in | (uintptr_t)k_in | (uintptr_t)v_in | (uintptr_t)q_norm_w |
+                (uintptr_t)k_norm_w | (uintptr_t)k_cache | (uintptr_t)v_cache | (uintptr_t)out) %
+                       16 == 0,
+               "qkv_rope_attn: vectors and caches must be 16-byte aligned");
+  if (total_slots > sx::kAttnClusterMaxSlots &&
+      sx::attn_scratch_bytes(num_q, total_slots, head_dim) > e->attn_part_bytes) {
+    set_error("qkv_rope_attn: ring of %u slots needs more attention scratch than the engine has",
+              total_slots);
+    return SX_ERR_UNSUPPORTED;
+  }
+  SX_TRY_CUDA(cudaSetDevice(e->device), "cudaSetDevice");
+  sx_status st = SX_OK;
+  sx::AttnFusedArgs a{};
+  a.inv_freq = engine_inv_freq(e, rotary_dim, theta, &st);
+  if (!a.inv_freq) return st;
+  a.q = q_in;
+  a.k = k_in;
+  a.v = v_in;
+  a.q_norm_w = q_norm_w;
+  a.k_norm_w = k_norm_w;
+  a.k_cache = k_cache;
+  a.v_cache = v_cache;
+  a.slots = active_slots;
+  a.step = step_params;
+  a.out = out;
+  a.head_dim = head_dim;
+  a.kv_dim = num_kv * head_dim;
+  a.num_q = num_q;
+  a.num_kv = num_kv;
+  a.rotary_dim = rotary_dim;
+  a.k_eq_v = k_eq_v ? 1u : 0u;
+  a.kv_bf16 = e->kv_bf16 ? 1u : 0u;
+  a.total_slots = total_slots;
+  a.scale = scale;
+  a.eps = eps;
+  a.sessions = instances;
+  a.qkv_ld = qkv_stride;
+  a.out_ld = num_q * head_dim;
+  a.cache_ld = (uint64_t)total_slots * num_kv * head_dim;
+  sx_host_bind_scratch(e, a);
+  return cuda_status(sx::launch_attn_fused(a, e->stream, false), "qkv_rope_attn launch");
+}
 SX_API sx_status sx_dispatch_argmax(sx_engine *e, const float *logits, uint32_t n,
                                     uint32_t *out_token) {
   SX_CHECK_ARG(e, "dispatch: null engine");

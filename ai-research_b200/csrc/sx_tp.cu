@@ -23,11 +23,13 @@ constexpr uint32_t kP2pMaxRanks = 8;
 constexpr uint32_t kP2pMaxCount = 16384;  // floats per all-reduce (hidden sizes up to 16384)
 constexpr size_t kP2pFlagBytes = 256;
 constexpr size_t kP2pBytes = kP2pFlagBytes + sizeof(float) * 2ull * kP2pMaxRanks * kP2pMaxCount;
+constexpr uint64_t kP2pDefaultWaitNs = 2000000000ull;  // 2 s for the peers' flags
 struct P2pArgs {
   uint8_t *ws[kP2pMaxRanks];  // every rank's workspace, mapped into this process (own: local)
   uint32_t nranks, rank;
   uint32_t *gen;              // this rank's call counter (device), equal on all ranks
   uint32_t *err;
+  uint64_t wait_ns;           // how long a call waits for the other ranks' flags
 };
 }  // namespace sx
 
@@ -163,6 +165,11 @@ namespace {
 SX_DEV void st_release_sys(uint32_t *p, uint32_t v) {
   asm volatile("st.release.sys.global.u32 [%0], %1;\n" ::"l"(p), "r"(v) : "memory");
 }
+SX_DEV uint64_t globaltimer_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;\n" : "=l"(t));
+  return t;
+}
 SX_DEV uint32_t ld_acquire_sys(const uint32_t *p) {
   uint32_t v;
   asm volatile("ld.acquire.sys.global.u32 %0, [%1];\n" : "=r"(v) : "l"(p) : "memory");
@@ -200,16 +207,17 @@ __global__ void __launch_bounds__(512) p2p_allreduce_kernel(float *buf, uint32_t
   __threadfence_system();
   __syncthreads();
   if (tid < a.nranks) st_release_sys(flags(a.ws[tid]) + a.rank, g);
-  // 2. wait for every rank's data of call g
+  // 2. wait for every rank's data of call g, at most a.wait_ns of global time: a rank that
+  // never comes makes the call record kDevWaitTimeout and finish, not hang
   if (tid < a.nranks) {
     const uint32_t *f = flags(a.ws[a.rank]) + tid;
-    uint32_t spins = 0;
+    const uint64_t t0 = globaltimer_ns();
     while ((int32_t)(ld_acquire_sys(f) - g) < 0) {
-      if (++spins > (1u << 24)) {  // ~1 s of polling: a rank that never came
+      if (globaltimer_ns() - t0 > a.wait_ns) {
         atomicOr(&late, 1u);
         break;
       }
-      __nanosleep(32);
+      __nanosleep(64);
     }
   }
   __syncthreads();
@@ -223,53 +231,79 @@ __global__ void __launch_bounds__(512) p2p_allreduce_kernel(float *buf, uint32_t
   }
 }
 
-// Maps every rank's workspace into this process: handles exchanged with one NCCL all-gather.
-sx_status p2p_setup(const NcclApi &api, sx_comm *c) {
-  if (c->nranks > sx::kP2pMaxRanks) return SX_ERR_UNSUPPORTED;
+// Maps every rank's workspace into this process.  Every rank takes the same collective steps
+// whatever happens locally -- one NCCL all-gather of {IPC handle, ok} records, then one NCCL
+// min-reduce of "everything worked here" -- so all ranks reach the same verdict: either every
+// rank has every peer mapped, or none keeps the peer path (and each unmaps what it opened).
+// The exchange buffer is allocated before the communicator exists (sx_comm_create), so a rank
+// that cannot take part returns before any collective.
+struct HandleRec {
+  cudaIpcMemHandle_t h;
+  uint32_t ok;
+  uint32_t pad[3];
+};
+
+sx_status p2p_setup(const NcclApi &api, sx_comm *c, void *xbuf) {
   cudaStream_t s = c->e->stream;
-  void *ws = nullptr, *gen = nullptr, *hbuf = nullptr;
-  sx_status st = sx_host_cuda_status(cudaMalloc(&ws, sx::kP2pBytes), "peer workspace");
-  if (st == SX_OK) st = sx_host_cuda_status(cudaMemset(ws, 0, sx::kP2pBytes), "peer workspace");
-  if (st == SX_OK) st = sx_host_cuda_status(cudaMalloc(&gen, 256), "peer counter");
-  if (st == SX_OK) st = sx_host_cuda_status(cudaMemset(gen, 0, 256), "peer counter");
-  if (st == SX_OK)
-    st = sx_host_cuda_status(cudaMalloc(&hbuf, sizeof(cudaIpcMemHandle_t) * c->nranks),
-                             "ipc handle exchange");
-  cudaIpcMemHandle_t mine{};
-  std::vector<cudaIpcMemHandle_t> all(c->nranks);
-  if (st == SX_OK) st = sx_host_cuda_status(cudaIpcGetMemHandle(&mine, ws), "cudaIpcGetMemHandle");
-  if (st == SX_OK)
-    st = sx_host_cuda_status(
-        cudaMemcpy(static_cast<uint8_t *>(hbuf) + sizeof(mine) * c->rank, &mine, sizeof(mine),
-                   cudaMemcpyHostToDevice),
-        "ipc handle upload");
-  if (st == SX_OK)
-    st = nccl_status(api,
-                     api.all_gather(static_cast<uint8_t *>(hbuf) + sizeof(mine) * c->rank, hbuf,
-                                    sizeof(mine), ncclUint8, c->comm, s),
-                     "ncclAllGather (ipc handles)");
+  uint32_t ok = c->nranks <= sx::kP2pMaxRanks ? 1u : 0u;
+  void *ws = nullptr, *gen = nullptr;
+  if (ok && cudaMalloc(&ws, sx::kP2pBytes) != cudaSuccess) ok = 0;
+  if (ok && cudaMemset(ws, 0, sx::kP2pBytes) != cudaSuccess) ok = 0;
+  if (ok && cudaMalloc(&gen, 256) != cudaSuccess) ok = 0;
+  if (ok && cudaMemset(gen, 0, 256) != cudaSuccess) ok = 0;
+  HandleRec mine{};
+  c->ws = static_cast<uint8_t *>(ws);  // freed by p2p_teardown on any failure below
+  c->pa.gen = static_cast<uint32_t *>(gen);
+  if (ok && cudaIpcGetMemHandle(&mine.h, ws) != cudaSuccess) ok = 0;
+  mine.ok = ok;
+  cudaGetLastError();  // a local failure is reported through the agreement, not as sticky state
+  // 1. the all-gather runs on every rank, whatever `ok` is
+  HandleRec *recs = static_cast<HandleRec *>(xbuf);
+  uint32_t *vote = reinterpret_cast<uint32_t *>(recs + c->nranks);
+  sx_status st = sx_host_cuda_status(cudaMemcpy(recs + c->rank, &mine, sizeof(mine),
+                                                cudaMemcpyHostToDevice),
+                                     "ipc handle upload");
+  if (st != SX_OK) return st;  // the exchange buffer itself is unusable: nothing can agree
+  st = nccl_status(api,
+                   api.all_gather(recs + c->rank, recs, sizeof(HandleRec), ncclUint8, c->comm, s),
+                   "ncclAllGather (ipc handles)");
+  std::vector<HandleRec> all(c->nranks);
   if (st == SX_OK) st = sx_host_cuda_status(cudaStreamSynchronize(s), "ipc handle exchange");
   if (st == SX_OK)
-    st = sx_host_cuda_status(cudaMemcpy(all.data(), hbuf, sizeof(mine) * c->nranks,
+    st = sx_host_cuda_status(cudaMemcpy(all.data(), recs, sizeof(HandleRec) * c->nranks,
                                         cudaMemcpyDeviceToHost),
                              "ipc handle download");
-  if (hbuf) cudaFree(hbuf);
-  c->ws = static_cast<uint8_t *>(ws);
-  c->pa.gen = static_cast<uint32_t *>(gen);
-  for (uint32_t r = 0; r < c->nranks && st == SX_OK; ++r) {
+  if (st != SX_OK) return st;
+  for (uint32_t r = 0; r < c->nranks && r < sx::kP2pMaxRanks; ++r) {
+    ok = ok && all[r].ok;
+    if (!ok) break;
     if (r == c->rank) {
       c->pa.ws[r] = static_cast<uint8_t *>(ws);
       continue;
     }
     void *p = nullptr;
-    st = sx_host_cuda_status(cudaIpcOpenMemHandle(&p, all[r], cudaIpcMemLazyEnablePeerAccess),
-                             "cudaIpcOpenMemHandle");
+    if (cudaIpcOpenMemHandle(&p, all[r].h, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+      cudaGetLastError();
+      ok = 0;
+      break;
+    }
     c->pa.ws[r] = static_cast<uint8_t *>(p);
   }
+  // 2. agree: the peer path stays only if it worked on every rank
+  st = sx_host_cuda_status(cudaMemcpy(vote, &ok, 4, cudaMemcpyHostToDevice), "peer vote upload");
+  if (st == SX_OK)
+    st = nccl_status(api, api.all_reduce(vote, vote, 1, ncclUint32, ncclMin, c->comm, s),
+                     "ncclAllReduce (peer vote)");
+  uint32_t agreed = 0;
+  if (st == SX_OK) st = sx_host_cuda_status(cudaStreamSynchronize(s), "peer vote");
+  if (st == SX_OK)
+    st = sx_host_cuda_status(cudaMemcpy(&agreed, vote, 4, cudaMemcpyDeviceToHost), "peer vote");
   c->pa.nranks = c->nranks;
   c->pa.rank = c->rank;
   c->pa.err = c->e->err_dev;
-  return st;
+  c->pa.wait_ns = sx::kP2pDefaultWaitNs;
+  if (st != SX_OK) return st;
+  return agreed ? SX_OK : SX_ERR_UNSUPPORTED;
 }
 
 void p2p_teardown(sx_comm *c) {
@@ -311,6 +345,12 @@ SX_API sx_status sx_comm_create(sx_engine *e, const uint8_t id[128], uint32_t nr
   if (st != SX_OK) return st;
   ncclUniqueId u;
   memcpy(&u, id, 128);
+  // the handle-exchange buffer, before any collective (a rank that cannot allocate it leaves
+  // before ncclCommInitRank, like any other rank that fails to join)
+  void *xbuf = nullptr;
+  st = sx_host_cuda_status(cudaMalloc(&xbuf, sizeof(HandleRec) * (nranks + 1)),
+                           "ipc handle exchange buffer");
+  if (st != SX_OK) return st;
   sx_comm *c = new sx_comm();
   c->e = e;
   c->nranks = nranks;
@@ -318,12 +358,24 @@ SX_API sx_status sx_comm_create(sx_engine *e, const uint8_t id[128], uint32_t nr
   st = nccl_status(api, api.comm_init_rank(&c->comm, (int)nranks, u, (int)rank),
                    "ncclCommInitRank");
   if (st != SX_OK) {
+    cudaFree(xbuf);
     delete c;
     return st;
   }
-  // map the peer all-reduce's workspaces (collective: every rank does it here); NCCL stays the
-  // all-reduce until sx_comm_set_allreduce(c, 0) selects the peer kernel
-  if (nranks > 1 && p2p_setup(api, c) != SX_OK) p2p_teardown(c);
+  // map the peer all-reduce's workspaces (collective: every rank does it here and all ranks
+  // agree on the outcome); NCCL stays the all-reduce until sx_comm_set_allreduce(c, 0)
+  // selects the peer kernel, which then succeeds on every rank or on none
+  if (nranks > 1) {
+    st = p2p_setup(api, c, xbuf);
+    if (st != SX_OK) p2p_teardown(c);
+    if (st == SX_ERR_UNSUPPORTED) st = SX_OK;  // agreed: NCCL only, on every rank
+  }
+  cudaFree(xbuf);
+  if (st != SX_OK) {
+    if (c->comm) api.comm_destroy(c->comm);
+    delete c;
+    return st;
+  }
   *out = c;
   return SX_OK;
 }
@@ -344,6 +396,25 @@ SX_API sx_status sx_comm_set_allreduce(sx_comm *c, int use_nccl) {
 
 SX_API int sx_comm_allreduce_is_nccl(const sx_comm *c) { return c && c->p2p ? 0 : 1; }
 
+SX_API sx_status sx_comm_set_wait_ns(sx_comm *c, uint64_t wait_ns) {
+  if (!c || wait_ns == 0) {
+    sx_host_set_error("comm: null communicator or zero wait");
+    return SX_ERR_INVALID;
+  }
+  c->pa.wait_ns = wait_ns;
+  return SX_OK;
+}
+
+SX_API sx_status sx_comm_allreduce(sx_comm *c, float *buf, uint32_t count) {
+  if (!c || !buf || count == 0) {
+    sx_host_set_error("comm allreduce: bad arguments");
+    return SX_ERR_INVALID;
+  }
+  sx_status st = sx_host_cuda_status(cudaSetDevice(c->e->device), "cudaSetDevice");
+  if (st == SX_OK) st = sx_host_allreduce(c, buf, count, c->e->stream);
+  return st;
+}
+
 SX_API void sx_comm_destroy(sx_comm *c) {
   if (!c) return;
   NcclApi api;
@@ -360,7 +431,13 @@ uint32_t sx_host_comm_ranks(const sx_comm *c) { return c ? c->nranks : 1; }
 uint32_t sx_host_comm_rank(const sx_comm *c) { return c ? c->rank : 0; }
 
 sx_status sx_host_allreduce(sx_comm *c, float *buf, size_t count, cudaStream_t s) {
-  if (c && c->p2p && count <= sx::kP2pMaxCount && ((uintptr_t)buf & 15) == 0) {
+  if (c && c->p2p) {
+    // never fall back to NCCL for one call: the other ranks would be in the peer kernel
+    if (count > sx::kP2pMaxCount || ((uintptr_t)buf & 15) != 0) {
+      sx_host_set_error("peer all-reduce: %zu floats at %p (at most %u, 16-byte aligned)", count,
+                        (void *)buf, sx::kP2pMaxCount);
+      return SX_ERR_UNSUPPORTED;
+    }
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(1);
     cfg.blockDim = dim3(512);

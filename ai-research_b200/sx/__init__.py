@@ -226,6 +226,11 @@ _SIGS = {
         _S,
         [_P, _P, _P, _P, _P, _P, _P, _U32, _U32, _U32, _F, _U32, _U32],
     ),
+    "sx_dispatch_qkv_rope_attn": (
+        _S,
+        [_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _U32, _U32, _U32, _U32, _U32, _F, _F, _F,
+         _U32, _U32, _U32],
+    ),
     "sx_dispatch_argmax": (_S, [_P, _P, _U32, _P]),
     "sx_decode_attn_noalloc": (
         _S,
@@ -242,6 +247,8 @@ _SIGS = {
     "sx_comm_destroy": (None, [_P]),
     "sx_comm_set_allreduce": (_S, [_P, _I]),
     "sx_comm_allreduce_is_nccl": (_I, [_P]),
+    "sx_comm_allreduce": (_S, [_P, _P, _U32]),
+    "sx_comm_set_wait_ns": (_S, [_P, _U64]),
     "sx_model_destroy": (None, [_P]),
     "sx_model_synth_weights": (_S, [_P, _U64]),
     "sx_model_fill_kv": (_S, [_P, _U64]),
@@ -487,6 +494,16 @@ class Engine:
             self.h, _ptr(q), _ptr(k_cache), _ptr(v_cache), _ptr(slots), _ptr(step), _ptr(out),
             head_dim, kv_dim, gqa_ratio, scale, num_q_heads, total_slots))
 
+    def qkv_rope_attn(self, q_in, k_in, v_in, q_norm_w, k_norm_w, k_cache, v_cache, slots, step,
+                      out, num_q, num_kv, head_dim, rotary_dim, k_eq_v, theta, eps, scale,
+                      total_slots, instances=1, qkv_stride=0):
+        """The decode graph's fused qkv_rope + decode attention kernel (sx_dispatch_qkv_rope_attn)."""
+        check(lib().sx_dispatch_qkv_rope_attn(
+            self.h, _ptr(q_in), _ptr(k_in), _ptr(v_in), _ptr(q_norm_w), _ptr(k_norm_w),
+            _ptr(k_cache), _ptr(v_cache), _ptr(slots), _ptr(step), _ptr(out), num_q, num_kv,
+            head_dim, rotary_dim, int(k_eq_v), theta, eps, scale, total_slots, instances,
+            qkv_stride))
+
     def argmax(self, logits, n, out):
         check(lib().sx_dispatch_argmax(self.h, _ptr(logits), n, _ptr(out)))
 
@@ -617,6 +634,14 @@ class Comm:
     @property
     def allreduce_is_nccl(self) -> bool:
         return bool(lib().sx_comm_allreduce_is_nccl(self.h))
+
+    def allreduce(self, buf, count: int) -> None:
+        """sx_comm_allreduce: in-place sum of `count` floats at a device pointer over the ranks."""
+        check(lib().sx_comm_allreduce(self.h, _ptr(buf), count))
+
+    def set_wait_ns(self, wait_ns: int) -> None:
+        """How long the peer all-reduce waits for the other ranks' flags."""
+        check(lib().sx_comm_set_wait_ns(self.h, wait_ns))
 
     def close(self):
         if getattr(self, "h", None):

@@ -429,7 +429,13 @@ def main():
         try:
             comm.set_allreduce(args.allreduce == "nccl")
         except sx.SxError:
-            args.allreduce = "nccl"  # peer workspaces unavailable: every rank keeps NCCL
+            # sx_comm_create agreed on the peer workspaces across the ranks, so this happens on
+            # every rank or on none: all keep NCCL
+            args.allreduce = "nccl"
+        picks = [None] * world
+        dist.all_gather_object(picks, args.allreduce)
+        if len(set(picks)) != 1:
+            raise RuntimeError(f"ranks chose different all-reduces: {picks}")
         cfgd.update(tp_size=world, tp_rank=rank, reference_graph=0)
     stream = torch.cuda.ExternalStream(eng.stream)
     model = sx.Model(eng, sx.model_config(**cfgd), comm)

@@ -224,6 +224,26 @@ SX_API sx_status sx_dispatch_decode_attn(sx_engine *e, const float *q, const voi
                                          uint32_t head_dim, uint32_t kv_dim, uint32_t gqa_ratio,
                                          float scale, uint32_t num_q_heads,
                                          uint32_t total_slots);
+/* recordQkvRope followed by recordDecodeAttn (kernels.zig:116-129, qkv_rope.wgsl +
+ * decode_attn.wgsl) as the one fused kernel the decode graph runs: q heads and the new k
+ * RMS-normalised with their gains and rotated over the first rotary_dim elements, v
+ * unit-normalised, the new K/V stored at step_params[1] in the engine's KV precision, then
+ * attention of every q head over the slot list (the current slot's K/V taken from the values
+ * just stored).  q_in is not modified.  `instances` independent problems run in one launch:
+ * instance i reads q_in / k_in / v_in at + i * qkv_stride floats, its caches at
+ * + i * total_slots * num_kv * head_dim elements, its slot list at + i * total_slots, its step
+ * record at + 4 i, and writes out at + i * num_q * head_dim (several instances need a ring of at
+ * most 1024 slots).  Vectors and caches 16-byte aligned; head_dim 64/128/256/512; 1, 2, 4 or 8
+ * q heads per kv head. */
+SX_API sx_status sx_dispatch_qkv_rope_attn(sx_engine *e, const float *q_in, const float *k_in,
+                                           const float *v_in, const float *q_norm_w,
+                                           const float *k_norm_w, void *k_cache, void *v_cache,
+                                           const uint32_t *active_slots,
+                                           const uint32_t *step_params, float *out,
+                                           uint32_t num_q, uint32_t num_kv, uint32_t head_dim,
+                                           uint32_t rotary_dim, uint32_t k_eq_v, float theta,
+                                           float eps, float scale, uint32_t total_slots,
+                                           uint32_t instances, uint32_t qkv_stride);
 SX_API sx_status sx_dispatch_argmax(sx_engine *e, const float *logits, uint32_t n,
                                     uint32_t *out_token);
 /* No counterpart in the reference.  Decode attention that allocates nothing, for callers that
@@ -385,9 +405,20 @@ SX_API void sx_comm_destroy(sx_comm *c);
  * peer-to-peer kernel over NVLink -- each rank stores its vector into every rank's workspace
  * (mapped through CUDA IPC when the communicator is made), releases a flag, waits for all the
  * flags with a bounded poll and sums in rank order.  Choose before creating the model (its
- * graphs capture the choice).  The reference has no multi-GPU path. */
+ * graphs capture the choice).  sx_comm_create maps the workspaces collectively and all ranks
+ * agree on the result, so selecting the peer kernel succeeds on every rank or fails
+ * (SX_ERR_UNSUPPORTED) on every rank.  The reference has no multi-GPU path. */
 SX_API sx_status sx_comm_set_allreduce(sx_comm *c, int use_nccl);
 SX_API int sx_comm_allreduce_is_nccl(const sx_comm *c);
+/* The row-parallel all-reduce alone (the op the per-token graph captures twice per layer):
+ * in-place sum of count floats at the device pointer buf over all ranks, asynchronous on the
+ * engine stream.  With the peer kernel, buf must be 16-byte aligned and count <= 16384; a
+ * rank that does not arrive within the wait limit makes the call record a device error
+ * (SX_ERR_DEVICE from the next sx_engine_sync) instead of hanging. */
+SX_API sx_status sx_comm_allreduce(sx_comm *c, float *buf, uint32_t count);
+/* How long the peer all-reduce waits for the other ranks' flags (default 2 s); applies to
+ * calls launched or graphs recorded after it. */
+SX_API sx_status sx_comm_set_wait_ns(sx_comm *c, uint64_t wait_ns);
 /* sx_model_create for a tensor-parallel rank: cfg->tp_size / tp_rank must match the
  * communicator; cfg->reference_graph must be 0. */
 SX_API sx_status sx_model_create_tp(sx_engine *e, const sx_model_config *cfg, sx_comm *comm,

@@ -68,7 +68,15 @@ def assert_close_bf16_operands(got, want, what="values", frac=1e-2, scale_tol=1e
     err = np.abs(got - want)
     bad = int(np.count_nonzero(err > 1e-3 + 1e-2 * np.abs(want)))
     scale = float(np.abs(want).max())
-    assert bad <= max(1, int(frac * err.size)), (
-        f"{what}: {bad} of {err.size} elements out of the elementwise tolerance")
-    assert err.max() <= scale_tol * scale, (
-        f"{what}: worst err {err.max():.3e} above {scale_tol} of the scale {scale:.3e}")
+    stats = (f"{bad} of {err.size} elements past the elementwise bound, worst err "
+             f"{err.max():.3e} = {err.max() / max(scale, 1e-30):.2e} of the scale {scale:.3e}")
+    assert bad <= max(1, int(frac * err.size)), f"{what}: {stats} (allowed fraction {frac})"
+    assert err.max() <= scale_tol * scale, f"{what}: {stats} (allowed {scale_tol} of the scale)"
+
+
+# With a bf16 KV cache on top of bf16 operands, every cached K/V element is a second place
+# where the two sides round f32 values that may differ by an ulp: more elements move a little
+# (measured on the bf16-cache prefill test, 8 q heads per kv head: 41 of 4096 logits past the
+# elementwise bound), while the scale bound, which a wrong slot, head or operand breaks by
+# orders of magnitude, stays as tight.
+BF16_KV_FRAC = 5e-2

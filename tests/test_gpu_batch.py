@@ -189,3 +189,42 @@ def test_batch_rejects_bad_requests(engine):
         sx.Model(engine, sx.model_config(**tiny_cfg(num_sessions=9)))
     with pytest.raises(sx.SxError):
         sx.Model(engine, sx.model_config(**tiny_cfg(num_sessions=2, reference_graph=1)))
+
+
+def c5_cfg(**kw):
+    """BASELINE config 5's model shape: H 1536, 8 q / 1 kv heads x 256, I 6144, Q4_0 layers,
+    Q8_0 LM head over the full 262144 vocabulary, 32 + 512 + 96 ring, bf16 KV cache (what
+    bench.py --case sessions runs), with fewer layers so that the checker finishes in seconds
+    (layer 4 is a full-attention layer: rot 64, theta 1e6)."""
+    cfg = tiny_cfg(vocab_size=262144, hidden_size=1536, intermediate_size=6144, num_layers=5,
+                   num_q_heads=8, num_kv_heads=1, num_global_kv_heads=1, head_dim=256,
+                   global_head_dim=256, num_anchors=32, window_size=512, num_recall=96,
+                   full_every=5, kv_bf16=1, num_sessions=8)
+    cfg.update(kw)
+    return cfg
+
+
+def test_config5_shape_batch8_bf16_kv_matches_checker(engine):
+    """sx_decode_batch at n = 8 on config 5's shape with the bf16 cache against one checker
+    model per session in its bf16-cache mode (forward.zig:19-75 per session).  Logits use the
+    double-rounding allowance of conftest.assert_close_bf16_operands: a cached element rounded
+    from f32 values one ulp apart on the two sides differs by 2^-8."""
+    from tests.conftest import assert_close_bf16_operands
+    cfg = c5_cfg()
+    starts = [700, 31, 5000, 12, 99999, 544, 2, 1234]  # wrapped windows, young rings
+    model, refs, rings = make_sessions(engine, cfg, seed=55, starts=starts, n_recall=0)
+    rng = np.random.default_rng(56)
+    for i, s in enumerate(starts):  # recall tiers of different fill
+        for r in range(int(rng.integers(0, 97)) if s > 600 else 0):
+            c = int(rng.integers(0, s))
+            rings[i].write_recall(0, r, c)
+            refs[i].ring.write_recall(0, r, c)
+    clocks, tokens = list(starts), [7 + 3 * s for s in range(8)]
+    for t in range(3):
+        for i, (tok, rtok, lg, rlg) in enumerate(step_all(model, refs, rings, cfg, 55, clocks,
+                                                          tokens, 8)):
+            assert_close_bf16_operands(lg, rlg, what=f"session {i} step {t} logits")
+            if tok != rtok:
+                assert margin_top2(rlg) < 1e-3, f"session {i} step {t}: {tok} vs {rtok}"
+            tokens[i] = tok
+        clocks = [c + 1 for c in clocks]

@@ -16,6 +16,7 @@ import pytest
 
 import sx
 from oracle import oracle as orc
+from tests.conftest import BF16_KV_FRAC
 from tests.conftest import assert_close_bf16_operands as assert_close
 from tests.test_gpu_model import margin_top2, tiny_cfg
 
@@ -137,3 +138,60 @@ def test_prefill_rejects_bad_tokens(engine):
     rings = [sx.Ring(1, 4, 8, 4)]
     with pytest.raises(sx.SxError):
         model.prefill_batch([p], rings, [0], sessions=[2])  # session beyond the model's two
+
+
+@pytest.mark.parametrize("head_dim,nq,nkv", [(256, 8, 1), (128, 4, 2), (64, 4, 2)])
+def test_prefill_bf16_kv_matches_checker(engine, head_dim, nq, nkv):
+    """The bf16-KV prefill attention (the cached-row loads of pf_attn_kernel for 8, 4 and 2
+    elements per lane) against the checker in its bf16-cache, bf16-operand mode."""
+    cfg = tiny_cfg(num_sessions=3, num_layers=3, kv_bf16=1, head_dim=head_dim,
+                   global_head_dim=head_dim, num_q_heads=nq, num_kv_heads=nkv,
+                   num_global_kv_heads=nkv, hidden_size=512, intermediate_size=1024)
+    seed = 41
+    model = sx.Model(engine, sx.model_config(**cfg))
+    model.synth_weights(seed)
+    lens = [11, 3, 12]
+    prompts = prompts_for(cfg, seed, lens)
+    rings = [sx.Ring(1, cfg["num_anchors"], cfg["window_size"], cfg["num_recall"]) for _ in lens]
+    logits = np.zeros((3, cfg["vocab_size"]), np.float32)
+    toks = model.prefill_batch(prompts, rings, [0] * 3, logits_out=logits)
+    for s, p in enumerate(prompts):
+        _, rtok, rlg = checker_prefill(cfg, seed, p)
+        assert_close(logits[s], rlg, what=f"session {s} prefill logits", frac=BF16_KV_FRAC)
+        check_token(int(toks[s]), rtok, rlg, f"session {s} prefill")
+
+
+def test_config5_shape_ragged_prefill_bf16_kv_then_batch8_decode(engine):
+    """Config 5 as bench.py --case sessions runs it (bf16 cache, 8 q heads per kv head, full
+    vocabulary), on ragged prompts of 8 sessions and fewer layers: the batched prefill against
+    the checker's token-by-token decode (bf16 operands, bf16 cache), then two batch-8 decode
+    steps from the caches the prefill wrote."""
+    from tests.test_gpu_batch import c5_cfg
+    cfg = c5_cfg(num_layers=5)
+    seed = 77
+    model = sx.Model(engine, sx.model_config(**cfg))
+    model.synth_weights(seed)
+    lens = [16, 40, 7, 64, 23, 1, 50, 33]
+    prompts = prompts_for(cfg, seed, lens)
+    rings = [sx.Ring(1, cfg["num_anchors"], cfg["window_size"], cfg["num_recall"]) for _ in lens]
+    logits = np.zeros((8, cfg["vocab_size"]), np.float32)
+    toks = model.prefill_batch(prompts, rings, [0] * 8, logits_out=logits)
+    refs = []
+    for s, p in enumerate(prompts):
+        ref, rtok, rlg = checker_prefill(cfg, seed, p)
+        assert_close(logits[s], rlg, what=f"session {s} prefill logits", frac=BF16_KV_FRAC)
+        check_token(int(toks[s]), rtok, rlg, f"session {s} prefill")
+        refs.append(ref)
+    clocks, tokens = list(lens), [int(t) for t in toks]
+    for step in range(2):
+        xs = np.stack([sx.synth_embed_row(cfg["hidden_size"], tokens[s], seed) for s in range(8)])
+        slots = [rings[s].activate_slot(0, clocks[s]) for s in range(8)]
+        lists = [rings[s].get_active_slots(0, clocks[s]) for s in range(8)]
+        lg = np.zeros((8, cfg["vocab_size"]), np.float32)
+        got = model.decode_batch(xs, clocks, slots, lists, True, lg)
+        for s in range(8):
+            rtok, rlg, _ = refs[s].forward(xs[s], clocks[s], True)
+            assert_close(lg[s], rlg, what=f"session {s} decode step {step}", frac=BF16_KV_FRAC)
+            check_token(int(got[s]), rtok, rlg, f"session {s} decode step {step}")
+            tokens[s] = int(got[s])
+        clocks = [c + 1 for c in clocks]

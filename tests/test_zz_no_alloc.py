@@ -3,9 +3,10 @@
 It serves callers that must not allocate device memory while decoding, for example a host
 whose GPU memory belongs to another allocator's fixed arena.  The test calls it through the
 C ABI twice in a row with different inputs (the shared scratch keeps the first call's
-partials) and compares each result with the engine-based sx_dispatch_decode_attn.  It makes
-its own first call before asking for an engine, so in a fresh process it also shows that the
-entry point works without one.  This file is collected last on purpose.
+partials) and compares each result with the CPU checker's decode attention
+(src/model/forward.zig:77-104) and with the engine-based sx_dispatch_decode_attn.  Its calls
+come before it asks for the engine fixture, so when this file runs alone in a fresh process
+they run with no engine in the process.  This file is collected last on purpose.
 """
 import ctypes
 
@@ -41,6 +42,7 @@ def _case(seed, num_q, num_kv, d, clock, n_recall):
 
     slot_arr = np.concatenate([slots, np.zeros(total - len(slots), np.uint32)]).view(np.int32)
     return dict(
+        q_host=q, k_host=k, v_host=v, slots_host=slots, num_kv=num_kv,
         q=torch.from_numpy(q).cuda(), k=bf16_dev(k), v=bf16_dev(v),
         slots=torch.from_numpy(slot_arr).cuda(),
         step=torch.from_numpy(np.array([clock, 0, len(slots), 0], np.int32)).cuda(),
@@ -56,7 +58,7 @@ def _noalloc(c, scale, out):
     sx.check(st)
 
 
-def test_noalloc_attention_matches_engine_path_twice(request):
+def test_noalloc_attention_matches_checker_and_engine_path_twice(request):
     cases = [(_case(1, 16, 8, 256, 7000, 40), 1.0), (_case(2, 8, 1, 256, 99999, 96), 1 / 16)]
     outs = []
     for c, scale in cases:  # two calls in a row share the fixed scratch
@@ -64,6 +66,10 @@ def test_noalloc_attention_matches_engine_path_twice(request):
         _noalloc(c, scale, o)
         outs.append(o)
     torch.cuda.synchronize()
+    for (c, scale), got in zip(cases, outs):
+        ref = orc.decode_attn(c["q_host"], c["k_host"], c["v_host"], c["slots_host"], c["num_q"],
+                              c["num_kv"], c["d"], c["total"], scale)
+        assert_close(got.cpu().numpy(), ref, atol=1e-4, rtol=1e-3, what="noalloc vs checker")
     engine = request.getfixturevalue("engine")
     for (c, scale), got in zip(cases, outs):
         want = torch.empty_like(got)
