@@ -285,6 +285,14 @@ sx_status run_op(sx_engine *e, cudaStream_t s, const Op &op, uint32_t *kernels) 
       *kernels += 1;
       return sx_host_tp_argmax(static_cast<const uint32_t *>(op.bind.at(0)), op.u[0],
                                static_cast<uint32_t *>(op.bind.at(1)), s);
+    case OP_STREAM: {
+      *kernels += 1;
+      SX_TRY_CUDA(cudaMemsetAsync(op.bind.at(0), 0, 4ull * (op.u[0] + 1), s), "counter reset");
+      return cuda_status(sx::launch_stream(static_cast<const sx::Phase *>(op.dev), op.u[0],
+                                           static_cast<uint32_t *>(op.bind.at(0)), e->err_dev,
+                                           e->num_sms, s),
+                         "streaming decode launch");
+    }
     case OP_PERSIST: {
       *kernels += 1;
       SX_TRY_CUDA(cudaMemsetAsync(e->persist_bar, 0, 8, s), "barrier reset");
@@ -583,6 +591,8 @@ SX_API sx_status sx_engine_create(int device, sx_quant_mode mode, uint32_t flags
     if (st) break;
     st = cuda_status(sx::prepare_persist_kernel(), "persistent kernel attributes");
     if (st) break;
+    st = cuda_status(sx::prepare_stream_kernel(), "streaming kernel attributes");
+    if (st) break;
     st = cuda_status(sx::prepare_prefill_kernel(), "prefill kernel attributes");
   } while (0);
   if (st != SX_OK) {
@@ -779,9 +789,11 @@ static void cmd_release_graph(sx_cmd *c) {
   if (c->exec) cudaGraphExecDestroy(c->exec);
   if (c->graph) cudaGraphDestroy(c->graph);
   if (c->d_phases) cudaFree(c->d_phases);
+  if (c->d_ctr) cudaFree(c->d_ctr);
   c->exec = nullptr;
   c->graph = nullptr;
   c->d_phases = nullptr;
+  c->d_ctr = nullptr;
 }
 
 // Persistent command buffer: the recorded H2D copies, then the GEMV_FUSED / ATTN_FUSED
@@ -790,6 +802,7 @@ static void cmd_release_graph(sx_cmd *c) {
 // and q's shared-memory layout ends below the attention work items (the o projection).
 static sx_status build_persistent(sx_cmd *c) {
   sx_engine *e = c->e;
+  const bool stream = c->persistent == kPersistStream;
   std::vector<Op> head, tail;
   std::vector<sx::Phase> ph;
   for (const Op &op : c->ops) {
@@ -810,6 +823,15 @@ static sx_status build_persistent(sx_cmd *c) {
         }
         p.kind = sx::kPhaseGemv;
         p.g = op.gemv;
+        if (stream) {
+          if (!sx::stream_gemv_variant(op.qt, op.geglu, op.gemv, e->num_sms, &p.variant)) {
+            set_error("streaming graph: GEMV k=%u batch=%u has no streaming form", op.gemv.k,
+                      op.gemv.batch);
+            return SX_ERR_UNSUPPORTED;
+          }
+          ph.push_back(p);
+          continue;
+        }
         if (!sx::persist_gemv_variant(op.qt, op.geglu, op.gemv, sx::persist_smem_bytes(),
                                       &p.variant, &p.smem_off)) {
           set_error("persistent graph: GEMV k=%u batch=%u has no persistent instantiation",
@@ -829,6 +851,15 @@ static sx_status build_persistent(sx_cmd *c) {
         sx_status fst = SX_OK;
         p.at.inv_freq = engine_inv_freq(e, op.attn_rot, op.attn_theta, &fst);
         if (!p.at.inv_freq) return fst;
+        if (stream) {
+          if (!sx::stream_attn_variant(p.at, &p.variant)) {
+            set_error("streaming graph: attention head_dim=%u gqa=%u has no streaming form",
+                      p.at.head_dim, p.at.num_q / (p.at.num_kv ? p.at.num_kv : 1));
+            return SX_ERR_UNSUPPORTED;
+          }
+          ph.push_back(p);
+          continue;
+        }
         if (!sx::persist_attn_variant(p.at, &p.variant)) {
           set_error("persistent graph: attention head_dim=%u gqa=%u has no persistent "
                     "instantiation", p.at.head_dim, p.at.num_q / (p.at.num_kv ? p.at.num_kv : 1));
@@ -849,9 +880,13 @@ static sx_status build_persistent(sx_cmd *c) {
   const size_t bytes = sizeof(sx::Phase) * ph.size();
   SX_TRY_CUDA(cudaMalloc(&c->d_phases, bytes), "phase table");
   SX_TRY_CUDA(cudaMemcpy(c->d_phases, ph.data(), bytes, cudaMemcpyHostToDevice), "phase table");
-  Op run{OP_PERSIST};
+  Op run{stream ? OP_STREAM : OP_PERSIST};
   run.u[0] = (uint32_t)ph.size();
   run.dev = c->d_phases;
+  if (stream) {
+    SX_TRY_CUDA(cudaMalloc(&c->d_ctr, 4 * (ph.size() + 1)), "phase counters");
+    run.bind = {c->d_ctr};
+  }
   c->ops = head;
   c->ops.push_back(run);
   c->ops.insert(c->ops.end(), tail.begin(), tail.end());
@@ -873,7 +908,7 @@ SX_API sx_status sx_cmd_begin(sx_cmd *c) {
   c->poison_msg.clear();
   c->recording = true;
   c->kernels = 0;
-  c->persistent = false;
+  c->persistent = kPersistNone;
   return SX_OK;
 }
 

@@ -115,6 +115,26 @@ SX_DEV float inv_rms(float ss, uint32_t n, float eps) {
   return __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)n), eps)));
 }
 
+// The threads that run a prologue / x staging and how they synchronise: the whole CTA
+// (__syncthreads) in the GEMV kernels, the consumer warps alone (a named barrier) in the
+// streaming decode kernel, whose producer warp never joins them.
+struct CtaSync {
+  SX_DEV void operator()() const { __syncthreads(); }
+  SX_DEV uint32_t threads() const { return blockDim.x; }
+};
+
+// Sum over the synchronising threads; `red` holds >= 32 floats.  All of them get the result.
+template <typename Sync>
+SX_DEV float group_block_sum(float v, float *red, const Sync &sync) {
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = (int)(sync.threads() + 31) >> 5;
+  v = warp_sum(v);
+  sync();
+  if (lane == 0) red[wid] = v;
+  sync();
+  float t = lane < nw ? red[lane] : 0.0f;
+  return warp_sum(t);
+}
+
 // ---------------------------------------------------------------------------------------
 // Fused input prologues (replace a separate norm launch).  Each CTA computes the GEMV input
 // for all batch rows into shared memory with one round trip to global memory:
@@ -123,15 +143,16 @@ SX_DEV float inv_rms(float ss, uint32_t n, float eps) {
 //              CTA 0 writes xn to x_out; xin = rmsnorm(xn, w)         (add_rmsnorm.wgsl)
 constexpr int kProPer = 8;  // elements per thread held in registers: K <= 512 * 8
 
-SX_DEV void run_prologue(const GemvArgs &a, float *xin, float *red) {
-  const uint32_t K = a.k;
+template <typename Sync = CtaSync>
+SX_DEV void run_prologue(const GemvArgs &a, float *xin, float *red, const Sync &sync = Sync()) {
+  const uint32_t K = a.k, nthr = sync.threads();
   for (uint32_t j = 0; j < a.batch; ++j) {
     float *xo = xin + (size_t)j * K;
     const float *x = a.x + (size_t)j * a.ldx;
     float xv[kProPer], mv[kProPer], pw[kProPer], nw[kProPer];
 #pragma unroll
     for (int q = 0; q < kProPer; ++q) {
-      uint32_t i = threadIdx.x + q * blockDim.x;
+      uint32_t i = threadIdx.x + q * nthr;
       bool in = i < K;
       xv[q] = in ? __ldcg(x + i) : 0.0f;  // activations: through L2 (see stage_x)
       nw[q] = in ? a.pro_w[i] : 0.0f;
@@ -148,7 +169,7 @@ SX_DEV void run_prologue(const GemvArgs &a, float *xin, float *red) {
         float ss = 0.0f;
 #pragma unroll
         for (int q = 0; q < kProPer; ++q) ss = fmaf(mv[q], mv[q], ss);
-        rm = inv_rms(block_sum(ss, red), K, a.eps);
+        rm = inv_rms(group_block_sum(ss, red, sync), K, a.eps);
       }
 #pragma unroll
       for (int q = 0; q < kProPer; ++q) {
@@ -159,7 +180,7 @@ SX_DEV void run_prologue(const GemvArgs &a, float *xin, float *red) {
       if (blockIdx.x == 0) {
 #pragma unroll
         for (int q = 0; q < kProPer; ++q) {
-          uint32_t i = threadIdx.x + q * blockDim.x;
+          uint32_t i = threadIdx.x + q * nthr;
           if (i < K) a.pro_x_out[(size_t)j * a.ldx + i] = xv[q];
         }
       }
@@ -167,21 +188,22 @@ SX_DEV void run_prologue(const GemvArgs &a, float *xin, float *red) {
     float ss = 0.0f;
 #pragma unroll
     for (int q = 0; q < kProPer; ++q) ss = fmaf(xv[q], xv[q], ss);
-    float r = inv_rms(block_sum(ss, red), K, a.eps);
+    float r = inv_rms(group_block_sum(ss, red, sync), K, a.eps);
 #pragma unroll
     for (int q = 0; q < kProPer; ++q) {
-      uint32_t i = threadIdx.x + q * blockDim.x;
+      uint32_t i = threadIdx.x + q * nthr;
       if (i < K) xo[i] = __fmul_rn(__fmul_rn(xv[q], r), nw[q]);
     }
-    __syncthreads();
+    sync();
   }
 }
 
 // Activation -> B fragments.  Item (blk, j, c, jj) converts elements 32*blk + 8*jj + 2c,+1
 // of batch row j into the hi/lo pair words and reduces the block sum for the offset term.
-template <int QT>
+template <int QT, typename Sync = CtaSync>
 SX_DEV void stage_x(const GemvArgs &a, const float *src, uint32_t ld, uint8_t *smem,
-                    const Layout &L, bool src_global) {
+                    const Layout &L, bool src_global, const Sync &sync = Sync()) {
+  const uint32_t nthr = sync.threads();
   uint32_t *xf = reinterpret_cast<uint32_t *>(smem + L.xfrag);
   float *corr = reinterpret_cast<float *>(smem + L.corr);
   float *xscale = reinterpret_cast<float *>(smem + L.misc);
@@ -195,15 +217,15 @@ SX_DEV void stage_x(const GemvArgs &a, const float *src, uint32_t ld, uint8_t *s
     // precision: max |x| * 2^e < 2^15.
     for (uint32_t j = 0; j < a.batch; ++j) {
       float mx = 0.0f;
-      for (uint32_t i = tid; i < a.k; i += blockDim.x)
+      for (uint32_t i = tid; i < a.k; i += nthr)
         mx = fmaxf(mx, fabsf(src_global ? __ldcg(src + j * ld + i) : src[j * ld + i]));
       mx = warp_max(mx);
-      __syncthreads();
+      sync();
       if ((tid & 31) == 0) red[tid >> 5] = mx;
-      __syncthreads();
+      sync();
       if (tid == 0) {
         float m = 0.0f;
-        for (int w = 0; w < (int)(blockDim.x >> 5); ++w) m = fmaxf(m, red[w]);
+        for (int w = 0; w < (int)(nthr >> 5); ++w) m = fmaxf(m, red[w]);
         int e = 0;
         if (m > 0.0f && isfinite(m)) {
           int ex;
@@ -214,14 +236,14 @@ SX_DEV void stage_x(const GemvArgs &a, const float *src, uint32_t ld, uint8_t *s
         xexp[j] = e;
         xscale[j] = ldexpf(1.0f, -e);
       }
-      __syncthreads();
+      sync();
     }
   } else {
     if (tid < (int)a.batch) {
       xscale[tid] = 2.0f;
       xexp[tid] = 0;
     }
-    __syncthreads();
+    sync();
   }
 
   // One thread per group of 8 consecutive elements (block blk, word jj of each of the four
@@ -232,7 +254,7 @@ SX_DEV void stage_x(const GemvArgs &a, const float *src, uint32_t ld, uint8_t *s
   for (uint32_t j = 0; j < a.batch; ++j) {
     // Q8: multiply by 2^e (exact for a power of two, e in [-100, 100])
     const float p2 = QT == 8 ? __int_as_float((xexp[j] + 127) << 23) : 1.0f;
-    for (uint32_t gi = tid; gi < gpad; gi += blockDim.x) {
+    for (uint32_t gi = tid; gi < gpad; gi += nthr) {
       const uint32_t blk = gi >> 2, jj = gi & 3;
       float part = 0.0f;
       if (gi < groups) {
@@ -288,7 +310,7 @@ SX_DEV void stage_x(const GemvArgs &a, const float *src, uint32_t ld, uint8_t *s
         corr[((blk >> 1) * a.batch + j) * 2 + (blk & 1)] = (QT == 4 ? 12.0f : 1152.0f) * part;
     }
   }
-  __syncthreads();
+  sync();
 }
 
 // One 32-element block of one 16-row tile: two chained m16n8k16 MMAs per column set, the

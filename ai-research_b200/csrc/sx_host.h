@@ -67,6 +67,7 @@ enum OpKind {
   OP_GEMV_FUSED,  // multi-segment GEMV with fused prologue / epilogue (model graph)
   OP_ATTN_FUSED,  // qkv_rope + decode attention + combine (model graph)
   OP_PERSIST,     // the GEMV_FUSED / ATTN_FUSED run of a persistent command buffer
+  OP_STREAM,      // the same run as one streaming decode launch (sx_stream.cu)
   OP_ALLREDUCE,   // tensor parallel: in-place sum all-reduce of u[0] floats at dev
   OP_ALLGATHER,   // tensor parallel: bind[0] (u[0] u32 words per rank) -> bind[1]
   OP_TP_ARGMAX,   // tensor parallel: merge u[0] ranks' argmax candidates bind[0] -> bind[1]
@@ -101,16 +102,19 @@ struct sx_cmd {
   cudaGraph_t graph = nullptr;
   cudaGraphExec_t exec = nullptr;
   uint32_t kernels = 0;
-  // persistent: the fused kernels run as phases of one cooperative launch (sx_persist.cu)
-  bool persistent = false;
+  // persistent: the fused kernels run as phases of one cooperative launch -- kPersistPhases
+  // (sx_persist.cu, grid barriers) or kPersistStream (sx_stream.cu, producer-warp weight ring)
+  int persistent = 0;
   sx::Phase *d_phases = nullptr;
+  uint32_t *d_ctr = nullptr;  // kPersistStream: per-phase completion counters + abort word
 };
+constexpr int kPersistNone = 0, kPersistPhases = 1, kPersistStream = 2;
 
 
 // Append an op (including the internal host<->device copy ops) to a recording command buffer.
 void sx_host_push_op(sx_cmd *c, const Op &op);
 // record the command buffer's fused kernels as one persistent launch (sx_persist.cu)
-inline void sx_host_set_persistent(sx_cmd *c, bool on) { c->persistent = on; }
+inline void sx_host_set_persistent(sx_cmd *c, int kind) { c->persistent = kind; }
 void sx_host_set_error(const char *fmt, ...);  // printf-style
 // tensor parallel (sx_tp.cu): collectives and the argmax-candidate merge on stream s
 sx_status sx_host_allreduce(sx_comm *c, float *buf, size_t count, cudaStream_t s);

@@ -211,6 +211,18 @@ bool persist_gemv_variant(int qt, bool geglu, const GemvArgs &a, uint32_t smem_l
 bool persist_attn_variant(const AttnFusedArgs &a, uint32_t *variant);
 cudaError_t prepare_persist_kernel();
 
+// Streaming decode kernel (sx_stream.cu): the same phase table as one cooperative launch whose
+// producer warp streams every GEMV phase's weights through a shared-memory ring.  ctr: one
+// completion counter per phase plus an abort word (n + 1 words), zeroed before every launch.
+uint32_t stream_smem_bytes();
+uint32_t stream_threads();
+// false when the call has no streaming form (batch > 1, fewer than 16 block pairs, ...)
+bool stream_gemv_variant(int qt, bool geglu, const GemvArgs &a, int num_sms, uint32_t *variant);
+bool stream_attn_variant(const AttnFusedArgs &a, uint32_t *variant);
+cudaError_t prepare_stream_kernel();
+cudaError_t launch_stream(const Phase *phases, uint32_t n, uint32_t *ctr, uint32_t *err,
+                          int num_sms, cudaStream_t s);
+
 // Batch-prefill Q4_0 projection GEMM (sx_prefill.cu): y[t][n] = x[t][:] . bf16(deq(w[n][:]))
 cudaError_t prepare_prefill_kernel();
 cudaError_t launch_prefill_q4(const void *w, const void *x, float *y, uint32_t t, uint32_t n,

@@ -328,7 +328,7 @@ sx::GemvArgs gemv1(const sx_buffer *w, const sx_buffer *x, sx_buffer *y, uint32_
 // nb: sessions stepped together (1 for the one-session graphs); every GEMV runs with batch nb
 // (row j = session j) and the attention with one grid layer per session.
 sx_status record_forward_fused(sx_model *m, sx_cmd *cmd, bool logits, bool io,
-                               bool persistent, uint32_t nb = 1) {
+                               int persistent, uint32_t nb = 1) {
   const sx_model_config &c = m->c;
   const uint32_t H = c.hidden_size, I = m->I, L = c.num_layers;
   const bool tp = m->comm != nullptr;
@@ -499,7 +499,10 @@ sx_status record_forward_fused(sx_model *m, sx_cmd *cmd, bool logits, bool io,
 
 sx_status record_graph(sx_model *m, sx_cmd *cmd, bool logits, bool io) {
   if (m->c.reference_graph == 1) return record_forward(m, cmd, logits, io);
-  return record_forward_fused(m, cmd, logits, io, m->c.reference_graph == 2);
+  const int kind = m->c.reference_graph == 2   ? kPersistPhases
+                   : m->c.reference_graph == 3 ? kPersistStream
+                                               : kPersistNone;
+  return record_forward_fused(m, cmd, logits, io, kind);
 }
 
 // rows x cols of the synthetic matrix (seed, stream), starting at global row `grow0` and
@@ -544,7 +547,7 @@ sx_status create_model(sx_engine *e, const sx_model_config *cfg, sx_comm *comm, 
   bool ok = c.vocab_size > 0 && c.hidden_size % 32 == 0 && c.intermediate_size % 32 == 0 &&
             c.num_layers > 0 && c.num_q_heads > 0 && c.num_kv_heads > 0 &&
             c.num_q_heads % c.num_kv_heads == 0 && c.window_size > 0 && c.head_dim > 0 &&
-            (c.num_q_heads * c.head_dim) % 32 == 0 && c.reference_graph <= 2;
+            (c.num_q_heads * c.head_dim) % 32 == 0 && c.reference_graph <= 3;
   if (c.full_every)
     ok = ok && c.num_global_kv_heads > 0 && c.num_q_heads % c.num_global_kv_heads == 0 &&
          c.global_head_dim > 0;

@@ -50,9 +50,13 @@ def parse():
     ap.add_argument("--impl", default="sx", choices=["sx", "reference"])
     ap.add_argument("--layers", type=int, default=48)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--graph", choices=["persistent", "fused"], default="fused",
-                    help="persistent: one cooperative launch per token; fused: 5 kernels per "
-                         "layer chained with programmatic dependent launch")
+    ap.add_argument("--no-kernel-lines", action="store_true",
+                    help="skip the stand-alone config 1-3 kernel measurements")
+    ap.add_argument("--graph", choices=["stream", "persistent", "fused"], default="fused",
+                    help="stream: one launch per token with a producer warp per SM streaming "
+                         "the weights through a shared-memory ring (one GPU); persistent: one "
+                         "cooperative launch per token with grid barriers; fused: 5 kernels "
+                         "per layer chained with programmatic dependent launch")
     ap.add_argument("--case", choices=["geglu", "q4_head", "attn", "prefill", "sessions"],
                     help="profiling case: launch one kernel of the step standalone "
                          "(--launches times) on synthetic data and exit; prints no JSON line")
@@ -255,13 +259,148 @@ def load_peaks():
     return 6650.0, "fallback"
 
 
-def profiled_traffic():
-    """dram read+write bytes per launch of the GeGLU kernel from the committed ncu summary."""
-    f = ROOT / "profiles" / "gate_up_geglu_q4_12b.md"
+def profiled_traffic(key: str):
+    """dram read + write bytes per launch of one kernel at one shape, from the ncu captures
+    recorded in profiles/dram_traffic.json (None when that shape was not captured)."""
+    f = ROOT / "profiles" / "dram_traffic.json"
     if not f.exists():
         return None
-    m = re.search(r"traffic_bytes_per_launch:\s*([0-9]+)", f.read_text())
-    return int(m.group(1)) if m else None
+    entry = json.loads(f.read_text()).get("kernels", {}).get(key)
+    return int(entry["dram_bytes_per_launch"]) if entry else None
+
+
+def graph_time_ms(torch, eng, launch, reps=5):
+    """Device time of one call of `launch()` (which issues work on the engine stream): the
+    calls are captured once into a CUDA graph and the graph is replayed `reps` times between
+    CUDA events on the replay stream."""
+    s = torch.cuda.Stream()
+    eng.set_stream(s.cuda_stream)
+    try:
+        with torch.cuda.stream(s):
+            launch()  # warm-up outside the capture (first-use set-up)
+        s.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=s):
+            launch()
+        with torch.cuda.stream(s):
+            g.replay()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(s)
+            for _ in range(reps):
+                g.replay()
+            e1.record(s)
+        s.synchronize()
+        return e0.elapsed_time(e1) / reps
+    finally:
+        eng.set_stream(None)
+
+
+def kernel_lines(torch, eng, peak) -> dict:
+    """BASELINE configs 1-3 as stand-alone kernels, each over copies larger than L2 so that the
+    bytes come from HBM: c1, the 6144 x 1536 Q4_0 GEMV over 64 weight copies in one graph; c2,
+    the GeGLU MLP (gate+up, then down; H 1536, I 6144) over 64 weight sets at batch 1 and 8; c3,
+    the fused q/k norm + RoPE + cache write + attention over 256 independent 640-slot rings
+    (8 q heads, 1 kv head, D 256, bf16 cache) in one launch."""
+    import sx
+
+    out = {}
+
+    def synth(m, k, copies, seed):
+        """`copies` device copies (torch uint8 tensors) of one synthetic packed Q4_0 matrix."""
+        words = sx.quantized_row_words(k, sx.QUANT_Q4)
+        ref = torch.empty(m * words, dtype=torch.int32, device="cuda")
+        eng.synth_weights(sx.QUANT_Q4, ref, 0, m, k, seed, 1)
+        nb = sx.packed_bytes(m, k, sx.QUANT_Q4)
+        first = torch.empty(nb, dtype=torch.uint8, device="cuda")
+        eng.sync()
+        torch.cuda.synchronize()
+        buf = eng.wrap(first.data_ptr(), nb)
+        buf.repack_device(ref.data_ptr(), m, k, sx.QUANT_Q4)
+        eng.sync()
+        buf.close()
+        return [first] + [first.clone() for _ in range(copies - 1)], nb
+
+    # ---- c1
+    M, K, C = 6144, 1536, 64
+    w, nb = synth(M, K, C, SEED + 11)
+    x = torch.randn(K, device="cuda").to(torch.bfloat16).float()
+    y = torch.empty(M, device="cuda")
+    ms = graph_time_ms(torch, eng, lambda: [eng.gemv(sx.QUANT_Q4, b, x, y, M, K, 1)
+                                             for b in w])
+    alg = M * K // 32 * 20 + 4 * K + 4 * M
+    per = ms / C
+    out["c1_gemv_q4_6144x1536"] = {
+        "us_per_call": per * 1e3, "algorithmic_bytes_per_call": alg,
+        "achieved_gbs": alg / (per / 1e3) / 1e9, "frac": alg / (per / 1e3) / 1e9 / peak,
+        "copies": C, "working_set_mb": C * nb / 1e6,
+        "traffic": profiled_traffic("gemv_q4_6144x1536"),
+        "timing": "64 launches on distinct weight copies captured in one CUDA graph"}
+    del w
+    # ---- c2
+    H, I = 1536, 6144
+    wg, _ = synth(I, H, 2 * C, SEED + 12)
+    wd, _ = synth(H, I, C, SEED + 13)
+    sets = [(wg[2 * i], wg[2 * i + 1], wd[i]) for i in range(C)]
+    for batch in (1, 8):
+        xb = torch.randn(batch, H, device="cuda")
+        act = torch.empty(batch, I, device="cuda")
+        yb = torch.empty(batch, H, device="cuda")
+
+        def mlp():
+            for g, u, d in sets:
+                eng.gate_up(g, u, xb, act, I, H, batch)
+                eng.gemv(sx.QUANT_Q4, d, act, yb, H, I, batch)
+
+        ms = graph_time_ms(torch, eng, mlp)
+        alg = 3 * (I * H // 32 * 20) + batch * 4 * (2 * H + 2 * I)
+        per = ms / C
+        out[f"c2_geglu_mlp_b{batch}"] = {
+            "us_per_step": per * 1e3, "algorithmic_bytes_per_step": alg,
+            "achieved_gbs": alg / (per / 1e3) / 1e9, "frac": alg / (per / 1e3) / 1e9 / peak,
+            "tokens_per_s": batch / (per / 1e3), "copies": C,
+            "timing": "64 (gate+up, down) launch pairs on distinct weight sets in one CUDA graph"}
+    del sets, wg, wd
+    # ---- c3
+    n, G, D, total = 256, 8, 256, 640
+    rng = np.random.default_rng(SEED + 3)
+    stride = (G + 2) * D
+    qkv = torch.randn(n * stride, device="cuda")
+    kc = torch.randn(n * total * D, device="cuda").to(torch.bfloat16).view(torch.int16)
+    vc = torch.randn(n * total * D, device="cuda").to(torch.bfloat16).view(torch.int16)
+    qn = torch.ones(D, device="cuda")
+    kn = torch.ones(D, device="cuda")
+    slots = np.zeros((n, total), np.uint32)
+    steps = np.zeros((n, 4), np.uint32)
+    for i in range(n):
+        ring = sx.Ring(1, 32, 512, 96)
+        c = int(rng.integers(544, 100000))
+        ring.prefill(0, c)
+        for r in range(96):
+            ring.write_recall(0, r, int(rng.integers(0, c)))
+        sl = ring.activate_slot(0, c)
+        a = ring.get_active_slots(0, c)
+        slots[i, :len(a)] = a
+        steps[i] = (c, sl, len(a), 0)
+        ring.close()
+    d_slots = torch.from_numpy(slots.view(np.int32)).cuda()
+    d_steps = torch.from_numpy(steps.view(np.int32)).cuda()
+    att = torch.empty(n * G * D, device="cuda")
+    p0 = qkv.data_ptr()
+
+    def attn():
+        eng.qkv_rope_attn(p0, p0 + 4 * G * D, p0 + 4 * (G + 1) * D, qn, kn, kc, vc, d_slots,
+                          d_steps, att, G, 1, D, 64, 0, 1e6, 1e-6, 1.0 / 16, total, n, stride)
+
+    ms = graph_time_ms(torch, eng, attn, reps=10)
+    live = int(steps[:, 2].sum())
+    alg = live * D * 2 * 2 + n * (stride + G * D) * 4 + n * total * 4
+    out["c3_attention_640slot_x256"] = {
+        "us_per_launch": ms * 1e3, "instances": n, "live_slots": live,
+        "algorithmic_bytes_per_launch": alg, "achieved_gbs": alg / (ms / 1e3) / 1e9,
+        "frac": alg / (ms / 1e3) / 1e9 / peak, "working_set_mb": 2 * n * total * D * 2 / 1e6,
+        "traffic": profiled_traffic("attn_cluster_c3_x256"),
+        "timing": "one launch over 256 independent rings (168 MB of bf16 K/V), graph replays"}
+    return out
 
 
 class ClockSampler:
@@ -318,61 +457,60 @@ class ClockSampler:
 
 
 # ----------------------------------------------------------------------------------------
-class CpuSample:
-    """The CPU checker (restatement of the reference's Q4 decode path) on a bounded sample of
-    one token: two 12B-width layers (one sliding, one full attention, 640 live slots) and
-    16384 of the 262144 LM-head rows, extrapolated x24 (layers) and x16 (head)."""
+class CpuToken:
+    """The CPU checker (restatement of the reference's Q4 decode path, oracle/) running whole
+    decode tokens of the benchmarked workload: 48 12B-width layers with 640 live ring slots, the
+    full 262144-row Q8_0 LM head and the argmax, on all host cores."""
 
-    def __init__(self):
+    def __init__(self, layers: int = 48):
         from oracle import oracle as orc
 
-        self.orc = orc
         self.cores = os.cpu_count() or 1
-        cfg = model_cfg_dict(2)
-        cfg["vocab_size"] = 16  # the head is timed separately on a row sample
-        cfg["full_every"] = 2
+        t0 = time.perf_counter()
+        cfg = model_cfg_dict(layers)
         self.m = orc.Model(cfg, SEED, nthreads=self.cores)
         self.m.fill_kv(SEED)
         self.m.ring.prefill(0, START_CLOCK)
         self.m.synth_recall(START_CLOCK, 96, SEED)
-        self.head_rows = 262144 // 16
-        self.w8 = orc.synth_q8(self.head_rows, 3840, SEED, 2)
-        self.x = orc.synth_embed_row(3840, 5, SEED)
+        self.setup_s = time.perf_counter() - t0
+        self.layers = layers
+        self.token = 5
         self.k = 0
 
     def step(self) -> float:
-        """Seconds per token extrapolated from one sample."""
+        """Seconds for one whole token (greedy: the sampled token feeds the next step)."""
+        from oracle import oracle as orc
+
+        x = orc.synth_embed_row(3840, self.token, SEED)
         t0 = time.perf_counter()
-        self.m.forward(self.x, START_CLOCK + self.k, want_logits=False)
-        t1 = time.perf_counter()
-        self.orc.gemv_q8(self.w8, self.x, self.head_rows, 3840)
-        t2 = time.perf_counter()
+        tok, _, _ = self.m.forward(x, START_CLOCK + self.k, want_logits=True)
+        dt = time.perf_counter() - t0
+        self.token = int(tok)
         self.k += 1
-        return 24 * (t1 - t0) + 16 * (t2 - t1)
+        return dt
 
     def describe(self, n) -> str:
-        return (f"{n} samples of 2 of 48 12B-width layers + 16384 of 262144 LM-head rows "
-                f"(CPU checker, {self.cores} threads), extrapolated x24 / x16 to one token")
+        return (f"{n} whole tokens of the c4 workload ({self.layers} layers, 640 live slots, "
+                f"262144-row Q8_0 head + argmax) on the CPU checker with {self.cores} threads "
+                f"(model set-up {self.setup_s:.1f} s, untimed)")
 
 
-def cpu_baseline(budget_s: float = 20.0) -> dict:
-    cs = CpuSample()
-    times = []
-    t_end = time.perf_counter() + budget_s
-    while time.perf_counter() < t_end and len(times) < 20:
-        times.append(cs.step())
-    per_token = statistics.median(times)
-    return {"value": 1.0 / per_token, "unit": UNIT, "cores": cs.cores, "kind": "port",
-            "sample": cs.describe(len(times))}
+def cpu_baseline(tokens: int = 4) -> dict:
+    ct = CpuToken()
+    ct.step()  # warm-up token
+    times = [ct.step() for _ in range(tokens)]
+    per_token = sum(times) / len(times)
+    return {"value": 1.0 / per_token, "unit": UNIT, "cores": ct.cores, "kind": "port",
+            "sample": ct.describe(tokens)}
 
 
 def run_reference(args, rank, world):
     if rank != 0:
         return
-    cs = CpuSample()
+    ct = CpuToken()
     for _ in range(args.warmup):
-        cs.step()
-    steps = [cs.step() for _ in range(args.steps)]
+        ct.step()
+    steps = [ct.step() for _ in range(args.steps)]
     per_token = sum(steps) / len(steps)
     value = 1.0 / per_token
     line = {
@@ -380,14 +518,17 @@ def run_reference(args, rank, world):
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": per_token * 1e3,
         "higher_is_better": True, "scaling": "strong" if world > 1 else "weak",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": "c4: 12B-shape Q4_0 decode, batch 1, 48 layers, H 3840, "
-                               "16q/8kv x 256, I 15360, vocab 262144, 640 live ring slots",
+        "config": {"workload": "c4: 12B-shape Q4_0 greedy decode, batch 1, 48 layers, H 3840, "
+                               "16q/8kv x 256, I 15360, vocab 262144 (Q8_0 head), 640 live ring "
+                               "slots",
                    "parallelism": "cpu"},
-        "cpu_baseline": {"value": value, "unit": UNIT, "cores": cs.cores, "kind": "port",
-                         "sample": cs.describe(args.steps)},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": ct.cores, "kind": "port",
+                         "sample": ct.describe(args.steps)},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "timed_s": sum(steps),
         "note": ("the reference's own CPU path is Zig and cannot be built here (no zig "
-                 "toolchain); timed the C restatement of its Q4 decode path instead"),
+                 "toolchain); timed the C restatement of its Q4 decode path instead, whole "
+                 "tokens"),
     }
     print(json.dumps(line), flush=True)
 
@@ -418,7 +559,7 @@ def main():
     import sx
 
     cfgd = model_cfg_dict(args.layers)
-    cfgd["reference_graph"] = 2 if args.graph == "persistent" else 0
+    cfgd["reference_graph"] = {"persistent": 2, "stream": 3}.get(args.graph, 0)
     eng = sx.Engine(local)
     comm = None
     if world > 1:
@@ -527,12 +668,14 @@ def main():
         x = sx.synth_embed_row(H, token, SEED)
         s = ring.activate_slot(0, c)
         token = model.forward_token(x, c, s, ring.get_active_slots(0, c), True)
+    stream_tokens = []
     t0 = time.perf_counter()
     for i in range(args.steps):
         c = START_CLOCK + nsteps + args.warmup + i
         x = sx.synth_embed_row(H, token, SEED)
         s = ring.activate_slot(0, c)
         token = model.forward_token(x, c, s, ring.get_active_slots(0, c), True)
+        stream_tokens.append(token)
     e2e_s = time.perf_counter() - t0
     if dist is not None:
         t = torch.tensor([e2e_s], device="cuda")
@@ -567,7 +710,12 @@ def main():
     eng.sync()
     launch_ms = e0.elapsed_time(e1) / (reps * len(wbufs))
     achieved = gu_bytes / (launch_ms / 1e3) / 1e9
-    traffic = profiled_traffic()
+    traffic = profiled_traffic(f"gate_up_q4_{I}x{H}")
+    kernels = None
+    if world == 1 and args.layers == 48 and not args.no_kernel_lines:
+        kernels = kernel_lines(torch, eng, peak)
+    import hashlib
+    tok_bytes = np.asarray(stream_tokens, np.uint32).tobytes()
 
     alg = algorithmic_bytes_per_token(cfgd)
     line = {
@@ -582,15 +730,20 @@ def main():
             "parallelism": f"tp{world} ({'NCCL' if args.allreduce == 'nccl' else 'one-shot peer'} "
                            f"all-reduce x2 per layer, vocab-parallel head)"
                            if world > 1 else "single",
-            "graph": ("one persistent cooperative launch per token"
-                      if cfgd["reference_graph"] == 2
-                      else "5 kernels per layer + LM head, programmatic dependent launch"),
+            "graph": {2: "one persistent cooperative launch per token (grid barriers)",
+                      3: "one streaming launch per token (producer warp per SM, weight ring)"}
+                     .get(cfgd["reference_graph"],
+                          "5 kernels per layer + LM head, programmatic dependent launch"),
             "l2": "inputs larger than L2 (8.1 GB of weights+KV read per step)",
             "algorithmic_bytes_per_token": alg["total"],
             "hbm_gbs_per_token_rate": alg["total"] * value / 1e9,
         },
         "e2e": {"value": e2e, "unit": UNIT,
                 "h2d_bytes_per_step": 4 * H + 4 * total_slots + 16, "d2h_bytes_per_step": 4},
+        # the e2e leg's greedy token stream (same inputs for every GPU count: a tensor-parallel
+        # run must reproduce the one-GPU stream)
+        "tokens_sha256": hashlib.sha256(tok_bytes).hexdigest(),
+        "tokens_head": [int(t) for t in stream_tokens[:8]],
         "gpu_launches": kernels_per_token * args.steps,
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                      "frac": achieved / peak, "traffic": traffic,
@@ -599,6 +752,8 @@ def main():
                      "peak_kind": peak_kind + " (burst copy)"},
         "clocks": clk,
     }
+    if kernels is not None:
+        line["kernels"] = kernels
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline()
     if rank == 0:

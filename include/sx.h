@@ -292,7 +292,11 @@ typedef struct {
   uint32_t reference_graph;  /* graph of one token: 1 = the reference's op-by-op graph through
                                 the record API (14 launches per layer); 0 = the fused graph (5
                                 launches per layer); 2 = the fused graph's kernels as phases of
-                                one persistent cooperative launch per token */
+                                one persistent cooperative launch per token; 3 = the streaming
+                                decode kernel: one cooperative launch per token in which a
+                                producer warp per SM streams every layer's weights through a
+                                shared-memory ring while the other warps compute (one session,
+                                one GPU) */
   uint32_t tp_size;          /* tensor-parallel ranks (0 or 1: one GPU); with tp_size > 1 the
                                 model holds rank tp_rank's shard (sx_tp_shard_plan) and must be
                                 created with sx_model_create_tp */

@@ -599,28 +599,40 @@ float orc_synth_normal(uint64_t seed, uint64_t stream, uint64_t idx) {
   return (float)s / 37837.23f;
 }
 
-void orc_synth_q4(uint32_t *dst, size_t rows, size_t cols, uint64_t seed, uint64_t stream) {
-  size_t nb = cols / 32;
-  for (size_t r = 0; r < rows; ++r)
-    for (size_t b = 0; b < nb; ++b) {
-      uint64_t idx = r * nb + b;
-      uint32_t *blk = dst + idx * 5;
-      float z = orc_synth_normal(seed, stream, idx * 8);
+/* Synthetic blocks, rows in parallel (the values depend only on (seed, stream, block index),
+ * so the split does not change them). */
+typedef struct {
+  uint32_t *dst;
+  size_t nb;
+  uint64_t seed, stream;
+  int q8;
+} orc_synth_ctx;
+
+static void orc_synth_rows(void *p, size_t r0, size_t r1) {
+  const orc_synth_ctx *c = (const orc_synth_ctx *)p;
+  const int words = c->q8 ? 9 : 5, step = c->q8 ? 16 : 8;
+  for (size_t r = r0; r < r1; ++r)
+    for (size_t b = 0; b < c->nb; ++b) {
+      uint64_t idx = r * c->nb + b;
+      uint32_t *blk = c->dst + idx * (size_t)words;
+      float z = orc_synth_normal(c->seed, c->stream, idx * (uint64_t)step);
       blk[0] = f2u(orc_f16_round(fabsf(z) * 0.02f));
-      for (int j = 1; j <= 4; ++j) blk[j] = (uint32_t)orc_hash(seed, stream, idx * 8 + j);
+      for (int j = 1; j < words; ++j)
+        blk[j] = (uint32_t)orc_hash(c->seed, c->stream, idx * (uint64_t)step + (uint64_t)j);
     }
 }
 
+static int g_synth_threads = 1;
+void orc_set_synth_threads(int threads) { g_synth_threads = threads < 1 ? 1 : threads; }
+
+void orc_synth_q4(uint32_t *dst, size_t rows, size_t cols, uint64_t seed, uint64_t stream) {
+  orc_synth_ctx c = {dst, cols / 32, seed, stream, 0};
+  orc_parallel_for(rows, g_synth_threads, orc_synth_rows, &c);
+}
+
 void orc_synth_q8(uint32_t *dst, size_t rows, size_t cols, uint64_t seed, uint64_t stream) {
-  size_t nb = cols / 32;
-  for (size_t r = 0; r < rows; ++r)
-    for (size_t b = 0; b < nb; ++b) {
-      uint64_t idx = r * nb + b;
-      uint32_t *blk = dst + idx * 9;
-      float z = orc_synth_normal(seed, stream, idx * 16);
-      blk[0] = f2u(orc_f16_round(fabsf(z) * 0.02f));
-      for (int j = 1; j <= 8; ++j) blk[j] = (uint32_t)orc_hash(seed, stream, idx * 16 + j);
-    }
+  orc_synth_ctx c = {dst, cols / 32, seed, stream, 1};
+  orc_parallel_for(rows, g_synth_threads, orc_synth_rows, &c);
 }
 
 void orc_synth_bf16_normal(uint16_t *dst, size_t n, uint64_t seed, uint64_t stream,
@@ -699,6 +711,7 @@ orc_model *orc_model_create(const orc_model_config *cfg, uint64_t seed, int thre
   m->c = *cfg;
   m->threads = threads;
   m->seed = seed;
+  orc_set_synth_threads(threads);
   const orc_model_config *c = &m->c;
   uint32_t H = c->hidden_size, I = c->intermediate_size;
   uint32_t total_slots = c->num_anchors + c->window_size + c->num_recall;

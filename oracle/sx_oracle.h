@@ -89,6 +89,8 @@ uint32_t orc_ring_total_slots(const orc_ring *r);
 /* ---- synthetic inputs (identical integer generator to libsx's) ---- */
 uint64_t orc_hash(uint64_t seed, uint64_t stream, uint64_t idx);
 float orc_synth_normal(uint64_t seed, uint64_t stream, uint64_t idx);
+/* threads used by orc_synth_q4 / orc_synth_q8 (orc_model_create sets its own count) */
+void orc_set_synth_threads(int threads);
 void orc_synth_q4(uint32_t *dst, size_t rows, size_t cols, uint64_t seed, uint64_t stream);
 void orc_synth_q8(uint32_t *dst, size_t rows, size_t cols, uint64_t seed, uint64_t stream);
 void orc_synth_bf16_normal(uint16_t *dst, size_t n, uint64_t seed, uint64_t stream,

@@ -137,6 +137,63 @@ def test_prefill_graph_skips_logits(engine, reference_graph):
         assert model.kernels_per_token(False) == per_layer * cfg["num_layers"]
 
 
+def mid_cfg(**kw):
+    """The smallest shapes the streaming graph (reference_graph 3) accepts: every GEMV input at
+    least 16 block pairs (K >= 1024)."""
+    return tiny_cfg(vocab_size=8192, hidden_size=1024, intermediate_size=2048, num_q_heads=16,
+                    num_kv_heads=8, num_global_kv_heads=8, head_dim=64, global_head_dim=64, **kw)
+
+
+@pytest.mark.parametrize("kv_f32", [False, True])
+def test_stream_graph_greedy_decode_matches_checker(engine, engine_f32kv, kv_f32):
+    """Graph mode 3 (sx_stream.cu: one launch per token, producer-warp weight ring) against the
+    checker, with the window wrapping twice."""
+    from tests.conftest import assert_close_bf16_operands
+    eng = engine_f32kv if kv_f32 else engine
+    cfg = mid_cfg(kv_bf16=0 if kv_f32 else 1, reference_graph=3)
+    res = run_decode(eng, cfg, seed=23, steps=20, start_clock=0)
+    for i, (tok, rtok, lg, rlg) in enumerate(res):
+        if kv_f32:
+            assert_close(lg, rlg, what=f"logits step {i}")
+        else:  # cached K/V rounded to bf16 on both sides: the double-rounding allowance
+            assert_close_bf16_operands(lg, rlg, what=f"logits step {i}")
+        if tok != rtok:
+            assert margin_top2(rlg) < 1e-3, f"step {i}: token {tok} vs {rtok}"
+
+
+def test_stream_graph_equals_fused_graph_bits(engine):
+    """The streaming kernel sums each tile's chunk partials in a different order than the fused
+    GEMV kernels, so the two graphs agree within the f32 tolerance; both against each other
+    over a recall tier and a large clock."""
+    outs = []
+    for g in (0, 3):
+        cfg = mid_cfg(reference_graph=g)
+        res = run_decode(engine, cfg, seed=31, steps=4, start_clock=70000, n_recall=4)
+        outs.append(res)
+    for i, ((t0, r0, l0, _), (t3, r3, l3, rl)) in enumerate(zip(*outs)):
+        assert_close(l3, l0, what=f"stream vs fused logits step {i}")
+        assert_close(l3, rl, what=f"stream vs checker logits step {i}")
+
+
+def test_stream_graph_12b_width_full_vocab(engine):
+    cfg = tiny_cfg(vocab_size=262144, hidden_size=3840, intermediate_size=15360, num_layers=2,
+                   num_q_heads=16, num_kv_heads=8, num_global_kv_heads=8, head_dim=256,
+                   global_head_dim=256, num_anchors=32, window_size=512, num_recall=96,
+                   full_every=2, reference_graph=3)
+    res = run_decode(engine, cfg, seed=5, steps=3, start_clock=5000, n_recall=96)
+    for i, (tok, rtok, lg, rlg) in enumerate(res):
+        assert_close(lg, rlg, what=f"logits step {i}")
+        if tok != rtok:
+            assert margin_top2(rlg) < 1e-3
+
+
+def test_stream_graph_is_one_launch_and_rejects_small_k(engine):
+    model = sx.Model(engine, sx.model_config(**mid_cfg(reference_graph=3)))
+    assert model.kernels_per_token(True) == model.kernels_per_token(False) == 1
+    with pytest.raises(sx.SxError):  # K = 256: fewer than 16 block pairs per row
+        sx.Model(engine, sx.model_config(**tiny_cfg(reference_graph=3)))
+
+
 def test_forward_token_rejects_oversized_slot_list(engine):
     cfg = tiny_cfg()
     model = sx.Model(engine, sx.model_config(**cfg))
