@@ -176,6 +176,13 @@ SX_DEV void dq8_word(uint32_t u, uint32_t &lo, uint32_t &hi) {
   hi = prmt(v, 0x64646464u, 0x4342u);  // bytes 2,3
 }
 
+// f16x2 (1152 + q0, 1152 + q1) -> (q0, q1), exact (both are f16 integers)
+SX_DEV uint32_t sub_f16x2_1152(uint32_t v) {
+  uint32_t r;
+  asm("sub.rn.f16x2 %0, %1, %2;\n" : "=r"(r) : "r"(v), "r"(0x64806480u));
+  return r;
+}
+
 // ---------------------------------------------------------------------------
 // loads
 SX_DEV uint4 ldg_stream(const void *p) {

@@ -141,7 +141,18 @@ namespace {
 sx_status do_gemv(sx_engine *e, cudaStream_t s, int qt, bool geglu, const void *w0,
                   const void *w1, const float *x, float *y, uint32_t m, uint32_t k,
                   uint32_t batch) {
-  SX_CHECK_ARG(qt == 4 || qt == 8, "gemv: unsupported quant mode (bf16 GEMV is not built)");
+  if (qt == 0) {  // mode none: bf16 weights (gemv_bf16.wgsl)
+    SX_CHECK_ARG(m > 0 && k > 0 && k % 8 == 0 && batch >= 1 && batch <= 8,
+                 "gemv bf16: need m > 0, k a multiple of 8 and batch 1..8 (m=%u k=%u batch=%u)",
+                 m, k, batch);
+    SX_CHECK_ARG(w0 && x && y && (!geglu || w1), "gemv: null pointer");
+    SX_CHECK_ARG(((uintptr_t)w0 | (uintptr_t)(geglu ? w1 : w0) | (uintptr_t)x) % 16 == 0,
+                 "gemv bf16: weights and x must be 16-byte aligned");
+    return cuda_status(sx::launch_gemv_bf16(geglu, (const uint16_t *)w0, (const uint16_t *)w1, x,
+                                            y, m, k, batch, e->num_sms, s),
+                       "gemv bf16 launch");
+  }
+  SX_CHECK_ARG(qt == 4 || qt == 8, "gemv: unsupported quant mode");
   sx_status st = check_gemv_shape(qt, geglu, false, m, k, batch);
   if (st != SX_OK) return st;
   SX_CHECK_ARG(w0 && x && y && (!geglu || w1), "gemv: null pointer");
@@ -227,7 +238,9 @@ sx_status run_op(sx_engine *e, cudaStream_t s, const Op &op, uint32_t *kernels) 
   switch (op.kind) {
     case OP_GEMV:
     case OP_GEMV_LOGITS: {
-      int qt = op.kind == OP_GEMV_LOGITS ? 8 : qt_of(e->mode);
+      // the logits GEMV is Q8 when the layers are quantised, bf16 in mode none
+      // (kernels.zig:38: Q8 for q4, the layer format otherwise)
+      int qt = op.kind == OP_GEMV_LOGITS ? (e->mode == SX_QUANT_NONE ? 0 : 8) : qt_of(e->mode);
       *kernels += 1;
       return do_gemv(e, s, qt, false, op.bind.at(0), nullptr, (const float *)op.bind.at(1),
                      (float *)op.bind.at(2), op.u[0], op.u[1], 1);
@@ -406,7 +419,7 @@ SX_API uint64_t sx_packed_bytes(uint32_t rows, uint32_t cols, sx_quant_mode mode
   uint64_t chunks = (uint64_t)sx::tiles_of(rows) * sx::pairs_of(cols);
   if (mode == SX_QUANT_Q4) return chunks * sx::kQ4ChunkBytes;
   if (mode == SX_QUANT_Q8) return chunks * sx::kQ8ChunkBytes;
-  return 0;
+  return (uint64_t)rows * cols * 2;  // bf16 rows as the reference stores them (mode none)
 }
 
 SX_API void sx_rope_inv_freq(float *out, uint32_t rotary_dim, float theta) {
@@ -517,8 +530,8 @@ SX_API uint32_t sx_ring_active_slots(const sx_ring *r, uint32_t layer, uint64_t 
 SX_API sx_status sx_engine_create(int device, sx_quant_mode mode, uint32_t flags,
                                   sx_engine **out) {
   SX_CHECK_ARG(out, "engine: null out");
-  SX_CHECK_ARG(mode == SX_QUANT_Q4 || mode == SX_QUANT_Q8,
-               "engine: only the Q4_0 / Q8_0 modes are built");
+  SX_CHECK_ARG(mode == SX_QUANT_Q4 || mode == SX_QUANT_Q8 || mode == SX_QUANT_NONE,
+               "engine: unknown quant mode %d", (int)mode);
   int n = 0;
   SX_TRY_CUDA(cudaGetDeviceCount(&n), "cudaGetDeviceCount");
   SX_CHECK_ARG(device >= 0 && device < n, "engine: device %d out of range (%d devices)", device, n);
@@ -696,7 +709,16 @@ SX_API sx_status sx_buffer_read(sx_buffer *b, uint64_t offset, void *dst, uint64
 SX_API sx_status sx_buffer_repack_device(sx_buffer *dst, const void *ref_words_device,
                                          uint32_t rows, uint32_t cols, sx_quant_mode mode) {
   SX_CHECK_ARG(dst && ref_words_device, "repack: null argument");
-  SX_CHECK_ARG(mode == SX_QUANT_Q4 || mode == SX_QUANT_Q8, "repack: mode must be Q4 or Q8");
+  if (mode == SX_QUANT_NONE) {  // bf16 rows are stored as given
+    SX_CHECK_ARG(rows > 0 && cols > 0 && cols % 8 == 0, "repack: bf16 cols must be a multiple of 8");
+    SX_CHECK_ARG(sx_packed_bytes(rows, cols, mode) <= dst->bytes, "repack: destination too small");
+    SX_TRY_CUDA(cudaSetDevice(dst->e->device), "cudaSetDevice");
+    SX_TRY_CUDA(cudaMemcpyAsync(dst->d, ref_words_device, sx_packed_bytes(rows, cols, mode),
+                                cudaMemcpyDeviceToDevice, dst->e->stream),
+                "bf16 copy");
+    return SX_OK;
+  }
+  SX_CHECK_ARG(mode == SX_QUANT_Q4 || mode == SX_QUANT_Q8, "repack: unknown mode");
   SX_CHECK_ARG(rows > 0 && cols > 0 && cols % 32 == 0, "repack: cols must be a multiple of 32");
   SX_CHECK_ARG(sx_packed_bytes(rows, cols, mode) <= dst->bytes,
                "repack: destination holds %llu B, need %llu", (unsigned long long)dst->bytes,
@@ -726,7 +748,12 @@ SX_API sx_status sx_buffer_quantize_device(sx_buffer *dst, const void *bf16_devi
   SX_CHECK_ARG(dst && bf16_device, "quantize_device: null argument");
   sx_engine *e = dst->e;
   SX_TRY_CUDA(cudaSetDevice(e->device), "cudaSetDevice");
-  SX_CHECK_ARG(mode == SX_QUANT_Q4 || mode == SX_QUANT_Q8, "quantize_device: mode must be Q4 or Q8");
+  if (mode == SX_QUANT_NONE) {  // createWeightBuffer in mode none keeps the bf16 values
+    sx_status st = sx_buffer_repack_device(dst, bf16_device, rows, cols, mode);
+    if (st == SX_OK) st = cuda_status(cudaStreamSynchronize(e->stream), "bf16 copy sync");
+    return st;
+  }
+  SX_CHECK_ARG(mode == SX_QUANT_Q4 || mode == SX_QUANT_Q8, "quantize_device: unknown mode");
   SX_CHECK_ARG(rows > 0 && cols > 0 && cols % 32 == 0,
                "quantize_device: cols must be a multiple of 32");
   SX_CHECK_ARG(sx_packed_bytes(rows, cols, mode) <= dst->bytes,
@@ -746,9 +773,10 @@ SX_API sx_status sx_buffer_quantize_device(sx_buffer *dst, const void *bf16_devi
 SX_API sx_status sx_buffer_upload_weights(sx_buffer *dst, const uint32_t *ref_words,
                                           uint32_t rows, uint32_t cols, sx_quant_mode mode) {
   SX_CHECK_ARG(dst && ref_words, "upload_weights: null argument");
-  SX_CHECK_ARG(mode == SX_QUANT_Q4 || mode == SX_QUANT_Q8, "upload_weights: mode must be Q4 or Q8");
-  SX_CHECK_ARG(rows > 0 && cols > 0 && cols % 32 == 0,
-               "upload_weights: cols must be a multiple of 32");
+  SX_CHECK_ARG(mode == SX_QUANT_Q4 || mode == SX_QUANT_Q8 || mode == SX_QUANT_NONE,
+               "upload_weights: unknown mode");
+  SX_CHECK_ARG(rows > 0 && cols > 0 && cols % (mode == SX_QUANT_NONE ? 8 : 32) == 0,
+               "upload_weights: cols must be a multiple of 32 (8 for bf16)");
   sx_engine *e = dst->e;
   SX_TRY_CUDA(cudaSetDevice(e->device), "cudaSetDevice");
   uint64_t bytes = (uint64_t)rows * sx_quantized_row_words(cols, mode) * 4;

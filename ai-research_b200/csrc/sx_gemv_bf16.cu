@@ -1,0 +1,156 @@
+// sx_gemv_bf16.cu -- the bf16-weight layer GEMVs of the engine's mode "none" (the reference's
+// --gpu mode: GpuEngine.init picks gemv_bf16.wgsl for every projection and the logits,
+// src/gpu/kernels.zig:36-41; weights are the checkpoint's bf16 values, row-major, K / 2 u32
+// words per row, model_gpu.zig:51-56).
+//
+// Semantics (gemv_bf16.wgsl:1-63): y[r] = sum_k f32(W[r][k]) * x[k] with f32 accumulation;
+// the gate+up variant returns gelu_tanh(Wg[r] . x) * (Wu[r] . x) (kernels.zig:94-115).  (The
+// reference binds its Q4 gate+up shader in this mode, kernels.zig:41, which would read bf16
+// rows as Q4 blocks; this build runs the bf16 product the mode's weights hold.)
+//
+// HBM-bound: 2 bytes per weight.  One warp per row (rows strided over every warp of the grid),
+// each lane streaming 16-byte pieces (8 weights) with four loads in flight, x read through L1
+// (it is small and shared by every row), f32 FMAs, a warp-shuffle sum.  Up to 8 batch rows
+// share each weight load.
+#include "sx_common.cuh"
+#include "sx_internal.h"
+
+namespace sx {
+namespace {
+
+constexpr int kBfThreads = 256;
+constexpr int kBfUnroll = 4;
+
+SX_DEV float gelu_tanh_bf(float x) {
+  // kernels.zig:94-97, same operation order as the Q4/Q8 GEMV epilogue
+  float x3 = __fmul_rn(__fmul_rn(x, x), x);
+  float inner = __fmul_rn(0.7978845608f, __fadd_rn(x, __fmul_rn(0.044715f, x3)));
+  return __fmul_rn(__fmul_rn(0.5f, x), __fadd_rn(1.0f, tanhf(inner)));
+}
+
+template <int NMAT, int B>
+__global__ void __launch_bounds__(kBfThreads) gemv_bf16_kernel(const uint16_t *__restrict__ w0,
+                                                               const uint16_t *__restrict__ w1,
+                                                               const float *__restrict__ x,
+                                                               float *__restrict__ y, uint32_t m,
+                                                               uint32_t k, uint32_t ldx,
+                                                               uint32_t ldy) {
+  pdl_launch_dependents();
+  pdl_wait();
+  const uint32_t lane = threadIdx.x & 31;
+  const uint32_t nwarps = gridDim.x * (kBfThreads / 32);
+  const uint32_t k8 = k / 8;  // 16-byte pieces per row
+  for (uint32_t row = blockIdx.x * (kBfThreads / 32) + (threadIdx.x >> 5); row < m; row += nwarps) {
+    float acc[NMAT][B];
+#pragma unroll
+    for (int mm = 0; mm < NMAT; ++mm)
+#pragma unroll
+      for (int b = 0; b < B; ++b) acc[mm][b] = 0.0f;
+    const uint4 *wr[NMAT];
+    wr[0] = reinterpret_cast<const uint4 *>(w0 + (size_t)row * k);
+    if (NMAT == 2) wr[NMAT - 1] = reinterpret_cast<const uint4 *>(w1 + (size_t)row * k);
+    for (uint32_t p0 = lane; p0 < k8; p0 += 32 * kBfUnroll) {
+      uint4 wv[kBfUnroll][NMAT];
+#pragma unroll
+      for (int u = 0; u < kBfUnroll; ++u) {
+        const uint32_t p = p0 + u * 32;
+#pragma unroll
+        for (int mm = 0; mm < NMAT; ++mm)
+          wv[u][mm] = p < k8 ? ldg_stream(wr[mm] + p) : make_uint4(0, 0, 0, 0);
+      }
+#pragma unroll
+      for (int u = 0; u < kBfUnroll; ++u) {
+        const uint32_t p = p0 + u * 32;
+        if (p >= k8) break;
+#pragma unroll
+        for (int b = 0; b < B; ++b) {
+          const float4 *xp = reinterpret_cast<const float4 *>(x + (size_t)b * ldx + (size_t)p * 8);
+          const float4 xa = __ldg(xp), xb = __ldg(xp + 1);
+          const float xs[8] = {xa.x, xa.y, xa.z, xa.w, xb.x, xb.y, xb.z, xb.w};
+#pragma unroll
+          for (int mm = 0; mm < NMAT; ++mm) {
+            const uint32_t ws[4] = {wv[u][mm].x, wv[u][mm].y, wv[u][mm].z, wv[u][mm].w};
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              acc[mm][b] = fmaf(u2f(ws[q] << 16), xs[2 * q], acc[mm][b]);
+              acc[mm][b] = fmaf(u2f(ws[q] & 0xFFFF0000u), xs[2 * q + 1], acc[mm][b]);
+            }
+          }
+        }
+      }
+    }
+#pragma unroll
+    for (int mm = 0; mm < NMAT; ++mm)
+#pragma unroll
+      for (int b = 0; b < B; ++b) acc[mm][b] = warp_sum(acc[mm][b]);
+    if (lane == 0) {
+#pragma unroll
+      for (int b = 0; b < B; ++b)
+        y[(size_t)b * ldy + row] =
+            NMAT == 2 ? __fmul_rn(gelu_tanh_bf(acc[0][b]), acc[NMAT - 1][b]) : acc[0][b];
+    }
+  }
+}
+
+template <int NMAT, int B>
+cudaError_t launch_bf(const uint16_t *w0, const uint16_t *w1, const float *x, float *y, uint32_t m,
+                      uint32_t k, uint32_t ldx, uint32_t ldy, int num_sms, cudaStream_t s) {
+  const uint32_t warps = (m + 0u);
+  uint32_t grid = num_sms * 8;
+  const uint32_t need = (warps + kBfThreads / 32 - 1) / (kBfThreads / 32);
+  if (need < grid) grid = need;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(kBfThreads);
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, gemv_bf16_kernel<NMAT, B>, w0, w1, x, y, m, k, ldx, ldy);
+}
+
+template <int NMAT>
+cudaError_t launch_bf_b(const uint16_t *w0, const uint16_t *w1, const float *x, float *y,
+                        uint32_t m, uint32_t k, uint32_t batch, int num_sms, cudaStream_t s) {
+  switch (batch) {
+    case 1: return launch_bf<NMAT, 1>(w0, w1, x, y, m, k, k, m, num_sms, s);
+    case 2: return launch_bf<NMAT, 2>(w0, w1, x, y, m, k, k, m, num_sms, s);
+    case 3: return launch_bf<NMAT, 3>(w0, w1, x, y, m, k, k, m, num_sms, s);
+    case 4: return launch_bf<NMAT, 4>(w0, w1, x, y, m, k, k, m, num_sms, s);
+    case 5: return launch_bf<NMAT, 5>(w0, w1, x, y, m, k, k, m, num_sms, s);
+    case 6: return launch_bf<NMAT, 6>(w0, w1, x, y, m, k, k, m, num_sms, s);
+    case 7: return launch_bf<NMAT, 7>(w0, w1, x, y, m, k, k, m, num_sms, s);
+    case 8: return launch_bf<NMAT, 8>(w0, w1, x, y, m, k, k, m, num_sms, s);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+// bf16(0.02 N(0,1)) at element i of the stream: the mode-none synthetic checkpoint, bit-equal
+// to the CPU checker's orc_synth_bf16_normal(..., 0, 0.02)
+__global__ void synth_bf16_kernel(uint16_t *dst, uint64_t n, uint64_t seed, uint64_t stream) {
+  for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < n;
+       i += (uint64_t)gridDim.x * blockDim.x)
+    dst[i] = bf16_bits_rne(fmaf(0.02f, synth_normal(seed, stream, i), 0.0f));
+}
+
+}  // namespace
+
+cudaError_t launch_gemv_bf16(bool geglu, const uint16_t *w0, const uint16_t *w1, const float *x,
+                             float *y, uint32_t m, uint32_t k, uint32_t batch, int num_sms,
+                             cudaStream_t s) {
+  if (m == 0 || k % 8 != 0 || batch < 1 || batch > 8) return cudaErrorInvalidValue;
+  return geglu ? launch_bf_b<2>(w0, w1, x, y, m, k, batch, num_sms, s)
+               : launch_bf_b<1>(w0, w0, x, y, m, k, batch, num_sms, s);
+}
+
+cudaError_t launch_synth_bf16(uint16_t *dst, uint64_t n, uint64_t seed, uint64_t stream_id,
+                              cudaStream_t s) {
+  uint64_t blocks = (n + 255) / 256;
+  if (blocks > 148 * 64) blocks = 148 * 64;
+  synth_bf16_kernel<<<(uint32_t)blocks, 256, 0, s>>>(dst, n, seed, stream_id);
+  return cudaGetLastError();
+}
+
+}  // namespace sx

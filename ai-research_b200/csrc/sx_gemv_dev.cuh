@@ -143,25 +143,37 @@ SX_DEV float group_block_sum(float v, float *red, const Sync &sync) {
 //              CTA 0 writes xn to x_out; xin = rmsnorm(xn, w)         (add_rmsnorm.wgsl)
 constexpr int kProPer = 8;  // elements per thread held in registers: K <= 512 * 8
 
-template <typename Sync = CtaSync>
-SX_DEV void run_prologue(const GemvArgs &a, float *xin, float *red, const Sync &sync = Sync()) {
+// The prologue's norm gains (weights: they do not depend on the producer of x, so a caller may
+// load them before it waits for that producer).
+struct ProGains {
+  float nw[kProPer], pw[kProPer];
+};
+SX_DEV void load_prologue_gains(const GemvArgs &a, uint32_t nthr, ProGains &gn) {
+#pragma unroll
+  for (int q = 0; q < kProPer; ++q) {
+    const uint32_t i = threadIdx.x + q * nthr;
+    const bool in = i < a.k;
+    gn.nw[q] = in ? a.pro_w[i] : 0.0f;
+    gn.pw[q] = (in && a.pro == kProResid && a.pro_post_w) ? a.pro_post_w[i] : 0.0f;
+  }
+}
+
+template <typename Sync>
+SX_DEV void run_prologue_gains(const GemvArgs &a, float *xin, float *red, const Sync &sync,
+                               const ProGains &gn) {
   const uint32_t K = a.k, nthr = sync.threads();
   for (uint32_t j = 0; j < a.batch; ++j) {
     float *xo = xin + (size_t)j * K;
     const float *x = a.x + (size_t)j * a.ldx;
-    float xv[kProPer], mv[kProPer], pw[kProPer], nw[kProPer];
+    float xv[kProPer], mv[kProPer];
+    const float *pw = gn.pw, *nw = gn.nw;
 #pragma unroll
     for (int q = 0; q < kProPer; ++q) {
       uint32_t i = threadIdx.x + q * nthr;
       bool in = i < K;
       xv[q] = in ? __ldcg(x + i) : 0.0f;  // activations: through L2 (see stage_x)
-      nw[q] = in ? a.pro_w[i] : 0.0f;
       mv[q] = 0.0f;
-      pw[q] = 0.0f;
-      if (a.pro == kProResid) {
-        mv[q] = in ? __ldcg(a.pro_mlp + (size_t)j * a.ldx + i) : 0.0f;
-        pw[q] = (in && a.pro_post_w) ? a.pro_post_w[i] : 0.0f;
-      }
+      if (a.pro == kProResid) mv[q] = in ? __ldcg(a.pro_mlp + (size_t)j * a.ldx + i) : 0.0f;
     }
     if (a.pro == kProResid) {
       float rm = 1.0f;
@@ -196,6 +208,13 @@ SX_DEV void run_prologue(const GemvArgs &a, float *xin, float *red, const Sync &
     }
     sync();
   }
+}
+
+template <typename Sync = CtaSync>
+SX_DEV void run_prologue(const GemvArgs &a, float *xin, float *red, const Sync &sync = Sync()) {
+  ProGains gn;
+  load_prologue_gains(a, sync.threads(), gn);
+  run_prologue_gains(a, xin, red, sync, gn);
 }
 
 // Activation -> B fragments.  Item (blk, j, c, jj) converts elements 32*blk + 8*jj + 2c,+1
@@ -354,6 +373,12 @@ SX_DEV bool better(float v, uint32_t i, float bv, uint32_t bi) {
 template <int QT, int NMAT, int NSETS, int S>
 SX_DEV void gemv_body(const GemvArgs &a, uint8_t *smem, bool prefetch, bool run,
                           bool standalone) {
+  // Q8 GeGLU: the f16 weights 1152 + q get the 1152 taken off exactly (q is an f16 integer)
+  // before the MMA.  The offset form carries ~16x the signal through the tensor core's f32
+  // accumulation; a GeGLU product turns that rounding, where the gate is near zero and the up
+  // value large, into a relative error of the (small) product above the path's tolerance.
+  // The Q8 LM head keeps the offset form (one logical op less per two weights).
+  constexpr bool EXACT8 = QT == 8 && NMAT == 2;
   constexpr int CB = QTraits<QT>::kChunk;
   constexpr int SO = QTraits<QT>::kScaleOff;
   constexpr bool PRIV = kPrivScales && NSETS == 1;  // lane-private scale copies
@@ -588,11 +613,18 @@ SX_DEV void gemv_body(const GemvArgs &a, uint8_t *smem, bool prefetch, bool run,
             dq8_word(q.w, h1l, h1h);
             a0[0] = g0l; a0[1] = h0l; a0[2] = g0h; a0[3] = h0h;
             a1[0] = g1l; a1[1] = h1l; a1[2] = g1h; a1[3] = h1h;
+            if (EXACT8) {
+#pragma unroll
+              for (int r = 0; r < 4; ++r) {
+                a0[r] = sub_f16x2_1152(a0[r]);
+                a1[r] = sub_f16x2_1152(a1[r]);
+              }
+            }
           }
           const float sg = hb ? sc.z : sc.x, sg8 = hb ? sc.w : sc.y;
 #pragma unroll
           for (int s = 0; s < NSETS; ++s)
-            block_mma<QT>(a0, a1, xb[hb][s], cr[hb][s], sg, sg8, acc[m][s]);
+            block_mma<QT>(a0, a1, xb[hb][s], EXACT8 ? 0.0f : cr[hb][s], sg, sg8, acc[m][s]);
         }
       }
       xp += xstride;

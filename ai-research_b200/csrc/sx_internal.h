@@ -66,6 +66,15 @@ size_t gemv_workers(int num_sms);
 constexpr uint32_t kGemvPrologueMaxK = 4096;  // fused norm prologues hold K / 512 <= 8 per thread
 constexpr uint32_t kMaxGemvTiles = 262144;
 
+// bf16-weight GEMV of the engine's mode none (sx_gemv_bf16.cu): y[b][r] = W[r] . x[b] with
+// row-major bf16 W (k % 8 == 0, 16-byte aligned rows and x), or the GeGLU of two matrices
+cudaError_t launch_gemv_bf16(bool geglu, const uint16_t *w0, const uint16_t *w1, const float *x,
+                             float *y, uint32_t m, uint32_t k, uint32_t batch, int num_sms,
+                             cudaStream_t s);
+// synthetic bf16(0.02 N(0,1)) weights, element i of (seed, stream)
+cudaError_t launch_synth_bf16(uint16_t *dst, uint64_t n, uint64_t seed, uint64_t stream_id,
+                              cudaStream_t s);
+
 // quantizeMatrix on the device: nblocks 32-value bf16 blocks -> reference block words
 cudaError_t launch_quantize(int qt, const void *bf16, uint32_t *ref, uint64_t nblocks,
                             cudaStream_t s);

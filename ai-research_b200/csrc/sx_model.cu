@@ -69,6 +69,10 @@ struct sx_model {
   std::vector<sx_buffer *> buffers;
   std::vector<sx_set *> sets;
   uint64_t weight_bytes = 0;
+  // layer weight format = the engine mode (kernels.zig:36-41): Q4_0, Q8_0 or bf16 (none); the
+  // LM head is Q8_0 in the quantised modes and bf16 in mode none (model_gpu.zig:161)
+  sx_quant_mode lmode = SX_QUANT_Q4, hmode = SX_QUANT_Q8;
+  int lqt = 4;  // GEMV format code of the layers: 4, 8, 0 (bf16)
 };
 
 namespace {
@@ -151,23 +155,23 @@ sx_status alloc_model(sx_model *m) {
     M_TRY(mk_buf(m, 4ull * H, &B.post_attn));
     M_TRY(mk_buf(m, 4ull * H, &B.post_ffn));
     // q | k | v back to back: the fused projection streams them as one run of chunks
-    const uint64_t qb = sx_packed_bytes(B.q_dim, H, SX_QUANT_Q4);
-    const uint64_t kvb_w = sx_packed_bytes(B.kv_dim, H, SX_QUANT_Q4);
+    const uint64_t qb = sx_packed_bytes(B.q_dim, H, m->lmode);
+    const uint64_t kvb_w = sx_packed_bytes(B.kv_dim, H, m->lmode);
     sx_buffer *qkv = nullptr;
     M_TRY(mk_buf(m, qb + 2 * kvb_w, &qkv));
     M_TRY(mk_view(m, qkv, 0, qb, &B.wq));
     M_TRY(mk_view(m, qkv, qb, kvb_w, &B.wk));
     M_TRY(mk_view(m, qkv, qb + kvb_w, kvb_w, &B.wv));
-    M_TRY(mk_buf(m, sx_packed_bytes(H, B.q_dim, SX_QUANT_Q4), &B.wo));
-    M_TRY(mk_buf(m, sx_packed_bytes(I, H, SX_QUANT_Q4), &B.wg));
-    M_TRY(mk_buf(m, sx_packed_bytes(I, H, SX_QUANT_Q4), &B.wu));
-    M_TRY(mk_buf(m, sx_packed_bytes(H, I, SX_QUANT_Q4), &B.wd));
+    M_TRY(mk_buf(m, sx_packed_bytes(H, B.q_dim, m->lmode), &B.wo));
+    M_TRY(mk_buf(m, sx_packed_bytes(I, H, m->lmode), &B.wg));
+    M_TRY(mk_buf(m, sx_packed_bytes(I, H, m->lmode), &B.wu));
+    M_TRY(mk_buf(m, sx_packed_bytes(H, I, m->lmode), &B.wd));
     M_TRY(mk_buf(m, (uint64_t)m->total_slots * B.kv_dim * kvb * S, &B.kc));
     M_TRY(mk_buf(m, (uint64_t)m->total_slots * B.kv_dim * kvb * S, &B.vc));
     m->weight_bytes += B.wq->bytes + B.wk->bytes + B.wv->bytes + B.wo->bytes + B.wg->bytes +
                        B.wu->bytes + B.wd->bytes;
   }
-  M_TRY(mk_buf(m, sx_packed_bytes(V, H, SX_QUANT_Q8), &m->lm_head));
+  M_TRY(mk_buf(m, sx_packed_bytes(V, H, m->hmode), &m->lm_head));
   M_TRY(mk_buf(m, 4ull * H, &m->final_norm));
   m->weight_bytes += m->lm_head->bytes;
 
@@ -391,8 +395,8 @@ sx_status record_forward_fused(sx_model *m, sx_cmd *cmd, bool logits, bool io,
     q.pf_base[1] = B.k_eq_v ? nullptr : B.vc->d;
     q.pf_row_bytes = B.kv_dim * (c.kv_bf16 ? 2u : 4u);
     q.pf_max = m->total_slots;
-    M_TRY(sx_host_check_gemv(4, false, true, B.q_dim + 2 * B.kv_dim, H, nb));
-    push_gemv(m, cmd, q, 4, false);
+    M_TRY(sx_host_check_gemv(m->lqt, false, true, B.q_dim + 2 * B.kv_dim, H, nb));
+    push_gemv(m, cmd, q, m->lqt, false);
 
     // fused qkv_rope + attention
     Op at{OP_ATTN_FUSED};
@@ -432,10 +436,10 @@ sx_status record_forward_fused(sx_model *m, sx_cmd *cmd, bool logits, bool io,
     sx_host_push_op(cmd, at);
 
     // o projection
-    M_TRY(sx_host_check_gemv(4, false, false, H, B.q_dim, nb));
+    M_TRY(sx_host_check_gemv(m->lqt, false, false, H, B.q_dim, nb));
     sx::GemvArgs o = gemv1(B.wo, m->attn_out, m->mlp_out, H, B.q_dim);
     o.batch = nb;
-    push_gemv(m, cmd, o, 4, false);
+    push_gemv(m, cmd, o, m->lqt, false);
     if (tp) push_allreduce(m, cmd, m->mlp_out, H);  // row-parallel o: sum of the ranks' parts
 
     // gate+up GeGLU with the post-attention residual and pre-FFN norm
@@ -449,14 +453,14 @@ sx_status record_forward_fused(sx_model *m, sx_cmd *cmd, bool logits, bool io,
     g.pro_x_out = (float *)m->x2->d;
     g.eps = eps;
     g.batch = nb;
-    M_TRY(sx_host_check_gemv(4, true, true, I, H, nb));
-    push_gemv(m, cmd, g, 4, true);
+    M_TRY(sx_host_check_gemv(m->lqt, true, true, I, H, nb));
+    push_gemv(m, cmd, g, m->lqt, true);
 
     // down projection
-    M_TRY(sx_host_check_gemv(4, false, false, H, I, nb));
+    M_TRY(sx_host_check_gemv(m->lqt, false, false, H, I, nb));
     sx::GemvArgs d = gemv1(B.wd, m->act, m->mlp_out, H, I);
     d.batch = nb;
-    push_gemv(m, cmd, d, 4, false);
+    push_gemv(m, cmd, d, m->lqt, false);
     if (tp) push_allreduce(m, cmd, m->mlp_out, H);  // row-parallel down
   }
   if (logits) {
@@ -511,6 +515,15 @@ sx_status synth_matrix(sx_model *m, sx_buffer *dst, uint32_t rows, uint32_t cols
                        sx_quant_mode mode, uint64_t seed, uint64_t stream, void *tmp,
                        uint64_t tmp_bytes, uint32_t grow0 = 0, uint32_t gblk0 = 0,
                        uint32_t gnb = 0) {
+  if (mode == SX_QUANT_NONE) {  // bf16 values written in place (one GPU: no slices)
+    if (grow0 || gblk0 || (gnb && gnb != cols / 32)) {
+      sx_host_set_error("synth: bf16 weights are not sliced for tensor parallelism");
+      return SX_ERR_UNSUPPORTED;
+    }
+    return sx_host_cuda_status(sx::launch_synth_bf16((uint16_t *)dst->d, (uint64_t)rows * cols,
+                                                     seed, stream, m->e->stream),
+                               "synth bf16");
+  }
   const uint64_t row_bytes = sx_quantized_row_words(cols, mode) * 4;
   uint64_t chunk = tmp_bytes / row_bytes;
   chunk = (chunk / 16) * 16;
@@ -569,8 +582,13 @@ sx_status create_model(sx_engine *e, const sx_model_config *cfg, sx_comm *comm, 
     sx_host_set_error("model_create: config.kv_bf16 must match the engine's KV precision flag");
     return SX_ERR_INVALID;
   }
-  if (e->mode != SX_QUANT_Q4) {
-    sx_host_set_error("model_create: the model path is the Q4_0 engine mode");
+  if (e->mode == SX_QUANT_NONE && c.reference_graph != 1) {
+    sx_host_set_error("model_create: bf16 layers (engine mode none) run the reference's op-by-op "
+                      "graph (reference_graph 1)");
+    return SX_ERR_UNSUPPORTED;
+  }
+  if (e->mode != SX_QUANT_Q4 && (c.tp_size > 1 || c.num_sessions > 1)) {
+    sx_host_set_error("model_create: tensor parallelism and batched sessions need Q4_0 layers");
     return SX_ERR_UNSUPPORTED;
   }
   cudaSetDevice(e->device);
@@ -578,6 +596,9 @@ sx_status create_model(sx_engine *e, const sx_model_config *cfg, sx_comm *comm, 
   m->e = e;
   m->c = c;
   m->comm = comm;
+  m->lmode = e->mode;
+  m->hmode = e->mode == SX_QUANT_NONE ? SX_QUANT_NONE : SX_QUANT_Q8;
+  m->lqt = e->mode == SX_QUANT_Q4 ? 4 : e->mode == SX_QUANT_Q8 ? 8 : 0;
   sx_status st = alloc_model(m);
   for (int lg = 0; lg < 2 && st == SX_OK; ++lg)
     for (int io = 0; io < 2 && st == SX_OK; ++io) {
@@ -676,7 +697,7 @@ SX_API sx_status sx_model_synth_weights(sx_model *m, uint64_t seed) {
     // and intermediate rows), 32-column blocks of o/down (the same split of their K)
     auto mat = [&](sx_buffer *b, uint32_t rows, uint32_t cols, uint32_t kind, uint32_t grow0,
                    uint32_t gblk0, uint32_t gnb) {
-      return synth_matrix(m, b, rows, cols, SX_QUANT_Q4, seed, stream_of(l, kind), tmp, tmp_bytes,
+      return synth_matrix(m, b, rows, cols, m->lmode, seed, stream_of(l, kind), tmp, tmp_bytes,
                           grow0, gblk0, gnb);
     };
     const uint32_t hd = B.head_dim, q_glob = c.num_q_heads * hd;
@@ -693,7 +714,7 @@ SX_API sx_status sx_model_synth_weights(sx_model *m, uint64_t seed) {
     B.layer_scalar = sx::bf16_bits_to_f32(sx::bf16_bits_rne(fmaf(0.05f, z, 1.0f)));
   }
   if (st == SX_OK)
-    st = synth_matrix(m, m->lm_head, m->V, H, SX_QUANT_Q8, seed, 2, tmp, tmp_bytes, tp.vocab0);
+    st = synth_matrix(m, m->lm_head, m->V, H, m->hmode, seed, 2, tmp, tmp_bytes, tp.vocab0);
   if (st == SX_OK)
     st = sx_host_cuda_status(
         sx::launch_synth_gain((float *)m->final_norm->d, H, seed, 3, e->stream), "synth gain");
@@ -910,9 +931,9 @@ extern "C" SX_API sx_status sx_prefill_batch(sx_model *m, uint32_t T, const floa
     return SX_ERR_INVALID;
   }
   const sx_model_config &c = m->c;
-  if (m->comm || c.reference_graph == 1) {
-    sx_host_set_error("prefill_batch: runs on one GPU with the fused kernels (tp_size <= 1, "
-                      "reference_graph != 1)");
+  if (m->comm || c.reference_graph == 1 || m->lmode != SX_QUANT_Q4) {
+    sx_host_set_error("prefill_batch: runs on one GPU with the fused kernels and Q4_0 layers "
+                      "(tp_size <= 1, reference_graph != 1, engine mode Q4)");
     return SX_ERR_UNSUPPORTED;
   }
   const uint32_t H = c.hidden_size, I = m->I, ts = m->total_slots, L = c.num_layers;

@@ -40,11 +40,11 @@ constexpr uint32_t kSConsumers = kSW * 32;      // consumer threads (warps 0..15
 constexpr int kSThreads = kSConsumers + 32;     // + the producer warp (warp 16)
 constexpr int kSStages = 7;
 constexpr uint32_t kSStageBytes = 20480;        // 32 Q4 chunks, 16 GeGLU pairs, 16 Q8 chunks
-constexpr int kSRedSlots = 4;
-constexpr uint32_t kSRedSlotFloats = kSW * 16 * 2;  // warps x tile rows x (up to 2) matrices
+constexpr uint32_t kSGroupTiles = 8;  // tiles whose partial sums are reduced together
+constexpr uint32_t kSTileFloats = kSW * 16 * 2;  // warps x tile rows x (up to 2) matrices
 constexpr uint32_t kSSmem = 227 * 1024;
 constexpr uint32_t kSRingOff = kSSmem - kSStages * kSStageBytes;
-constexpr uint32_t kSRedOff = kSRingOff - kSRedSlots * kSRedSlotFloats * 4;
+constexpr uint32_t kSRedOff = kSRingOff - kSGroupTiles * kSTileFloats * 4;
 constexpr uint32_t kSMetaOff = kSRedOff - 256;
 constexpr uint32_t kSPhaseArea = kSMetaOff;     // x fragments / attention work items
 constexpr long long kSWaitCycles = 4000000000ll;  // ~2 s at 1.9 GHz
@@ -134,8 +134,6 @@ struct HalfSync {
 struct SMeta {
   uint64_t full[kSStages];
   uint64_t empty[kSStages];
-  uint32_t slot_cnt[kSRedSlots];
-  uint32_t slot_owner[kSRedSlots];
   uint32_t flag[4];       // [0]: phase-wait outcome for the consumers; [2], [3]: attention halves
   uint32_t item_last[2];  // attention: "this item merges its head" per half
 };
@@ -179,6 +177,8 @@ SX_DEV void stream_producer(const Phase *__restrict__ ph, uint32_t n, SMeta *met
                                a.pf_row_bytes);
       }
     }
+    // stage j carries chunks [c0 + j spc, c0 + (j + 1) spc) of each matrix, one bulk copy
+    // each (matrix m at + m spc cb)
     for (uint32_t base = 0; base < nch; base += spc, ++st) {
       const uint32_t s = st % kSStages, use = st / kSStages;
       const uint32_t full = smem_u32(&meta->full[s]), empty = smem_u32(&meta->empty[s]);
@@ -190,8 +190,9 @@ SX_DEV void stream_producer(const Phase *__restrict__ ph, uint32_t n, SMeta *met
         mbar_arrive_expect_tx(full, cnt * cb * nmat);
         const uint32_t dst = smem_u32(ring + s * kSStageBytes);
         for (int m = 0; m < nmat; ++m)
-          bulk_g2s(dst + m * spc * cb, static_cast<const uint8_t *>(a.w[0][m]) + (size_t)(c0 + base) * cb,
-                   cnt * cb, full);
+          bulk_g2s(dst + m * spc * cb,
+                   static_cast<const uint8_t *>(a.w[0][m]) + (size_t)(c0 + base) * cb, cnt * cb,
+                   full);
       }
       __syncwarp();
     }
@@ -208,6 +209,7 @@ struct Emit {
 template <int QT, int NMAT>
 __device__ __noinline__ void stream_gemv(const GemvArgs &a, uint8_t *smem, SMeta *meta,
                                          uint8_t *ring, float *red, uint32_t &st, bool ok,
+                                         const uint32_t *ctr, uint32_t wait_p,
                                          uint32_t *abort_w, uint32_t *err) {
   constexpr int CB = QTraits<QT>::kChunk;
   constexpr int SO = QTraits<QT>::kScaleOff;
@@ -222,14 +224,15 @@ __device__ __noinline__ void stream_gemv(const GemvArgs &a, uint8_t *smem, SMeta
   const uint32_t nch = (ct1 - ct0) * P;
   ConsumerSync sync;
 
-  if (tid < kSRedSlots) {
-    meta->slot_cnt[tid] = 0;
-    meta->slot_owner[tid] = ct0 + tid;
-  }
+  // the norm gains do not depend on the previous phase: load them, then wait for it
+  ProGains gn;
+  if (pro) load_prologue_gains(a, kSConsumers, gn);
+  if (wait_p != kNoPhase)
+    ok = wait_phase(ctr, wait_p, abort_w, err, threadIdx.x == 0, &meta->flag[0], sync) && ok;
   // input: residual / norm prologue, then the B fragments (x is read through L2)
   float *xin = reinterpret_cast<float *>(smem + L.xin);
   if (pro) {
-    run_prologue(a, xin, reinterpret_cast<float *>(smem + L.misc + 64), sync);
+    run_prologue_gains(a, xin, reinterpret_cast<float *>(smem + L.misc + 64), sync, gn);
     stage_x<QT>(a, xin, a.k, smem, L, false, sync);
   } else {
     stage_x<QT>(a, a.x, a.ldx, smem, L, true, sync);
@@ -254,72 +257,49 @@ __device__ __noinline__ void stream_gemv(const GemvArgs &a, uint8_t *smem, SMeta
     }
     return s;
   };
-  // this warp's partial sums of tile t -> slot; the 16th warp to deposit adds and writes
-  auto deposit = [&](uint32_t t, const float (&acc)[NMAT][2]) {
-    const uint32_t slot = (t - ct0) % kSRedSlots;
-    if (lane == 0 && ok) {
-      const volatile uint32_t *own = &meta->slot_owner[slot];
-      if (*own != t) {
-        const long long t0 = clock64();
-        while (*own != t) {
-          if (aborted(abort_w)) {
-            ok = false;
-            break;
-          }
-          if (clock64() - t0 > kSWaitCycles) {
-            set_abort(abort_w, err);
-            ok = false;
-            break;
-          }
-        }
-      }
+  // one row of tile tt: scale, GeGLU, write, track the argmax
+  auto emit = [&](uint32_t tt, uint32_t row, const float (&v)[NMAT]) {
+    uint32_t tl;
+    const int s = seg_of(tt, tl);
+    const uint32_t r = tl * 16 + row;
+    if (r >= a.rows[s]) return;
+    float out = v[0] * xs;
+    if (NMAT == 2) out = __fmul_rn(gelu_tanh_dev(out), v[NMAT - 1] * xs);
+    a.y[s][r] = out;
+    if (a.epi == kEpiArgmax) {
+      const uint32_t gi = a.row_base[s] + r;
+      const float ov = isnan(out) ? -INFINITY : out;
+      if (best.bi == 0xFFFFFFFFu || better(ov, gi, best.bv, best.bi)) best = {ov, gi};
     }
-    ok = __shfl_sync(0xffffffffu, (uint32_t)ok, 0) != 0;
-    if (!ok) return;
-    float *r = red + slot * kSRedSlotFloats + warp * 16 * NMAT;  // [row][m]
-    if (cvalid) {
+  };
+  // A tile's chunks are spread over all sixteen warps (chunk offset o goes to warp o mod 16):
+  // each warp stores its partial sums of a tile (plain shared stores), and after every group of
+  // kSGroupTiles tiles all consumer threads add the sixteen partials of each row in warp order.
+  const uint32_t ntiles = ct1 - ct0;
+  auto deposit = [&](uint32_t rt, const float (&acc)[NMAT][2]) {
+    if (!cvalid) return;
+    float *r = red + ((rt % kSGroupTiles) * kSW + warp) * 16 * NMAT;  // [row][m]
 #pragma unroll
-      for (int m = 0; m < NMAT; ++m) {
-        r[g * NMAT + m] = acc[m][0];
-        r[(g + 8) * NMAT + m] = acc[m][1];
-      }
+    for (int m = 0; m < NMAT; ++m) {
+      r[g * NMAT + m] = acc[m][0];
+      r[(g + 8) * NMAT + m] = acc[m][1];
     }
-    __threadfence_block();
-    __syncwarp();
-    uint32_t old = 0;
-    if (lane == 0) old = atomicAdd(&meta->slot_cnt[slot], 1u);
-    old = __shfl_sync(0xffffffffu, old, 0);
-    if (old != kSW - 1) return;
-    __threadfence_block();
-    if (lane < 16) {
+  };
+  auto flush = [&](uint32_t grp) {
+    csync();  // every warp has deposited every tile of the group
+    const uint32_t rt = grp * kSGroupTiles + tid / 16, row = tid % 16;
+    if (tid < kSGroupTiles * 16 && rt < ntiles && ok) {
       float v[NMAT];
 #pragma unroll
       for (int m = 0; m < NMAT; ++m) v[m] = 0.0f;
-      const float *base = red + slot * kSRedSlotFloats + lane * NMAT;
+      const float *b = red + (rt % kSGroupTiles) * kSW * 16 * NMAT + row * NMAT;
 #pragma unroll 4
       for (int w = 0; w < kSW; ++w)
 #pragma unroll
-        for (int m = 0; m < NMAT; ++m) v[m] += base[w * 16 * NMAT + m];
-      uint32_t tl;
-      const int s = seg_of(t, tl);
-      const uint32_t row = tl * 16 + lane;
-      if (row < a.rows[s]) {
-        float out = v[0] * xs;
-        if (NMAT == 2) out = __fmul_rn(gelu_tanh_dev(out), v[NMAT - 1] * xs);
-        a.y[s][row] = out;
-        if (a.epi == kEpiArgmax) {
-          const uint32_t gi = a.row_base[s] + row;
-          const float ov = isnan(out) ? -INFINITY : out;
-          if (best.bi == 0xFFFFFFFFu || better(ov, gi, best.bv, best.bi)) best = {ov, gi};
-        }
-      }
+        for (int m = 0; m < NMAT; ++m) v[m] += b[w * 16 * NMAT + m];
+      emit(ct0 + rt, row, v);
     }
-    __syncwarp();
-    if (lane == 0) {
-      meta->slot_cnt[slot] = 0;
-      __threadfence_block();
-      *reinterpret_cast<volatile uint32_t *>(&meta->slot_owner[slot]) = t + kSRedSlots;
-    }
+    csync();  // the group's buffer is free again
   };
 
   float acc[NMAT][2];
@@ -328,8 +308,8 @@ __device__ __noinline__ void stream_gemv(const GemvArgs &a, uint8_t *smem, SMeta
   uint4 xb[2] = {make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0)};
   float cr[2] = {0.0f, 0.0f};
   // this warp's next chunk: offset o = base + u * 16 + warp in the CTA's run; its tile / pair
-  uint32_t tile = ct0 + warp / P, pair = warp % P;
-  uint32_t cur = 0xFFFFFFFFu;
+  // (every warp has a chunk in every tile: P >= 16)
+  uint32_t tile = ct0 + warp / P, pair = warp % P, cur = tile;
   for (uint32_t base = 0; base < nch; base += SPC, ++st) {
     const uint32_t s = st % kSStages, par = (st / kSStages) & 1;
     if (ok) ok = mbar_wait_or_abort(smem_u32(&meta->full[s]), par, abort_w, err);
@@ -338,11 +318,12 @@ __device__ __noinline__ void stream_gemv(const GemvArgs &a, uint8_t *smem, SMeta
     for (uint32_t u = 0; u < U; ++u) {
       const uint32_t o = base + u * kSW + warp;
       if (o < nch) {
-        if (tile != cur) {
-          if (cur != 0xFFFFFFFFu) deposit(cur, acc);
+        if (tile != cur) {  // the previous tile is done for this warp
+          deposit(cur - ct0, acc);
 #pragma unroll
           for (int m = 0; m < NMAT; ++m) acc[m][0] = acc[m][1] = 0.0f;
           cur = tile;
+          if ((tile - ct0) % kSGroupTiles == 0) flush((tile - ct0) / kSGroupTiles - 1);
         }
         if (ok) {
           const uint8_t *ch = stage + (u * kSW + warp) * CB;
@@ -386,9 +367,8 @@ __device__ __noinline__ void stream_gemv(const GemvArgs &a, uint8_t *smem, SMeta
             }
           }
         }
-        // advance to this warp's next chunk (16 further on)
-        pair += kSW;
-        while (pair >= P) {
+        pair += kSW;  // this warp's next chunk is 16 further on
+        if (pair >= P) {
           pair -= P;
           ++tile;
         }
@@ -397,7 +377,10 @@ __device__ __noinline__ void stream_gemv(const GemvArgs &a, uint8_t *smem, SMeta
     __syncwarp();
     if (lane == 0) mbar_arrive(smem_u32(&meta->empty[s]));
   }
-  if (cur != 0xFFFFFFFFu) deposit(cur, acc);
+  if (ntiles > 0) {
+    deposit(cur - ct0, acc);
+    flush((ntiles - 1) / kSGroupTiles);
+  }
 
   if (a.epi == kEpiArgmax) {
     // warp -> CTA (shared memory) -> grid (one candidate per CTA; the last CTA merges)
@@ -542,12 +525,11 @@ __global__ void __launch_bounds__(kSThreads, 1)
   for (uint32_t p = 0; p < n; ++p) {
     const Phase &cur = ph[p];
     if (cur.kind == kPhaseGemv) {
-      if (p > 0) ok = wait_phase(ctr, p - 1, abort_w, err, threadIdx.x == 0, &meta->flag[0],
-                                 ConsumerSync()) && ok;
+      const uint32_t wp = p > 0 ? p - 1 : kNoPhase;
       switch (cur.variant) {
-        case 0: stream_gemv<4, 1>(cur.g, smem, meta, ring, red, st, ok, abort_w, err); break;
-        case 1: stream_gemv<4, 2>(cur.g, smem, meta, ring, red, st, ok, abort_w, err); break;
-        default: stream_gemv<8, 1>(cur.g, smem, meta, ring, red, st, ok, abort_w, err); break;
+        case 0: stream_gemv<4, 1>(cur.g, smem, meta, ring, red, st, ok, ctr, wp, abort_w, err); break;
+        case 1: stream_gemv<4, 2>(cur.g, smem, meta, ring, red, st, ok, ctr, wp, abort_w, err); break;
+        default: stream_gemv<8, 1>(cur.g, smem, meta, ring, red, st, ok, ctr, wp, abort_w, err); break;
       }
     } else {
       const uint32_t v = cur.variant, gi = (v >> 1) & 3;

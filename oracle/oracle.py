@@ -36,6 +36,7 @@ class OrcConfig(C.Structure):
         ("kv_bf16", _U32), ("has_post_norms", _U32), ("full_every", _U32),
         ("attention_k_eq_v", _U32),
         ("rms_norm_eps", _F), ("rope_theta", _F), ("rope_theta_full", _F), ("attn_scale", _F),
+        ("layer_quant", _U32),
     ]
 
 
@@ -53,6 +54,8 @@ _SIGS = {
     "orc_gemv_q8": (None, [_P, _P, _P, _SZ, _SZ, _I]),
     "orc_gate_up_geglu_q4": (None, [_P, _P, _P, _P, _SZ, _SZ, _I]),
     "orc_gemv_bf16": (None, [_P, _P, _P, _SZ, _SZ]),
+    "orc_gemv_bf16_mt": (None, [_P, _P, _P, _SZ, _SZ, _I]),
+    "orc_gate_up_geglu_q8": (None, [_P, _P, _P, _P, _SZ, _SZ, _I]),
     "orc_rmsnorm": (None, [_P, _P, _P, _SZ, _F]),
     "orc_unit_rmsnorm": (None, [_P, _P, _SZ, _F]),
     "orc_add_rmsnorm": (None, [_P, _P, _P, _P, _SZ, _F, _F]),
@@ -188,9 +191,24 @@ def gate_up_geglu_q4(wg, wu, x, rows, cols):
 
 def gemv_bf16(w_bf16, x, rows, cols):
     y = np.zeros(rows, np.float32)
-    lib().orc_gemv_bf16(_p(y), _p(np.ascontiguousarray(x, np.float32)),
-                        _p(np.ascontiguousarray(w_bf16, np.uint16)), rows, cols)
+    lib().orc_gemv_bf16_mt(_p(y), _p(np.ascontiguousarray(x, np.float32)),
+                           _p(np.ascontiguousarray(w_bf16, np.uint16)), rows, cols, threads())
     return y
+
+
+def gate_up_geglu_q8(wg, wu, x, rows, cols):
+    y = np.zeros(rows, np.float32)
+    lib().orc_gate_up_geglu_q8(_p(y), _p(np.ascontiguousarray(wg, np.uint32)),
+                               _p(np.ascontiguousarray(wu, np.uint32)),
+                               _p(np.ascontiguousarray(x, np.float32)), rows, cols, threads())
+    return y
+
+
+def gate_up_geglu_bf16(wg, wu, x, rows, cols):
+    """kernels.zig gatedMlp's product with bf16 weights: gelu_tanh(Wg x) * (Wu x)."""
+    g = gemv_bf16(wg, x, rows, cols)
+    u = gemv_bf16(wu, x, rows, cols)
+    return np.array([gelu_tanh(float(a)) * b for a, b in zip(g, u)], np.float32)
 
 
 def rmsnorm(x, w, eps=1e-6):
@@ -344,7 +362,9 @@ class Model:
 
     def __init__(self, cfg: dict, seed: int, nthreads: int | None = None):
         names = {f for f, _ in OrcConfig._fields_}
-        c = OrcConfig(**{k: v for k, v in cfg.items() if k in names})
+        kw = {k: v for k, v in cfg.items() if k in names}
+        kw.setdefault("layer_quant", QUANT_Q4)
+        c = OrcConfig(**kw)
         self.cfg = dict(cfg)
         self.h = lib().orc_model_create(C.byref(c), seed, nthreads or threads())
         self.ring = Ring.borrow(lib().orc_model_ring(self.h))

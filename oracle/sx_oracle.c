@@ -313,6 +313,21 @@ void orc_gate_up_geglu_q4(float *y, const uint32_t *wg, const uint32_t *wu, cons
   orc_gemv_ctx c = {y, wg, wu, x, cols, 0};
   orc_parallel_for(rows, threads, orc_geglu_range, &c);
 }
+/* fused_mlp_q8.wgsl:1-127 (dequantised i8 * d times x, the Q8 GEMV's row order) */
+static void orc_geglu_q8_range(void *p, size_t b, size_t e) {
+  orc_gemv_ctx *c = (orc_gemv_ctx *)p;
+  size_t rw = (c->cols / 32) * 9;
+  for (size_t r = b; r < e; ++r) {
+    float g = orc_row_q8(c->w + r * rw, c->x, c->cols);
+    float u = orc_row_q8(c->w2 + r * rw, c->x, c->cols);
+    c->y[r] = orc_gelu_tanh(g) * u;
+  }
+}
+void orc_gate_up_geglu_q8(float *y, const uint32_t *wg, const uint32_t *wu, const float *x,
+                          size_t rows, size_t cols, int threads) {
+  orc_gemv_ctx c = {y, wg, wu, x, cols, 0};
+  orc_parallel_for(rows, threads, orc_geglu_q8_range, &c);
+}
 static void orc_geglu_w(float *y, const uint32_t *wg, const uint32_t *wu, const float *x,
                         size_t rows, size_t cols, int threads, int wbf16) {
   orc_gemv_ctx c = {y, wg, wu, x, cols, wbf16};
@@ -346,6 +361,31 @@ static float orc_dot_f32(const float *a, const float *b, size_t n) {
 /* kernels.zig:68-73 */
 void orc_gemv_bf16(float *y, const float *x, const uint16_t *w, size_t rows, size_t cols) {
   for (size_t r = 0; r < rows; ++r) y[r] = orc_dot_bf16(w + r * cols, x, cols);
+}
+typedef struct {
+  float *y;
+  const uint16_t *w, *w2;
+  const float *x;
+  size_t cols;
+} orc_bf16_ctx;
+static void orc_gemv_bf16_range(void *p, size_t b, size_t e) {
+  orc_bf16_ctx *c = (orc_bf16_ctx *)p;
+  for (size_t r = b; r < e; ++r) c->y[r] = orc_dot_bf16(c->w + r * c->cols, c->x, c->cols);
+}
+/* kernels.zig:76-92: the row split of gemvParallel */
+void orc_gemv_bf16_mt(float *y, const float *x, const uint16_t *w, size_t rows, size_t cols,
+                      int threads) {
+  orc_bf16_ctx c = {y, w, NULL, x, cols};
+  orc_parallel_for(rows, threads, orc_gemv_bf16_range, &c);
+}
+/* kernels.zig:100-115 gatedMlp's gate/up products with bf16 weights */
+static void orc_geglu_bf16_range(void *p, size_t b, size_t e) {
+  orc_bf16_ctx *c = (orc_bf16_ctx *)p;
+  for (size_t r = b; r < e; ++r) {
+    float g = orc_dot_bf16(c->w + r * c->cols, c->x, c->cols);
+    float u = orc_dot_bf16(c->w2 + r * c->cols, c->x, c->cols);
+    c->y[r] = orc_gelu_tanh(g) * u;
+  }
 }
 
 /* kernels.zig:46-52 (norm weights already widened to f32, model_gpu.zig:64-73) */
@@ -706,6 +746,26 @@ static uint32_t *orc_alloc_q(size_t rows, size_t cols, int mode) {
   return (uint32_t *)malloc(sizeof(uint32_t) * rows * orc_quantized_row_words(cols, mode));
 }
 
+/* a layer matrix in the model's layer format: quantised blocks (synthetic, quant.zig layout)
+ * or bf16 values bf16(0.02 N(0,1)) (the mode-none checkpoint stand-in) */
+static uint32_t *orc_layer_matrix(const orc_model_config *c, size_t rows, size_t cols,
+                                  uint64_t seed, uint64_t stream) {
+  uint32_t *w = orc_alloc_q(rows, cols, (int)c->layer_quant);
+  if (c->layer_quant == ORC_QUANT_Q8)
+    orc_synth_q8(w, rows, cols, seed, stream);
+  else if (c->layer_quant == ORC_QUANT_NONE)
+    orc_synth_bf16_normal((uint16_t *)w, rows * cols, seed, stream, 0.0f, 0.02f);
+  else
+    orc_synth_q4(w, rows, cols, seed, stream);
+  return w;
+}
+
+/* y = W x in the layer format (gemv_q4.wgsl / gemv_q8.wgsl / gemv_bf16.wgsl) */
+static void orc_proj(const orc_model *m, float *y, const uint32_t *w, const float *x, size_t rows,
+                     size_t cols);
+static void orc_proj_geglu(const orc_model *m, float *y, const uint32_t *wg, const uint32_t *wu,
+                           const float *x, size_t rows, size_t cols);
+
 orc_model *orc_model_create(const orc_model_config *cfg, uint64_t seed, int threads) {
   orc_model *m = (orc_model *)calloc(1, sizeof(orc_model));
   m->c = *cfg;
@@ -730,23 +790,19 @@ orc_model *orc_model_create(const orc_model_config *cfg, uint64_t seed, int thre
     L->theta = full ? c->rope_theta_full : c->rope_theta;
     if (L->q_dim > max_q) max_q = L->q_dim;
     if (L->kv_dim > max_kv) max_kv = L->kv_dim;
-    L->wq = orc_alloc_q(L->q_dim, H, ORC_QUANT_Q4);
-    L->wk = orc_alloc_q(L->kv_dim, H, ORC_QUANT_Q4);
-    L->wv = orc_alloc_q(L->kv_dim, H, ORC_QUANT_Q4);
-    L->wo = orc_alloc_q(H, L->q_dim, ORC_QUANT_Q4);
-    L->wg = orc_alloc_q(I, H, ORC_QUANT_Q4);
-    L->wu = orc_alloc_q(I, H, ORC_QUANT_Q4);
-    L->wd = orc_alloc_q(H, I, ORC_QUANT_Q4);
-    orc_synth_q4(L->wq, L->q_dim, H, seed, orc_stream(l, ORC_T_Q));
-    orc_synth_q4(L->wk, L->kv_dim, H, seed, orc_stream(l, ORC_T_K));
-    if (L->k_eq_v)
-      memcpy(L->wv, L->wk, sizeof(uint32_t) * L->kv_dim * (H / 32) * 5);
-    else
-      orc_synth_q4(L->wv, L->kv_dim, H, seed, orc_stream(l, ORC_T_V));
-    orc_synth_q4(L->wo, H, L->q_dim, seed, orc_stream(l, ORC_T_O));
-    orc_synth_q4(L->wg, I, H, seed, orc_stream(l, ORC_T_GATE));
-    orc_synth_q4(L->wu, I, H, seed, orc_stream(l, ORC_T_UP));
-    orc_synth_q4(L->wd, H, I, seed, orc_stream(l, ORC_T_DOWN));
+    L->wq = orc_layer_matrix(c, L->q_dim, H, seed, orc_stream(l, ORC_T_Q));
+    L->wk = orc_layer_matrix(c, L->kv_dim, H, seed, orc_stream(l, ORC_T_K));
+    if (L->k_eq_v) {
+      L->wv = orc_alloc_q(L->kv_dim, H, (int)c->layer_quant);
+      memcpy(L->wv, L->wk,
+             sizeof(uint32_t) * L->kv_dim * orc_quantized_row_words(H, (int)c->layer_quant));
+    } else {
+      L->wv = orc_layer_matrix(c, L->kv_dim, H, seed, orc_stream(l, ORC_T_V));
+    }
+    L->wo = orc_layer_matrix(c, H, L->q_dim, seed, orc_stream(l, ORC_T_O));
+    L->wg = orc_layer_matrix(c, I, H, seed, orc_stream(l, ORC_T_GATE));
+    L->wu = orc_layer_matrix(c, I, H, seed, orc_stream(l, ORC_T_UP));
+    L->wd = orc_layer_matrix(c, H, I, seed, orc_stream(l, ORC_T_DOWN));
     L->in_norm = (float *)malloc(sizeof(float) * H);
     L->post_attn = (float *)malloc(sizeof(float) * H);
     L->pre_ffn = (float *)malloc(sizeof(float) * H);
@@ -766,8 +822,13 @@ orc_model *orc_model_create(const orc_model_config *cfg, uint64_t seed, int thre
     L->k_cache = (float *)calloc((size_t)total_slots * L->kv_dim, sizeof(float));
     L->v_cache = (float *)calloc((size_t)total_slots * L->kv_dim, sizeof(float));
   }
-  m->lm_head = orc_alloc_q(c->vocab_size, H, ORC_QUANT_Q8);
-  orc_synth_q8(m->lm_head, c->vocab_size, H, seed, 2);
+  if (c->layer_quant == ORC_QUANT_NONE) {
+    m->lm_head = orc_alloc_q(c->vocab_size, H, ORC_QUANT_NONE);
+    orc_synth_bf16_normal((uint16_t *)m->lm_head, (size_t)c->vocab_size * H, seed, 2, 0.0f, 0.02f);
+  } else {
+    m->lm_head = orc_alloc_q(c->vocab_size, H, ORC_QUANT_Q8);
+    orc_synth_q8(m->lm_head, c->vocab_size, H, seed, 2);
+  }
   m->final_norm = (float *)malloc(sizeof(float) * H);
   orc_synth_gain_f32(m->final_norm, H, seed, 3);
   m->ring = orc_ring_create(1, c->num_anchors, c->window_size, c->num_recall);
@@ -852,6 +913,27 @@ static void orc_round_bf16(orc_model *m, float *v, size_t n) {
   for (size_t i = 0; i < n; ++i) v[i] = orc_bf16_to_f32(orc_bf16_from_f32(v[i]));
 }
 
+static void orc_proj(const orc_model *m, float *y, const uint32_t *w, const float *x, size_t rows,
+                     size_t cols) {
+  if (m->c.layer_quant == ORC_QUANT_Q8)
+    orc_gemv_q8(y, w, x, rows, cols, m->threads);
+  else if (m->c.layer_quant == ORC_QUANT_NONE)
+    orc_gemv_bf16_mt(y, x, (const uint16_t *)w, rows, cols, m->threads);
+  else
+    orc_gemv_q4_w(y, w, x, rows, cols, m->threads, m->act_bf16);
+}
+static void orc_proj_geglu(const orc_model *m, float *y, const uint32_t *wg, const uint32_t *wu,
+                           const float *x, size_t rows, size_t cols) {
+  if (m->c.layer_quant == ORC_QUANT_Q8) {
+    orc_gate_up_geglu_q8(y, wg, wu, x, rows, cols, m->threads);
+  } else if (m->c.layer_quant == ORC_QUANT_NONE) {
+    orc_bf16_ctx c = {y, (const uint16_t *)wg, (const uint16_t *)wu, x, cols};
+    orc_parallel_for(rows, m->threads, orc_geglu_bf16_range, &c);
+  } else {
+    orc_geglu_w(y, wg, wu, x, rows, cols, m->threads, m->act_bf16);
+  }
+}
+
 uint32_t orc_model_forward(orc_model *m, const float *x_in, uint64_t clock, int want_logits,
                            float *logits_out, float *x_out) {
   const orc_model_config *c = &m->c;
@@ -865,29 +947,33 @@ uint32_t orc_model_forward(orc_model *m, const float *x_in, uint64_t clock, int 
     orc_layer *L = &m->layers[l];
     orc_rmsnorm(m->normed, m->x, L->in_norm, H, eps);
     orc_round_bf16(m, m->normed, H);
-    orc_gemv_q4_w(m->q, L->wq, m->normed, L->q_dim, H, m->threads, m->act_bf16);
-    orc_gemv_q4_w(m->k, L->wk, m->normed, L->kv_dim, H, m->threads, m->act_bf16);
-    orc_gemv_q4_w(m->v, L->wv, m->normed, L->kv_dim, H, m->threads, m->act_bf16);
+    orc_proj(m, m->q, L->wq, m->normed, L->q_dim, H);
+    orc_proj(m, m->k, L->wk, m->normed, L->kv_dim, H);
+    orc_proj(m, m->v, L->wv, m->normed, L->kv_dim, H);
     orc_qkv_rope(m->q, m->k, m->v, L->q_norm, L->k_norm, L->k_cache, L->v_cache, c->kv_bf16,
                  c->num_q_heads, L->num_kv, L->head_dim, L->rot, L->k_eq_v, L->inv_freq, eps,
                  clock, slot, total_slots);
     orc_decode_attn(m->attn, m->q, L->k_cache, L->v_cache, m->slots, n, c->num_q_heads,
                     L->num_kv, L->head_dim, total_slots, c->attn_scale);
     orc_round_bf16(m, m->attn, L->q_dim);
-    orc_gemv_q4_w(m->mlp, L->wo, m->attn, H, L->q_dim, m->threads, m->act_bf16);
+    orc_proj(m, m->mlp, L->wo, m->attn, H, L->q_dim);
     if (c->has_post_norms) orc_rmsnorm(m->mlp, m->mlp, L->post_attn, H, eps);
     orc_add_rmsnorm(m->x, m->mlp, L->pre_ffn, m->normed, H, eps, 1.0f);
     orc_round_bf16(m, m->normed, H);
-    orc_geglu_w(m->act, L->wg, L->wu, m->normed, I, H, m->threads, m->act_bf16);
+    orc_proj_geglu(m, m->act, L->wg, L->wu, m->normed, I, H);
     orc_round_bf16(m, m->act, I);
-    orc_gemv_q4_w(m->mlp, L->wd, m->act, H, I, m->threads, m->act_bf16);
+    orc_proj(m, m->mlp, L->wd, m->act, H, I);
     if (c->has_post_norms) orc_rmsnorm(m->mlp, m->mlp, L->post_ffn, H, eps);
     orc_add_rmsnorm(m->x, m->mlp, L->in_norm, m->normed, H, eps, L->layer_scalar);
   }
   if (x_out) memcpy(x_out, m->x, sizeof(float) * H);
   if (!want_logits) return 0;
   orc_rmsnorm(m->normed, m->x, m->final_norm, H, eps);
-  orc_gemv_q8(m->logits, m->lm_head, m->normed, c->vocab_size, H, m->threads);
+  if (c->layer_quant == ORC_QUANT_NONE)
+    orc_gemv_bf16_mt(m->logits, m->normed, (const uint16_t *)m->lm_head, c->vocab_size, H,
+                     m->threads);
+  else
+    orc_gemv_q8(m->logits, m->lm_head, m->normed, c->vocab_size, H, m->threads);
   if (logits_out) memcpy(logits_out, m->logits, sizeof(float) * c->vocab_size);
   return orc_argmax(m->logits, c->vocab_size);
 }

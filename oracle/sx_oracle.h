@@ -50,6 +50,12 @@ void orc_gate_up_geglu_q4(float *y, const uint32_t *wg, const uint32_t *wu, cons
 
 /* ---- kernels.zig ---- */
 void orc_gemv_bf16(float *y, const float *x, const uint16_t *w, size_t rows, size_t cols);
+/* the same on `threads` threads (rows split; each row's sum is unchanged) */
+void orc_gemv_bf16_mt(float *y, const float *x, const uint16_t *w, size_t rows, size_t cols,
+                      int threads);
+/* fused_mlp_q8.wgsl: act[r] = gelu_tanh(Wg[r].x) * (Wu[r].x) with Q8_0 weights */
+void orc_gate_up_geglu_q8(float *y, const uint32_t *wg, const uint32_t *wu, const float *x,
+                          size_t rows, size_t cols, int threads);
 void orc_rmsnorm(float *out, const float *in, const float *w, size_t n, float eps);
 void orc_unit_rmsnorm(float *out, const float *in, size_t n, float eps);
 void orc_add_rmsnorm(float *x, const float *r, const float *w, float *y, size_t n, float eps,
@@ -105,6 +111,10 @@ typedef struct {
   uint32_t num_anchors, window_size, num_recall;
   uint32_t kv_bf16, has_post_norms, full_every, attention_k_eq_v;
   float rms_norm_eps, rope_theta, rope_theta_full, attn_scale;
+  /* layer weight format (kernels.zig:36-41 GpuEngine.init by mode): ORC_QUANT_Q4 (Q4_0
+   * layers), ORC_QUANT_Q8 (Q8_0 layers) or ORC_QUANT_NONE (bf16 layers); the LM head is Q8_0
+   * in both quantised modes and bf16 otherwise (kernels.zig:38, model_gpu.zig:161) */
+  uint32_t layer_quant;
 } orc_model_config;
 
 typedef struct orc_model orc_model;
