@@ -293,6 +293,13 @@ inline cudaError_t allow_max_dynamic_smem(K kernel) {
                               optin - (int)fa.sharedSizeBytes);
 }
 
+// Indirect dispatch (record*Indirect, kernels.zig:84-134): an op recorded behind a device-side
+// dispatch record {x, y, z} does nothing when any of the three is zero (the quiescence gate
+// wrote zeros).  Read after the dependency wait.
+SX_DEV bool gate_closed(const uint32_t *gate) {
+  return gate != nullptr && (gate[0] == 0u || gate[1] == 0u || gate[2] == 0u);
+}
+
 // Programmatic dependent launch: wait for the producer grid's memory before reading it.
 SX_DEV void pdl_wait() { asm volatile("griddepcontrol.wait;\n" ::: "memory"); }
 SX_DEV void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;\n" ::); }

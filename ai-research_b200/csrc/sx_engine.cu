@@ -140,8 +140,9 @@ namespace {
 
 sx_status do_gemv(sx_engine *e, cudaStream_t s, int qt, bool geglu, const void *w0,
                   const void *w1, const float *x, float *y, uint32_t m, uint32_t k,
-                  uint32_t batch) {
+                  uint32_t batch, const uint32_t *gate = nullptr) {
   if (qt == 0) {  // mode none: bf16 weights (gemv_bf16.wgsl)
+    SX_CHECK_ARG(gate == nullptr, "gemv bf16: indirect dispatch is not built for mode none");
     SX_CHECK_ARG(m > 0 && k > 0 && k % 8 == 0 && batch >= 1 && batch <= 8,
                  "gemv bf16: need m > 0, k a multiple of 8 and batch 1..8 (m=%u k=%u batch=%u)",
                  m, k, batch);
@@ -171,15 +172,18 @@ sx_status do_gemv(sx_engine *e, cudaStream_t s, int qt, bool geglu, const void *
   a.ldx = k;
   a.pro = sx::kProNone;
   a.epi = sx::kEpiPlain;
+  a.gate = gate;
   sx_host_bind_scratch(e, a);
   return cuda_status(sx::launch_gemv(qt, geglu, a, e->num_sms, s, true), "gemv launch");
 }
 
 sx_status do_norm(cudaStream_t s, bool add, float *x, const float *r, const float *w, float *y,
-                  uint32_t n, uint32_t batch, float eps, float scalar) {
+                  uint32_t n, uint32_t batch, float eps, float scalar,
+                  const uint32_t *gate = nullptr) {
   SX_CHECK_ARG(n > 0 && batch > 0, "rmsnorm: empty input");
   SX_CHECK_ARG(x && w && y && (!add || r), "rmsnorm: null pointer");
   sx::NormArgs a{x, r, w, y, n, batch, n, eps, scalar};
+  a.gate = gate;
   return cuda_status(sx::launch_rmsnorm(add, a, s), "rmsnorm launch");
 }
 
@@ -187,7 +191,7 @@ sx_status do_qkv_rope(sx_engine *e, cudaStream_t s, const float *q_in, const flo
                       const float *v_in, const float *qnw, const float *knw, float *q_out,
                       void *kc, void *vc, const uint32_t *step, uint32_t num_q, uint32_t num_kv,
                       uint32_t head_dim, uint32_t rot, uint32_t k_eq_v, float theta, float eps,
-                      uint32_t total_slots) {
+                      uint32_t total_slots, const uint32_t *gate = nullptr) {
   SX_CHECK_ARG(num_q > 0 && head_dim > 0 && head_dim <= 4096 && rot <= head_dim && rot % 2 == 0,
                "qkv_rope: bad shape (num_q=%u head_dim=%u rot=%u)", num_q, head_dim, rot);
   SX_CHECK_ARG(total_slots > 0, "qkv_rope: total_slots must be > 0");
@@ -197,13 +201,14 @@ sx_status do_qkv_rope(sx_engine *e, cudaStream_t s, const float *q_in, const flo
   sx::QkvRopeArgs a{q_in, k_in, v_in, qnw, knw, q_out, kc, vc, step, freq,
                     num_q, num_kv, head_dim, rot, k_eq_v, e->kv_bf16 ? 1u : 0u, total_slots,
                     eps, e->err_dev};
+  a.gate = gate;
   return cuda_status(sx::launch_qkv_rope(a, s), "qkv_rope launch");
 }
 
 sx_status do_attn(sx_engine *e, cudaStream_t s, const float *q, const void *kc, const void *vc,
                   const uint32_t *slots, const uint32_t *step, float *out, uint32_t head_dim,
                   uint32_t kv_dim, uint32_t gqa, float scale, uint32_t num_q,
-                  uint32_t total_slots) {
+                  uint32_t total_slots, const uint32_t *gate = nullptr) {
   SX_CHECK_ARG(head_dim == 64 || head_dim == 128 || head_dim == 256 || head_dim == 512,
                "decode_attn: head_dim must be 64/128/256/512 (got %u)", head_dim);
   SX_CHECK_ARG(gqa == 1 || gqa == 2 || gqa == 4 || gqa == 8,
@@ -221,6 +226,7 @@ sx_status do_attn(sx_engine *e, cudaStream_t s, const float *q, const void *kc, 
   }
   sx::AttnArgs a{q, kc, vc, slots, step, out, e->attn_part, head_dim, kv_dim,
                  gqa, num_q, total_slots, e->kv_bf16 ? 1u : 0u, scale, e->err_dev};
+  a.gate = gate;
   return cuda_status(sx::launch_decode_attn(a, s), "decode_attn launch");
 }
 
@@ -243,33 +249,43 @@ sx_status run_op(sx_engine *e, cudaStream_t s, const Op &op, uint32_t *kernels) 
       int qt = op.kind == OP_GEMV_LOGITS ? (e->mode == SX_QUANT_NONE ? 0 : 8) : qt_of(e->mode);
       *kernels += 1;
       return do_gemv(e, s, qt, false, op.bind.at(0), nullptr, (const float *)op.bind.at(1),
-                     (float *)op.bind.at(2), op.u[0], op.u[1], 1);
+                     (float *)op.bind.at(2), op.u[0], op.u[1], 1, op.gate);
     }
     case OP_GATE_UP:
       *kernels += 1;
       return do_gemv(e, s, qt_of(e->mode), true, op.bind.at(0), op.bind.at(1),
-                     (const float *)op.bind.at(2), (float *)op.bind.at(3), op.u[0], op.u[1], 1);
+                     (const float *)op.bind.at(2), (float *)op.bind.at(3), op.u[0], op.u[1], 1,
+                     op.gate);
     case OP_ADD_RMSNORM:
       *kernels += 1;
       return do_norm(s, true, (float *)op.bind.at(0), (const float *)op.bind.at(1),
                      (const float *)op.bind.at(2), (float *)op.bind.at(3), op.u[0], 1, op.f[0],
-                     op.f[1]);
+                     op.f[1], op.gate);
     case OP_RMSNORM:
       *kernels += 1;
       return do_norm(s, false, (float *)op.bind.at(0), nullptr, (const float *)op.bind.at(1),
-                     (float *)op.bind.at(2), op.u[0], 1, op.f[0], 1.0f);
+                     (float *)op.bind.at(2), op.u[0], 1, op.f[0], 1.0f, op.gate);
     case OP_ATTN:
       *kernels += 2;
       return do_attn(e, s, (const float *)op.bind.at(0), op.bind.at(1), op.bind.at(2),
                      (const uint32_t *)op.bind.at(3), (const uint32_t *)op.bind.at(5),
-                     (float *)op.bind.at(4), op.u[0], op.u[1], op.u[2], op.f[0], op.u[3], op.u[4]);
+                     (float *)op.bind.at(4), op.u[0], op.u[1], op.u[2], op.f[0], op.u[3], op.u[4],
+                     op.gate);
     case OP_QKV_ROPE:
       *kernels += 1;
       return do_qkv_rope(e, s, (const float *)op.bind.at(0), (const float *)op.bind.at(1),
                          (const float *)op.bind.at(2), (const float *)op.bind.at(3),
                          (const float *)op.bind.at(4), (float *)op.bind.at(5), op.bind.at(6),
                          op.bind.at(7), (const uint32_t *)op.bind.at(8), op.u[0], op.u[1],
-                         op.u[2], op.u[3], op.u[4], op.f[0], op.f[1], op.u[5]);
+                         op.u[2], op.u[3], op.u[4], op.f[0], op.f[1], op.u[5], op.gate);
+    case OP_QGATE: {
+      *kernels += 1;
+      sx::GateArgs g = op.qgate;
+      g.x = (const float *)op.bind.at(0);
+      g.x_prev = (float *)op.bind.at(1);
+      g.ind = (uint32_t *)op.bind.at(2);
+      return cuda_status(sx::launch_quiescence_gate(g, s), "quiescence gate launch");
+    }
     case OP_ARGMAX:
       *kernels += 2;
       return do_argmax(e, s, (const float *)op.bind.at(0), op.u[0], (uint32_t *)op.bind.at(1));
@@ -1062,6 +1078,125 @@ SX_API void sx_record_qkv_rope(sx_engine *e, sx_cmd *c, sx_set *set, uint32_t nu
   op.f[1] = eps;
   push_op(c, op, set);
 }
+// ---- quiescence gate and indirect records (kernels.zig:84-138, model_dispatch.zig:45-101)
+SX_API void sx_record_quiescence_gate(sx_engine *e, sx_cmd *c, sx_set *set,
+                                      const sx_quiescence_gate_pc *pc) {
+  if (!record_guard(e, c, set, 3, "record_quiescence_gate")) return;
+  if (!pc || pc->hidden_size == 0 || pc->num_cmds > 16) {
+    poison(c, SX_ERR_INVALID, "record_quiescence_gate: null push constants, hidden_size 0 or "
+                              "more than 16 commands");
+    return;
+  }
+  const sx_buffer *xb = set->b[0], *pb = set->b[1], *ib = set->b[2];
+  if (xb->bytes < 4ull * pc->hidden_size || pb->bytes < 4ull * pc->hidden_size ||
+      ib->bytes < 12ull * ((uint64_t)pc->base_cmd_idx + pc->num_cmds)) {
+    poison(c, SX_ERR_INVALID, "record_quiescence_gate: a bound buffer is too small");
+    return;
+  }
+  Op op{OP_QGATE};
+  op.qgate.h = pc->hidden_size;
+  op.qgate.threshold_sq = pc->threshold_sq;
+  op.qgate.base = pc->base_cmd_idx;
+  op.qgate.num_cmds = pc->num_cmds;
+  for (int i = 0; i < 16; ++i) op.qgate.targets[i] = pc->targets[i];
+  push_op(c, op, set);
+}
+
+// the dispatch record {x, y, z} at byte `offset` of `ind` (12 bytes, 4-byte aligned)
+static const uint32_t *indirect_record(sx_cmd *c, sx_buffer *ind, uint64_t offset,
+                                       const char *name) {
+  if (!ind || offset % 4 != 0 || offset + 12 > ind->bytes) {
+    std::string m = std::string(name) + ": indirect buffer missing, misaligned or too small";
+    poison(c, SX_ERR_INVALID, m.c_str());
+    return nullptr;
+  }
+  return reinterpret_cast<const uint32_t *>(static_cast<const uint8_t *>(ind->d) + offset);
+}
+
+SX_API void sx_record_gemv_indirect(sx_engine *e, sx_cmd *c, sx_set *set, uint32_t m, uint32_t k,
+                                    sx_buffer *ind, uint64_t offset) {
+  if (!record_guard(e, c, set, 3, "record_gemv_indirect")) return;
+  const uint32_t *g = indirect_record(c, ind, offset, "record_gemv_indirect");
+  if (!g) return;
+  Op op{OP_GEMV};
+  op.u[0] = m;
+  op.u[1] = k;
+  op.gate = g;
+  push_op(c, op, set);
+}
+SX_API void sx_record_gate_up_indirect(sx_engine *e, sx_cmd *c, sx_set *set, uint32_t m,
+                                       uint32_t k, sx_buffer *ind, uint64_t offset) {
+  if (!record_guard(e, c, set, 4, "record_gate_up_indirect")) return;
+  const uint32_t *g = indirect_record(c, ind, offset, "record_gate_up_indirect");
+  if (!g) return;
+  Op op{OP_GATE_UP};
+  op.u[0] = m;
+  op.u[1] = k;
+  op.gate = g;
+  push_op(c, op, set);
+}
+SX_API void sx_record_add_rmsnorm_indirect(sx_engine *e, sx_cmd *c, sx_set *set, uint32_t h,
+                                           float eps, float scalar, sx_buffer *ind,
+                                           uint64_t offset) {
+  if (!record_guard(e, c, set, 4, "record_add_rmsnorm_indirect")) return;
+  const uint32_t *g = indirect_record(c, ind, offset, "record_add_rmsnorm_indirect");
+  if (!g) return;
+  Op op{OP_ADD_RMSNORM};
+  op.u[0] = h;
+  op.f[0] = eps;
+  op.f[1] = scalar;
+  op.gate = g;
+  push_op(c, op, set);
+}
+SX_API void sx_record_rmsnorm_indirect(sx_engine *e, sx_cmd *c, sx_set *set, uint32_t h,
+                                       float eps, sx_buffer *ind, uint64_t offset) {
+  if (!record_guard(e, c, set, 3, "record_rmsnorm_indirect")) return;
+  const uint32_t *g = indirect_record(c, ind, offset, "record_rmsnorm_indirect");
+  if (!g) return;
+  Op op{OP_RMSNORM};
+  op.u[0] = h;
+  op.f[0] = eps;
+  op.gate = g;
+  push_op(c, op, set);
+}
+SX_API void sx_record_decode_attn_indirect(sx_engine *e, sx_cmd *c, sx_set *set,
+                                           uint32_t head_dim, uint32_t kv_dim, uint32_t gqa_ratio,
+                                           float inv_sqrt_dim, uint32_t num_q_heads,
+                                           uint32_t total_slots, sx_buffer *ind,
+                                           uint64_t offset) {
+  if (!record_guard(e, c, set, 6, "record_decode_attn_indirect")) return;
+  const uint32_t *g = indirect_record(c, ind, offset, "record_decode_attn_indirect");
+  if (!g) return;
+  Op op{OP_ATTN};
+  op.u[0] = head_dim;
+  op.u[1] = kv_dim;
+  op.u[2] = gqa_ratio;
+  op.u[3] = num_q_heads;
+  op.u[4] = total_slots;
+  op.f[0] = inv_sqrt_dim;
+  op.gate = g;
+  push_op(c, op, set);
+}
+SX_API void sx_record_qkv_rope_indirect(sx_engine *e, sx_cmd *c, sx_set *set, uint32_t num_q,
+                                        uint32_t num_kv, uint32_t head_dim, uint32_t rotary_dim,
+                                        uint32_t k_eq_v, float theta, float eps,
+                                        uint32_t total_slots, sx_buffer *ind, uint64_t offset) {
+  if (!record_guard(e, c, set, 9, "record_qkv_rope_indirect")) return;
+  const uint32_t *g = indirect_record(c, ind, offset, "record_qkv_rope_indirect");
+  if (!g) return;
+  Op op{OP_QKV_ROPE};
+  op.u[0] = num_q;
+  op.u[1] = num_kv;
+  op.u[2] = head_dim;
+  op.u[3] = rotary_dim;
+  op.u[4] = k_eq_v;
+  op.u[5] = total_slots;
+  op.f[0] = theta;
+  op.f[1] = eps;
+  op.gate = g;
+  push_op(c, op, set);
+}
+
 SX_API void sx_record_argmax(sx_engine *e, sx_cmd *c, sx_set *set, uint32_t vocab) {
   if (!record_guard(e, c, set, 2, "record_argmax")) return;
   Op op{OP_ARGMAX};
@@ -1219,6 +1354,24 @@ SX_API sx_status sx_dispatch_qkv_rope_attn(
   a.cache_ld = (uint64_t)total_slots * num_kv * head_dim;
   sx_host_bind_scratch(e, a);
   return cuda_status(sx::launch_attn_fused(a, e->stream, false), "qkv_rope_attn launch");
+}
+SX_API sx_status sx_dispatch_quiescence_gate(sx_engine *e, const float *x_curr, float *x_prev,
+                                             uint32_t *indirect_args,
+                                             const sx_quiescence_gate_pc *pc) {
+  SX_CHECK_ARG(e && x_curr && x_prev && indirect_args && pc, "quiescence_gate: null argument");
+  SX_CHECK_ARG(pc->hidden_size > 0 && pc->num_cmds <= 16,
+               "quiescence_gate: hidden_size must be > 0 and num_cmds <= 16");
+  SX_TRY_CUDA(cudaSetDevice(e->device), "cudaSetDevice");
+  sx::GateArgs g{};
+  g.x = x_curr;
+  g.x_prev = x_prev;
+  g.ind = indirect_args;
+  g.h = pc->hidden_size;
+  g.threshold_sq = pc->threshold_sq;
+  g.base = pc->base_cmd_idx;
+  g.num_cmds = pc->num_cmds;
+  for (int i = 0; i < 16; ++i) g.targets[i] = pc->targets[i];
+  return cuda_status(sx::launch_quiescence_gate(g, e->stream), "quiescence gate launch");
 }
 SX_API sx_status sx_dispatch_argmax(sx_engine *e, const float *logits, uint32_t n,
                                     uint32_t *out_token) {

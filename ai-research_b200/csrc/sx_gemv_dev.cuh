@@ -470,6 +470,10 @@ SX_DEV void gemv_body(const GemvArgs &a, uint8_t *smem, bool prefetch, bool run,
     pdl_launch_dependents();
     // 2. wait for the producer of x, bring x into shared memory and build the B fragments
     pdl_wait();
+    if (gate_closed(a.gate)) {  // recorded behind a closed dispatch record: do nothing
+      cp_async_wait<0>();
+      return;
+    }
   }
   float *xin = reinterpret_cast<float *>(smem + L.xin);
   const float *xsrc = a.x;

@@ -68,6 +68,7 @@ enum OpKind {
   OP_ATTN_FUSED,  // qkv_rope + decode attention + combine (model graph)
   OP_PERSIST,     // the GEMV_FUSED / ATTN_FUSED run of a persistent command buffer
   OP_STREAM,      // the same run as one streaming decode launch (sx_stream.cu)
+  OP_QGATE,       // quiescence gate (quiescence_gate.wgsl)
   OP_ALLREDUCE,   // tensor parallel: in-place sum all-reduce of u[0] floats at dev
   OP_ALLGATHER,   // tensor parallel: bind[0] (u[0] u32 words per rank) -> bind[1]
   OP_TP_ARGMAX,   // tensor parallel: merge u[0] ranks' argmax candidates bind[0] -> bind[1]
@@ -91,6 +92,9 @@ struct Op {
   uint32_t attn_rot = 0;
   float attn_theta = 0.0f;
   sx_comm *comm = nullptr;  // OP_ALLREDUCE / OP_ALLGATHER
+  // record*Indirect: device address of the op's dispatch record {x, y, z} (null: always runs)
+  const uint32_t *gate = nullptr;
+  sx::GateArgs qgate{};     // OP_QGATE
 };
 
 struct sx_cmd {

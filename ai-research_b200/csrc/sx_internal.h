@@ -46,6 +46,7 @@ struct GemvArgs {
   const uint32_t *pf_slots, *pf_step;
   const void *pf_base[2];
   uint32_t pf_row_bytes, pf_max;
+  const uint32_t *gate;  // indirect dispatch record {x, y, z}: a zero skips the call (or null)
 };
 
 // Per-device kernel attributes (dynamic shared memory limits); called at engine creation,
@@ -103,6 +104,7 @@ struct NormArgs {
   float *y;           // output
   uint32_t n, batch, ld;
   float eps, scalar;
+  const uint32_t *gate = nullptr;  // indirect dispatch record (see gate_closed)
 };
 cudaError_t launch_rmsnorm(bool add, const NormArgs &a, cudaStream_t s);
 
@@ -115,8 +117,23 @@ struct QkvRopeArgs {
   uint32_t num_q, num_kv, head_dim, rotary_dim, k_eq_v, kv_bf16, total_slots;
   float eps;
   uint32_t *err;
+  const uint32_t *gate = nullptr;  // indirect dispatch record (see gate_closed)
 };
 cudaError_t launch_qkv_rope(const QkvRopeArgs &a, cudaStream_t s);
+
+// quiescence_gate.wgsl: mean (x - x_prev)^2 over h (32-lane strided sums and tree, as the
+// shader), x_prev = x, then num_cmds dispatch records {targets[c], 1, 1} (the layer runs:
+// mean >= threshold_sq or threshold_sq <= 0) or {0, 0, 0} at ind + 3 (base + c)
+struct GateArgs {
+  const float *x;
+  float *x_prev;
+  uint32_t *ind;
+  uint32_t h;
+  float threshold_sq;
+  uint32_t base, num_cmds;
+  uint32_t targets[16];
+};
+cudaError_t launch_quiescence_gate(const GateArgs &a, cudaStream_t s);
 
 struct AttnArgs {
   const float *q;
@@ -128,6 +145,7 @@ struct AttnArgs {
   uint32_t head_dim, kv_dim, gqa, num_q, total_slots, kv_bf16;
   float scale;
   uint32_t *err;
+  const uint32_t *gate = nullptr;  // indirect dispatch record (see gate_closed)
 };
 size_t attn_scratch_bytes(uint32_t num_q, uint32_t total_slots, uint32_t head_dim);
 cudaError_t launch_decode_attn(const AttnArgs &a, cudaStream_t s);

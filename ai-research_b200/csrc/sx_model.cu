@@ -28,6 +28,8 @@ struct LayerBufs {
   sx_set *s_qkv_rope = nullptr, *s_attn = nullptr, *s_o = nullptr, *s_gate_up = nullptr;
   sx_set *s_down = nullptr, *s_pre_ffn = nullptr, *s_post_attn = nullptr, *s_post_ffn = nullptr;
   sx_set *s_post_ffn_add = nullptr;
+  sx_buffer *x_prev = nullptr;  // quiescence-gate history (model_gpu.zig:132), zero at start
+  sx_set *s_gate = nullptr;     // {x, x_prev, indirect records} (model_gpu.zig:156)
 };
 
 enum Tensor : uint32_t {
@@ -53,6 +55,7 @@ struct sx_model {
   sx_buffer *attn_out = nullptr, *slots = nullptr, *act = nullptr, *mlp_out = nullptr;
   sx_buffer *logits = nullptr, *token = nullptr, *step = nullptr;
   sx_buffer *lm_head = nullptr, *final_norm = nullptr;
+  sx_buffer *ind = nullptr;  // 16 dispatch records of 12 bytes per layer (model_gpu.zig:107)
   sx_set *s_final_norm = nullptr, *s_logits = nullptr, *s_argmax = nullptr;
   sx_cmd *cmd[2][2] = {{nullptr, nullptr}, {nullptr, nullptr}};  // [want_logits][io]
   // independent sessions: activation rows [S][...], KV caches [S][slots][kv_dim] (session 0
@@ -171,6 +174,8 @@ sx_status alloc_model(sx_model *m) {
     m->weight_bytes += B.wq->bytes + B.wk->bytes + B.wv->bytes + B.wo->bytes + B.wg->bytes +
                        B.wu->bytes + B.wd->bytes;
   }
+  M_TRY(mk_buf(m, 16ull * 12 * c.num_layers, &m->ind));
+  for (uint32_t l = 0; l < c.num_layers; ++l) M_TRY(mk_buf(m, 4ull * H, &m->L[l].x_prev));
   M_TRY(mk_buf(m, sx_packed_bytes(V, H, m->hmode), &m->lm_head));
   M_TRY(mk_buf(m, 4ull * H, &m->final_norm));
   m->weight_bytes += m->lm_head->bytes;
@@ -192,7 +197,10 @@ sx_status alloc_model(sx_model *m) {
     M_TRY(mk_set(m, {m->mlp_out, B.post_attn, m->mlp_out}, &B.s_post_attn));
     M_TRY(mk_set(m, {m->mlp_out, B.post_ffn, m->mlp_out}, &B.s_post_ffn));
     M_TRY(mk_set(m, {m->x, m->mlp_out, B.in_norm, m->normed}, &B.s_post_ffn_add));
+    M_TRY(mk_set(m, {m->x, B.x_prev, m->ind}, &B.s_gate));
+    M_TRY(sx_host_cuda_status(cudaMemset(B.x_prev->d, 0, 4ull * H), "x_prev zero"));
   }
+  M_TRY(sx_host_cuda_status(cudaMemset(m->ind->d, 0, m->ind->bytes), "indirect records zero"));
   M_TRY(mk_set(m, {m->x, m->final_norm, m->normed}, &m->s_final_norm));
   M_TRY(mk_set(m, {m->lm_head, m->normed, m->logits}, &m->s_logits));
   M_TRY(mk_set(m, {m->logits, m->token}, &m->s_argmax));
@@ -254,6 +262,62 @@ void record_layer(sx_model *m, sx_cmd *cmd, uint32_t l) {
   sx_record_barrier(e, cmd);
 }
 
+// recordLayerIndirect (model_dispatch.zig:45-101): the quiescence gate writes the dispatch
+// records of the layer's 13 commands (16 slots per layer), every command reads its record
+void record_layer_indirect(sx_model *m, sx_cmd *cmd, uint32_t l) {
+  sx_engine *e = m->e;
+  const sx_model_config &c = m->c;
+  LayerBufs &B = m->L[l];
+  const uint32_t H = c.hidden_size, I = m->I;
+  const float eps = c.rms_norm_eps;
+  const uint32_t gqa = m->nq / B.num_kv;
+  sx_quiescence_gate_pc pc{};
+  pc.hidden_size = H;
+  pc.threshold_sq = c.quiescence_threshold;
+  pc.base_cmd_idx = l * 16;
+  pc.num_cmds = 13;
+  // the reference's workgroup counts (here they only need to be non-zero)
+  const uint32_t t[13] = {1, (B.q_dim + 3) / 4, (B.kv_dim + 3) / 4, (B.kv_dim + 3) / 4,
+                          m->nq + B.num_kv, m->nq, (H + 3) / 4, 1, 1, (I + 3) / 4,
+                          (H + 3) / 4, 1, 1};
+  for (int i = 0; i < 13; ++i) pc.targets[i] = t[i];
+  sx_record_quiescence_gate(e, cmd, B.s_gate, &pc);
+  sx_record_barrier(e, cmd);
+  const uint64_t base = (uint64_t)l * 16 * 12;
+  sx_buffer *ind = m->ind;
+  sx_record_rmsnorm_indirect(e, cmd, B.s_input_norm, H, eps, ind, base + 0 * 12);
+  sx_record_barrier(e, cmd);
+  sx_record_gemv_indirect(e, cmd, B.s_q, B.q_dim, H, ind, base + 1 * 12);
+  sx_record_gemv_indirect(e, cmd, B.s_k, B.kv_dim, H, ind, base + 2 * 12);
+  sx_record_gemv_indirect(e, cmd, B.s_v, B.kv_dim, H, ind, base + 3 * 12);
+  sx_record_barrier(e, cmd);
+  sx_record_qkv_rope_indirect(e, cmd, B.s_qkv_rope, m->nq, B.num_kv, B.head_dim, B.rot, B.k_eq_v,
+                              B.theta, eps, m->total_slots, ind, base + 4 * 12);
+  sx_record_barrier(e, cmd);
+  sx_record_decode_attn_indirect(e, cmd, B.s_attn, B.head_dim, B.kv_dim, gqa, c.attn_scale,
+                                 m->nq, m->total_slots, ind, base + 5 * 12);
+  sx_record_barrier(e, cmd);
+  sx_record_gemv_indirect(e, cmd, B.s_o, H, B.q_dim, ind, base + 6 * 12);
+  if (c.has_post_norms) {
+    sx_record_barrier(e, cmd);
+    sx_record_rmsnorm_indirect(e, cmd, B.s_post_attn, H, eps, ind, base + 7 * 12);
+  }
+  sx_record_barrier(e, cmd);
+  sx_record_add_rmsnorm_indirect(e, cmd, B.s_pre_ffn, H, eps, 1.0f, ind, base + 8 * 12);
+  sx_record_barrier(e, cmd);
+  sx_record_gate_up_indirect(e, cmd, B.s_gate_up, I, H, ind, base + 9 * 12);
+  sx_record_barrier(e, cmd);
+  sx_record_gemv_indirect(e, cmd, B.s_down, H, I, ind, base + 10 * 12);
+  if (c.has_post_norms) {
+    sx_record_barrier(e, cmd);
+    sx_record_rmsnorm_indirect(e, cmd, B.s_post_ffn, H, eps, ind, base + 11 * 12);
+  }
+  sx_record_barrier(e, cmd);
+  sx_record_add_rmsnorm_indirect(e, cmd, B.s_post_ffn_add, H, eps, B.layer_scalar, ind,
+                                 base + 12 * 12);
+  sx_record_barrier(e, cmd);
+}
+
 // recordForwardGraph (model_dispatch.zig:103-129), optionally wrapped in the per-token
 // host<->device copies of gpuDispatchForwardToken (model_dispatch.zig:136-146).
 sx_status record_forward(sx_model *m, sx_cmd *cmd, bool logits, bool io) {
@@ -272,7 +336,13 @@ sx_status record_forward(sx_model *m, sx_cmd *cmd, bool logits, bool io) {
     sx_host_push_op(cmd, s);
   }
   sx_record_barrier(e, cmd);
-  for (uint32_t l = 0; l < c.num_layers; ++l) record_layer(m, cmd, l);
+  // layers below num_layers / 3 are recorded direct, the rest behind the quiescence gate
+  // (model_dispatch.zig:107-118)
+  const uint32_t dense_limit = c.num_layers / 3;
+  for (uint32_t l = 0; l < c.num_layers; ++l) {
+    if (l < dense_limit) record_layer(m, cmd, l);
+    else record_layer_indirect(m, cmd, l);
+  }
   if (logits) {
     sx_record_rmsnorm(e, cmd, m->s_final_norm, c.hidden_size, c.rms_norm_eps);
     sx_record_barrier(e, cmd);
@@ -581,6 +651,11 @@ sx_status create_model(sx_engine *e, const sx_model_config *cfg, sx_comm *comm, 
   if ((c.kv_bf16 != 0) != e->kv_bf16) {
     sx_host_set_error("model_create: config.kv_bf16 must match the engine's KV precision flag");
     return SX_ERR_INVALID;
+  }
+  if (c.quiescence_threshold > 0.0f && c.reference_graph != 1) {
+    sx_host_set_error("model_create: a positive quiescence threshold needs the op-by-op graph "
+                      "(reference_graph 1), whose gated layers read device-side dispatch records");
+    return SX_ERR_UNSUPPORTED;
   }
   if (e->mode == SX_QUANT_NONE && c.reference_graph != 1) {
     sx_host_set_error("model_create: bf16 layers (engine mode none) run the reference's op-by-op "

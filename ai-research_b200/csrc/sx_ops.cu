@@ -38,6 +38,7 @@ __global__ void __launch_bounds__(1024) rmsnorm_kernel(NormArgs a) {
   __shared__ float red[32];
   pdl_launch_dependents();
   pdl_wait();
+  if (gate_closed(a.gate)) return;
   float *x = a.x + (size_t)blockIdx.x * a.ld;
   const float *r = ADD ? a.r + (size_t)blockIdx.x * a.ld : nullptr;
   float *y = a.y + (size_t)blockIdx.x * a.ld;
@@ -67,6 +68,7 @@ __global__ void __launch_bounds__(128) qkv_rope_kernel(QkvRopeArgs a) {
   extern __shared__ float sh[];  // head_dim floats + 32 reduction slots
   pdl_launch_dependents();
   pdl_wait();
+  if (gate_closed(a.gate)) return;
   float *vec = sh;
   float *red = sh + a.head_dim;
   const uint32_t D = a.head_dim, half = a.rotary_dim / 2;
@@ -191,6 +193,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_split_kernel(AttnArgs a)
   extern __shared__ float sh[];
   pdl_launch_dependents();
   pdl_wait();
+  if (gate_closed(a.gate)) return;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t D = a.head_dim;  // == 32 * DPL
   const uint32_t kvh = blockIdx.x, chunk = blockIdx.y, nchunks = gridDim.y;
@@ -280,6 +283,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_split_kernel(AttnArgs a)
 __global__ void attn_combine_kernel(AttnArgs a, uint32_t nchunks) {
   pdl_launch_dependents();
   pdl_wait();
+  if (gate_closed(a.gate)) return;
   const uint32_t qh = blockIdx.x, D = a.head_dim;
   const float *base = a.part + (size_t)qh * nchunks * (D + 2);
   float M = -INFINITY;
@@ -534,6 +538,44 @@ cudaError_t prepare_ops_kernels() {
   for (cudaError_t x : r)
     if (x != cudaSuccess) return x;
   return cudaSuccess;
+}
+
+// quiescence_gate.wgsl:1-62, one 32-thread CTA with the shader's order of operations: lane l
+// accumulates (x[i] - x_prev[i])^2 for i = l, l + 32, ... (no fused multiply-add, like the
+// CPU restatement) and copies x into x_prev, the partials fold 16, 8, 4, 2, lane 0 adds the
+// last two, divides by h and writes the dispatch records.
+__global__ void __launch_bounds__(32) quiescence_gate_kernel(GateArgs a) {
+  __shared__ float s[32];
+  pdl_launch_dependents();
+  pdl_wait();
+  const uint32_t lane = threadIdx.x;
+  float acc = 0.0f;
+  for (uint32_t i = lane; i < a.h; i += 32) {
+    const float c = a.x[i];
+    const float d = __fsub_rn(c, a.x_prev[i]);
+    acc = __fadd_rn(acc, __fmul_rn(d, d));
+    a.x_prev[i] = c;
+  }
+  s[lane] = acc;
+  __syncwarp();
+  for (uint32_t w = 16; w >= 2; w >>= 1) {
+    if (lane < w) s[lane] = __fadd_rn(s[lane], s[lane + w]);
+    __syncwarp();
+  }
+  if (lane == 0) {
+    const float mean_sq = __fdiv_rn(__fadd_rn(s[0], s[1]), (float)a.h);
+    const bool active = (mean_sq >= a.threshold_sq) || (a.threshold_sq <= 0.0f);
+    for (uint32_t c = 0; c < a.num_cmds && c < 16; ++c) {
+      uint32_t *rec = a.ind + 3ull * (a.base + c);
+      rec[0] = active ? a.targets[c] : 0u;
+      rec[1] = active ? 1u : 0u;
+      rec[2] = active ? 1u : 0u;
+    }
+  }
+}
+
+cudaError_t launch_quiescence_gate(const GateArgs &a, cudaStream_t s) {
+  return launch_pdl(quiescence_gate_kernel, dim3(1), dim3(32), 0, s, a);
 }
 
 cudaError_t launch_rmsnorm(bool add, const NormArgs &a, cudaStream_t s) {

@@ -70,10 +70,19 @@ class ModelConfig(C.Structure):
         ("tp_size", C.c_uint32),
         ("tp_rank", C.c_uint32),
         ("num_sessions", C.c_uint32),
+        ("quiescence_threshold", C.c_float),
     ]
 
     def as_dict(self) -> dict:
         return {name: getattr(self, name) for name, _ in self._fields_}
+
+
+class QuiescenceGatePC(C.Structure):
+    """sx_quiescence_gate_pc (QuiescenceGatePushConstants, src/gpu/kernels.zig:10-16)."""
+
+    _fields_ = [("hidden_size", C.c_uint32), ("threshold_sq", C.c_float),
+                ("base_cmd_idx", C.c_uint32), ("num_cmds", C.c_uint32),
+                ("targets", C.c_uint32 * 16)]
 
 
 class TpShard(C.Structure):
@@ -125,6 +134,7 @@ def model_config(**kw) -> ModelConfig:
         tp_size=1,
         tp_rank=0,
         num_sessions=1,
+        quiescence_threshold=0.0,
     )
     base.update(kw)
     return ModelConfig(**base)
@@ -212,6 +222,16 @@ _SIGS = {
     "sx_record_decode_attn": (None, [_P, _P, _P, _U32, _U32, _U32, _F, _U32, _U32]),
     "sx_record_qkv_rope": (None, [_P, _P, _P, _U32, _U32, _U32, _U32, _U32, _F, _F, _U32]),
     "sx_record_argmax": (None, [_P, _P, _P, _U32]),
+    "sx_record_quiescence_gate": (None, [_P, _P, _P, _P]),
+    "sx_record_gemv_indirect": (None, [_P, _P, _P, _U32, _U32, _P, _U64]),
+    "sx_record_gate_up_indirect": (None, [_P, _P, _P, _U32, _U32, _P, _U64]),
+    "sx_record_add_rmsnorm_indirect": (None, [_P, _P, _P, _U32, _F, _F, _P, _U64]),
+    "sx_record_rmsnorm_indirect": (None, [_P, _P, _P, _U32, _F, _P, _U64]),
+    "sx_record_decode_attn_indirect": (None, [_P, _P, _P, _U32, _U32, _U32, _F, _U32, _U32, _P,
+                                               _U64]),
+    "sx_record_qkv_rope_indirect": (None, [_P, _P, _P, _U32, _U32, _U32, _U32, _U32, _F, _F,
+                                            _U32, _P, _U64]),
+    "sx_dispatch_quiescence_gate": (_S, [_P, _P, _P, _P, _P]),
     "sx_record_barrier": (None, [_P, _P]),
     "sx_submit": (_S, [_P, _P, _U64]),
     "sx_dispatch_gemv": (_S, [_P, _I, _P, _P, _P, _U32, _U32, _U32]),
@@ -451,6 +471,37 @@ class Engine:
 
     def record_argmax(self, cmd, s, vocab):
         lib().sx_record_argmax(self.h, cmd.h, s.h, vocab)
+
+    def record_quiescence_gate(self, cmd, s, pc: "QuiescenceGatePC"):
+        lib().sx_record_quiescence_gate(self.h, cmd.h, s.h, C.byref(pc))
+
+    def record_gemv_indirect(self, cmd, s, m, k, ind, offset):
+        lib().sx_record_gemv_indirect(self.h, cmd.h, s.h, m, k, ind.h, offset)
+
+    def record_gate_up_indirect(self, cmd, s, m, k, ind, offset):
+        lib().sx_record_gate_up_indirect(self.h, cmd.h, s.h, m, k, ind.h, offset)
+
+    def record_add_rmsnorm_indirect(self, cmd, s, h, eps, scalar, ind, offset):
+        lib().sx_record_add_rmsnorm_indirect(self.h, cmd.h, s.h, h, eps, scalar, ind.h, offset)
+
+    def record_rmsnorm_indirect(self, cmd, s, h, eps, ind, offset):
+        lib().sx_record_rmsnorm_indirect(self.h, cmd.h, s.h, h, eps, ind.h, offset)
+
+    def record_decode_attn_indirect(self, cmd, s, head_dim, kv_dim, gqa_ratio, inv_sqrt_dim,
+                                    num_q_heads, total_slots, ind, offset):
+        lib().sx_record_decode_attn_indirect(self.h, cmd.h, s.h, head_dim, kv_dim, gqa_ratio,
+                                             inv_sqrt_dim, num_q_heads, total_slots, ind.h,
+                                             offset)
+
+    def record_qkv_rope_indirect(self, cmd, s, num_q, num_kv, head_dim, rotary_dim, k_eq_v,
+                                 theta, eps, total_slots, ind, offset):
+        lib().sx_record_qkv_rope_indirect(self.h, cmd.h, s.h, num_q, num_kv, head_dim,
+                                          rotary_dim, int(k_eq_v), theta, eps, total_slots,
+                                          ind.h, offset)
+
+    def quiescence_gate(self, x_curr, x_prev, ind, pc: "QuiescenceGatePC"):
+        check(lib().sx_dispatch_quiescence_gate(self.h, _ptr(x_curr), _ptr(x_prev), _ptr(ind),
+                                                C.byref(pc)))
 
     def record_barrier(self, cmd):
         lib().sx_record_barrier(self.h, cmd.h)

@@ -179,6 +179,44 @@ SX_API void sx_record_decode_attn(sx_engine *e, sx_cmd *c, sx_set *set, uint32_t
 SX_API void sx_record_qkv_rope(sx_engine *e, sx_cmd *c, sx_set *set, uint32_t num_q,
                                uint32_t num_kv, uint32_t head_dim, uint32_t rotary_dim,
                                uint32_t k_eq_v, float theta, float eps, uint32_t total_slots);
+/* kernels.zig:10-16 QuiescenceGatePushConstants */
+typedef struct {
+  uint32_t hidden_size;
+  float threshold_sq;
+  uint32_t base_cmd_idx;
+  uint32_t num_cmds;
+  uint32_t targets[16];
+} sx_quiescence_gate_pc;
+/* recordQuiescenceGate (kernels.zig:136-138, quiescence_gate.wgsl): set {X_curr, X_prev,
+ * Indirect_args}.  mean((X_curr - X_prev)^2) over hidden_size, X_prev = X_curr, then for
+ * c < num_cmds the dispatch record {targets[c], 1, 1} (the layer runs: mean >= threshold_sq
+ * or threshold_sq <= 0) or {0, 0, 0} at u32 3 (base_cmd_idx + c) of Indirect_args. */
+SX_API void sx_record_quiescence_gate(sx_engine *e, sx_cmd *c, sx_set *set,
+                                      const sx_quiescence_gate_pc *pc);
+/* record*Indirect (kernels.zig:84-87, 96-99, 104-107, 112-115, 120-123, 130-134): the op
+ * reads its dispatch record {x, y, z} (three u32 at byte `offset` of `ind`) on the device when
+ * it runs and does nothing when any of the three is zero.  CUDA grids are fixed when the op is
+ * recorded, so a non-zero record runs the whole op (the reference's workgroup counts come from
+ * the gate's `targets`, which only need to be non-zero here).  The attention variant takes
+ * num_q_heads, which the reference takes from the record's x. */
+SX_API void sx_record_gemv_indirect(sx_engine *e, sx_cmd *c, sx_set *set, uint32_t m, uint32_t k,
+                                    sx_buffer *ind, uint64_t offset);
+SX_API void sx_record_gate_up_indirect(sx_engine *e, sx_cmd *c, sx_set *set, uint32_t m,
+                                       uint32_t k, sx_buffer *ind, uint64_t offset);
+SX_API void sx_record_add_rmsnorm_indirect(sx_engine *e, sx_cmd *c, sx_set *set, uint32_t h,
+                                           float eps, float scalar, sx_buffer *ind,
+                                           uint64_t offset);
+SX_API void sx_record_rmsnorm_indirect(sx_engine *e, sx_cmd *c, sx_set *set, uint32_t h,
+                                       float eps, sx_buffer *ind, uint64_t offset);
+SX_API void sx_record_decode_attn_indirect(sx_engine *e, sx_cmd *c, sx_set *set,
+                                           uint32_t head_dim, uint32_t kv_dim, uint32_t gqa_ratio,
+                                           float inv_sqrt_dim, uint32_t num_q_heads,
+                                           uint32_t total_slots, sx_buffer *ind,
+                                           uint64_t offset);
+SX_API void sx_record_qkv_rope_indirect(sx_engine *e, sx_cmd *c, sx_set *set, uint32_t num_q,
+                                        uint32_t num_kv, uint32_t head_dim, uint32_t rotary_dim,
+                                        uint32_t k_eq_v, float theta, float eps,
+                                        uint32_t total_slots, sx_buffer *ind, uint64_t offset);
 /* recordArgmax (kernels.zig:139-142): set {Logits, OutToken}; first index of the maximum
  * (the CPU rule, kernels.zig:164-174) */
 SX_API void sx_record_argmax(sx_engine *e, sx_cmd *c, sx_set *set, uint32_t vocab);
@@ -244,6 +282,10 @@ SX_API sx_status sx_dispatch_qkv_rope_attn(sx_engine *e, const float *q_in, cons
                                            uint32_t rotary_dim, uint32_t k_eq_v, float theta,
                                            float eps, float scale, uint32_t total_slots,
                                            uint32_t instances, uint32_t qkv_stride);
+/* The quiescence gate alone on device vectors (asynchronous on the engine stream). */
+SX_API sx_status sx_dispatch_quiescence_gate(sx_engine *e, const float *x_curr, float *x_prev,
+                                             uint32_t *indirect_args,
+                                             const sx_quiescence_gate_pc *pc);
 SX_API sx_status sx_dispatch_argmax(sx_engine *e, const float *logits, uint32_t n,
                                     uint32_t *out_token);
 /* No counterpart in the reference.  Decode attention that allocates nothing, for callers that
@@ -307,6 +349,12 @@ typedef struct {
                                 one batched pass (config 2 batch 8, config 5 sessions).  At
                                 most 8; needs the fused graph (reference_graph 0), tp_size <= 1
                                 and a ring of at most 1024 slots. */
+  float quiescence_threshold; /* model_gpu.zig:75 quiescence_thresh: layers l >= num_layers / 3
+                                are recorded behind the quiescence gate and skipped when the
+                                residual entering them moved less than this (mean square) since
+                                the last token (model_dispatch.zig:45-118); 0 runs every layer.
+                                A positive threshold needs the op-by-op graph
+                                (reference_graph 1). */
 } sx_model_config;
 
 /* sizeof(sx_model_config): bindings check their mirror of the struct against it. */

@@ -36,7 +36,7 @@ class OrcConfig(C.Structure):
         ("kv_bf16", _U32), ("has_post_norms", _U32), ("full_every", _U32),
         ("attention_k_eq_v", _U32),
         ("rms_norm_eps", _F), ("rope_theta", _F), ("rope_theta_full", _F), ("attn_scale", _F),
-        ("layer_quant", _U32),
+        ("layer_quant", _U32), ("quiescence_threshold", _F),
     ]
 
 
@@ -55,6 +55,8 @@ _SIGS = {
     "orc_gate_up_geglu_q4": (None, [_P, _P, _P, _P, _SZ, _SZ, _I]),
     "orc_gemv_bf16": (None, [_P, _P, _P, _SZ, _SZ]),
     "orc_gemv_bf16_mt": (None, [_P, _P, _P, _SZ, _SZ, _I]),
+    "orc_quiescence_gate": (_I, [_P, _P, _U32, _F, _P]),
+    "orc_model_gate_stats": (None, [_P, _P, _P]),
     "orc_gate_up_geglu_q8": (None, [_P, _P, _P, _P, _SZ, _SZ, _I]),
     "orc_rmsnorm": (None, [_P, _P, _P, _SZ, _F]),
     "orc_unit_rmsnorm": (None, [_P, _P, _SZ, _F]),
@@ -202,6 +204,15 @@ def gate_up_geglu_q8(wg, wu, x, rows, cols):
                                _p(np.ascontiguousarray(wu, np.uint32)),
                                _p(np.ascontiguousarray(x, np.float32)), rows, cols, threads())
     return y
+
+
+def quiescence_gate(x, x_prev, threshold_sq):
+    """quiescence_gate.wgsl on one vector: (runs, mean_sq); x_prev (float32 array) is updated."""
+    ms = np.zeros(1, np.float32)
+    x = np.ascontiguousarray(x, np.float32)
+    assert x_prev.dtype == np.float32 and x_prev.flags.c_contiguous
+    r = lib().orc_quiescence_gate(_p(x), _p(x_prev), x.size, threshold_sq, _p(ms))
+    return bool(r), float(ms[0])
 
 
 def gate_up_geglu_bf16(wg, wu, x, rows, cols):
@@ -390,6 +401,14 @@ class Model:
         xo = np.zeros(self.cfg["hidden_size"], np.float32)
         tok = lib().orc_model_forward(self.h, _p(x), clock, int(want_logits), _p(logits), _p(xo))
         return int(tok), logits, xo
+
+    def gate_stats(self):
+        """(mean_sq[layers], active[layers]) of the last forward's quiescence gates."""
+        n = self.cfg["num_layers"]
+        ms = np.zeros(n, np.float32)
+        act = np.zeros(n, np.uint32)
+        lib().orc_model_gate_stats(self.h, _p(ms), _p(act))
+        return ms, act
 
     def kv_dim(self, layer):
         return int(lib().orc_model_kv_dim(self.h, layer))

@@ -731,6 +731,9 @@ typedef struct {
 
 struct orc_model {
   orc_model_config c;
+  float *x_prev;        /* [num_layers][H] quiescence-gate history (model_gpu.zig:132) */
+  float *gate_mean_sq;  /* [num_layers] last forward's gate statistic */
+  uint32_t *gate_active;
   int threads;
   uint64_t seed;
   orc_layer *layers;
@@ -832,6 +835,9 @@ orc_model *orc_model_create(const orc_model_config *cfg, uint64_t seed, int thre
   m->final_norm = (float *)malloc(sizeof(float) * H);
   orc_synth_gain_f32(m->final_norm, H, seed, 3);
   m->ring = orc_ring_create(1, c->num_anchors, c->window_size, c->num_recall);
+  m->x_prev = (float *)calloc((size_t)c->num_layers * H, sizeof(float));
+  m->gate_mean_sq = (float *)calloc(c->num_layers, sizeof(float));
+  m->gate_active = (uint32_t *)calloc(c->num_layers, sizeof(uint32_t));
   m->x = (float *)malloc(sizeof(float) * H);
   m->normed = (float *)malloc(sizeof(float) * H);
   m->mlp = (float *)malloc(sizeof(float) * H);
@@ -854,6 +860,7 @@ void orc_model_destroy(orc_model *m) {
     free(L->q_norm); free(L->k_norm); free(L->inv_freq); free(L->k_cache); free(L->v_cache);
   }
   free(m->layers);
+  free(m->x_prev); free(m->gate_mean_sq); free(m->gate_active);
   free(m->lm_head); free(m->final_norm);
   orc_ring_destroy(m->ring);
   free(m->x); free(m->normed); free(m->mlp); free(m->q); free(m->attn); free(m->k);
@@ -934,6 +941,35 @@ static void orc_proj_geglu(const orc_model *m, float *y, const uint32_t *wg, con
   }
 }
 
+/* quiescence_gate.wgsl:1-62: lane l sums (X_curr[i] - X_prev[i])^2 over i = l, l + 32, ...
+ * (copying X_curr into X_prev), the 32 partial sums are folded 16, 8, 4, 2 and the last two
+ * added; the layer runs when mean_sq >= threshold_sq or threshold_sq <= 0 */
+int orc_quiescence_gate(const float *x, float *x_prev, uint32_t n, float threshold_sq,
+                        float *mean_sq) {
+  float s[32];
+  for (uint32_t lane = 0; lane < 32; ++lane) {
+    float acc = 0.0f;
+    for (uint32_t i = lane; i < n; i += 32) {
+      float d = x[i] - x_prev[i];
+      acc = acc + d * d;
+      x_prev[i] = x[i];
+    }
+    s[lane] = acc;
+  }
+  for (uint32_t w = 16; w >= 2; w >>= 1)
+    for (uint32_t lane = 0; lane < w; ++lane) s[lane] = s[lane] + s[lane + w];
+  float ms = (s[0] + s[1]) / (float)n;
+  if (mean_sq) *mean_sq = ms;
+  return (ms >= threshold_sq) || (threshold_sq <= 0.0f);
+}
+
+void orc_model_gate_stats(const orc_model *m, float *mean_sq, uint32_t *active) {
+  for (uint32_t l = 0; l < m->c.num_layers; ++l) {
+    if (mean_sq) mean_sq[l] = m->gate_mean_sq[l];
+    if (active) active[l] = m->gate_active[l];
+  }
+}
+
 uint32_t orc_model_forward(orc_model *m, const float *x_in, uint64_t clock, int want_logits,
                            float *logits_out, float *x_out) {
   const orc_model_config *c = &m->c;
@@ -943,8 +979,19 @@ uint32_t orc_model_forward(orc_model *m, const float *x_in, uint64_t clock, int 
   memcpy(m->x, x_in, sizeof(float) * H);
   uint32_t slot = orc_ring_activate_slot(m->ring, 0, clock);
   uint32_t n = orc_ring_active_slots(m->ring, 0, clock, m->slots);
+  const uint32_t dense_limit = c->num_layers / 3;  /* model_dispatch.zig:107 */
   for (uint32_t l = 0; l < c->num_layers; ++l) {
     orc_layer *L = &m->layers[l];
+    m->gate_active[l] = 1;
+    m->gate_mean_sq[l] = 0.0f;
+    if (l >= dense_limit) {
+      /* recordLayerIndirect: the gate sees the residual entering the layer; a quiescent
+       * layer's 13 commands dispatch nothing (the residual passes through, no K/V write) */
+      m->gate_active[l] = (uint32_t)orc_quiescence_gate(m->x, m->x_prev + (size_t)l * H, H,
+                                                        c->quiescence_threshold,
+                                                        &m->gate_mean_sq[l]);
+      if (!m->gate_active[l]) continue;
+    }
     orc_rmsnorm(m->normed, m->x, L->in_norm, H, eps);
     orc_round_bf16(m, m->normed, H);
     orc_proj(m, m->q, L->wq, m->normed, L->q_dim, H);

@@ -115,6 +115,9 @@ typedef struct {
    * layers), ORC_QUANT_Q8 (Q8_0 layers) or ORC_QUANT_NONE (bf16 layers); the LM head is Q8_0
    * in both quantised modes and bf16 otherwise (kernels.zig:38, model_gpu.zig:161) */
   uint32_t layer_quant;
+  /* model_gpu.zig:75 quiescence_thresh: layers l >= num_layers / 3 run behind the quiescence
+   * gate (model_dispatch.zig:112-118); 0 lets every layer run */
+  float quiescence_threshold;
 } orc_model_config;
 
 typedef struct orc_model orc_model;
@@ -124,6 +127,12 @@ orc_ring *orc_model_ring(orc_model *m);
 uint32_t orc_model_forward(orc_model *m, const float *x_in, uint64_t clock, int want_logits,
                            float *logits_out, float *x_out);
 void orc_model_fill_kv(orc_model *m, uint64_t seed);
+/* quiescence_gate.wgsl:1-62 on one vector: mean of (x - x_prev)^2 with the shader's 32-lane
+ * strided sums and tree; x_prev becomes x; returns 1 when the layer runs */
+int orc_quiescence_gate(const float *x, float *x_prev, uint32_t n, float threshold_sq,
+                        float *mean_sq);
+/* per-layer gate outcome of the last forward: mean_sq[l], active[l] (1 for ungated layers) */
+void orc_model_gate_stats(const orc_model *m, float *mean_sq, uint32_t *active);
 void orc_model_set_act_bf16(orc_model *m, int on);
 void orc_model_synth_recall(orc_model *m, uint64_t clock, uint32_t n_recall, uint64_t seed);
 float *orc_model_kcache(orc_model *m, uint32_t layer);
