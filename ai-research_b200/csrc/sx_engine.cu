@@ -622,6 +622,8 @@ SX_API sx_status sx_engine_create(int device, sx_quant_mode mode, uint32_t flags
     if (st) break;
     st = cuda_status(sx::prepare_stream_kernel(), "streaming kernel attributes");
     if (st) break;
+    st = cuda_status(sx::prepare_archive_kernels(), "archive kernel attributes");
+    if (st) break;
     st = cuda_status(sx::prepare_prefill_kernel(), "prefill kernel attributes");
   } while (0);
   if (st != SX_OK) {

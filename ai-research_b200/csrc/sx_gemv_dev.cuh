@@ -204,7 +204,11 @@ SX_DEV void run_prologue_gains(const GemvArgs &a, float *xin, float *red, const 
 #pragma unroll
     for (int q = 0; q < kProPer; ++q) {
       uint32_t i = threadIdx.x + q * nthr;
-      if (i < K) xo[i] = __fmul_rn(__fmul_rn(xv[q], r), nw[q]);
+      if (i < K) {
+        const float v = __fmul_rn(__fmul_rn(xv[q], r), nw[q]);
+        xo[i] = v;
+        if (a.pro_norm_out != nullptr && blockIdx.x == 0) a.pro_norm_out[(size_t)j * K + i] = v;
+      }
     }
     sync();
   }

@@ -26,6 +26,7 @@ struct GemvArgs {
   const float *pro_mlp;     // kProResid: sublayer output added to x
   const float *pro_post_w;  // kProResid: optional post-norm gain of the sublayer output
   float *pro_x_out;         // kProResid: updated residual stream (must not alias x)
+  float *pro_norm_out;      // optional: the normed input rows, written by CTA 0
   float pro_scalar;         // kProResid: layer scalar
   float eps;
   int epi;
@@ -249,6 +250,34 @@ bool stream_attn_variant(const AttnFusedArgs &a, uint32_t *variant);
 cudaError_t prepare_stream_kernel();
 cudaError_t launch_stream(const Phase *phases, uint32_t n, uint32_t *ctr, uint32_t *err,
                           int num_sms, cudaStream_t s);
+
+// The recall tier on the device (sx_archive.cu): DiffArchive + integrateMemory over the
+// model's caches.  Capacity up to kArchiveMaxCapacity entries (the selection holds every score
+// in shared memory).
+constexpr uint32_t kArchiveMaxCapacity = 16384;
+struct ArchiveLayer {
+  void *k_cache, *v_cache;  // session 0's cache of the layer, [slot][kv_dim]
+  uint32_t kv_dim;
+};
+struct ArchiveArgs {
+  const float *normed;      // the token's final normed state [dim]
+  float *prev;              // the previous token's [dim]
+  float *vectors;           // [capacity][dim] unit vectors
+  uint64_t *timestamp, *last_accessed;
+  uint32_t *access_count;
+  float *salience;
+  void *kv;                 // [capacity][layers][2][max_kv] in the cache format
+  float *scores;            // [capacity]
+  uint32_t *state;          // count, write_head, appended, append index, selected count
+  uint32_t *selected;       // [num_recall] archive indices in rank order
+  uint64_t *sel_ts;         // [num_recall] their timestamps
+  const ArchiveLayer *layers;
+  uint32_t dim, capacity, num_layers, max_kv, kv_bf16, num_recall, recall_start, slot;
+  uint64_t clock;
+  float alpha, beta, gamma, lambda;
+};
+cudaError_t prepare_archive_kernels();
+cudaError_t launch_archive_integrate(const ArchiveArgs &a, cudaStream_t s);
 
 // Batch-prefill Q4_0 projection GEMM (sx_prefill.cu): y[t][n] = x[t][:] . bf16(deq(w[n][:]))
 cudaError_t prepare_prefill_kernel();

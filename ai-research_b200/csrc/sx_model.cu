@@ -543,6 +543,7 @@ sx_status record_forward_fused(sx_model *m, sx_cmd *cmd, bool logits, bool io,
     h.pro_scalar = P.layer_scalar;
     h.pro_w = (const float *)m->final_norm->d;
     h.pro_x_out = (float *)m->x->d;
+    h.pro_norm_out = (float *)m->normed->d;  // the final normed state (recall tier's query)
     h.eps = eps;
     h.epi = sx::kEpiArgmax;
     h.token = (uint32_t *)m->token->d;
@@ -1221,3 +1222,178 @@ extern "C" SX_API sx_status sx_prefill_batch(sx_model *m, uint32_t T, const floa
   }
   return sx_engine_sync(e);
 }
+
+// ---------------------------------------------------------------------------------------
+// The recall tier on the device (sx_archive.cu): DiffArchive + integrateMemory over this
+// model's caches (session 0) and the caller's ring.
+struct sx_archive {
+  sx_model *m = nullptr;
+  sx::ArchiveArgs a{};
+  void *block = nullptr;            // one device allocation for everything below
+  sx::ArchiveLayer *d_layers = nullptr;
+  uint32_t *h_out = nullptr;        // pinned: state[5] | selected[R] | timestamps (u64)[R]
+  uint32_t count = 0;
+};
+
+extern "C" {
+
+SX_API sx_status sx_archive_create(sx_model *m, uint32_t capacity, const sx_salience_config *cfg,
+                                   sx_archive **out) {
+  if (!m || !out || capacity == 0 || capacity > sx::kArchiveMaxCapacity) {
+    sx_host_set_error("archive_create: need a model and 1 <= capacity <= %u",
+                      sx::kArchiveMaxCapacity);
+    return SX_ERR_INVALID;
+  }
+  if (m->c.num_recall > 1024 || m->comm) {
+    sx_host_set_error("archive_create: at most 1024 recall slots, one GPU");
+    return SX_ERR_UNSUPPORTED;
+  }
+  sx_engine *e = m->e;
+  M_TRY(sx_host_cuda_status(cudaSetDevice(e->device), "cudaSetDevice"));
+  const uint32_t H = m->c.hidden_size, L = m->c.num_layers, R = m->c.num_recall;
+  uint32_t max_kv = 0;
+  for (const LayerBufs &B : m->L) max_kv = B.kv_dim > max_kv ? B.kv_dim : max_kv;
+  const size_t eb = m->c.kv_bf16 ? 2 : 4;
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    size_t o = off;
+    off = (off + bytes + 255) & ~(size_t)255;
+    return o;
+  };
+  const size_t o_prev = take(4ull * H), o_vec = take(4ull * capacity * H);
+  const size_t o_ts = take(8ull * capacity), o_la = take(8ull * capacity);
+  const size_t o_ac = take(4ull * capacity), o_sal = take(4ull * capacity);
+  const size_t o_kv = take((size_t)capacity * L * 2 * max_kv * eb), o_sc = take(4ull * capacity);
+  const size_t o_st = take(64), o_sel = take(4ull * (R + 1)), o_sts = take(8ull * (R + 1));
+  const size_t o_lay = take(sizeof(sx::ArchiveLayer) * L);
+  sx_archive *a = new sx_archive();
+  a->m = m;
+  sx_status st = sx_host_cuda_status(cudaMalloc(&a->block, off), "archive memory");
+  if (st == SX_OK)
+    st = sx_host_cuda_status(cudaMemset(a->block, 0, off), "archive memory");
+  if (st == SX_OK)
+    st = sx_host_cuda_status(
+        cudaHostAlloc((void **)&a->h_out, 4 * (8 + 3 * (R + 1)), cudaHostAllocDefault),
+        "archive readback");
+  if (st != SX_OK) {
+    sx_archive_destroy(a);
+    return st;
+  }
+  uint8_t *b = static_cast<uint8_t *>(a->block);
+  std::vector<sx::ArchiveLayer> lay(L);
+  for (uint32_t l = 0; l < L; ++l) lay[l] = {m->L[l].kc->d, m->L[l].vc->d, m->L[l].kv_dim};
+  a->d_layers = reinterpret_cast<sx::ArchiveLayer *>(b + o_lay);
+  st = sx_host_cuda_status(cudaMemcpy(a->d_layers, lay.data(), sizeof(sx::ArchiveLayer) * L,
+                                      cudaMemcpyHostToDevice),
+                           "archive layers");
+  if (st != SX_OK) {
+    sx_archive_destroy(a);
+    return st;
+  }
+  sx::ArchiveArgs &A = a->a;
+  A.normed = (const float *)m->normed->d;
+  A.prev = reinterpret_cast<float *>(b + o_prev);
+  A.vectors = reinterpret_cast<float *>(b + o_vec);
+  A.timestamp = reinterpret_cast<uint64_t *>(b + o_ts);
+  A.last_accessed = reinterpret_cast<uint64_t *>(b + o_la);
+  A.access_count = reinterpret_cast<uint32_t *>(b + o_ac);
+  A.salience = reinterpret_cast<float *>(b + o_sal);
+  A.kv = b + o_kv;
+  A.scores = reinterpret_cast<float *>(b + o_sc);
+  A.state = reinterpret_cast<uint32_t *>(b + o_st);
+  A.selected = reinterpret_cast<uint32_t *>(b + o_sel);
+  A.sel_ts = reinterpret_cast<uint64_t *>(b + o_sts);
+  A.layers = a->d_layers;
+  A.dim = H;
+  A.capacity = capacity;
+  A.num_layers = L;
+  A.max_kv = max_kv;
+  A.kv_bf16 = m->c.kv_bf16 ? 1u : 0u;
+  A.num_recall = R;
+  A.recall_start = m->c.num_anchors + m->c.window_size;
+  // SalienceConfig defaults (memory.zig:5-7)
+  A.alpha = cfg ? cfg->alpha : 1.0f;
+  A.beta = cfg ? cfg->beta : 0.5f;
+  A.gamma = cfg ? cfg->gamma : 1.0f;
+  A.lambda = cfg ? cfg->lambda : 1.0f / 2048.0f;
+  *out = a;
+  return SX_OK;
+}
+
+SX_API void sx_archive_destroy(sx_archive *a) {
+  if (!a) return;
+  cudaSetDevice(a->m->e->device);
+  cudaStreamSynchronize(a->m->e->stream);
+  if (a->block) cudaFree(a->block);
+  if (a->h_out) cudaFreeHost(a->h_out);
+  delete a;
+}
+
+SX_API sx_status sx_archive_integrate(sx_archive *a, sx_ring *ring, uint64_t clock,
+                                     uint32_t *n_selected, uint32_t *selected) {
+  if (!a || !ring) {
+    sx_host_set_error("archive_integrate: null argument");
+    return SX_ERR_INVALID;
+  }
+  if (sx_ring_total_slots(ring) != a->m->total_slots) {
+    sx_host_set_error("archive_integrate: the ring does not match the model's slots");
+    return SX_ERR_INVALID;
+  }
+  sx_engine *e = a->m->e;
+  M_TRY(sx_host_cuda_status(cudaSetDevice(e->device), "cudaSetDevice"));
+  sx::ArchiveArgs A = a->a;
+  A.clock = clock;
+  A.slot = sx_ring_slot_index(ring, clock);
+  M_TRY(sx_host_cuda_status(sx::launch_archive_integrate(A, e->stream), "archive launch"));
+  const uint32_t R = A.num_recall;
+  uint32_t *h = a->h_out;
+  M_TRY(sx_host_cuda_status(cudaMemcpyAsync(h, A.state, 4 * 5, cudaMemcpyDeviceToHost, e->stream),
+                            "archive readback"));
+  M_TRY(sx_host_cuda_status(
+      cudaMemcpyAsync(h + 8, A.selected, 4ull * R, cudaMemcpyDeviceToHost, e->stream),
+      "archive readback"));
+  M_TRY(sx_host_cuda_status(
+      cudaMemcpyAsync(h + 8 + (R + 1), A.sel_ts, 8ull * R, cudaMemcpyDeviceToHost, e->stream),
+      "archive readback"));
+  M_TRY(sx_engine_sync(e));
+  a->count = h[0];
+  const uint32_t k = R ? h[4] : 0;
+  const uint64_t *ts = reinterpret_cast<const uint64_t *>(h + 8 + (R + 1));
+  // clearRecall, then writeRecallKV's bookkeeping for every rank (memory_inject.zig:39-45);
+  // the model's ring keeps one bookkeeping layer, read by every layer
+  sx_ring_clear_recall(ring);
+  for (uint32_t r = 0; r < k; ++r) sx_ring_write_recall(ring, 0, r, ts[r]);
+  if (n_selected) *n_selected = k;
+  if (selected)
+    for (uint32_t r = 0; r < k; ++r) selected[r] = h[8 + r];
+  return SX_OK;
+}
+
+SX_API uint32_t sx_archive_count(const sx_archive *a) { return a ? a->count : 0; }
+
+SX_API sx_status sx_archive_entry(sx_archive *a, uint32_t i, float *vec, uint64_t *timestamp,
+                                  uint64_t *last_accessed, uint32_t *access_count,
+                                  float *salience) {
+  if (!a || i >= a->a.capacity) {
+    sx_host_set_error("archive_entry: index out of range");
+    return SX_ERR_INVALID;
+  }
+  sx_engine *e = a->m->e;
+  M_TRY(sx_host_cuda_status(cudaSetDevice(e->device), "cudaSetDevice"));
+  M_TRY(sx_host_cuda_status(cudaStreamSynchronize(e->stream), "archive sync"));
+  const sx::ArchiveArgs &A = a->a;
+  cudaError_t ce = cudaSuccess;
+  if (vec && ce == cudaSuccess)
+    ce = cudaMemcpy(vec, A.vectors + (size_t)i * A.dim, 4ull * A.dim, cudaMemcpyDeviceToHost);
+  if (timestamp && ce == cudaSuccess)
+    ce = cudaMemcpy(timestamp, A.timestamp + i, 8, cudaMemcpyDeviceToHost);
+  if (last_accessed && ce == cudaSuccess)
+    ce = cudaMemcpy(last_accessed, A.last_accessed + i, 8, cudaMemcpyDeviceToHost);
+  if (access_count && ce == cudaSuccess)
+    ce = cudaMemcpy(access_count, A.access_count + i, 4, cudaMemcpyDeviceToHost);
+  if (salience && ce == cudaSuccess)
+    ce = cudaMemcpy(salience, A.salience + i, 4, cudaMemcpyDeviceToHost);
+  return sx_host_cuda_status(ce, "archive entry readback");
+}
+
+}  // extern "C"

@@ -284,6 +284,11 @@ _SIGS = {
     "sx_model_vcache": (_P, [_P, _U32]),
     "sx_model_weight_bytes": (_U64, [_P]),
     "sx_model_kernels_per_token": (_U32, [_P, _I]),
+    "sx_archive_create": (_S, [_P, _U32, _P, C.POINTER(_P)]),
+    "sx_archive_destroy": (None, [_P]),
+    "sx_archive_integrate": (_S, [_P, _P, _U64, _P, _P]),
+    "sx_archive_count": (_U32, [_P]),
+    "sx_archive_entry": (_S, [_P, _U32, _P, _P, _P, _P, _P]),
 }
 
 
@@ -838,3 +843,39 @@ class Model:
 
     def kernels_per_token(self, want_logits: bool = True) -> int:
         return int(lib().sx_model_kernels_per_token(self.h, int(want_logits)))
+
+
+class Archive:
+    """The recall tier on the device (sx_archive_*): DiffArchive + integrateMemory over a model."""
+
+    def __init__(self, model: "Model", capacity: int):
+        h = C.c_void_p()
+        check(lib().sx_archive_create(model.h, capacity, None, C.byref(h)))
+        self.h = h
+        self.model = model
+        self.recall = model.cfg.num_recall
+        self.dim = model.cfg.hidden_size
+
+    def close(self):
+        if getattr(self, "h", None):
+            lib().sx_archive_destroy(self.h)
+            self.h = None
+
+    __del__ = _quiet_close
+
+    def integrate(self, ring: "Ring", clock: int) -> np.ndarray:
+        n = C.c_uint32()
+        sel = np.zeros(max(self.recall, 1), np.uint32)
+        check(lib().sx_archive_integrate(self.h, ring.h, clock, C.byref(n), sel.ctypes.data))
+        return sel[: n.value]
+
+    @property
+    def count(self) -> int:
+        return int(lib().sx_archive_count(self.h))
+
+    def entry(self, i: int):
+        v = np.zeros(self.dim, np.float32)
+        ts, la, ac, sal = C.c_uint64(), C.c_uint64(), C.c_uint32(), C.c_float()
+        check(lib().sx_archive_entry(self.h, i, v.ctypes.data, C.byref(ts), C.byref(la),
+                                     C.byref(ac), C.byref(sal)))
+        return v, ts.value, la.value, ac.value, sal.value

@@ -426,6 +426,41 @@ SX_API uint64_t sx_model_weight_bytes(sx_model *m);
 SX_API uint32_t sx_model_kernels_per_token(sx_model *m, int want_logits);
 
 /* ---------------------------------------------------------------------------------------
+ * The recall tier on the device: DiffArchive (memory.zig:19-151) and integrateMemory
+ * (memory_inject.zig:17-46) over the model's own KV caches (session 0).  The reference keeps
+ * its archive on the CPU and copies K/V through the CPU ring, which its GPU decode never reads;
+ * here the archive, its K/V rows and the recall slots all live in device memory.
+ * ------------------------------------------------------------------------------------- */
+/* memory.zig:5-7 SalienceConfig (defaults alpha 1, beta 0.5, gamma 1, lambda 1/2048) */
+typedef struct {
+  float alpha, beta, gamma, lambda;
+} sx_salience_config;
+typedef struct sx_archive sx_archive;
+/* DiffArchive.initWithKV (memory.zig:28-52) for model m: `capacity` unit vectors of
+ * hidden_size floats, their metadata and each entry's K/V rows of every layer in the model's
+ * cache format (1 <= capacity <= 16384; the reference uses 8192, main.zig:19).  cfg NULL: the
+ * defaults. */
+SX_API sx_status sx_archive_create(sx_model *m, uint32_t capacity, const sx_salience_config *cfg,
+                                   sx_archive **out);
+SX_API void sx_archive_destroy(sx_archive *a);
+/* integrateMemory (memory_inject.zig:17-46) after the token at `clock` was decoded with logits
+ * (its final normed state is the query): when the state's cosine similarity to the previous
+ * token's is below 0.98 it is appended with salience |delta| and the token's K/V rows; the
+ * min(num_recall, count) entries of highest score alpha cos + beta exp(-lambda dt) +
+ * gamma salience (memory.zig:113-151, the reference's selection order) are copied into recall
+ * slots anchors + window + rank of every layer's cache, and `ring`'s recall tier is rewritten
+ * with their timestamps (clearRecall + writeRecallKV).  Synchronous.  n_selected / selected
+ * (num_recall entries, archive indices in rank order) are optional. */
+SX_API sx_status sx_archive_integrate(sx_archive *a, sx_ring *ring, uint64_t clock,
+                                     uint32_t *n_selected, uint32_t *selected);
+SX_API uint32_t sx_archive_count(const sx_archive *a);
+/* entry i: unit vector (hidden_size floats), timestamp, last access, access count, salience
+ * (any pointer may be NULL) */
+SX_API sx_status sx_archive_entry(sx_archive *a, uint32_t i, float *vec, uint64_t *timestamp,
+                                  uint64_t *last_accessed, uint32_t *access_count,
+                                  float *salience);
+
+/* ---------------------------------------------------------------------------------------
  * Tensor-parallel decode (new: the reference runs on one GPU).  One engine, communicator and
  * model per GPU.  Column-parallel q (num_q_heads / N heads), k / v (num_kv_heads / N and
  * num_global_kv_heads / N heads: the GQA ratio is preserved), gate / up (intermediate / N

@@ -56,6 +56,15 @@ _SIGS = {
     "orc_gemv_bf16": (None, [_P, _P, _P, _SZ, _SZ]),
     "orc_gemv_bf16_mt": (None, [_P, _P, _P, _SZ, _SZ, _I]),
     "orc_quiescence_gate": (_I, [_P, _P, _U32, _F, _P]),
+    "orc_archive_create": (_P, [_P, _U32, _F, _F, _F, _F]),
+    "orc_archive_destroy": (None, [_P]),
+    "orc_archive_integrate": (_U32, [_P, _U64, _P]),
+    "orc_archive_count": (_U32, [_P]),
+    "orc_archive_entry": (None, [_P, _U32, _P, _P, _P, _P, _P]),
+    "orc_archive_scan": (_U32, [_P, _P, _U64, _P, _U32]),
+    "orc_archive_create_dim": (_P, [_U32, _U32, _F, _F, _F, _F]),
+    "orc_archive_append": (None, [_P, _U64, _F, _P]),
+    "orc_archive_write_head": (_U32, [_P]),
     "orc_model_gate_stats": (None, [_P, _P, _P]),
     "orc_gate_up_geglu_q8": (None, [_P, _P, _P, _P, _SZ, _SZ, _I]),
     "orc_rmsnorm": (None, [_P, _P, _P, _SZ, _F]),
@@ -422,3 +431,54 @@ class Model:
         n = self.kv_dim(layer) * (self.cfg["num_anchors"] + self.cfg["window_size"] +
                                   self.cfg["num_recall"])
         return np.ctypeslib.as_array(lib().orc_model_vcache(self.h, layer), shape=(n,))
+
+
+class Archive:
+    """memory.zig DiffArchive with the recall injection of memory_inject.zig, on a checker
+    model (its caches, ring and final normed state)."""
+
+    def __init__(self, model: "Model | None", capacity: int, alpha=1.0, beta=0.5, gamma=1.0,
+                 lam=1.0 / 2048.0, dim: int | None = None):
+        self.model = model  # keeps the model alive
+        if model is None:  # DiffArchive.init: vectors and metadata only
+            self.h = lib().orc_archive_create_dim(dim, capacity, alpha, beta, gamma, lam)
+            self.dim, self.recall = dim, 0
+        else:
+            self.h = lib().orc_archive_create(model.h, capacity, alpha, beta, gamma, lam)
+            self.dim = model.cfg["hidden_size"]
+            self.recall = model.cfg["num_recall"]
+
+    def append(self, timestamp, salience, vector):
+        lib().orc_archive_append(self.h, timestamp, salience,
+                                 _p(np.ascontiguousarray(vector, np.float32)))
+
+    @property
+    def write_head(self) -> int:
+        return int(lib().orc_archive_write_head(self.h))
+
+    def __del__(self):
+        if getattr(self, "h", None):
+            lib().orc_archive_destroy(self.h)
+            self.h = None
+
+    def integrate(self, clock) -> np.ndarray:
+        sel = np.zeros(max(self.recall, 1), np.uint32)
+        n = lib().orc_archive_integrate(self.h, clock, _p(sel))
+        return sel[:n]
+
+    @property
+    def count(self) -> int:
+        return int(lib().orc_archive_count(self.h))
+
+    def entry(self, i):
+        v = np.zeros(self.dim, np.float32)
+        ts, la, ac, sal = C.c_uint64(), C.c_uint64(), C.c_uint32(), C.c_float()
+        lib().orc_archive_entry(self.h, i, _p(v), C.byref(ts), C.byref(la), C.byref(ac),
+                                C.byref(sal))
+        return v, ts.value, la.value, ac.value, sal.value
+
+    def scan(self, query, now, top_k) -> np.ndarray:
+        out = np.zeros(max(top_k, 1), np.uint32)
+        n = lib().orc_archive_scan(self.h, _p(np.ascontiguousarray(query, np.float32)), now,
+                                   _p(out), top_k)
+        return out[:n]

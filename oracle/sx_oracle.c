@@ -1024,3 +1024,208 @@ uint32_t orc_model_forward(orc_model *m, const float *x_in, uint64_t clock, int 
   if (logits_out) memcpy(logits_out, m->logits, sizeof(float) * c->vocab_size);
   return orc_argmax(m->logits, c->vocab_size);
 }
+
+/* ------------------------------------------------------------------------- */
+/* memory.zig:19-151 DiffArchive, diff.zig:9-57, memory_inject.zig:17-46 */
+struct orc_archive {
+  orc_model *m;
+  uint32_t dim, capacity, count, write_head, max_kv;
+  float alpha, beta, gamma, lambda;
+  float *vectors;            /* [capacity][dim] unit-normalised */
+  uint64_t *timestamp, *last_accessed;
+  uint32_t *access_count;
+  float *salience;
+  float *kv;                 /* [capacity][layers][2][max_kv] */
+  float *scores;             /* scan scratch */
+  uint32_t *indices;
+  float *prev_normed;        /* scratch.prev_normed_x */
+};
+
+orc_archive *orc_archive_create(orc_model *m, uint32_t capacity, float alpha, float beta,
+                                float gamma, float lambda) {
+  orc_archive *a = (orc_archive *)calloc(1, sizeof(orc_archive));
+  a->m = m;
+  a->dim = m->c.hidden_size;
+  a->capacity = capacity;
+  a->alpha = alpha;
+  a->beta = beta;
+  a->gamma = gamma;
+  a->lambda = lambda;
+  for (uint32_t l = 0; l < m->c.num_layers; ++l)
+    if (m->layers[l].kv_dim > a->max_kv) a->max_kv = m->layers[l].kv_dim;
+  a->vectors = (float *)calloc((size_t)capacity * a->dim, sizeof(float));
+  a->timestamp = (uint64_t *)calloc(capacity, sizeof(uint64_t));
+  a->last_accessed = (uint64_t *)calloc(capacity, sizeof(uint64_t));
+  a->access_count = (uint32_t *)calloc(capacity, sizeof(uint32_t));
+  a->salience = (float *)calloc(capacity, sizeof(float));
+  a->kv = (float *)calloc((size_t)capacity * m->c.num_layers * 2 * a->max_kv, sizeof(float));
+  a->scores = (float *)calloc(capacity, sizeof(float));
+  a->indices = (uint32_t *)calloc(capacity, sizeof(uint32_t));
+  a->prev_normed = (float *)calloc(a->dim, sizeof(float));
+  return a;
+}
+
+orc_archive *orc_archive_create_dim(uint32_t dim, uint32_t capacity, float alpha, float beta,
+                                    float gamma, float lambda) {
+  orc_archive *a = (orc_archive *)calloc(1, sizeof(orc_archive));
+  a->dim = dim;
+  a->capacity = capacity;
+  a->alpha = alpha;
+  a->beta = beta;
+  a->gamma = gamma;
+  a->lambda = lambda;
+  a->vectors = (float *)calloc((size_t)capacity * dim, sizeof(float));
+  a->timestamp = (uint64_t *)calloc(capacity, sizeof(uint64_t));
+  a->last_accessed = (uint64_t *)calloc(capacity, sizeof(uint64_t));
+  a->access_count = (uint32_t *)calloc(capacity, sizeof(uint32_t));
+  a->salience = (float *)calloc(capacity, sizeof(float));
+  a->scores = (float *)calloc(capacity, sizeof(float));
+  a->indices = (uint32_t *)calloc(capacity, sizeof(uint32_t));
+  a->prev_normed = (float *)calloc(dim, sizeof(float));
+  return a;
+}
+
+void orc_archive_append(orc_archive *a, uint64_t timestamp, float salience, const float *vector) {
+  float ss = 0.0f;
+  for (uint32_t i = 0; i < a->dim; ++i) ss += vector[i] * vector[i];
+  float inv = ss > 1e-12f ? 1.0f / sqrtf(ss) : 0.0f;
+  uint32_t idx = a->write_head;
+  for (uint32_t i = 0; i < a->dim; ++i) a->vectors[(size_t)idx * a->dim + i] = vector[i] * inv;
+  a->timestamp[idx] = timestamp;
+  a->last_accessed[idx] = timestamp;
+  a->access_count[idx] = 0;
+  a->salience[idx] = salience;
+  a->write_head = (idx + 1) % a->capacity;
+  if (a->count < a->capacity) a->count += 1;
+}
+
+uint32_t orc_archive_write_head(const orc_archive *a) { return a->write_head; }
+
+void orc_archive_destroy(orc_archive *a) {
+  if (!a) return;
+  free(a->vectors); free(a->timestamp); free(a->last_accessed); free(a->access_count);
+  free(a->salience); free(a->kv); free(a->scores); free(a->indices); free(a->prev_normed);
+  free(a);
+}
+
+uint32_t orc_archive_count(const orc_archive *a) { return a->count; }
+
+void orc_archive_entry(const orc_archive *a, uint32_t i, float *vec, uint64_t *timestamp,
+                       uint64_t *last_accessed, uint32_t *access_count, float *salience) {
+  if (vec) memcpy(vec, a->vectors + (size_t)i * a->dim, sizeof(float) * a->dim);
+  if (timestamp) *timestamp = a->timestamp[i];
+  if (last_accessed) *last_accessed = a->last_accessed[i];
+  if (access_count) *access_count = a->access_count[i];
+  if (salience) *salience = a->salience[i];
+}
+
+/* memory.zig:145-151 score */
+static float orc_archive_score(const orc_archive *a, const float *query, uint64_t now,
+                               uint32_t i) {
+  const float *row = a->vectors + (size_t)i * a->dim;
+  float dot = 0.0f;
+  for (uint32_t k = 0; k < a->dim; ++k) dot += query[k] * row[k];
+  uint64_t dt = now > a->timestamp[i] ? now - a->timestamp[i] : 0;  /* now -| timestamp */
+  float recency = expf(-a->lambda * (float)dt);
+  return a->alpha * dot + a->beta * recency + a->gamma * a->salience[i];
+}
+
+/* memory.zig:113-143 scan: scores, then k rounds of selection with swaps (strict > keeps the
+ * first position of a maximum), then the selected entries' access metadata */
+uint32_t orc_archive_scan(orc_archive *a, const float *query, uint64_t now, uint32_t *out,
+                          uint32_t top_k) {
+  uint32_t n = a->count;
+  if (n == 0) return 0;
+  for (uint32_t i = 0; i < n; ++i) {
+    a->scores[i] = orc_archive_score(a, query, now, i);
+    a->indices[i] = i;
+  }
+  uint32_t k = top_k < n ? top_k : n;
+  for (uint32_t slot = 0; slot < k; ++slot) {
+    uint32_t best = slot;
+    for (uint32_t j = slot + 1; j < n; ++j)
+      if (a->scores[j] > a->scores[best]) best = j;
+    float ts = a->scores[slot];
+    a->scores[slot] = a->scores[best];
+    a->scores[best] = ts;
+    uint32_t ti = a->indices[slot];
+    a->indices[slot] = a->indices[best];
+    a->indices[best] = ti;
+    out[slot] = a->indices[slot];
+  }
+  for (uint32_t r = 0; r < k; ++r) {
+    a->last_accessed[out[r]] = now;
+    a->access_count[out[r]] += 1;
+  }
+  return k;
+}
+
+uint32_t orc_archive_integrate(orc_archive *a, uint64_t clock, uint32_t *selected) {
+  orc_model *m = a->m;
+  const uint32_t H = a->dim, L = m->c.num_layers;
+  const float *cur = m->normed, *prev = a->prev_normed;
+  /* diff.zig:9-35 computeDelta (threshold 0): norm = sqrt(sum (cur - prev)^2) */
+  float sum_sq = 0.0f;
+  for (uint32_t i = 0; i < H; ++i) {
+    float d = cur[i] - prev[i];
+    sum_sq += d * d;
+  }
+  float delta_norm = sqrtf(sum_sq);
+  /* diff.zig:37-52 cosineSimilarity(prev, cur) */
+  float dot = 0.0f, na = 0.0f, nb = 0.0f;
+  for (uint32_t i = 0; i < H; ++i) {
+    dot += prev[i] * cur[i];
+    na += prev[i] * prev[i];
+    nb += cur[i] * cur[i];
+  }
+  float denom = sqrtf(na) * sqrtf(nb);
+  float sim = denom < 1e-12f ? 0.0f : dot / denom;
+  if (sim < 0.98f) {  /* LANDMARK_SIMILARITY_THRESHOLD */
+    uint32_t idx = a->write_head;
+    /* memory.zig:91-111 appendWithMeta: unit-normalised copy, metadata */
+    float ss = 0.0f;
+    for (uint32_t i = 0; i < H; ++i) ss += cur[i] * cur[i];
+    float inv = ss > 1e-12f ? 1.0f / sqrtf(ss) : 0.0f;
+    for (uint32_t i = 0; i < H; ++i) a->vectors[(size_t)idx * H + i] = cur[i] * inv;
+    a->timestamp[idx] = clock;
+    a->last_accessed[idx] = clock;
+    a->access_count[idx] = 0;
+    a->salience[idx] = delta_norm;
+    a->write_head = (idx + 1) % a->capacity;
+    if (a->count < a->capacity) a->count += 1;
+    /* memory.zig:70-79 copyKVFromRing: the token's K/V rows of every layer */
+    uint32_t slot = orc_ring_slot_index(m->ring, clock);
+    for (uint32_t l = 0; l < L; ++l) {
+      orc_layer *Ly = &m->layers[l];
+      float *dst = a->kv + (((size_t)idx * L + l) * 2) * a->max_kv;
+      memset(dst, 0, sizeof(float) * 2 * a->max_kv);
+      memcpy(dst, Ly->k_cache + (size_t)slot * Ly->kv_dim, sizeof(float) * Ly->kv_dim);
+      memcpy(dst + a->max_kv, Ly->v_cache + (size_t)slot * Ly->kv_dim, sizeof(float) * Ly->kv_dim);
+    }
+  }
+  memcpy(a->prev_normed, cur, sizeof(float) * H);
+  uint32_t recall = m->c.num_recall;
+  if (recall == 0) {
+    orc_ring_clear_recall(m->ring);
+    return 0;
+  }
+  uint32_t k = orc_archive_scan(a, cur, clock, selected, recall);
+  orc_ring_clear_recall(m->ring);
+  /* memory.zig:81-89 copyKVToRing -> ring_buffer.zig writeRecallKV (slot recallStart + rank,
+   * clock = the entry's timestamp) */
+  uint32_t total = m->c.num_anchors + m->c.window_size + m->c.num_recall;
+  for (uint32_t rank = 0; rank < k; ++rank) {
+    uint32_t mi = selected[rank];
+    uint32_t slot = m->c.num_anchors + m->c.window_size + rank;
+    for (uint32_t l = 0; l < L; ++l) {
+      orc_layer *Ly = &m->layers[l];
+      const float *src = a->kv + (((size_t)mi * L + l) * 2) * a->max_kv;
+      memcpy(Ly->k_cache + (size_t)slot * Ly->kv_dim, src, sizeof(float) * Ly->kv_dim);
+      memcpy(Ly->v_cache + (size_t)slot * Ly->kv_dim, src + a->max_kv, sizeof(float) * Ly->kv_dim);
+    }
+    /* the model's ring keeps one bookkeeping layer: every layer attends over its slot list */
+    orc_ring_write_recall(m->ring, 0, rank, a->timestamp[mi]);
+  }
+  (void)total;
+  return k;
+}

@@ -139,6 +139,32 @@ float *orc_model_kcache(orc_model *m, uint32_t layer);
 float *orc_model_vcache(orc_model *m, uint32_t layer);
 uint32_t orc_model_kv_dim(orc_model *m, uint32_t layer);
 
+/* ---- memory.zig DiffArchive + diff.zig + memory_inject.zig integrateMemory, on a model's
+ * ring and caches (layer K/V rows of kv_dim values, f32 or bf16-rounded like the model) ---- */
+typedef struct orc_archive orc_archive;
+/* initWithKV (memory.zig:28-52); SalienceConfig defaults alpha 1, beta 0.5, gamma 1,
+ * lambda 1/2048 (memory.zig:5-7) */
+orc_archive *orc_archive_create(orc_model *m, uint32_t capacity, float alpha, float beta,
+                                float gamma, float lambda);
+void orc_archive_destroy(orc_archive *a);
+/* integrateMemory (memory_inject.zig:17-46) after the model's last forward (with logits, whose
+ * final normed state it reads) at `clock`; returns the number of recalled entries and their
+ * archive indices in rank order */
+uint32_t orc_archive_integrate(orc_archive *a, uint64_t clock, uint32_t *selected);
+/* DiffArchive.init (memory.zig:24-26): vectors and metadata only, no model, no K/V */
+orc_archive *orc_archive_create_dim(uint32_t dim, uint32_t capacity, float alpha, float beta,
+                                    float gamma, float lambda);
+/* appendWithMeta (memory.zig:91-111) */
+void orc_archive_append(orc_archive *a, uint64_t timestamp, float salience, const float *vector);
+uint32_t orc_archive_write_head(const orc_archive *a);
+uint32_t orc_archive_count(const orc_archive *a);
+/* entry i: unit vector (dim floats), timestamp, last access, access count, salience */
+void orc_archive_entry(const orc_archive *a, uint32_t i, float *vec, uint64_t *timestamp,
+                       uint64_t *last_accessed, uint32_t *access_count, float *salience);
+/* scan alone (memory.zig:113-143) with an explicit query: top_k indices in rank order */
+uint32_t orc_archive_scan(orc_archive *a, const float *query, uint64_t now, uint32_t *out,
+                          uint32_t top_k);
+
 #ifdef __cplusplus
 }
 #endif

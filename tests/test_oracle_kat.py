@@ -188,3 +188,28 @@ def test_rope_partial_rotates_prefix_only():
     n0 = v[:half] ** 2 + v[half:rot] ** 2
     n1 = out[:half] ** 2 + out[half:rot] ** 2
     assert np.allclose(n0, n1, rtol=1e-5)
+
+
+# ---- memory.zig:153-175: the archive's own tests, on the checker's restatement
+def test_archive_recall_ranks_cosine_match_above_recency():
+    a = orc.Archive(None, 8, dim=4)
+    a.append(0, 0.5, [1, 0, 0, 0])
+    a.append(1, 0.5, [0, 1, 0, 0])
+    idx = a.scan(np.array([1, 0, 0, 0], np.float32), 2, 2)
+    assert len(idx) == 2 and idx[0] == 0
+
+
+def test_archive_wraps_and_caps_count():
+    a = orc.Archive(None, 3, dim=2)
+    for t, v in enumerate(([1, 0], [0, 1], [1, 1], [-1, 0])):
+        a.append(t, 0.0, v)
+    assert a.count == 3 and a.write_head == 1
+
+
+def test_archive_scan_is_selection_with_swaps():
+    # equal scores resolve by position after the swaps of memory.zig:123-134, not by index:
+    # scores [1, 1, 5] (salience only, zero vectors) select 2, then 1, then 0
+    a = orc.Archive(None, 4, alpha=0.0, beta=0.0, gamma=1.0, dim=2)
+    for sal in (1.0, 1.0, 5.0):
+        a.append(0, sal, [0, 0])
+    assert list(a.scan(np.zeros(2, np.float32), 0, 3)) == [2, 1, 0]
