@@ -142,7 +142,6 @@ sx_status do_gemv(sx_engine *e, cudaStream_t s, int qt, bool geglu, const void *
                   const void *w1, const float *x, float *y, uint32_t m, uint32_t k,
                   uint32_t batch, const uint32_t *gate = nullptr) {
   if (qt == 0) {  // mode none: bf16 weights (gemv_bf16.wgsl)
-    SX_CHECK_ARG(gate == nullptr, "gemv bf16: indirect dispatch is not built for mode none");
     SX_CHECK_ARG(m > 0 && k > 0 && k % 8 == 0 && batch >= 1 && batch <= 8,
                  "gemv bf16: need m > 0, k a multiple of 8 and batch 1..8 (m=%u k=%u batch=%u)",
                  m, k, batch);
@@ -150,7 +149,7 @@ sx_status do_gemv(sx_engine *e, cudaStream_t s, int qt, bool geglu, const void *
     SX_CHECK_ARG(((uintptr_t)w0 | (uintptr_t)(geglu ? w1 : w0) | (uintptr_t)x) % 16 == 0,
                  "gemv bf16: weights and x must be 16-byte aligned");
     return cuda_status(sx::launch_gemv_bf16(geglu, (const uint16_t *)w0, (const uint16_t *)w1, x,
-                                            y, m, k, batch, e->num_sms, s),
+                                            y, m, k, batch, e->num_sms, s, gate),
                        "gemv bf16 launch");
   }
   SX_CHECK_ARG(qt == 4 || qt == 8, "gemv: unsupported quant mode");

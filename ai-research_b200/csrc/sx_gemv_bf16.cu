@@ -34,9 +34,11 @@ __global__ void __launch_bounds__(kBfThreads) gemv_bf16_kernel(const uint16_t *_
                                                                const float *__restrict__ x,
                                                                float *__restrict__ y, uint32_t m,
                                                                uint32_t k, uint32_t ldx,
-                                                               uint32_t ldy) {
+                                                               uint32_t ldy,
+                                                               const uint32_t *gate) {
   pdl_launch_dependents();
   pdl_wait();
+  if (gate_closed(gate)) return;  // recorded behind a closed dispatch record
   const uint32_t lane = threadIdx.x & 31;
   const uint32_t nwarps = gridDim.x * (kBfThreads / 32);
   const uint32_t k8 = k / 8;  // 16-byte pieces per row
@@ -94,10 +96,11 @@ __global__ void __launch_bounds__(kBfThreads) gemv_bf16_kernel(const uint16_t *_
 
 template <int NMAT, int B>
 cudaError_t launch_bf(const uint16_t *w0, const uint16_t *w1, const float *x, float *y, uint32_t m,
-                      uint32_t k, uint32_t ldx, uint32_t ldy, int num_sms, cudaStream_t s) {
-  const uint32_t warps = (m + 0u);
+                      uint32_t k, uint32_t ldx, uint32_t ldy, int num_sms, cudaStream_t s,
+                      const uint32_t *gate) {
+  // one warp per row, at most eight 256-thread CTAs per SM
   uint32_t grid = num_sms * 8;
-  const uint32_t need = (warps + kBfThreads / 32 - 1) / (kBfThreads / 32);
+  const uint32_t need = (m + kBfThreads / 32 - 1) / (kBfThreads / 32);
   if (need < grid) grid = need;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
@@ -108,21 +111,22 @@ cudaError_t launch_bf(const uint16_t *w0, const uint16_t *w1, const float *x, fl
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, gemv_bf16_kernel<NMAT, B>, w0, w1, x, y, m, k, ldx, ldy);
+  return cudaLaunchKernelEx(&cfg, gemv_bf16_kernel<NMAT, B>, w0, w1, x, y, m, k, ldx, ldy, gate);
 }
 
 template <int NMAT>
 cudaError_t launch_bf_b(const uint16_t *w0, const uint16_t *w1, const float *x, float *y,
-                        uint32_t m, uint32_t k, uint32_t batch, int num_sms, cudaStream_t s) {
+                        uint32_t m, uint32_t k, uint32_t batch, int num_sms, cudaStream_t s,
+                        const uint32_t *gate) {
   switch (batch) {
-    case 1: return launch_bf<NMAT, 1>(w0, w1, x, y, m, k, k, m, num_sms, s);
-    case 2: return launch_bf<NMAT, 2>(w0, w1, x, y, m, k, k, m, num_sms, s);
-    case 3: return launch_bf<NMAT, 3>(w0, w1, x, y, m, k, k, m, num_sms, s);
-    case 4: return launch_bf<NMAT, 4>(w0, w1, x, y, m, k, k, m, num_sms, s);
-    case 5: return launch_bf<NMAT, 5>(w0, w1, x, y, m, k, k, m, num_sms, s);
-    case 6: return launch_bf<NMAT, 6>(w0, w1, x, y, m, k, k, m, num_sms, s);
-    case 7: return launch_bf<NMAT, 7>(w0, w1, x, y, m, k, k, m, num_sms, s);
-    case 8: return launch_bf<NMAT, 8>(w0, w1, x, y, m, k, k, m, num_sms, s);
+    case 1: return launch_bf<NMAT, 1>(w0, w1, x, y, m, k, k, m, num_sms, s, gate);
+    case 2: return launch_bf<NMAT, 2>(w0, w1, x, y, m, k, k, m, num_sms, s, gate);
+    case 3: return launch_bf<NMAT, 3>(w0, w1, x, y, m, k, k, m, num_sms, s, gate);
+    case 4: return launch_bf<NMAT, 4>(w0, w1, x, y, m, k, k, m, num_sms, s, gate);
+    case 5: return launch_bf<NMAT, 5>(w0, w1, x, y, m, k, k, m, num_sms, s, gate);
+    case 6: return launch_bf<NMAT, 6>(w0, w1, x, y, m, k, k, m, num_sms, s, gate);
+    case 7: return launch_bf<NMAT, 7>(w0, w1, x, y, m, k, k, m, num_sms, s, gate);
+    case 8: return launch_bf<NMAT, 8>(w0, w1, x, y, m, k, k, m, num_sms, s, gate);
     default: return cudaErrorInvalidValue;
   }
 }
@@ -139,10 +143,10 @@ __global__ void synth_bf16_kernel(uint16_t *dst, uint64_t n, uint64_t seed, uint
 
 cudaError_t launch_gemv_bf16(bool geglu, const uint16_t *w0, const uint16_t *w1, const float *x,
                              float *y, uint32_t m, uint32_t k, uint32_t batch, int num_sms,
-                             cudaStream_t s) {
+                             cudaStream_t s, const uint32_t *gate) {
   if (m == 0 || k % 8 != 0 || batch < 1 || batch > 8) return cudaErrorInvalidValue;
-  return geglu ? launch_bf_b<2>(w0, w1, x, y, m, k, batch, num_sms, s)
-               : launch_bf_b<1>(w0, w0, x, y, m, k, batch, num_sms, s);
+  return geglu ? launch_bf_b<2>(w0, w1, x, y, m, k, batch, num_sms, s, gate)
+               : launch_bf_b<1>(w0, w0, x, y, m, k, batch, num_sms, s, gate);
 }
 
 cudaError_t launch_synth_bf16(uint16_t *dst, uint64_t n, uint64_t seed, uint64_t stream_id,

@@ -72,7 +72,7 @@ constexpr uint32_t kMaxGemvTiles = 262144;
 // row-major bf16 W (k % 8 == 0, 16-byte aligned rows and x), or the GeGLU of two matrices
 cudaError_t launch_gemv_bf16(bool geglu, const uint16_t *w0, const uint16_t *w1, const float *x,
                              float *y, uint32_t m, uint32_t k, uint32_t batch, int num_sms,
-                             cudaStream_t s);
+                             cudaStream_t s, const uint32_t *gate = nullptr);
 // synthetic bf16(0.02 N(0,1)) weights, element i of (seed, stream)
 cudaError_t launch_synth_bf16(uint16_t *dst, uint64_t n, uint64_t seed, uint64_t stream_id,
                               cudaStream_t s);

@@ -57,10 +57,13 @@ def parse():
                          "the weights through a shared-memory ring (one GPU); persistent: one "
                          "cooperative launch per token with grid barriers; fused: 5 kernels "
                          "per layer chained with programmatic dependent launch")
-    ap.add_argument("--case", choices=["geglu", "q4_head", "attn", "prefill", "sessions"],
+    ap.add_argument("--case", choices=["geglu", "q4_head", "attn", "prefill", "sessions", "c1",
+                                       "c3"],
                     help="profiling case: launch one kernel of the step standalone "
                          "(--launches times) on synthetic data and exit; prints no JSON line")
     ap.add_argument("--launches", type=int, default=3)
+    ap.add_argument("--rows", type=int, default=15360,
+                    help="--case geglu: gate/up rows (15360 / N is one tensor-parallel rank's)")
     ap.add_argument("--allreduce", choices=["peer", "nccl"], default="peer",
                     help="tensor parallel (N > 1): the one-shot peer all-reduce (NCCL when its "
                          "workspaces cannot be mapped) or NCCL")
@@ -148,8 +151,11 @@ def run_sessions(eng, args, rank=0):
 
 def run_case(args):
     """Small standalone workloads for ncu captures of the step's kernels:
-    geglu   -- the fused gate+up GeGLU GEMV of one 12B layer (2 x 15360 x 3840 Q4_0, 73.8 MB)
+    geglu   -- the fused gate+up GeGLU GEMV of one 12B layer (2 x rows x 3840 Q4_0; rows 15360
+               is 73.8 MB, one GPU; 15360 / N is a tensor-parallel rank's share)
     q4_head -- a 262144 x 3840 Q4_0 GEMV (629 MB), the steady-state streaming case
+    c1      -- BASELINE config 1: the 6144 x 1536 Q4_0 GEMV
+    c3      -- BASELINE config 3: the fused attention over 256 independent 640-slot rings
     attn    -- one 12B-width layer token (16 q / 8 kv heads x 256, 640 live slots), whose
                second kernel is the fused attention
     prefill -- the tcgen05 Q4_0 GEMM on config 5's projection shapes (TFLOP/s per shape)
@@ -213,8 +219,24 @@ def run_case(args):
             s = ring.activate_slot(0, c)
             model.forward_token(sx.synth_embed_row(3840, 5, SEED), c, s,
                                 ring.get_active_slots(0, c), want_logits=False)
+    elif args.case == "c3":
+        # 256 independent 640-slot rings in one launch of the fused kernel
+        n, G, D, total = 256, 8, 256, 640
+        stride = (G + 2) * D
+        qkv = torch.randn(n * stride, device="cuda", generator=g)
+        kc = torch.randn(n * total * D, device="cuda", generator=g).to(torch.bfloat16)
+        vc = torch.randn(n * total * D, device="cuda", generator=g).to(torch.bfloat16)
+        ones = torch.ones(D, device="cuda")
+        slots = torch.arange(total, dtype=torch.int32, device="cuda").repeat(n)
+        steps = torch.tensor([[50000 + i, 40 + i % 500, total, 0] for i in range(n)],
+                             dtype=torch.int32, device="cuda")
+        out = torch.empty(n * G * D, device="cuda")
+        p0 = qkv.data_ptr()
+        for _ in range(args.launches):
+            eng.qkv_rope_attn(p0, p0 + 4 * G * D, p0 + 4 * (G + 1) * D, ones, ones, kc, vc, slots,
+                              steps, out, G, 1, D, 64, 0, 1e6, 1e-6, 1.0 / 16, total, n, stride)
     else:
-        m, k = (15360, 3840) if args.case == "geglu" else (262144, 3840)
+        m, k = {"geglu": (args.rows, 3840), "c1": (6144, 1536)}.get(args.case, (262144, 3840))
         w0, w1 = packed(m, k), (packed(m, k) if args.case == "geglu" else None)
         x = torch.randn(k, device="cuda", generator=g)
         y = torch.empty(m, device="cuda")
