@@ -81,7 +81,7 @@ def c5_config(**kw):
     return sx.model_config(**d)
 
 
-def run_sessions(eng, args, rank=0):
+def run_sessions(eng, args, rank=0, print_lines=True):
     import torch
     import sx
 
@@ -109,9 +109,10 @@ def run_sessions(eng, args, rank=0):
     T = int(lens.sum())
     ms_p = ev[0].elapsed_time(ev[1])
     flops = T * cfg.num_layers * 2.0 * H * (cfg.num_q_heads * 256 + 2 * 256 + 8 * 256 + 3 * 6144)
-    print(json.dumps({"case": "c5_prefill", "sessions": 8, "tokens": T, "ms": ms_p,
-                      "tok_s": T / (ms_p / 1e3), "gemm_tflops": flops / (ms_p / 1e3) / 1e12}),
-          flush=True)
+    if print_lines:
+        print(json.dumps({"case": "c5_prefill", "sessions": 8, "tokens": T, "ms": ms_p,
+                          "tok_s": T / (ms_p / 1e3), "gemm_tflops": flops / (ms_p / 1e3) / 1e12}),
+              flush=True)
     clocks = [int(n) for n in lens]
     tokens = [int(t) for t in toks]
     steps = 128
@@ -142,11 +143,14 @@ def run_sessions(eng, args, rank=0):
     ev[3].record(stream)
     eng.sync()
     ms_dev = ev[2].elapsed_time(ev[3]) / reps
-    print(json.dumps({"case": "c5_decode_batch8", "sessions": 8, "steps": steps,
-                      "e2e_ms_per_step": ms_d, "e2e_tok_s": 8 / (ms_d / 1e3),
-                      "device_ms_per_step": ms_dev, "device_tok_s": 8 / (ms_dev / 1e3)}),
-          flush=True)
+    if print_lines:
+        print(json.dumps({"case": "c5_decode_batch8", "sessions": 8, "steps": steps,
+                          "e2e_ms_per_step": ms_d, "e2e_tok_s": 8 / (ms_d / 1e3),
+                          "device_ms_per_step": ms_dev, "device_tok_s": 8 / (ms_dev / 1e3)}),
+              flush=True)
     model.close()
+    return {"prompt_tokens": T, "prefill_ms": ms_p, "decode_e2e_ms_per_step": ms_d,
+            "decode_device_ms_per_step": ms_dev, "steps": steps}
 
 
 def run_case(args):
@@ -165,7 +169,9 @@ def run_case(args):
     import torch
     import sx
 
-    eng = sx.Engine(0)
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    eng = sx.Engine(local)
     g = torch.Generator(device="cuda").manual_seed(SEED)
 
     def packed(m, k):
@@ -201,7 +207,36 @@ def run_case(args):
         eng.close()
         return
     if args.case == "sessions":
-        run_sessions(eng, args)
+        world = int(os.environ.get("WORLD_SIZE", "1"))
+        if world == 1:
+            run_sessions(eng, args)
+        else:
+            # BASELINE config 5 across the node: rank r prefills and decodes sessions
+            # 8r .. 8r + 7 of the 64 seeded prompts on its own GPU (its own weight copy, no
+            # collective on the data path); the process group only gathers the timings
+            import torch.distributed as dist
+            from datetime import timedelta
+
+            rank = int(os.environ.get("RANK", "0"))
+            dist.init_process_group("gloo", timeout=timedelta(seconds=300))
+            r = run_sessions(eng, args, rank=rank, print_lines=False)
+            allr = [None] * world
+            dist.all_gather_object(allr, r)
+            if rank == 0:
+                T = sum(x["prompt_tokens"] for x in allr)
+                pm = max(x["prefill_ms"] for x in allr)
+                dm = max(x["decode_e2e_ms_per_step"] for x in allr)
+                dd = max(x["decode_device_ms_per_step"] for x in allr)
+                print(json.dumps({"case": "c5_sessions_multi_gpu", "n_gpus": world,
+                                  "sessions": 8 * world, "prompt_tokens": T,
+                                  "prefill_ms_max_over_ranks": pm,
+                                  "prefill_tok_s": T / (pm / 1e3),
+                                  "decode_tok_s_e2e": 8 * world / (dm / 1e3),
+                                  "decode_tok_s_device": 8 * world / (dd / 1e3),
+                                  "decode_steps": allr[0]["steps"], "per_rank": allr}),
+                      flush=True)
+            dist.barrier()
+            dist.destroy_process_group()
         eng.close()
         return
     if args.case == "attn":
