@@ -778,7 +778,7 @@ def main():
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True,
-        "scaling": "strong" if world > 1 else "weak", "vs_baseline": None, "dtype": "f32 (Q4_0/Q8_0 weights)",
+        "scaling": "strong" if world > 1 else "weak", "vs_baseline": None, "dtype": "f32 accumulate (Q4_0/Q8_0 weights exact; x enters the MMA as a bf16 hi+lo pair, 16 significant bits)",
         "data": "synthetic (seeded random-init 12B-shaped weights, BASELINE distributions)",
         "config": {
             "workload": f"c4: 12B-shape Q4_0 greedy decode, batch 1, {args.layers} layers, H 3840, "
