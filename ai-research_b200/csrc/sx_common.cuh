@@ -272,6 +272,27 @@ SX_DEV void cp_async16_if(uint32_t dst, const void *src, bool p) {
       "l"(src), "r"((uint32_t)p)
       : "memory");
 }
+// L2 eviction priority for data read once per token (weights, past K/V rows): such lines are
+// replaced first, so the streams do not push activations, norm gains and code out of L2.
+SX_DEV uint64_t l2_evict_first_policy() {
+  uint64_t pol;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;\n" : "=l"(pol));
+  return pol;
+}
+SX_DEV void cp_async16_if_ef(uint32_t dst, const void *src, bool p, uint64_t pol) {
+  asm volatile(
+      "{\n .reg .pred q;\n setp.ne.b32 q, %2, 0;\n"
+      " @q cp.async.cg.shared.global.L2::cache_hint [%0], [%1], 16, %3;\n}\n" ::"r"(dst),
+      "l"(src), "r"((uint32_t)p), "l"(pol)
+      : "memory");
+}
+SX_DEV void bulk_g2s_ef(uint32_t dst, const void *src, uint32_t bytes, uint32_t bar, uint64_t pol) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, "
+      "[%3], %4;\n" ::"r"(dst),
+      "l"(src), "r"(bytes), "r"(bar), "l"(pol)
+      : "memory");
+}
 SX_DEV void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
 template <int N>
 SX_DEV void cp_async_wait() {

@@ -142,6 +142,7 @@ SX_DEV float group_block_sum(float v, float *red, const Sync &sync) {
 //   kProResid: v = post_w ? rmsnorm(mlp, post_w) : mlp; xn = (x + v) * scalar;
 //              CTA 0 writes xn to x_out; xin = rmsnorm(xn, w)         (add_rmsnorm.wgsl)
 constexpr int kProPer = 8;  // elements per thread held in registers: K <= 512 * 8
+constexpr int kProMaxParts = 8;  // partial vectors a residual prologue adds (pro_mlp_parts)
 
 // The prologue's norm gains (weights: they do not depend on the producer of x, so a caller may
 // load them before it waits for that producer).
@@ -173,7 +174,18 @@ SX_DEV void run_prologue_gains(const GemvArgs &a, float *xin, float *red, const 
       bool in = i < K;
       xv[q] = in ? __ldcg(x + i) : 0.0f;  // activations: through L2 (see stage_x)
       mv[q] = 0.0f;
-      if (a.pro == kProResid) mv[q] = in ? __ldcg(a.pro_mlp + (size_t)j * a.ldx + i) : 0.0f;
+      if (a.pro == kProResid && in) mv[q] = __ldcg(a.pro_mlp + (size_t)j * a.ldx + i);
+    }
+    if (a.pro == kProResid && a.pro_mlp_parts > 1) {
+      // a sublayer output delivered as partial vectors, added in part order (the batch-1 Q4
+      // calls take stage_x_q4b1, which keeps four parts' loads in flight)
+#pragma unroll 1
+      for (uint32_t p = 1; p < a.pro_mlp_parts; ++p)
+#pragma unroll
+        for (int q = 0; q < kProPer; ++q) {
+          const uint32_t i = threadIdx.x + q * nthr;
+          if (i < K) mv[q] += __ldcg(a.pro_mlp + (size_t)p * a.pro_mlp_ld + (size_t)j * a.ldx + i);
+        }
     }
     if (a.pro == kProResid) {
       float rm = 1.0f;
@@ -336,6 +348,180 @@ SX_DEV void stage_x(const GemvArgs &a, const float *src, uint32_t ld, uint8_t *s
   sync();
 }
 
+// ---------------------------------------------------------------------------------------
+// Batch-1 Q4 input staging with the fused prologue, in one pass: thread t owns the group of 8
+// consecutive input elements 8 t .. 8 t + 7 (block t / 4, word t % 4 of the fragment layout
+// built by stage_x), so the normalised values go from registers straight into the B fragments
+// (no f32 staging in shared memory) and each of the prologue's two sums costs one barrier
+// (separate reduction buffers).  The norm gains do not depend on the producer of x and are
+// loaded before its wait (load_gains_q4b1).  Without a prologue a thread converts up to
+// kStageGroups groups (K <= 16384 with 512 threads).  Same operation order per element as
+// run_prologue; the sums of squares add a thread's 8 consecutive elements first.
+constexpr int kStageGroups = 4;
+struct GainsQ4B1 {
+  float nw[8], pw[8];
+};
+SX_HD bool al16(const void *p) { return ((uintptr_t)p & 15u) == 0; }
+SX_HD bool stage_q4b1_ok(const GemvArgs &a, uint32_t nthr) {
+  const uint32_t groups = 8 * pairs_of(a.k);  // 2 * pairs blocks x 4 groups
+  if (a.batch != 1 || a.k % 8 != 0 || !al16(a.x)) return false;
+  if (a.pro == kProNone) return groups <= kStageGroups * nthr;
+  if (groups > nthr || !al16(a.pro_w) || a.pro_norm_out != nullptr) return false;
+  if (a.pro == kProResid)
+    return al16(a.pro_mlp) && al16(a.pro_x_out) && (!a.pro_post_w || al16(a.pro_post_w)) &&
+           a.pro_mlp_parts <= (uint32_t)kProMaxParts &&
+           (a.pro_mlp_parts <= 1 || a.pro_mlp_ld % 4 == 0);
+  return true;
+}
+SX_DEV void load_gains_q4b1(const GemvArgs &a, GainsQ4B1 &gn) {
+  const uint32_t e0 = 8 * threadIdx.x;
+#pragma unroll
+  for (int q = 0; q < 8; ++q) gn.nw[q] = gn.pw[q] = 0.0f;
+  if (a.pro == kProNone || e0 >= a.k) return;
+  const float4 *w4 = reinterpret_cast<const float4 *>(a.pro_w + e0);
+  const float4 u0 = w4[0], u1 = w4[1];
+  gn.nw[0] = u0.x; gn.nw[1] = u0.y; gn.nw[2] = u0.z; gn.nw[3] = u0.w;
+  gn.nw[4] = u1.x; gn.nw[5] = u1.y; gn.nw[6] = u1.z; gn.nw[7] = u1.w;
+  if (a.pro == kProResid && a.pro_post_w) {
+    const float4 *p4 = reinterpret_cast<const float4 *>(a.pro_post_w + e0);
+    const float4 v0 = p4[0], v1 = p4[1];
+    gn.pw[0] = v0.x; gn.pw[1] = v0.y; gn.pw[2] = v0.z; gn.pw[3] = v0.w;
+    gn.pw[4] = v1.x; gn.pw[5] = v1.y; gn.pw[6] = v1.z; gn.pw[7] = v1.w;
+  }
+}
+SX_DEV void ld8(const float *p, float (&v)[8]) {
+  const float4 u0 = __ldcg(reinterpret_cast<const float4 *>(p));
+  const float4 u1 = __ldcg(reinterpret_cast<const float4 *>(p) + 1);
+  v[0] = u0.x; v[1] = u0.y; v[2] = u0.z; v[3] = u0.w;
+  v[4] = u1.x; v[5] = u1.y; v[6] = u1.z; v[7] = u1.w;
+}
+// sum over the CTA with one barrier: red holds kWarps floats for this reduction alone
+SX_DEV float cta_sum_1bar(float v, float *red) {
+  v = warp_sum(v);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+  __syncthreads();
+  const int lane = threadIdx.x & 31;
+  float t = lane < (int)(blockDim.x >> 5) ? red[lane] : 0.0f;
+  return warp_sum(t);
+}
+
+SX_DEV void stage_x_q4b1(const GemvArgs &a, uint8_t *smem, const Layout &L, const GainsQ4B1 &gn) {
+  uint32_t *xf = reinterpret_cast<uint32_t *>(smem + L.xfrag);
+  float *corr = reinterpret_cast<float *>(smem + L.corr);
+  float *xscale = reinterpret_cast<float *>(smem + L.misc);
+  int *xexp = reinterpret_cast<int *>(smem + L.misc + 32);
+  float *red = reinterpret_cast<float *>(smem + L.misc + 64);  // 2 x kWarps floats
+  const uint32_t K = a.k, nb = K / 32, nthr = blockDim.x, tid = threadIdx.x;
+  const uint32_t groups = 8 * pairs_of(K);
+  if (tid == 0) {
+    xscale[0] = 2.0f;
+    xexp[0] = 0;
+  }
+  float v[kStageGroups][8];
+  const int ng = a.pro == kProNone ? kStageGroups : 1;
+#pragma unroll
+  for (int k = 0; k < kStageGroups; ++k) {
+    const uint32_t gi = tid + k * nthr, blk = gi >> 2;
+    const bool live = k < ng && gi < groups && blk < nb;
+    if (live) {
+      ld8(a.x + 8 * gi, v[k]);
+    } else {
+#pragma unroll
+      for (int q = 0; q < 8; ++q) v[k][q] = 0.0f;
+    }
+  }
+  if (a.pro != kProNone) {
+    // one group per thread (K <= 8 * nthr)
+    const bool live = tid < groups && (tid >> 2) < nb;
+    float *xv = v[0];
+    if (a.pro == kProResid) {
+      float mv[8];
+      if (live) {
+        if (a.pro_mlp_parts <= 1) {
+          ld8(a.pro_mlp + 8 * tid, mv);
+        } else {
+          // partial vectors, added in part order: four parts' loads in flight at a time
+#pragma unroll
+          for (int p0 = 0; p0 < kProMaxParts; p0 += 4) {
+            float pv[4][8];
+#pragma unroll
+            for (int p = 0; p < 4; ++p) {
+              if ((uint32_t)(p0 + p) < a.pro_mlp_parts) {
+                ld8(a.pro_mlp + (size_t)(p0 + p) * a.pro_mlp_ld + 8 * tid, pv[p]);
+              } else {
+#pragma unroll
+                for (int q = 0; q < 8; ++q) pv[p][q] = 0.0f;
+              }
+            }
+#pragma unroll
+            for (int q = 0; q < 8; ++q) {
+              float m = p0 == 0 ? pv[0][q] : mv[q] + pv[0][q];
+#pragma unroll
+              for (int p = 1; p < 4; ++p)
+                if ((uint32_t)(p0 + p) < a.pro_mlp_parts) m += pv[p][q];
+              mv[q] = m;
+            }
+          }
+        }
+      } else {
+#pragma unroll
+        for (int q = 0; q < 8; ++q) mv[q] = 0.0f;
+      }
+      float rm = 1.0f;
+      if (a.pro_post_w) {
+        float ss = 0.0f;
+#pragma unroll
+        for (int q = 0; q < 8; ++q) ss = fmaf(mv[q], mv[q], ss);
+        rm = inv_rms(cta_sum_1bar(ss, red), K, a.eps);
+      }
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        float m = mv[q];
+        if (a.pro_post_w) m = __fmul_rn(__fmul_rn(m, rm), gn.pw[q]);
+        xv[q] = __fmul_rn(__fadd_rn(xv[q], m), a.pro_scalar);
+      }
+      if (blockIdx.x == 0 && live) {
+        float4 *o4 = reinterpret_cast<float4 *>(a.pro_x_out + 8 * tid);
+        o4[0] = make_float4(xv[0], xv[1], xv[2], xv[3]);
+        o4[1] = make_float4(xv[4], xv[5], xv[6], xv[7]);
+      }
+    }
+    float ss = 0.0f;
+#pragma unroll
+    for (int q = 0; q < 8; ++q) ss = fmaf(xv[q], xv[q], ss);
+    const float r = inv_rms(cta_sum_1bar(ss, red + kWarps), K, a.eps);
+#pragma unroll
+    for (int q = 0; q < 8; ++q) xv[q] = live ? __fmul_rn(__fmul_rn(xv[q], r), gn.nw[q]) : 0.0f;
+  }
+  // fragments: group gi = block gi / 4, word gi % 4 of each of the four lane columns
+  const uint32_t gpad = (groups + 31) & ~31u;
+#pragma unroll
+  for (int k = 0; k < kStageGroups; ++k) {
+    const uint32_t gi = tid + k * nthr;
+    if (k >= ng || gi >= gpad) break;  // warp-uniform: gpad is a multiple of 32
+    const uint32_t blk = gi >> 2, jj = gi & 3, pr = blk >> 1, hb = blk & 1;
+    float part = 0.0f;
+    if (gi < groups) {
+      uint32_t *hi_w = xf + ((pr * 2 * 4) * 2 + hb) * 4 + jj;
+      uint32_t *lo_w = xf + (((pr * 2 + 1) * 4) * 2 + hb) * 4 + jj;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        const float x0 = v[k][2 * c], x1 = v[k][2 * c + 1];
+        const __nv_bfloat162 h = __floats2bfloat162_rn(x0, x1);
+        const float h0 = __low2float(h), h1 = __high2float(h);
+        const __nv_bfloat162 l = __floats2bfloat162_rn(__fsub_rn(x0, h0), __fsub_rn(x1, h1));
+        hi_w[c * 8] = *reinterpret_cast<const uint32_t *>(&h);
+        lo_w[c * 8] = *reinterpret_cast<const uint32_t *>(&l);
+        part += (h0 + __low2float(l)) + (h1 + __high2float(l));
+      }
+    }
+    part += __shfl_xor_sync(0xffffffffu, part, 1);
+    part += __shfl_xor_sync(0xffffffffu, part, 2);
+    if (gi < groups && jj == 0) corr[pr * 2 + hb] = 12.0f * part;
+  }
+  __syncthreads();
+}
+
 // One 32-element block of one 16-row tile: two chained m16n8k16 MMAs per column set, the
 // offset term enters as the C operand, the block scale is applied to the f32 result.
 template <int QT>
@@ -435,6 +621,7 @@ SX_DEV void gemv_body(const GemvArgs &a, uint8_t *smem, bool prefetch, bool run,
   const bool s_lane = PRIV || lane < 8;
   // copy chunk i into stage i mod S; one commit group per chunk (empty past the end, so the
   // group count stays uniform)
+  const uint64_t pol = l2_evict_first_policy();  // weights are read once per token
   auto issue = [&](uint32_t i) {
     const bool live = i < n;
     const uint32_t stage = (i % S) * STAGE;
@@ -443,8 +630,8 @@ SX_DEV void gemv_body(const GemvArgs &a, uint8_t *smem, bool prefetch, bool run,
       const uint8_t *s = wsrc[m] + (size_t)i * CB;
 #pragma unroll
       for (int sub = 0; sub < CB / 512; ++sub)
-        cp_async16_if(q_dst + stage + m * KS + sub * 512, s + q_src + sub * 512, live);
-      cp_async16_if(s_dst + stage + m * KS, s + s_src, live && s_lane);
+        cp_async16_if_ef(q_dst + stage + m * KS + sub * 512, s + q_src + sub * 512, live, pol);
+      cp_async16_if_ef(s_dst + stage + m * KS, s + s_src, live && s_lane, pol);
     }
     cp_async_commit();
   };
@@ -456,6 +643,11 @@ SX_DEV void gemv_body(const GemvArgs &a, uint8_t *smem, bool prefetch, bool run,
     for (int st = 0; st < S - 1; ++st) issue(st);
   }
   if (!run) return;
+  // batch-1 Q4 calls of a kernel of its own stage x in one fused pass (stage_x_q4b1); its
+  // norm gains are weights, loaded before the dependency wait
+  const bool fast = QT == 4 && NSETS == 1 && standalone && stage_q4b1_ok(a, blockDim.x);
+  GainsQ4B1 gq;
+  if (fast) load_gains_q4b1(a, gq);
   if (standalone) {
     if (a.pf_slots != nullptr) {
       // the following attention's K/V rows, spread over the CTAs (slot j: thread j / grid of
@@ -482,7 +674,9 @@ SX_DEV void gemv_body(const GemvArgs &a, uint8_t *smem, bool prefetch, bool run,
   float *xin = reinterpret_cast<float *>(smem + L.xin);
   const float *xsrc = a.x;
   uint32_t xld = a.ldx;
-  if (pro) {
+  if (fast) {
+    stage_x_q4b1(a, smem, L, gq);
+  } else if (pro) {
     run_prologue(a, xin, reinterpret_cast<float *>(smem + L.misc + 64));
     xsrc = xin;
     xld = a.k;
@@ -508,7 +702,7 @@ SX_DEV void gemv_body(const GemvArgs &a, uint8_t *smem, bool prefetch, bool run,
     xsrc = xin;
     xld = a.k;
   }
-  stage_x<QT>(a, xsrc, xld, smem, L, xsrc == a.x);
+  if (!fast) stage_x<QT>(a, xsrc, xld, smem, L, xsrc == a.x);
 
   const uint4 *const xf4 = reinterpret_cast<const uint4 *>(smem + L.xfrag);
   const float *const corr = reinterpret_cast<const float *>(smem + L.corr);

@@ -72,6 +72,7 @@ enum OpKind {
   OP_ALLREDUCE,   // tensor parallel: in-place sum all-reduce of u[0] floats at dev
   OP_ALLGATHER,   // tensor parallel: bind[0] (u[0] u32 words per rank) -> bind[1]
   OP_TP_ARGMAX,   // tensor parallel: merge u[0] ranks' argmax candidates bind[0] -> bind[1]
+  OP_ATTN_BLOCK,  // q|k|v GEMV + qkv_rope + attention + o GEMV as one kernel (model graph)
 };
 
 struct Op {
@@ -89,6 +90,7 @@ struct Op {
   bool geglu = false;
   sx::GemvArgs gemv{};
   sx::AttnFusedArgs attnf{};
+  sx::AttnBlockArgs ab{};   // OP_ATTN_BLOCK
   uint32_t attn_rot = 0;
   float attn_theta = 0.0f;
   sx_comm *comm = nullptr;  // OP_ALLREDUCE / OP_ALLGATHER

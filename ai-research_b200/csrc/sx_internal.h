@@ -27,6 +27,9 @@ struct GemvArgs {
   const float *pro_post_w;  // kProResid: optional post-norm gain of the sublayer output
   float *pro_x_out;         // kProResid: updated residual stream (must not alias x)
   float *pro_norm_out;      // optional: the normed input rows, written by CTA 0
+  // kProResid: the sublayer output is the sum of pro_mlp_parts vectors pro_mlp_ld floats
+  // apart, added in order (0 or 1: one vector)
+  uint32_t pro_mlp_parts, pro_mlp_ld;
   float pro_scalar;         // kProResid: layer scalar
   float eps;
   int epi;
@@ -172,6 +175,34 @@ struct AttnFusedArgs {
 cudaError_t launch_attn_fused(const AttnFusedArgs &a, cudaStream_t s, bool pdl);
 // rings up to this many live slots run the cluster form (16 CTAs x 64 slots per kv head)
 constexpr uint32_t kAttnClusterMaxSlots = 1024;
+
+// The attention block of one decode layer as one kernel (sx_attn_block.cu): q|k|v projection
+// with its residual + input-norm prologue, q/k norm + RoPE + cache write, attention over the
+// active slots, and the o projection split by kv-head group into num_kv partial rows.
+struct AttnBlockArgs {
+  GemvArgs g;         // q|k|v: w[0..2][0] = wq, wk, wv (packed Q4_0), y[0..2] = q, k, v rows,
+                      // k = hidden size, batch 1, the input prologue fields
+  AttnFusedArgs at;   // q/k/v (= g.y), norm gains, RoPE table, caches, slots, step, scale, ...
+  const void *wo;     // packed Q4_0 o projection [o_rows][num_q * head_dim]
+  float *opart;       // [num_kv][o_rows]: the o projection of each group's columns
+  float *rec;         // [num_kv][ctas][G][head_dim + 2] attention records
+  uint32_t *cnt;      // [2 * num_kv + 1] arrival counters, zero at rest (the kernel clears them)
+  uint32_t o_rows;    // hidden size
+  uint32_t ctas;      // CTAs per kv-head group
+  uint32_t max_slots; // active slots per CTA the shared memory holds
+  uint32_t o_tiles;   // o-projection tiles per CTA the shared memory holds
+  uint64_t wait_ns;   // limit of each counter wait (GPU time)
+};
+struct AttnBlockPlan {
+  uint32_t ctas, max_slots, o_tiles, smem;
+};
+// false when the shape has no attention-block form (head_dim, GQA ratio, ring or shared memory)
+bool attn_block_plan(uint32_t hidden, uint32_t num_q, uint32_t num_kv, uint32_t head_dim,
+                     uint32_t total_slots, bool kv_bf16, int num_sms, uint32_t smem_limit,
+                     AttnBlockPlan *plan);
+cudaError_t launch_attn_block(const AttnBlockArgs &a, cudaStream_t s);
+constexpr uint32_t kAttnBlockSmemLimit = 227 * 1024 - 1024;  // dynamic, below the opt-in max
+cudaError_t prepare_attn_block_kernels();
 
 // ---------------------------------------------------------------------------------------
 // Batched prefill (sx_prefill_model.cu): per-token kernels around the tcgen05 GEMMs.

@@ -30,6 +30,8 @@ struct LayerBufs {
   sx_set *s_post_ffn_add = nullptr;
   sx_buffer *x_prev = nullptr;  // quiescence-gate history (model_gpu.zig:132), zero at start
   sx_set *s_gate = nullptr;     // {x, x_prev, indirect records} (model_gpu.zig:156)
+  // the layer's attention block as one kernel (sx_attn_block.cu); ctas == 0: not eligible
+  sx::AttnBlockPlan ab{};
 };
 
 enum Tensor : uint32_t {
@@ -56,6 +58,10 @@ struct sx_model {
   sx_buffer *logits = nullptr, *token = nullptr, *step = nullptr;
   sx_buffer *lm_head = nullptr, *final_norm = nullptr;
   sx_buffer *ind = nullptr;  // 16 dispatch records of 12 bytes per layer (model_gpu.zig:107)
+  // attention-block kernels (fused graph, one session, one GPU, Q4_0 layers): the o
+  // projection's per-group partial rows, the attention records, per-layer arrival counters
+  sx_buffer *ab_opart = nullptr, *ab_rec = nullptr, *ab_cnt = nullptr;
+  uint32_t ab_cnt_words = 0;  // counter words per layer
   sx_set *s_final_norm = nullptr, *s_logits = nullptr, *s_argmax = nullptr;
   sx_cmd *cmd[2][2] = {{nullptr, nullptr}, {nullptr, nullptr}};  // [want_logits][io]
   // independent sessions: activation rows [S][...], KV caches [S][slots][kv_dim] (session 0
@@ -175,6 +181,30 @@ sx_status alloc_model(sx_model *m) {
                        B.wu->bytes + B.wd->bytes;
   }
   M_TRY(mk_buf(m, 16ull * 12 * c.num_layers, &m->ind));
+  // attention-block plans: graph 0 with one session, one GPU and Q4_0 layers (the rows of the
+  // q|k|v projection are regrouped per kv head, which the packed Q4_0 tiles allow)
+  if (c.reference_graph == 0 && S == 1 && c.tp_size <= 1 && m->lmode == SX_QUANT_Q4) {
+    uint64_t rec = 0, opart = 0;
+    uint32_t max_kv_heads = 0;
+    for (uint32_t l = 0; l < c.num_layers; ++l) {
+      LayerBufs &B = m->L[l];
+      if (B.k_eq_v ||
+          !sx::attn_block_plan(H, m->nq, B.num_kv, B.head_dim, m->total_slots, c.kv_bf16 != 0,
+                               m->e->num_sms, sx::kAttnBlockSmemLimit, &B.ab))
+        B.ab = sx::AttnBlockPlan{};
+      if (!B.ab.ctas) continue;
+      const uint64_t r = (uint64_t)m->nq * B.ab.ctas * (B.head_dim + 2);
+      if (r > rec) rec = r;
+      if ((uint64_t)B.num_kv * H > opart) opart = (uint64_t)B.num_kv * H;
+      if (B.num_kv > max_kv_heads) max_kv_heads = B.num_kv;
+    }
+    if (rec) {
+      M_TRY(mk_buf(m, 4 * rec, &m->ab_rec));
+      M_TRY(mk_buf(m, 4 * opart, &m->ab_opart));
+      m->ab_cnt_words = 2 * max_kv_heads + 1;
+      M_TRY(mk_buf(m, 4ull * m->ab_cnt_words * c.num_layers, &m->ab_cnt));  // zeroed
+    }
+  }
   for (uint32_t l = 0; l < c.num_layers; ++l) M_TRY(mk_buf(m, 4ull * H, &m->L[l].x_prev));
   M_TRY(mk_buf(m, sx_packed_bytes(V, H, m->hmode), &m->lm_head));
   M_TRY(mk_buf(m, 4ull * H, &m->final_norm));
@@ -424,6 +454,7 @@ sx_status record_forward_fused(sx_model *m, sx_cmd *cmd, bool logits, bool io,
     LayerBufs &B = m->L[l];
     // q | k | v with the input norm (and, after layer 0, the previous layer's residual)
     // q | k | v rows of session j at qkv + j * base (base = q_dim + 2 kv_dim of this layer)
+    const bool blk = persistent == kPersistNone && nb == 1 && !tp && B.ab.ctas != 0;
     sx::GemvArgs q{};
     const sx_buffer *w3[3] = {B.wq, B.wk, B.wv};
     uint32_t r3[3] = {B.q_dim, B.kv_dim, B.kv_dim};
@@ -465,8 +496,10 @@ sx_status record_forward_fused(sx_model *m, sx_cmd *cmd, bool logits, bool io,
     q.pf_base[1] = B.k_eq_v ? nullptr : B.vc->d;
     q.pf_row_bytes = B.kv_dim * (c.kv_bf16 ? 2u : 4u);
     q.pf_max = m->total_slots;
-    M_TRY(sx_host_check_gemv(m->lqt, false, true, B.q_dim + 2 * B.kv_dim, H, nb));
-    push_gemv(m, cmd, q, m->lqt, false);
+    if (!blk) {
+      M_TRY(sx_host_check_gemv(m->lqt, false, true, B.q_dim + 2 * B.kv_dim, H, nb));
+      push_gemv(m, cmd, q, m->lqt, false);
+    }
 
     // fused qkv_rope + attention
     Op at{OP_ATTN_FUSED};
@@ -503,20 +536,47 @@ sx_status record_forward_fused(sx_model *m, sx_cmd *cmd, bool logits, bool io,
       sx_host_set_error("model: attention scratch too small for this ring / head count");
       return SX_ERR_UNSUPPORTED;
     }
-    sx_host_push_op(cmd, at);
+    if (blk) {
+      // q|k|v projection + qkv_rope + attention + o projection as one kernel; the o rows come
+      // out as one partial vector per kv-head group, summed by the gate+up prologue
+      Op ab{OP_ATTN_BLOCK};
+      sx::AttnBlockArgs &X = ab.ab;
+      X.g = q;
+      sx_host_bind_scratch(m->e, X.g);
+      X.at = A;
+      X.wo = B.wo->d;
+      X.opart = (float *)m->ab_opart->d;
+      X.rec = (float *)m->ab_rec->d;
+      X.cnt = (uint32_t *)m->ab_cnt->d + (size_t)l * m->ab_cnt_words;
+      X.o_rows = H;
+      X.ctas = B.ab.ctas;
+      X.max_slots = B.ab.max_slots;
+      X.o_tiles = B.ab.o_tiles;
+      X.wait_ns = 200000000ull;  // 0.2 s per counter wait
+      ab.attn_rot = B.rot;
+      ab.attn_theta = B.theta;
+      sx_host_push_op(cmd, ab);
+    } else {
+      sx_host_push_op(cmd, at);
 
-    // o projection
-    M_TRY(sx_host_check_gemv(m->lqt, false, false, H, B.q_dim, nb));
-    sx::GemvArgs o = gemv1(B.wo, m->attn_out, m->mlp_out, H, B.q_dim);
-    o.batch = nb;
-    push_gemv(m, cmd, o, m->lqt, false);
-    if (tp) push_allreduce(m, cmd, m->mlp_out, H);  // row-parallel o: sum of the ranks' parts
+      // o projection
+      M_TRY(sx_host_check_gemv(m->lqt, false, false, H, B.q_dim, nb));
+      sx::GemvArgs o = gemv1(B.wo, m->attn_out, m->mlp_out, H, B.q_dim);
+      o.batch = nb;
+      push_gemv(m, cmd, o, m->lqt, false);
+      if (tp) push_allreduce(m, cmd, m->mlp_out, H);  // row-parallel o: sum of the ranks' parts
+    }
 
     // gate+up GeGLU with the post-attention residual and pre-FFN norm
     sx::GemvArgs g = gemv1(B.wg, m->x, m->act, I, H);
     g.w[0][1] = B.wu->d;
     g.pro = sx::kProResid;
     g.pro_mlp = (const float *)m->mlp_out->d;
+    if (blk) {
+      g.pro_mlp = (const float *)m->ab_opart->d;
+      g.pro_mlp_parts = B.num_kv;
+      g.pro_mlp_ld = H;
+    }
     g.pro_post_w = c.has_post_norms ? (const float *)B.post_attn->d : nullptr;
     g.pro_scalar = 1.0f;
     g.pro_w = (const float *)B.pre_ffn->d;
@@ -631,7 +691,7 @@ sx_status create_model(sx_engine *e, const sx_model_config *cfg, sx_comm *comm, 
   bool ok = c.vocab_size > 0 && c.hidden_size % 32 == 0 && c.intermediate_size % 32 == 0 &&
             c.num_layers > 0 && c.num_q_heads > 0 && c.num_kv_heads > 0 &&
             c.num_q_heads % c.num_kv_heads == 0 && c.window_size > 0 && c.head_dim > 0 &&
-            (c.num_q_heads * c.head_dim) % 32 == 0 && c.reference_graph <= 3;
+            (c.num_q_heads * c.head_dim) % 32 == 0 && c.reference_graph <= 4;
   if (c.full_every)
     ok = ok && c.num_global_kv_heads > 0 && c.num_q_heads % c.num_global_kv_heads == 0 &&
          c.global_head_dim > 0;

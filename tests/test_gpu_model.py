@@ -69,7 +69,9 @@ def run_decode(engine, cfg, seed, steps, start_clock, n_recall=0):
     return results
 
 
-GRAPHS = [0, 1, 2]  # fused kernels, the reference's op-by-op graph, one persistent launch
+# fused kernels (the attention block as one kernel), the reference's op-by-op graph, one
+# persistent launch, fused kernels with the attention block as three launches
+GRAPHS = [0, 1, 2, 4]
 
 
 @pytest.mark.parametrize("reference_graph", GRAPHS)
@@ -78,8 +80,12 @@ def test_greedy_decode_matches_checker(engine, engine_f32kv, kv_f32, reference_g
     eng = engine_f32kv if kv_f32 else engine
     cfg = tiny_cfg(kv_bf16=0 if kv_f32 else 1, reference_graph=reference_graph)
     res = run_decode(eng, cfg, seed=3, steps=24, start_clock=0)  # window wraps twice
+    from tests.conftest import assert_close_bf16_operands
     for i, (tok, rtok, lg, rlg) in enumerate(res):
-        assert_close(lg, rlg, what=f"logits step {i}")
+        if kv_f32:
+            assert_close(lg, rlg, what=f"logits step {i}")
+        else:  # a cached element rounded from f32 values one ulp apart differs by 2^-8
+            assert_close_bf16_operands(lg, rlg, what=f"logits step {i}")
         if tok != rtok:
             assert margin_top2(rlg) < 1e-3, f"step {i}: token {tok} vs {rtok}"
 
@@ -105,7 +111,7 @@ def test_long_ring_uses_global_merge(engine):
             assert margin_top2(rlg) < 1e-3
 
 
-@pytest.mark.parametrize("reference_graph", [0, 2])
+@pytest.mark.parametrize("reference_graph", [0, 2, 4])
 def test_12b_width_two_layers_full_vocab(engine, reference_graph):
     # 12B layer shapes and full vocabulary with two layers (one sliding, one full attention)
     cfg = tiny_cfg(vocab_size=262144, hidden_size=3840, intermediate_size=15360, num_layers=2,
@@ -133,7 +139,9 @@ def test_prefill_graph_skips_logits(engine, reference_graph):
         assert model.kernels_per_token(False) == model.kernels_per_token(True) == 1
     else:
         assert model.kernels_per_token(False) < model.kernels_per_token(True)
-        per_layer = 14 if reference_graph else 5
+        # op-by-op: 14; fused: attention block + gate+up + down; graph 4: q|k|v, attention and
+        # o as separate launches
+        per_layer = {1: 14, 0: 3, 4: 5}[reference_graph]
         L = cfg["num_layers"]
         gates = (L - L // 3) if reference_graph == 1 else 0  # recordLayerIndirect's gate
         assert model.kernels_per_token(False) == per_layer * L + gates
@@ -311,3 +319,43 @@ def test_submit_deadline_returns_timeout_not_hang(engine):
     assert ei.value.status == sx.SX_ERR_TIMEOUT
     E.sync()
     E.submit_pre_recorded(cmd)  # default 5 s deadline is met
+
+
+def test_attention_block_config5_shape_matches_checker(engine):
+    """Graph 0's attention-block kernel (q|k|v, norm + RoPE + cache write, attention and the o
+    projection in one launch) on config 5's layer shape: one kv head read by 8 q heads, so all
+    148 CTAs form one group; head_dim 256; a 640-slot ring with a young window, then a wrapped
+    one with a recall tier.  Against the checker with the bf16-cache allowance (a cached element
+    rounded from f32 values one ulp apart differs by 2^-8)."""
+    from tests.conftest import assert_close_bf16_operands
+    cfg = tiny_cfg(vocab_size=8192, hidden_size=1536, intermediate_size=6144, num_layers=2,
+                   num_q_heads=8, num_kv_heads=1, num_global_kv_heads=1, head_dim=256,
+                   global_head_dim=256, num_anchors=32, window_size=512, num_recall=96,
+                   full_every=2)
+    for start, n_recall in ((3, 0), (4000, 40)):
+        res = run_decode(engine, cfg, seed=41, steps=3, start_clock=start, n_recall=n_recall)
+        for i, (tok, rtok, lg, rlg) in enumerate(res):
+            assert_close_bf16_operands(lg, rlg, what=f"start {start} logits step {i}")
+            if tok != rtok:
+                assert margin_top2(rlg) < 1e-3, f"start {start} step {i}: {tok} vs {rtok}"
+
+
+@pytest.mark.parametrize("kv_f32", [False, True])
+def test_attention_block_equals_separate_launches(engine, engine_f32kv, kv_f32):
+    """The attention block (graph 0) and its three separate launches (graph 4) compute the same
+    token: the block sums the o projection per kv-head group, so the logits agree within the f32
+    tolerance, not bit for bit; both also against the checker."""
+    eng = engine_f32kv if kv_f32 else engine
+    outs = []
+    for g in (0, 4):
+        cfg = mid_cfg(kv_bf16=0 if kv_f32 else 1, reference_graph=g)
+        outs.append(run_decode(eng, cfg, seed=37, steps=4, start_clock=900, n_recall=4))
+    from tests.conftest import assert_close_bf16_operands
+    for i, ((t0, _, l0, _), (t4, _, l4, rl)) in enumerate(zip(*outs)):
+        if kv_f32:
+            assert_close(l0, l4, what=f"block vs separate logits step {i}")
+            assert_close(l0, rl, what=f"block vs checker logits step {i}")
+        else:  # cached K/V rounded to bf16 from slightly different f32 values
+            assert_close_bf16_operands(l0, l4, what=f"block vs separate logits step {i}")
+        if t0 != t4:
+            assert margin_top2(rl) < 1e-3, f"step {i}: {t0} vs {t4}"
