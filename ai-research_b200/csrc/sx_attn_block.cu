@@ -293,15 +293,15 @@ __global__ void __launch_bounds__(kThreads, 1) attn_block_kernel(AttnBlockArgs a
 #pragma unroll
   for (int st = 0; st < S - 1; ++st) issue();
 
-  const bool gfast = stage_q4b1_ok(ga, blockDim.x);
-  GainsQ4B1 gains_a;
-  if (gfast) load_gains_q4b1(ga, gains_a);
+  const bool gfast = stage_q4_ok(ga, blockDim.x, L);
+  GainsQ4 gains_a;
+  if (gfast) load_gains_q4(ga, gains_a);
   pdl_launch_dependents();
   pdl_wait();
 
   // ---- phase A: q | k | v rows of the group ----
   if (gfast) {
-    stage_x_q4b1(ga, smem, L, gains_a);
+    stage_x_q4(ga, smem, L, gains_a);
   } else {
     float *xin = reinterpret_cast<float *>(smem + L.xin);
     run_prologue(ga, xin, reinterpret_cast<float *>(smem + L.misc + 64));
@@ -589,8 +589,16 @@ __global__ void __launch_bounds__(kThreads, 1) attn_block_kernel(AttnBlockArgs a
     const float *base = rec_base + (size_t)h * (D + 2) + 2 + d;
     const float *f = fw + h * C;
     float O = 0.0f;
-#pragma unroll 6
-    for (uint32_t r = 0; r < C; ++r) O = fmaf(__ldcg(base + (size_t)r * G * (D + 2)), f[r], O);
+    // up to 32 records' loads in flight, then the weighted sum in record order
+    for (uint32_t r0 = 0; r0 < C; r0 += 32) {
+      float rv[32];
+#pragma unroll
+      for (int r = 0; r < 32; ++r)
+        rv[r] = r0 + r < C ? __ldcg(base + (size_t)(r0 + r) * G * (D + 2)) : 0.0f;
+#pragma unroll
+      for (int r = 0; r < 32; ++r)
+        if (r0 + r < C) O = fmaf(rv[r], f[r0 + r], O);
+    }
     const float Ls = ls[h];
     xo[idx] = (ok_b && Ls > 0.0f) ? O / Ls : 0.0f;
   }

@@ -177,8 +177,8 @@ SX_DEV void run_prologue_gains(const GemvArgs &a, float *xin, float *red, const 
       if (a.pro == kProResid && in) mv[q] = __ldcg(a.pro_mlp + (size_t)j * a.ldx + i);
     }
     if (a.pro == kProResid && a.pro_mlp_parts > 1) {
-      // a sublayer output delivered as partial vectors, added in part order (the batch-1 Q4
-      // calls take stage_x_q4b1, which keeps four parts' loads in flight)
+      // a sublayer output delivered as partial vectors, added in part order (the Q4 calls of
+      // their own kernel take stage_x_q4, which keeps four parts' loads in flight)
 #pragma unroll 1
       for (uint32_t p = 1; p < a.pro_mlp_parts; ++p)
 #pragma unroll
@@ -349,31 +349,39 @@ SX_DEV void stage_x(const GemvArgs &a, const float *src, uint32_t ld, uint8_t *s
 }
 
 // ---------------------------------------------------------------------------------------
-// Batch-1 Q4 input staging with the fused prologue, in one pass: thread t owns the group of 8
-// consecutive input elements 8 t .. 8 t + 7 (block t / 4, word t % 4 of the fragment layout
-// built by stage_x), so the normalised values go from registers straight into the B fragments
-// (no f32 staging in shared memory) and each of the prologue's two sums costs one barrier
-// (separate reduction buffers).  The norm gains do not depend on the producer of x and are
-// loaded before its wait (load_gains_q4b1).  Without a prologue a thread converts up to
-// kStageGroups groups (K <= 16384 with 512 threads).  Same operation order per element as
-// run_prologue; the sums of squares add a thread's 8 consecutive elements first.
+// Q4 input staging with the fused prologue in one pass, batch 1..8: thread t owns the group of
+// 8 consecutive input elements 8 t .. 8 t + 7 of every batch row (block t / 4, word t % 4 of
+// the fragment layout built by stage_x), so the normalised values go from registers straight
+// into the B fragments (no f32 staging in shared memory), and each of the prologue's two sums
+// costs one barrier per pair of rows (separate reduction buffers in the unused f32 staging
+// area).  The norm gains do not depend on the producer of x and are loaded before its wait
+// (load_gains_q4).  Without a prologue a thread converts up to kStageGroups groups per row
+// (K <= 16384 with 512 threads).  Same operation order per element as run_prologue; a row's
+// sums of squares add a thread's 8 consecutive elements, then the warp, then the warps in
+// order, exactly as for batch 1, so every row of a batch is staged bit-identically to the same
+// row alone.
 constexpr int kStageGroups = 4;
-struct GainsQ4B1 {
+constexpr int kStageRows = 2;  // rows per prologue round (one barrier per sum per round)
+struct GainsQ4 {
   float nw[8], pw[8];
 };
 SX_HD bool al16(const void *p) { return ((uintptr_t)p & 15u) == 0; }
-SX_HD bool stage_q4b1_ok(const GemvArgs &a, uint32_t nthr) {
+SX_HD bool stage_q4_ok(const GemvArgs &a, uint32_t nthr, const Layout &L) {
   const uint32_t groups = 8 * pairs_of(a.k);  // 2 * pairs blocks x 4 groups
-  if (a.batch != 1 || a.k % 8 != 0 || !al16(a.x)) return false;
+  if (a.batch < 1 || a.batch > 8 || a.k % 8 != 0 || !al16(a.x) || (a.batch > 1 && a.ldx % 4 != 0))
+    return false;
   if (a.pro == kProNone) return groups <= kStageGroups * nthr;
-  if (groups > nthr || !al16(a.pro_w) || a.pro_norm_out != nullptr) return false;
+  const uint32_t rounds = (a.batch + kStageRows - 1) / kStageRows;
+  if (groups > nthr || !al16(a.pro_w) || a.pro_norm_out != nullptr ||
+      L.xin_bytes < rounds * 2 * kStageRows * kWarps * 4 || nthr != kThreads)
+    return false;
   if (a.pro == kProResid)
     return al16(a.pro_mlp) && al16(a.pro_x_out) && (!a.pro_post_w || al16(a.pro_post_w)) &&
            a.pro_mlp_parts <= (uint32_t)kProMaxParts &&
-           (a.pro_mlp_parts <= 1 || a.pro_mlp_ld % 4 == 0);
+           (a.pro_mlp_parts <= 1 || (a.batch == 1 && a.pro_mlp_ld % 4 == 0));
   return true;
 }
-SX_DEV void load_gains_q4b1(const GemvArgs &a, GainsQ4B1 &gn) {
+SX_DEV void load_gains_q4(const GemvArgs &a, GainsQ4 &gn) {
   const uint32_t e0 = 8 * threadIdx.x;
 #pragma unroll
   for (int q = 0; q < 8; ++q) gn.nw[q] = gn.pw[q] = 0.0f;
@@ -395,118 +403,50 @@ SX_DEV void ld8(const float *p, float (&v)[8]) {
   v[0] = u0.x; v[1] = u0.y; v[2] = u0.z; v[3] = u0.w;
   v[4] = u1.x; v[5] = u1.y; v[6] = u1.z; v[7] = u1.w;
 }
-// sum over the CTA with one barrier: red holds kWarps floats for this reduction alone
-SX_DEV float cta_sum_1bar(float v, float *red) {
-  v = warp_sum(v);
-  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+SX_DEV void zero8(float (&v)[8]) {
+#pragma unroll
+  for (int q = 0; q < 8; ++q) v[q] = 0.0f;
+}
+// R sums over the CTA with one barrier: red holds R x kWarps floats for these sums alone
+template <int R>
+SX_DEV void cta_sums_1bar(float (&v)[R], float *red) {
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+#pragma unroll
+  for (int r = 0; r < R; ++r) {
+    v[r] = warp_sum(v[r]);
+    if (lane == 0) red[r * kWarps + w] = v[r];
+  }
   __syncthreads();
-  const int lane = threadIdx.x & 31;
-  float t = lane < (int)(blockDim.x >> 5) ? red[lane] : 0.0f;
-  return warp_sum(t);
+#pragma unroll
+  for (int r = 0; r < R; ++r) {
+    const float t = lane < kWarps ? red[r * kWarps + lane] : 0.0f;
+    v[r] = warp_sum(t);
+  }
 }
 
-SX_DEV void stage_x_q4b1(const GemvArgs &a, uint8_t *smem, const Layout &L, const GainsQ4B1 &gn) {
+SX_DEV void stage_x_q4(const GemvArgs &a, uint8_t *smem, const Layout &L, const GainsQ4 &gn) {
   uint32_t *xf = reinterpret_cast<uint32_t *>(smem + L.xfrag);
   float *corr = reinterpret_cast<float *>(smem + L.corr);
   float *xscale = reinterpret_cast<float *>(smem + L.misc);
   int *xexp = reinterpret_cast<int *>(smem + L.misc + 32);
-  float *red = reinterpret_cast<float *>(smem + L.misc + 64);  // 2 x kWarps floats
-  const uint32_t K = a.k, nb = K / 32, nthr = blockDim.x, tid = threadIdx.x;
-  const uint32_t groups = 8 * pairs_of(K);
-  if (tid == 0) {
-    xscale[0] = 2.0f;
-    xexp[0] = 0;
+  // the f32 staging area is unused on this path: per round, [2 sums][kStageRows][kWarps]
+  float *red = reinterpret_cast<float *>(smem + L.xin);
+  const uint32_t K = a.k, nb = K / 32, nthr = blockDim.x, tid = threadIdx.x, B = a.batch;
+  const uint32_t groups = 8 * pairs_of(K), gpad = (groups + 31) & ~31u, nv = nv_of(B);
+  if (tid < B) {
+    xscale[tid] = 2.0f;
+    xexp[tid] = 0;
   }
-  float v[kStageGroups][8];
-  const int ng = a.pro == kProNone ? kStageGroups : 1;
-#pragma unroll
-  for (int k = 0; k < kStageGroups; ++k) {
-    const uint32_t gi = tid + k * nthr, blk = gi >> 2;
-    const bool live = k < ng && gi < groups && blk < nb;
-    if (live) {
-      ld8(a.x + 8 * gi, v[k]);
-    } else {
-#pragma unroll
-      for (int q = 0; q < 8; ++q) v[k][q] = 0.0f;
-    }
-  }
-  if (a.pro != kProNone) {
-    // one group per thread (K <= 8 * nthr)
-    const bool live = tid < groups && (tid >> 2) < nb;
-    float *xv = v[0];
-    if (a.pro == kProResid) {
-      float mv[8];
-      if (live) {
-        if (a.pro_mlp_parts <= 1) {
-          ld8(a.pro_mlp + 8 * tid, mv);
-        } else {
-          // partial vectors, added in part order: four parts' loads in flight at a time
-#pragma unroll
-          for (int p0 = 0; p0 < kProMaxParts; p0 += 4) {
-            float pv[4][8];
-#pragma unroll
-            for (int p = 0; p < 4; ++p) {
-              if ((uint32_t)(p0 + p) < a.pro_mlp_parts) {
-                ld8(a.pro_mlp + (size_t)(p0 + p) * a.pro_mlp_ld + 8 * tid, pv[p]);
-              } else {
-#pragma unroll
-                for (int q = 0; q < 8; ++q) pv[p][q] = 0.0f;
-              }
-            }
-#pragma unroll
-            for (int q = 0; q < 8; ++q) {
-              float m = p0 == 0 ? pv[0][q] : mv[q] + pv[0][q];
-#pragma unroll
-              for (int p = 1; p < 4; ++p)
-                if ((uint32_t)(p0 + p) < a.pro_mlp_parts) m += pv[p][q];
-              mv[q] = m;
-            }
-          }
-        }
-      } else {
-#pragma unroll
-        for (int q = 0; q < 8; ++q) mv[q] = 0.0f;
-      }
-      float rm = 1.0f;
-      if (a.pro_post_w) {
-        float ss = 0.0f;
-#pragma unroll
-        for (int q = 0; q < 8; ++q) ss = fmaf(mv[q], mv[q], ss);
-        rm = inv_rms(cta_sum_1bar(ss, red), K, a.eps);
-      }
-#pragma unroll
-      for (int q = 0; q < 8; ++q) {
-        float m = mv[q];
-        if (a.pro_post_w) m = __fmul_rn(__fmul_rn(m, rm), gn.pw[q]);
-        xv[q] = __fmul_rn(__fadd_rn(xv[q], m), a.pro_scalar);
-      }
-      if (blockIdx.x == 0 && live) {
-        float4 *o4 = reinterpret_cast<float4 *>(a.pro_x_out + 8 * tid);
-        o4[0] = make_float4(xv[0], xv[1], xv[2], xv[3]);
-        o4[1] = make_float4(xv[4], xv[5], xv[6], xv[7]);
-      }
-    }
-    float ss = 0.0f;
-#pragma unroll
-    for (int q = 0; q < 8; ++q) ss = fmaf(xv[q], xv[q], ss);
-    const float r = inv_rms(cta_sum_1bar(ss, red + kWarps), K, a.eps);
-#pragma unroll
-    for (int q = 0; q < 8; ++q) xv[q] = live ? __fmul_rn(__fmul_rn(xv[q], r), gn.nw[q]) : 0.0f;
-  }
-  // fragments: group gi = block gi / 4, word gi % 4 of each of the four lane columns
-  const uint32_t gpad = (groups + 31) & ~31u;
-#pragma unroll
-  for (int k = 0; k < kStageGroups; ++k) {
-    const uint32_t gi = tid + k * nthr;
-    if (k >= ng || gi >= gpad) break;  // warp-uniform: gpad is a multiple of 32
+  // fragments of group gi of row j: block gi / 4, word gi % 4 of each of the four lane columns
+  auto frag = [&](uint32_t gi, uint32_t j, const float (&x)[8]) {
     const uint32_t blk = gi >> 2, jj = gi & 3, pr = blk >> 1, hb = blk & 1;
     float part = 0.0f;
     if (gi < groups) {
-      uint32_t *hi_w = xf + ((pr * 2 * 4) * 2 + hb) * 4 + jj;
-      uint32_t *lo_w = xf + (((pr * 2 + 1) * 4) * 2 + hb) * 4 + jj;
+      uint32_t *hi_w = xf + ((((pr * nv + 2 * j) * 4) * 2 + hb) * 4 + jj);
+      uint32_t *lo_w = xf + ((((pr * nv + 2 * j + 1) * 4) * 2 + hb) * 4 + jj);
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
-        const float x0 = v[k][2 * c], x1 = v[k][2 * c + 1];
+        const float x0 = x[2 * c], x1 = x[2 * c + 1];
         const __nv_bfloat162 h = __floats2bfloat162_rn(x0, x1);
         const float h0 = __low2float(h), h1 = __high2float(h);
         const __nv_bfloat162 l = __floats2bfloat162_rn(__fsub_rn(x0, h0), __fsub_rn(x1, h1));
@@ -517,7 +457,118 @@ SX_DEV void stage_x_q4b1(const GemvArgs &a, uint8_t *smem, const Layout &L, cons
     }
     part += __shfl_xor_sync(0xffffffffu, part, 1);
     part += __shfl_xor_sync(0xffffffffu, part, 2);
-    if (gi < groups && jj == 0) corr[pr * 2 + hb] = 12.0f * part;
+    if (gi < groups && jj == 0) corr[(pr * B + j) * 2 + hb] = 12.0f * part;
+  };
+
+  if (a.pro == kProNone) {
+#pragma unroll 1
+    for (uint32_t j = 0; j < B; ++j) {
+      const float *xr = a.x + (size_t)j * a.ldx;
+      float v[kStageGroups][8];
+#pragma unroll
+      for (int k = 0; k < kStageGroups; ++k) {
+        const uint32_t gi = tid + k * nthr;
+        if (gi < groups && (gi >> 2) < nb) ld8(xr + 8 * gi, v[k]);
+        else zero8(v[k]);
+      }
+#pragma unroll
+      for (int k = 0; k < kStageGroups; ++k) {
+        const uint32_t gi = tid + k * nthr;
+        if (gi >= gpad) break;  // warp-uniform: gpad is a multiple of 32
+        frag(gi, j, v[k]);
+      }
+    }
+    __syncthreads();
+    return;
+  }
+
+  // with a prologue: one group per thread and row (K <= 8 * nthr), kStageRows rows per round
+  const bool live = tid < groups && (tid >> 2) < nb;
+#pragma unroll 1
+  for (uint32_t j0 = 0, round = 0; j0 < B; j0 += kStageRows, ++round) {
+    float *rr = red + round * 2 * kStageRows * kWarps;
+    float xv[kStageRows][8];
+#pragma unroll
+    for (int r = 0; r < kStageRows; ++r) {
+      if (live && j0 + r < B) ld8(a.x + (size_t)(j0 + r) * a.ldx + 8 * tid, xv[r]);
+      else zero8(xv[r]);
+    }
+    if (a.pro == kProResid) {
+      float mv[kStageRows][8];
+#pragma unroll
+      for (int r = 0; r < kStageRows; ++r) {
+        if (!live || j0 + r >= B) {
+          zero8(mv[r]);
+        } else if (a.pro_mlp_parts <= 1) {
+          ld8(a.pro_mlp + (size_t)(j0 + r) * a.ldx + 8 * tid, mv[r]);
+        } else {
+          // batch 1: partial vectors added in part order, four parts' loads in flight at a time
+#pragma unroll
+          for (int p0 = 0; p0 < kProMaxParts; p0 += 4) {
+            float pv[4][8];
+#pragma unroll
+            for (int p = 0; p < 4; ++p) {
+              if ((uint32_t)(p0 + p) < a.pro_mlp_parts)
+                ld8(a.pro_mlp + (size_t)(p0 + p) * a.pro_mlp_ld + 8 * tid, pv[p]);
+              else
+                zero8(pv[p]);
+            }
+#pragma unroll
+            for (int q = 0; q < 8; ++q) {
+              float m = p0 == 0 ? pv[0][q] : mv[r][q] + pv[0][q];
+#pragma unroll
+              for (int p = 1; p < 4; ++p)
+                if ((uint32_t)(p0 + p) < a.pro_mlp_parts) m += pv[p][q];
+              mv[r][q] = m;
+            }
+          }
+        }
+      }
+      float rm[kStageRows];
+#pragma unroll
+      for (int r = 0; r < kStageRows; ++r) rm[r] = 1.0f;
+      if (a.pro_post_w) {
+        float ss[kStageRows];
+#pragma unroll
+        for (int r = 0; r < kStageRows; ++r) {
+          ss[r] = 0.0f;
+#pragma unroll
+          for (int q = 0; q < 8; ++q) ss[r] = fmaf(mv[r][q], mv[r][q], ss[r]);
+        }
+        cta_sums_1bar<kStageRows>(ss, rr);
+#pragma unroll
+        for (int r = 0; r < kStageRows; ++r) rm[r] = inv_rms(ss[r], K, a.eps);
+      }
+#pragma unroll
+      for (int r = 0; r < kStageRows; ++r) {
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          float m = mv[r][q];
+          if (a.pro_post_w) m = __fmul_rn(__fmul_rn(m, rm[r]), gn.pw[q]);
+          xv[r][q] = __fmul_rn(__fadd_rn(xv[r][q], m), a.pro_scalar);
+        }
+        if (blockIdx.x == 0 && live && j0 + r < B) {
+          float4 *o4 = reinterpret_cast<float4 *>(a.pro_x_out + (size_t)(j0 + r) * a.ldx + 8 * tid);
+          o4[0] = make_float4(xv[r][0], xv[r][1], xv[r][2], xv[r][3]);
+          o4[1] = make_float4(xv[r][4], xv[r][5], xv[r][6], xv[r][7]);
+        }
+      }
+    }
+    float ss[kStageRows];
+#pragma unroll
+    for (int r = 0; r < kStageRows; ++r) {
+      ss[r] = 0.0f;
+#pragma unroll
+      for (int q = 0; q < 8; ++q) ss[r] = fmaf(xv[r][q], xv[r][q], ss[r]);
+    }
+    cta_sums_1bar<kStageRows>(ss, rr + kStageRows * kWarps);
+#pragma unroll
+    for (int r = 0; r < kStageRows; ++r) {
+      const float rs = inv_rms(ss[r], K, a.eps);
+#pragma unroll
+      for (int q = 0; q < 8; ++q) xv[r][q] = live ? __fmul_rn(__fmul_rn(xv[r][q], rs), gn.nw[q]) : 0.0f;
+      if (j0 + r < B && tid < gpad) frag(tid, j0 + r, xv[r]);
+    }
   }
   __syncthreads();
 }
@@ -643,11 +694,11 @@ SX_DEV void gemv_body(const GemvArgs &a, uint8_t *smem, bool prefetch, bool run,
     for (int st = 0; st < S - 1; ++st) issue(st);
   }
   if (!run) return;
-  // batch-1 Q4 calls of a kernel of its own stage x in one fused pass (stage_x_q4b1); its
-  // norm gains are weights, loaded before the dependency wait
-  const bool fast = QT == 4 && NSETS == 1 && standalone && stage_q4b1_ok(a, blockDim.x);
-  GainsQ4B1 gq;
-  if (fast) load_gains_q4b1(a, gq);
+  // Q4 calls of a kernel of their own stage x in one fused pass (stage_x_q4); the norm gains
+  // are weights, loaded before the dependency wait
+  const bool fast = QT == 4 && standalone && stage_q4_ok(a, blockDim.x, L);
+  GainsQ4 gq;
+  if (fast) load_gains_q4(a, gq);
   if (standalone) {
     if (a.pf_slots != nullptr) {
       // the following attention's K/V rows, spread over the CTAs (slot j: thread j / grid of
@@ -675,7 +726,7 @@ SX_DEV void gemv_body(const GemvArgs &a, uint8_t *smem, bool prefetch, bool run,
   const float *xsrc = a.x;
   uint32_t xld = a.ldx;
   if (fast) {
-    stage_x_q4b1(a, smem, L, gq);
+    stage_x_q4(a, smem, L, gq);
   } else if (pro) {
     run_prologue(a, xin, reinterpret_cast<float *>(smem + L.misc + 64));
     xsrc = xin;

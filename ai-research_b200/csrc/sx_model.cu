@@ -181,9 +181,9 @@ sx_status alloc_model(sx_model *m) {
                        B.wu->bytes + B.wd->bytes;
   }
   M_TRY(mk_buf(m, 16ull * 12 * c.num_layers, &m->ind));
-  // attention-block plans: graph 0 with one session, one GPU and Q4_0 layers (the rows of the
+  // attention-block plans: graph 4 with one session, one GPU and Q4_0 layers (the rows of the
   // q|k|v projection are regrouped per kv head, which the packed Q4_0 tiles allow)
-  if (c.reference_graph == 0 && S == 1 && c.tp_size <= 1 && m->lmode == SX_QUANT_Q4) {
+  if (c.reference_graph == 4 && S == 1 && c.tp_size <= 1 && m->lmode == SX_QUANT_Q4) {
     uint64_t rec = 0, opart = 0;
     uint32_t max_kv_heads = 0;
     for (uint32_t l = 0; l < c.num_layers; ++l) {

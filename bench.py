@@ -52,14 +52,14 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-kernel-lines", action="store_true",
                     help="skip the stand-alone config 1-3 kernel measurements")
-    ap.add_argument("--graph", choices=["stream", "persistent", "fused", "separate"],
+    ap.add_argument("--graph", choices=["stream", "persistent", "fused", "block"],
                     default="fused",
                     help="stream: one launch per token with a producer warp per SM streaming "
                          "the weights through a shared-memory ring (one GPU); persistent: one "
-                         "cooperative launch per token with grid barriers; fused: 3 kernels "
-                         "per layer (attention block, gate+up, down; 5 under tensor "
-                         "parallelism) chained with programmatic dependent launch; separate: the "
-                         "fused graph with q|k|v, attention and o as 3 launches")
+                         "cooperative launch per token with grid barriers; fused: 5 kernels "
+                         "per layer chained with programmatic dependent launch; block: the fused "
+                         "graph with q|k|v, attention and o as one attention-block kernel (one "
+                         "GPU)")
     ap.add_argument("--case", choices=["geglu", "q4_head", "attn", "prefill", "sessions", "c1",
                                        "c3"],
                     help="profiling case: launch one kernel of the step standalone "
@@ -619,7 +619,7 @@ def main():
     import sx
 
     cfgd = model_cfg_dict(args.layers)
-    cfgd["reference_graph"] = {"persistent": 2, "stream": 3, "separate": 4}.get(args.graph, 0)
+    cfgd["reference_graph"] = {"persistent": 2, "stream": 3, "block": 4}.get(args.graph, 0)
     eng = sx.Engine(local)
     comm = None
     if world > 1:
@@ -792,12 +792,10 @@ def main():
                            if world > 1 else "single",
             "graph": {2: "one persistent cooperative launch per token (grid barriers)",
                       3: "one streaming launch per token (producer warp per SM, weight ring)",
-                      4: "5 kernels per layer + LM head, programmatic dependent launch"}
+                      4: "3 kernels per layer (attention block, gate+up, down) + LM head, "
+                         "programmatic dependent launch"}
                      .get(cfgd["reference_graph"],
-                          "5 kernels per layer + LM head, programmatic dependent launch"
-                          if world > 1 else
-                          "3 kernels per layer (attention block, gate+up, down) + LM head, "
-                          "programmatic dependent launch"),
+                          "5 kernels per layer + LM head, programmatic dependent launch"),
             "l2": "inputs larger than L2 (8.1 GB of weights+KV read per step)",
             "algorithmic_bytes_per_token": alg["total"],
             "hbm_gbs_per_token_rate": alg["total"] * value / 1e9,

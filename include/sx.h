@@ -332,11 +332,11 @@ typedef struct {
   uint32_t attention_k_eq_v; /* types.zig:58                                            */
   float rms_norm_eps, rope_theta, rope_theta_full, attn_scale;
   uint32_t reference_graph;  /* graph of one token: 1 = the reference's op-by-op graph through
-                                the record API (14 launches per layer); 0 = the fused graph (3
-                                launches per layer for one session on one GPU with Q4_0 layers:
-                                attention block, gate+up, down; 5 otherwise); 4 = the fused graph
-                                with the attention block as its 3 separate launches (q|k|v,
-                                attention, o); 2 = the fused graph's kernels as phases of
+                                the record API (14 launches per layer); 0 = the fused graph (5
+                                launches per layer: q|k|v, attention, o, gate+up, down); 4 = the
+                                fused graph with q|k|v, attention and o as one attention-block
+                                kernel (3 launches per layer; one session, one GPU, Q4_0
+                                layers, else as 0); 2 = the fused graph's kernels as phases of
                                 one persistent cooperative launch per token; 3 = the streaming
                                 decode kernel: one cooperative launch per token in which a
                                 producer warp per SM streams every layer's weights through a

@@ -69,8 +69,8 @@ def run_decode(engine, cfg, seed, steps, start_clock, n_recall=0):
     return results
 
 
-# fused kernels (the attention block as one kernel), the reference's op-by-op graph, one
-# persistent launch, fused kernels with the attention block as three launches
+# fused kernels, the reference's op-by-op graph, one persistent launch, fused kernels with the
+# attention block (q|k|v, attention, o) as one kernel
 GRAPHS = [0, 1, 2, 4]
 
 
@@ -139,9 +139,9 @@ def test_prefill_graph_skips_logits(engine, reference_graph):
         assert model.kernels_per_token(False) == model.kernels_per_token(True) == 1
     else:
         assert model.kernels_per_token(False) < model.kernels_per_token(True)
-        # op-by-op: 14; fused: attention block + gate+up + down; graph 4: q|k|v, attention and
-        # o as separate launches
-        per_layer = {1: 14, 0: 3, 4: 5}[reference_graph]
+        # op-by-op: 14; fused: q|k|v, attention, o, gate+up, down; graph 4: attention block +
+        # gate+up + down
+        per_layer = {1: 14, 0: 5, 4: 3}[reference_graph]
         L = cfg["num_layers"]
         gates = (L - L // 3) if reference_graph == 1 else 0  # recordLayerIndirect's gate
         assert model.kernels_per_token(False) == per_layer * L + gates
@@ -322,7 +322,7 @@ def test_submit_deadline_returns_timeout_not_hang(engine):
 
 
 def test_attention_block_config5_shape_matches_checker(engine):
-    """Graph 0's attention-block kernel (q|k|v, norm + RoPE + cache write, attention and the o
+    """Graph 4's attention-block kernel (q|k|v, norm + RoPE + cache write, attention and the o
     projection in one launch) on config 5's layer shape: one kv head read by 8 q heads, so all
     148 CTAs form one group; head_dim 256; a 640-slot ring with a young window, then a wrapped
     one with a recall tier.  Against the checker with the bf16-cache allowance (a cached element
@@ -331,7 +331,7 @@ def test_attention_block_config5_shape_matches_checker(engine):
     cfg = tiny_cfg(vocab_size=8192, hidden_size=1536, intermediate_size=6144, num_layers=2,
                    num_q_heads=8, num_kv_heads=1, num_global_kv_heads=1, head_dim=256,
                    global_head_dim=256, num_anchors=32, window_size=512, num_recall=96,
-                   full_every=2)
+                   full_every=2, reference_graph=4)
     for start, n_recall in ((3, 0), (4000, 40)):
         res = run_decode(engine, cfg, seed=41, steps=3, start_clock=start, n_recall=n_recall)
         for i, (tok, rtok, lg, rlg) in enumerate(res):
@@ -342,12 +342,12 @@ def test_attention_block_config5_shape_matches_checker(engine):
 
 @pytest.mark.parametrize("kv_f32", [False, True])
 def test_attention_block_equals_separate_launches(engine, engine_f32kv, kv_f32):
-    """The attention block (graph 0) and its three separate launches (graph 4) compute the same
+    """The attention block (graph 4) and its three separate launches (graph 0) compute the same
     token: the block sums the o projection per kv-head group, so the logits agree within the f32
     tolerance, not bit for bit; both also against the checker."""
     eng = engine_f32kv if kv_f32 else engine
     outs = []
-    for g in (0, 4):
+    for g in (4, 0):
         cfg = mid_cfg(kv_bf16=0 if kv_f32 else 1, reference_graph=g)
         outs.append(run_decode(eng, cfg, seed=37, steps=4, start_clock=900, n_recall=4))
     from tests.conftest import assert_close_bf16_operands
