@@ -243,8 +243,16 @@ struct PfAttnArgs {
   uint32_t tokens, sessions, total_slots, num_q, num_kv, head_dim, kv_bf16;
   float scale;
   uint32_t *err;
+  // tensor-core form (pf_attn_tc_ok): work items {first token, tokens} of at most
+  // pf_attn_tc_tokens(G) consecutive tokens of one session; n_items of them
+  const uint32_t *items;
+  uint32_t n_items;
 };
 cudaError_t launch_pf_attn(const PfAttnArgs &a, cudaStream_t s);
+// whether the prefill attention of this shape runs on the tensor cores (then a.items is read)
+bool pf_attn_tc_ok(const PfAttnArgs &a);
+// tokens per tensor-core work item for G q heads per kv head (64 query rows per CTA)
+inline uint32_t pf_attn_tc_tokens(uint32_t g) { return g ? 64u / g : 0u; }
 cudaError_t launch_pf_geglu(const float *g, const float *u, void *h, size_t count, cudaStream_t s);
 
 // ---------------------------------------------------------------------------------------

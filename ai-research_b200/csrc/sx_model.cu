@@ -1031,7 +1031,8 @@ SX_API uint32_t sx_model_kernels_per_token(sx_model *m, int want_logits) {
 // requested rows (normally the last prompt token of each session).
 namespace {
 
-enum PfBuf { PF_XA, PF_XB, PF_MLP, PF_XN, PF_Y, PF_Y2, PF_Q, PF_META, PF_LISTS, PF_OUT, PF_NUM };
+enum PfBuf { PF_XA, PF_XB, PF_MLP, PF_XN, PF_Y, PF_Y2, PF_Q, PF_META, PF_LISTS, PF_OUT, PF_ITEMS,
+             PF_NUM };
 
 sx_status pf_ensure(sx_model *m, uint64_t T) {
   if (T <= m->pf_T) return SX_OK;
@@ -1046,7 +1047,9 @@ sx_status pf_ensure(sx_model *m, uint64_t T) {
       4 * T * H, 4 * T * H, 4 * T * H, 2 * T * wide, 4 * T * ywide, 4 * T * I,
       4 * T * m->max_q, 16 * T, 4 * T * ts,
       // out: row ids [8], normed rows [8][H], tokens [8], logits [8][V]
-      4 * 8 + 4 * 8 * H + 4 * 8 + 4ull * 8 * m->V};
+      4 * 8 + 4 * 8 * H + 4 * 8 + 4ull * 8 * m->V,
+      // tensor-core attention work items {first token, tokens}: up to two item sets
+      16 * T};
   for (int i = 0; i < PF_NUM; ++i)
     M_TRY(sx_host_cuda_status(cudaMalloc(&m->pf[i], bytes[i]), "prefill scratch"));
   m->pf_T = T;
@@ -1148,6 +1151,48 @@ extern "C" SX_API sx_status sx_prefill_batch(sx_model *m, uint32_t T, const floa
   M_TRY(cp(d_cnt, n_active, 4ull * T));
   M_TRY(cp(lists, active, 4ull * T * ts));
   if (n_out) M_TRY(cp(d_rows, out_rows, 4ull * n_out));
+  // tensor-core prefill attention: runs of up to 64 / G consecutive tokens of one session
+  // (G = q heads per kv head of a layer; at most two layer shapes, sliding and full)
+  uint32_t *d_items = (uint32_t *)m->pf[PF_ITEMS];
+  std::vector<std::pair<uint32_t, std::vector<uint32_t>>> item_sets;  // (tokens per item, items)
+  auto items_for = [&](uint32_t g, uint32_t *off, uint32_t *count) -> bool {
+    const uint32_t tb = sx::pf_attn_tc_tokens(g);
+    if (tb == 0) return false;
+    for (size_t i = 0; i < item_sets.size(); ++i)
+      if (item_sets[i].first == tb) {
+        *off = (uint32_t)i * 2 * T;
+        *count = (uint32_t)item_sets[i].second.size() / 2;
+        return true;
+      }
+    if (item_sets.size() == 2) return false;
+    std::vector<uint32_t> it;
+    for (uint32_t t = 0; t < T;) {
+      uint32_t n = 1;
+      while (t + n < T && n < tb && session[t + n] == session[t]) ++n;
+      it.push_back(t);
+      it.push_back(n);
+      t += n;
+    }
+    *off = (uint32_t)item_sets.size() * 2 * T;
+    *count = (uint32_t)it.size() / 2;
+    item_sets.emplace_back(tb, std::move(it));
+    return true;
+  };
+  std::vector<uint32_t> layer_items(2 * L, 0);  // per layer: offset, count (count 0: CUDA cores)
+  for (uint32_t l = 0; l < L; ++l) {
+    const LayerBufs &B = m->L[l];
+    sx::PfAttnArgs probe{};
+    probe.num_q = m->nq;
+    probe.num_kv = B.num_kv;
+    probe.head_dim = B.head_dim;
+    probe.kv_bf16 = c.kv_bf16 ? 1u : 0u;
+    probe.total_slots = ts;
+    if (sx::pf_attn_tc_ok(probe) && B.num_kv)
+      if (!items_for(m->nq / B.num_kv, &layer_items[2 * l], &layer_items[2 * l + 1]))
+        layer_items[2 * l + 1] = 0;
+  }
+  for (size_t i = 0; i < item_sets.size(); ++i)
+    M_TRY(cp(d_items + i * 2 * T, item_sets[i].second.data(), 4ull * item_sets[i].second.size()));
   const float eps = c.rms_norm_eps;
   auto run = [&](cudaError_t ce, const char *what) { return sx_host_cuda_status(ce, what); };
   for (uint32_t l = 0; l < L; ++l) {
@@ -1217,6 +1262,10 @@ extern "C" SX_API sx_status sx_prefill_batch(sx_model *m, uint32_t T, const floa
     aa.kv_bf16 = qa.kv_bf16;
     aa.scale = c.attn_scale;
     aa.err = e->err_dev;
+    if (layer_items[2 * l + 1]) {
+      aa.items = d_items + layer_items[2 * l];
+      aa.n_items = layer_items[2 * l + 1];
+    }
     M_TRY(run(sx::launch_pf_attn(aa, s), "prefill attention"));
     M_TRY(run(sx::launch_prefill_q4(B.wo->d, xn, mlp, T, H, B.q_dim, H, e->err_dev, s),
               "prefill o gemm"));

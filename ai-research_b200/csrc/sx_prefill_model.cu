@@ -313,6 +313,272 @@ __global__ void __launch_bounds__(kPfThreads, 1) pf_attn_kernel(PfAttnArgs a) {
   }
 }
 
+// ---------------------------------------------------------------------------------------
+// Tensor-core form of the prefill attention (head_dim 256, bf16 cache, G = 1, 2, 4 or 8 q heads
+// per kv head).  One CTA per (work item, kv head); a work item is a run of up to 64 / G
+// consecutive tokens of one session (built on the host), i.e. 64 query rows (token-major,
+// row = token * G + head).  The CTA ORs the item's per-token active-slot lists into one
+// 64-bit token mask per ring slot, compacts the slots with a nonzero mask into a key list
+// (ring-slot order), and streams that list's K/V rows through double-buffered shared-memory
+// tiles of 64 keys (cp.async gathers).  Per tile: S = Q K^T and O += P V on mma.m16n8k16 (bf16,
+// f32 accumulate), with q and p split into bf16 hi + lo (16 significant bits; K and V are
+// exact bf16), a key visible to a row only when its token listed that slot (the ring's own
+// causal and window mask), and an online softmax per row in f32.  8 warps: 4 row groups of
+// 16 x 2 halves of head_dim (both halves of a row group compute the same scores).  Each row
+// ends as bf16(O / L), like the CUDA-core kernel.
+constexpr int kTcRows = 64, kTcKeys = 64, kTcD = 256;
+constexpr int kTcStride = kTcD * 2 + 16;  // bytes per shared row: fragment loads conflict-free
+constexpr int kTcThreads = 256;
+constexpr uint32_t kTcMaxSlots = 1024;
+constexpr uint32_t kTcRowBytes = kTcRows * kTcStride;
+// qh | ql | k[2] | v[2] | tile masks [2][64] u64 | slot masks [1024] u64 | key list [1024] u32 |
+// scan [32] u32
+constexpr uint32_t kTcSmem = 6 * kTcRowBytes + 2 * kTcKeys * 8 + kTcMaxSlots * 8 +
+                             kTcMaxSlots * 4 + 32 * 4;
+
+SX_DEV uint32_t pack_bf16x2(float lo, float hi) {
+  const __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<const uint32_t *>(&h);
+}
+// x0, x1 -> bf16 hi pair and the bf16 pair of the residuals
+SX_DEV void split_bf16x2(float x0, float x1, uint32_t &hi, uint32_t &lo) {
+  const __nv_bfloat162 h = __floats2bfloat162_rn(x0, x1);
+  hi = *reinterpret_cast<const uint32_t *>(&h);
+  lo = pack_bf16x2(__fsub_rn(x0, __low2float(h)), __fsub_rn(x1, __high2float(h)));
+}
+SX_DEV void ldsm_x4_trans(uint32_t addr, uint32_t &r0, uint32_t &r1, uint32_t &r2, uint32_t &r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];\n"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+
+template <int G>
+__global__ void __launch_bounds__(kTcThreads, 1) pf_attn_tc_kernel(PfAttnArgs a) {
+  constexpr int TB = kTcRows / G;
+  constexpr uint32_t D = kTcD;
+  extern __shared__ __align__(128) uint8_t tsm[];
+  uint8_t *const qh = tsm, *const ql = qh + kTcRowBytes;
+  uint8_t *const kb = ql + kTcRowBytes;          // [2][64 rows]
+  uint8_t *const vb = kb + 2 * kTcRowBytes;      // [2][64 rows]
+  uint64_t *const tmask = reinterpret_cast<uint64_t *>(vb + 2 * kTcRowBytes);  // [2][64]
+  uint64_t *const umask = tmask + 2 * kTcKeys;   // [ts]
+  uint32_t *const ulist = reinterpret_cast<uint32_t *>(umask + kTcMaxSlots);
+  uint32_t *const scan = ulist + kTcMaxSlots;    // [32]
+  const uint32_t item = blockIdx.x, kvh = blockIdx.y;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, c = lane & 3;
+  const uint32_t ts = a.total_slots;
+  const uint32_t t0 = a.items[2 * item], nt = min(a.items[2 * item + 1], (uint32_t)TB);
+  const uint32_t sess = a.sess[t0];
+  const bool bad = sess >= a.sessions || t0 + nt > a.tokens;
+  if (bad && tid == 0) raise_error(a.err, kDevBadParams);
+  const size_t cache0 = (size_t)(bad ? 0 : sess) * a.cache_ld;
+
+  // 1. slot masks of the item's tokens, and q (hi / lo bf16) in shared memory
+  for (uint32_t i = tid; i < ts; i += kTcThreads) umask[i] = 0ull;
+  __syncthreads();
+  for (uint32_t r = 0; r < (bad ? 0u : nt); ++r) {
+    const uint32_t t = t0 + r, S = min(a.count[t], ts);
+    const uint32_t *list = a.slots + (size_t)t * ts;
+    for (uint32_t j = tid; j < S; j += kTcThreads) {
+      const uint32_t sl = list[j];
+      if (sl < ts) atomicOr(reinterpret_cast<unsigned long long *>(umask + sl), 1ull << r);
+      else raise_error(a.err, kDevBadSlot);
+    }
+  }
+  for (uint32_t pi = tid; pi < kTcRows * D / 2; pi += kTcThreads) {
+    const uint32_t row = pi / (D / 2), dp = pi % (D / 2), tr = row / G, h = row % G;
+    float2 x = make_float2(0.0f, 0.0f);
+    if (!bad && tr < nt)
+      x = *reinterpret_cast<const float2 *>(a.q + ((size_t)(t0 + tr) * a.num_q + kvh * G + h) * D + 2 * dp);
+    uint32_t hi, lo;
+    split_bf16x2(x.x, x.y, hi, lo);
+    *reinterpret_cast<uint32_t *>(qh + row * kTcStride + dp * 4) = hi;
+    *reinterpret_cast<uint32_t *>(ql + row * kTcStride + dp * 4) = lo;
+  }
+  __syncthreads();
+  // 2. key list: the slots with a nonzero mask, in slot order (block-wide exclusive scan)
+  constexpr uint32_t kPer = kTcMaxSlots / kTcThreads;
+  uint32_t cnt = 0;
+#pragma unroll
+  for (uint32_t k = 0; k < kPer; ++k) {
+    const uint32_t i = tid * kPer + k;
+    cnt += (i < ts && umask[i] != 0ull) ? 1u : 0u;
+  }
+  uint32_t incl = cnt;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const uint32_t v = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += v;
+  }
+  if (lane == 31) scan[warp] = incl;
+  __syncthreads();
+  uint32_t wbase = 0, n_u = 0;
+  for (int w = 0; w < kTcThreads / 32; ++w) {
+    if (w < warp) wbase += scan[w];
+    n_u += scan[w];
+  }
+  uint32_t pos = wbase + incl - cnt;
+#pragma unroll
+  for (uint32_t k = 0; k < kPer; ++k) {
+    const uint32_t i = tid * kPer + k;
+    if (i < ts && umask[i] != 0ull) ulist[pos++] = i;
+  }
+  __syncthreads();
+
+  // 3. key tiles: K and V rows of 64 keys per tile gathered with cp.async, double-buffered
+  const uint32_t ntiles = (n_u + kTcKeys - 1) / kTcKeys;
+  const uint8_t *const kc = static_cast<const uint8_t *>(a.k_cache);
+  const uint8_t *const vc = static_cast<const uint8_t *>(a.v_cache);
+  auto issue = [&](uint32_t tile) {
+    const uint32_t buf = tile & 1;
+    uint8_t *kd = kb + buf * kTcRowBytes, *vd = vb + buf * kTcRowBytes;
+    // 64 rows x 32 chunks of 16 B for each of K and V: 16 copies per thread
+    for (uint32_t q = tid; q < kTcKeys * 32; q += kTcThreads) {
+      const uint32_t kr = q >> 5, ch = q & 31, u = tile * kTcKeys + kr;
+      if (u < n_u) {
+        const size_t off = (cache0 + ((size_t)ulist[u] * a.num_kv + kvh) * D) * 2 + ch * 16;
+        cp_async16(smem_u32(kd + kr * kTcStride + ch * 16), kc + off);
+        cp_async16(smem_u32(vd + kr * kTcStride + ch * 16), vc + off);
+      } else {
+        *reinterpret_cast<uint4 *>(kd + kr * kTcStride + ch * 16) = make_uint4(0, 0, 0, 0);
+        *reinterpret_cast<uint4 *>(vd + kr * kTcStride + ch * 16) = make_uint4(0, 0, 0, 0);
+      }
+    }
+    if (tid < kTcKeys) {
+      const uint32_t u = tile * kTcKeys + tid;
+      tmask[buf * kTcKeys + tid] = u < n_u ? umask[ulist[u]] : 0ull;
+    }
+    cp_async_commit();
+  };
+  if (ntiles > 0) issue(0);
+
+  const int rg = warp & 3, dh = warp >> 2;
+  const uint32_t row0 = 16 * rg + g, row1 = row0 + 8;
+  const uint32_t tok0 = row0 / G, tok1 = row1 / G;
+  float o[16][4];
+#pragma unroll
+  for (int j = 0; j < 16; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.0f;
+  float m[2] = {-INFINITY, -INFINITY}, l[2] = {0.0f, 0.0f};
+  const uint8_t *const qh0 = qh + row0 * kTcStride + 4 * c, *const qh1 = qh + row1 * kTcStride + 4 * c;
+  const uint8_t *const ql0 = ql + row0 * kTcStride + 4 * c, *const ql1 = ql + row1 * kTcStride + 4 * c;
+  for (uint32_t tile = 0; tile < ntiles; ++tile) {
+    const uint32_t buf = tile & 1;
+    if (tile + 1 < ntiles) issue(tile + 1);
+    else cp_async_commit();
+    cp_async_wait<1>();
+    __syncthreads();
+    const uint8_t *const kd = kb + buf * kTcRowBytes, *const vd = vb + buf * kTcRowBytes;
+    // S = Q K^T for this warp's 16 rows x 64 keys
+    float sc[8][4];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) sc[j][0] = sc[j][1] = sc[j][2] = sc[j][3] = 0.0f;
+#pragma unroll 4
+    for (int kk = 0; kk < 16; ++kk) {
+      const uint32_t off = kk * 32;
+      uint32_t ah[4], al[4];
+      ah[0] = *reinterpret_cast<const uint32_t *>(qh0 + off);
+      ah[1] = *reinterpret_cast<const uint32_t *>(qh1 + off);
+      ah[2] = *reinterpret_cast<const uint32_t *>(qh0 + off + 16);
+      ah[3] = *reinterpret_cast<const uint32_t *>(qh1 + off + 16);
+      al[0] = *reinterpret_cast<const uint32_t *>(ql0 + off);
+      al[1] = *reinterpret_cast<const uint32_t *>(ql1 + off);
+      al[2] = *reinterpret_cast<const uint32_t *>(ql0 + off + 16);
+      al[3] = *reinterpret_cast<const uint32_t *>(ql1 + off + 16);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const uint8_t *krow = kd + (8 * j + g) * kTcStride + off + 4 * c;
+        const uint32_t b0 = *reinterpret_cast<const uint32_t *>(krow);
+        const uint32_t b1 = *reinterpret_cast<const uint32_t *>(krow + 16);
+        mma_bf16_16816(sc[j], ah, b0, b1);
+        mma_bf16_16816(sc[j], al, b0, b1);
+      }
+    }
+    // visibility (the token listed the slot) and scale, then the online softmax per row
+    const uint64_t *const tm = tmask + buf * kTcKeys;
+    float mx[2] = {-INFINITY, -INFINITY};
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const uint32_t key = 8 * j + 2 * c + (e & 1);
+        const uint32_t tok = e < 2 ? tok0 : tok1;
+        const bool vis = (tm[key] >> tok) & 1ull;
+        sc[j][e] = vis ? sc[j][e] * a.scale : -INFINITY;
+        mx[e >> 1] = fmaxf(mx[e >> 1], sc[j][e]);
+      }
+    float corr[2];
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+      mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], 1));
+      mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], 2));
+      const float mn = fmaxf(m[r], mx[r]);
+      corr[r] = m[r] == -INFINITY ? (mn == -INFINITY ? 1.0f : 0.0f) : expf(m[r] - mn);
+      m[r] = mn;
+    }
+    float ps[2] = {0.0f, 0.0f};
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float p = sc[j][e] == -INFINITY ? 0.0f : expf(sc[j][e] - m[e >> 1]);
+        sc[j][e] = p;
+        ps[e >> 1] += p;
+      }
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+      ps[r] += __shfl_xor_sync(0xffffffffu, ps[r], 1);
+      ps[r] += __shfl_xor_sync(0xffffffffu, ps[r], 2);
+      l[r] = fmaf(l[r], corr[r], ps[r]);
+    }
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      o[j][0] *= corr[0];
+      o[j][1] *= corr[0];
+      o[j][2] *= corr[1];
+      o[j][3] *= corr[1];
+    }
+    // O += P V over this warp's half of head_dim: 4 key steps of 16, 16 d tiles of 8
+    const uint32_t vbase = smem_u32(vd) + (lane & 7) * kTcStride + ((lane >> 3) & 1) * 8 * kTcStride +
+                           (dh * 128 + (lane >> 4) * 8) * 2;
+#pragma unroll
+    for (int s2 = 0; s2 < 4; ++s2) {
+      uint32_t ph[4], pl[4];
+      split_bf16x2(sc[2 * s2][0], sc[2 * s2][1], ph[0], pl[0]);
+      split_bf16x2(sc[2 * s2][2], sc[2 * s2][3], ph[1], pl[1]);
+      split_bf16x2(sc[2 * s2 + 1][0], sc[2 * s2 + 1][1], ph[2], pl[2]);
+      split_bf16x2(sc[2 * s2 + 1][2], sc[2 * s2 + 1][3], ph[3], pl[3]);
+#pragma unroll
+      for (int jd = 0; jd < 16; jd += 2) {
+        uint32_t b00, b01, b10, b11;
+        ldsm_x4_trans(vbase + s2 * 16 * kTcStride + jd * 16, b00, b01, b10, b11);
+        mma_bf16_16816(o[jd], ph, b00, b01);
+        mma_bf16_16816(o[jd], pl, b00, b01);
+        mma_bf16_16816(o[jd + 1], ph, b10, b11);
+        mma_bf16_16816(o[jd + 1], pl, b10, b11);
+      }
+    }
+    __syncthreads();  // every warp is done with this buffer before it is refilled
+  }
+  cp_async_wait<0>();
+  // 4. O / L as bf16
+  if (!bad) {
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+      const uint32_t row = r ? row1 : row0, tr = row / G, h = row % G;
+      if (tr >= nt) continue;
+      uint16_t *out = reinterpret_cast<uint16_t *>(a.out) +
+                      ((size_t)(t0 + tr) * a.num_q + kvh * G + h) * D + dh * 128 + 2 * c;
+#pragma unroll
+      for (int jd = 0; jd < 16; ++jd) {
+        const float v0 = l[r] > 0.0f ? o[jd][2 * r] / l[r] : 0.0f;
+        const float v1 = l[r] > 0.0f ? o[jd][2 * r + 1] / l[r] : 0.0f;
+        const uint32_t pk = (uint32_t)bf16_bits_rne(v0) | ((uint32_t)bf16_bits_rne(v1) << 16);
+        *reinterpret_cast<uint32_t *>(out + jd * 8) = pk;
+      }
+    }
+  }
+}
+
 // h = bf16(gelu_tanh(gate) * up), elementwise over [rows][n] (fused_mlp_q4.wgsl epilogue)
 __global__ void pf_geglu_kernel(const float *g, const float *u, uint16_t *h, size_t count) {
   for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < count;
@@ -346,6 +612,15 @@ cudaError_t launch_attn_g(const PfAttnArgs &a, cudaStream_t s) {
   }
 }
 
+template <int G>
+cudaError_t launch_attn_tc(const PfAttnArgs &a, cudaStream_t s) {
+  cudaError_t e = cudaFuncSetAttribute(pf_attn_tc_kernel<G>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kTcSmem);
+  if (e != cudaSuccess) return e;
+  pf_attn_tc_kernel<G><<<dim3(a.n_items, a.num_kv), kTcThreads, kTcSmem, s>>>(a);
+  return cudaGetLastError();
+}
+
 }  // namespace
 
 cudaError_t launch_pf_norm(const PfNormArgs &a, uint32_t rows, bool out_bf16, cudaStream_t s) {
@@ -375,8 +650,25 @@ cudaError_t launch_pf_qkv_rope(const PfQkvArgs &a, uint32_t tokens, cudaStream_t
   }
 }
 
+bool pf_attn_tc_ok(const PfAttnArgs &a) {
+  if (a.num_kv == 0 || a.num_q % a.num_kv) return false;
+  const uint32_t g = a.num_q / a.num_kv;
+  return (g == 1 || g == 2 || g == 4 || g == 8) && a.head_dim == kTcD && a.kv_bf16 &&
+         a.total_slots <= kTcMaxSlots;
+}
+
 cudaError_t launch_pf_attn(const PfAttnArgs &a, cudaStream_t s) {
   if (a.num_kv == 0 || a.num_q % a.num_kv) return cudaErrorInvalidValue;
+  if (a.items != nullptr && pf_attn_tc_ok(a)) {
+    if (a.n_items == 0) return cudaSuccess;
+    switch (a.num_q / a.num_kv) {
+      case 1: return launch_attn_tc<1>(a, s);
+      case 2: return launch_attn_tc<2>(a, s);
+      case 4: return launch_attn_tc<4>(a, s);
+      case 8: return launch_attn_tc<8>(a, s);
+      default: return cudaErrorInvalidValue;
+    }
+  }
   switch (a.head_dim) {
     case 64: return a.kv_bf16 ? launch_attn_g<2, true>(a, s) : launch_attn_g<2, false>(a, s);
     case 128: return a.kv_bf16 ? launch_attn_g<4, true>(a, s) : launch_attn_g<4, false>(a, s);

@@ -140,10 +140,12 @@ def test_prefill_rejects_bad_tokens(engine):
         model.prefill_batch([p], rings, [0], sessions=[2])  # session beyond the model's two
 
 
-@pytest.mark.parametrize("head_dim,nq,nkv", [(256, 8, 1), (128, 4, 2), (64, 4, 2)])
+@pytest.mark.parametrize("head_dim,nq,nkv", [(256, 8, 1), (256, 4, 2), (256, 2, 2), (128, 4, 2),
+                                             (64, 4, 2)])
 def test_prefill_bf16_kv_matches_checker(engine, head_dim, nq, nkv):
-    """The bf16-KV prefill attention (the cached-row loads of pf_attn_kernel for 8, 4 and 2
-    elements per lane) against the checker in its bf16-cache, bf16-operand mode."""
+    """The bf16-KV prefill attention against the checker in its bf16-cache, bf16-operand mode:
+    head_dim 256 runs the tensor-core kernel (8, 2 and 1 q heads per kv head: 8, 32 and 64
+    tokens per work item), 128 and 64 the CUDA-core kernel's 4- and 2-element cached-row loads."""
     cfg = tiny_cfg(num_sessions=3, num_layers=3, kv_bf16=1, head_dim=head_dim,
                    global_head_dim=head_dim, num_q_heads=nq, num_kv_heads=nkv,
                    num_global_kv_heads=nkv, hidden_size=512, intermediate_size=1024)
@@ -195,3 +197,23 @@ def test_config5_shape_ragged_prefill_bf16_kv_then_batch8_decode(engine):
             check_token(int(got[s]), rtok, rlg, f"session {s} decode step {step}")
             tokens[s] = int(got[s])
         clocks = [c + 1 for c in clocks]
+
+
+def test_long_prompts_tensor_core_attention_spans_several_key_tiles(engine):
+    """Prompts of 300 and 181 tokens on config 5's head shape (one kv head, 8 q heads, 640-slot
+    ring): each work item's key union covers several 64-key tiles, so the online softmax runs
+    across tiles and the last tile is partly empty; against the checker."""
+    from tests.test_gpu_batch import c5_cfg
+    cfg = c5_cfg(num_layers=2, num_sessions=2)
+    seed = 91
+    model = sx.Model(engine, sx.model_config(**cfg))
+    model.synth_weights(seed)
+    lens = [300, 181]
+    prompts = prompts_for(cfg, seed, lens)
+    rings = [sx.Ring(1, cfg["num_anchors"], cfg["window_size"], cfg["num_recall"]) for _ in lens]
+    logits = np.zeros((2, cfg["vocab_size"]), np.float32)
+    toks = model.prefill_batch(prompts, rings, [0] * 2, logits_out=logits)
+    for s, p in enumerate(prompts):
+        _, rtok, rlg = checker_prefill(cfg, seed, p)
+        assert_close(logits[s], rlg, what=f"session {s} prefill logits", frac=BF16_KV_FRAC)
+        check_token(int(toks[s]), rtok, rlg, f"session {s} prefill")
