@@ -312,6 +312,14 @@ sx_status run_op(sx_engine *e, cudaStream_t s, const Op &op, uint32_t *kernels) 
       if (!a.at.inv_freq) return fst;
       return cuda_status(sx::launch_attn_block(a, s), "attention block launch");
     }
+    case OP_ATTN_O: {
+      *kernels += 1;
+      sx::AttnOArgs a = op.ao;
+      sx_status fst = SX_OK;
+      a.at.inv_freq = engine_inv_freq(e, op.attn_rot, op.attn_theta, &fst);
+      if (!a.at.inv_freq) return fst;
+      return cuda_status(sx::launch_attn_o(a, s), "attention + o launch");
+    }
     case OP_ALLREDUCE:
       return sx_host_allreduce(op.comm, static_cast<float *>(op.dev), op.u[0], s);
     case OP_ALLGATHER:
@@ -626,6 +634,8 @@ SX_API sx_status sx_engine_create(int device, sx_quant_mode mode, uint32_t flags
     st = cuda_status(sx::prepare_ops_kernels(), "attention kernel attributes");
     if (st) break;
     st = cuda_status(sx::prepare_attn_block_kernels(), "attention block kernel attributes");
+    if (st) break;
+    st = cuda_status(sx::prepare_attn_o_kernels(), "attention + o kernel attributes");
     if (st) break;
     st = cuda_status(sx::prepare_persist_kernel(), "persistent kernel attributes");
     if (st) break;
@@ -985,7 +995,7 @@ SX_API sx_status sx_cmd_end(sx_cmd *c) {
   for (const Op &op : c->ops) {
     sx_status fst = SX_OK;
     if (op.kind == OP_QKV_ROPE && !engine_inv_freq(e, op.u[3], op.f[0], &fst)) return fst;
-    if ((op.kind == OP_ATTN_FUSED || op.kind == OP_ATTN_BLOCK) &&
+    if ((op.kind == OP_ATTN_FUSED || op.kind == OP_ATTN_BLOCK || op.kind == OP_ATTN_O) &&
         !engine_inv_freq(e, op.attn_rot, op.attn_theta, &fst))
       return fst;
   }

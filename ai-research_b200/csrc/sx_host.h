@@ -73,6 +73,7 @@ enum OpKind {
   OP_ALLGATHER,   // tensor parallel: bind[0] (u[0] u32 words per rank) -> bind[1]
   OP_TP_ARGMAX,   // tensor parallel: merge u[0] ranks' argmax candidates bind[0] -> bind[1]
   OP_ATTN_BLOCK,  // q|k|v GEMV + qkv_rope + attention + o GEMV as one kernel (model graph)
+  OP_ATTN_O,      // qkv_rope + attention + per-kv-head o projection (model graph)
 };
 
 struct Op {
@@ -91,6 +92,7 @@ struct Op {
   sx::GemvArgs gemv{};
   sx::AttnFusedArgs attnf{};
   sx::AttnBlockArgs ab{};   // OP_ATTN_BLOCK
+  sx::AttnOArgs ao{};       // OP_ATTN_O
   uint32_t attn_rot = 0;
   float attn_theta = 0.0f;
   sx_comm *comm = nullptr;  // OP_ALLREDUCE / OP_ALLGATHER

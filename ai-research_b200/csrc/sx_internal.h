@@ -202,6 +202,21 @@ bool attn_block_plan(uint32_t hidden, uint32_t num_q, uint32_t num_kv, uint32_t 
                      AttnBlockPlan *plan);
 cudaError_t launch_attn_block(const AttnBlockArgs &a, cudaStream_t s);
 constexpr uint32_t kAttnBlockSmemLimit = 227 * 1024 - 1024;  // dynamic, below the opt-in max
+
+// The cluster attention with the o projection of each kv head's q heads folded in
+// (sx_attn_o.cu): one session, one GPU, Q4_0 o projection; the o rows come out as one partial
+// vector per kv head, opart[kv head][row], which the gate+up prologue adds in kv-head order.
+struct AttnOArgs {
+  AttnFusedArgs at;   // the fused attention's arguments (out: the G x head_dim rows per head)
+  const void *wo;     // packed Q4_0 o projection [o_rows][num_q * head_dim]
+  float *opart;       // [num_kv][o_rows]
+  uint32_t o_rows;    // hidden size
+  uint32_t o_tiles;   // W_o tiles per CTA the shared memory holds (attn_o_plan)
+};
+bool attn_o_plan(uint32_t o_rows, uint32_t num_q, uint32_t num_kv, uint32_t head_dim,
+                 uint32_t total_slots, uint32_t smem_limit, uint32_t *o_tiles);
+cudaError_t launch_attn_o(const AttnOArgs &a, cudaStream_t s);
+cudaError_t prepare_attn_o_kernels();
 cudaError_t prepare_attn_block_kernels();
 
 // ---------------------------------------------------------------------------------------

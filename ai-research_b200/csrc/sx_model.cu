@@ -32,6 +32,8 @@ struct LayerBufs {
   sx_set *s_gate = nullptr;     // {x, x_prev, indirect records} (model_gpu.zig:156)
   // the layer's attention block as one kernel (sx_attn_block.cu); ctas == 0: not eligible
   sx::AttnBlockPlan ab{};
+  // the cluster attention with the o projection folded in (sx_attn_o.cu); 0: not eligible
+  uint32_t ao_tiles = 0;
 };
 
 enum Tensor : uint32_t {
@@ -181,6 +183,18 @@ sx_status alloc_model(sx_model *m) {
                        B.wu->bytes + B.wd->bytes;
   }
   M_TRY(mk_buf(m, 16ull * 12 * c.num_layers, &m->ind));
+  // attention + o plans: graph 0 with one session, one GPU and Q4_0 layers
+  if (c.reference_graph == 0 && S == 1 && c.tp_size <= 1 && m->lmode == SX_QUANT_Q4) {
+    uint64_t opart = 0;
+    for (uint32_t l = 0; l < c.num_layers; ++l) {
+      LayerBufs &B = m->L[l];
+      if (!sx::attn_o_plan(H, m->nq, B.num_kv, B.head_dim, m->total_slots,
+                           sx::kAttnBlockSmemLimit, &B.ao_tiles))
+        B.ao_tiles = 0;
+      if (B.ao_tiles && (uint64_t)B.num_kv * H > opart) opart = (uint64_t)B.num_kv * H;
+    }
+    if (opart) M_TRY(mk_buf(m, 4 * opart, &m->ab_opart));
+  }
   // attention-block plans: graph 4 with one session, one GPU and Q4_0 layers (the rows of the
   // q|k|v projection are regrouped per kv head, which the packed Q4_0 tiles allow)
   if (c.reference_graph == 4 && S == 1 && c.tp_size <= 1 && m->lmode == SX_QUANT_Q4) {
@@ -455,6 +469,7 @@ sx_status record_forward_fused(sx_model *m, sx_cmd *cmd, bool logits, bool io,
     // q | k | v with the input norm (and, after layer 0, the previous layer's residual)
     // q | k | v rows of session j at qkv + j * base (base = q_dim + 2 kv_dim of this layer)
     const bool blk = persistent == kPersistNone && nb == 1 && !tp && B.ab.ctas != 0;
+    const bool ao = persistent == kPersistNone && nb == 1 && !tp && B.ao_tiles != 0;
     sx::GemvArgs q{};
     const sx_buffer *w3[3] = {B.wq, B.wk, B.wv};
     uint32_t r3[3] = {B.q_dim, B.kv_dim, B.kv_dim};
@@ -556,6 +571,18 @@ sx_status record_forward_fused(sx_model *m, sx_cmd *cmd, bool logits, bool io,
       ab.attn_rot = B.rot;
       ab.attn_theta = B.theta;
       sx_host_push_op(cmd, ab);
+    } else if (ao) {
+      // qkv_rope + attention + this kv head's share of the o projection as one cluster kernel;
+      // the o rows come out as one partial vector per kv head, summed by the gate+up prologue
+      Op op{OP_ATTN_O};
+      op.ao.at = A;
+      op.ao.wo = B.wo->d;
+      op.ao.opart = (float *)m->ab_opart->d;
+      op.ao.o_rows = H;
+      op.ao.o_tiles = B.ao_tiles;
+      op.attn_rot = B.rot;
+      op.attn_theta = B.theta;
+      sx_host_push_op(cmd, op);
     } else {
       sx_host_push_op(cmd, at);
 
@@ -572,7 +599,7 @@ sx_status record_forward_fused(sx_model *m, sx_cmd *cmd, bool logits, bool io,
     g.w[0][1] = B.wu->d;
     g.pro = sx::kProResid;
     g.pro_mlp = (const float *)m->mlp_out->d;
-    if (blk) {
+    if (blk || ao) {
       g.pro_mlp = (const float *)m->ab_opart->d;
       g.pro_mlp_parts = B.num_kv;
       g.pro_mlp_ld = H;

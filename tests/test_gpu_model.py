@@ -139,9 +139,9 @@ def test_prefill_graph_skips_logits(engine, reference_graph):
         assert model.kernels_per_token(False) == model.kernels_per_token(True) == 1
     else:
         assert model.kernels_per_token(False) < model.kernels_per_token(True)
-        # op-by-op: 14; fused: q|k|v, attention, o, gate+up, down; graph 4: attention block +
-        # gate+up + down
-        per_layer = {1: 14, 0: 5, 4: 3}[reference_graph]
+        # op-by-op: 14; fused: q|k|v, attention with the o projection folded in, gate+up,
+        # down; graph 4: attention block + gate+up + down
+        per_layer = {1: 14, 0: 4, 4: 3}[reference_graph]
         L = cfg["num_layers"]
         gates = (L - L // 3) if reference_graph == 1 else 0  # recordLayerIndirect's gate
         assert model.kernels_per_token(False) == per_layer * L + gates
