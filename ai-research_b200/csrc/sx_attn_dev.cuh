@@ -390,6 +390,56 @@ SX_HD uint32_t attn_cluster_floats(int g, uint32_t d, uint32_t cl) {
          g * cl;
 }
 
+// The cluster merge of attn_cluster_item: every CTA holds its (M, L, O[D]) per q head in
+// rec [G][D + 2]; after the cluster barrier CTA r merges slice r of the G x D outputs from all
+// CL records over distributed shared memory, in rank order.
+template <int G, uint32_t D, int W>
+SX_DEV void attn_cluster_merge(const AttnFusedArgs &a, uint32_t kvh, float *rec, float *fw,
+                               float *ls, float *fl, int t) {
+  namespace cg = cooperative_groups;
+  cg::cluster_group cl = cg::this_cluster();
+  const uint32_t rank = cl.block_rank(), ncl = cl.num_blocks();
+  cl.sync();
+  // weights of the CL records per head: every CTA reads all CL x G (M, L) pairs at once
+  // (independent remote reads), then one thread per head folds them locally in record order
+  for (uint32_t i = t; i < G * ncl; i += W * 32) {
+    const uint32_t h = i / ncl, r = i % ncl;
+    const float *rr = cl.map_shared_rank(rec, r) + h * (D + 2);
+    fw[i] = rr[0];
+    fl[i] = rr[1];
+  }
+  __syncthreads();
+  if (t < G) {
+    float M = -INFINITY;
+    for (uint32_t r = 0; r < ncl; ++r) M = fmaxf(M, fw[t * ncl + r]);
+    float L = 0.0f;
+    for (uint32_t r = 0; r < ncl; ++r) {
+      const float f = M == -INFINITY ? 0.0f : expf(fw[t * ncl + r] - M);
+      L = fmaf(fl[t * ncl + r], f, L);
+      fw[t * ncl + r] = f;
+    }
+    ls[t] = L;
+  }
+  __syncthreads();
+  // this CTA's slice of the G x D outputs: the CL remote values of an output are loaded
+  // together, then summed in record order
+  const uint32_t per = (G * D + ncl - 1) / ncl, lo = rank * per, hi = min(G * D, lo + per);
+  for (uint32_t idx = lo + t; idx < hi; idx += W * 32) {
+    const uint32_t h = idx / D, d = idx % D;
+    float v[kClusterMax];
+#pragma unroll
+    for (uint32_t r = 0; r < (uint32_t)kClusterMax; ++r)
+      v[r] = r < ncl ? cl.map_shared_rank(rec, r)[h * (D + 2) + 2 + d] : 0.0f;
+    float O = 0.0f;
+#pragma unroll
+    for (uint32_t r = 0; r < (uint32_t)kClusterMax; ++r)
+      if (r < ncl) O = fmaf(v[r], fw[h * ncl + r], O);
+    const float L = ls[h];
+    a.out[(size_t)(kvh * G + h) * D + d] = L > 0.0f ? O / L : 0.0f;
+  }
+  cl.sync();  // the records stay readable until every CTA of the cluster is done
+}
+
 template <int DPL, int G, bool BF16, typename Wait>
 SX_DEV void attn_cluster_item(const AttnFusedArgs &a, uint32_t kvh, float *sh, Wait wait) {
   namespace cg = cooperative_groups;
@@ -430,45 +480,276 @@ SX_DEV void attn_cluster_item(const AttnFusedArgs &a, uint32_t kvh, float *sh, W
       rec[h * (D + 2) + 1] = L;
     }
   });
-  cl.sync();
-  // weights of the CL records per head: every CTA reads all CL x G (M, L) pairs at once
-  // (independent remote reads), then one thread per head folds them locally in record order
-  for (uint32_t i = t; i < G * ncl; i += W * 32) {
-    const uint32_t h = i / ncl, r = i % ncl;
-    const float *rr = cl.map_shared_rank(rec, r) + h * (D + 2);
-    fw[i] = rr[0];
-    fl[i] = rr[1];
+  attn_cluster_merge<G, D, W>(a, kvh, rec, fw, ls, fl, t);
+}
+
+// ---------------------------------------------------------------------------------------
+// Tensor-core form of the cluster work item for 8 q heads per kv head, head_dim 256 and a
+// bf16 cache (the shape of configs 3 and 5), run by the same 256 threads and cluster merge.
+// Before the dependency wait the CTA gathers its 64 slots' K and V rows into padded shared
+// rows with cp.async and stages the norm gains and the RoPE table; after it, one warp per
+// vector normalises and rotates the 8 q heads and the new k / v (qkv_rope.wgsl semantics, as
+// attn_norm_rope), q goes to shared memory as bf16 hi + lo rows 0..7 of a 16-row tile (rows
+// 8..15 zero), the current slot's row takes the new k / v, and
+//   S = Q K^T: warp w forms keys 8w..8w+7 for all 16 rows (mma.m16n8k16, bf16, f32 acc);
+//   the CTA's per-head maximum and sum over its 64 keys meet in shared memory;
+//   O = P V: warp w forms head_dim columns 32w..32w+31 (P split hi + lo, V by ldmatrix.trans);
+// and the CTA's (M, L, O) per head goes to the cluster merge.
+constexpr uint32_t kTcaStride = 528;  // bytes per shared row: 256 bf16 + 16 pad
+struct TcaLayout {
+  static constexpr uint32_t kt = 0, vt = kt + 64 * kTcaStride, qh = vt + 64 * kTcaStride,
+                            ql = qh + 16 * kTcaStride, qs = ql + 16 * kTcaStride,
+                            kn = qs + 8 * 256 * 4, vn = kn + 256 * 4, qg = vn + 256 * 4,
+                            kg = qg + 256 * 4, sn = kg + 256 * 4, cs = sn + 128 * 4,
+                            sp = cs + 128 * 4, wmax = sp + 8 * 64 * 4, wsum = wmax + 8 * 8 * 4,
+                            rec = wsum + 8 * 8 * 4, fw = rec + 8 * 258 * 4,
+                            fl = fw + 8 * kClusterMax * 4, ls = fl + 8 * kClusterMax * 4,
+                            slots = ls + 8 * 4, misc = slots + 64 * 4, total = misc + 16;
+};
+SX_DEV void tca_ldsm_x4_trans(uint32_t addr, uint32_t &r0, uint32_t &r1, uint32_t &r2,
+                              uint32_t &r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];\n"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+SX_DEV void tca_split(float x0, float x1, uint32_t &hi, uint32_t &lo) {
+  const __nv_bfloat162 h = __floats2bfloat162_rn(x0, x1);
+  hi = *reinterpret_cast<const uint32_t *>(&h);
+  const __nv_bfloat162 l = __floats2bfloat162_rn(__fsub_rn(x0, __low2float(h)), __fsub_rn(x1, __high2float(h)));
+  lo = *reinterpret_cast<const uint32_t *>(&l);
+}
+
+template <typename Wait>
+SX_DEV void attn_cluster_item_tc(const AttnFusedArgs &a, uint32_t kvh, float *sh, Wait wait) {
+  namespace cg = cooperative_groups;
+  cg::cluster_group cl = cg::this_cluster();
+  constexpr int G = 8, W = kFusedWarps;
+  constexpr uint32_t D = 256;
+  using TL = TcaLayout;
+  uint8_t *const sm = reinterpret_cast<uint8_t *>(sh);
+  const uint32_t rank = cl.block_rank();
+  const int t = threadIdx.x, warp = t >> 5, lane = t & 31, g = lane >> 2, c = lane & 3;
+  uint32_t *const slot_s = reinterpret_cast<uint32_t *>(sm + TL::slots);
+  uint32_t *const cur_s = reinterpret_cast<uint32_t *>(sm + TL::misc);
+  float *const qs = reinterpret_cast<float *>(sm + TL::qs);
+  float *const kn = reinterpret_cast<float *>(sm + TL::kn);
+  float *const vn = reinterpret_cast<float *>(sm + TL::vn);
+  float *const qg = reinterpret_cast<float *>(sm + TL::qg);
+  float *const kg = reinterpret_cast<float *>(sm + TL::kg);
+  float *const sn = reinterpret_cast<float *>(sm + TL::sn);
+  float *const cs = reinterpret_cast<float *>(sm + TL::cs);
+  float *const sp = reinterpret_cast<float *>(sm + TL::sp);
+  float *const wmax = reinterpret_cast<float *>(sm + TL::wmax);
+  float *const wsum = reinterpret_cast<float *>(sm + TL::wsum);
+  float *const rec = reinterpret_cast<float *>(sm + TL::rec);
+
+  const uint32_t slot = a.step[1];
+  uint32_t S = a.step[2];
+  const bool bad_step = S > a.total_slots || slot >= a.total_slots;
+  S = S > a.total_slots ? a.total_slots : S;
+  const uint32_t s0 = rank * kClusterSlots, s1 = min(S, s0 + kClusterSlots);
+  const uint32_t ns = s1 > s0 ? s1 - s0 : 0;
+
+  // 1. slot indices, K / V rows, norm gains and the RoPE table (none depends on q|k|v)
+  if (t == 0) *cur_s = 0xFFFFFFFFu;
+  __syncthreads();
+  if (t < kClusterSlots) {
+    const uint32_t sl = (uint32_t)t < ns ? __ldcg(a.slots + s0 + t) : 0xFFFFFFFFu;
+    slot_s[t] = sl;
+    if (sl == slot) *cur_s = (uint32_t)t;
   }
   __syncthreads();
-  if (t < G) {
-    float M = -INFINITY;
-    for (uint32_t r = 0; r < ncl; ++r) M = fmaxf(M, fw[t * ncl + r]);
-    float L = 0.0f;
-    for (uint32_t r = 0; r < ncl; ++r) {
-      const float f = M == -INFINITY ? 0.0f : expf(fw[t * ncl + r] - M);
-      L = fmaf(fl[t * ncl + r], f, L);
-      fw[t * ncl + r] = f;
+  for (uint32_t q = t; q < kClusterSlots * 32; q += W * 32) {
+    const uint32_t li = q >> 5, ch = q & 31, sl = slot_s[li];
+    uint8_t *kd = sm + TL::kt + li * kTcaStride + ch * 16;
+    uint8_t *vd = sm + TL::vt + li * kTcaStride + ch * 16;
+    if (sl < a.total_slots && sl != slot) {
+      const size_t off = ((size_t)sl * a.kv_dim + (size_t)kvh * D) * 2 + ch * 16;
+      cp_async16(smem_u32(kd), static_cast<const uint8_t *>(a.k_cache) + off);
+      cp_async16(smem_u32(vd), static_cast<const uint8_t *>(a.v_cache) + off);
+    } else {
+      *reinterpret_cast<uint4 *>(kd) = make_uint4(0, 0, 0, 0);
+      *reinterpret_cast<uint4 *>(vd) = make_uint4(0, 0, 0, 0);
     }
-    ls[t] = L;
+  }
+  cp_async_commit();
+  const uint32_t half = a.rotary_dim / 2;
+  const float fclock = (float)a.step[0];
+  for (uint32_t i = t; i < D; i += W * 32) {
+    qg[i] = a.q_norm_w[i];
+    kg[i] = a.k_norm_w[i];
+  }
+  for (uint32_t i = t; i < D / 2; i += W * 32) {
+    float sv = 0.0f, cv = 1.0f;
+    if (i < half) sincosf(__fmul_rn(fclock, a.inv_freq[i]), &sv, &cv);
+    sn[i] = sv;
+    cs[i] = cv;
+  }
+  wait();
+  if (bad_step && t == 0 && rank == 0 && kvh == 0) raise_error(a.err, kDevBadParams);
+  __syncthreads();
+  // 2. q / k norm + RoPE, k / v in the cache precision; rank 0 stores the new k / v
+  const bool slot_ok = slot < a.total_slots;
+  for (int vi = warp; vi < G + 2; vi += W) {
+    const float *src = vi < G ? a.q + (size_t)(kvh * G + vi) * D
+                              : (vi == G || a.k_eq_v ? a.k : a.v) + (size_t)kvh * D;
+    float *buf = vi < G ? qs + vi * D : (vi == G ? kn : vn);
+    float x[8];
+    float ss = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      x[i] = __ldcg(src + lane * 8 + i);
+      ss = fmaf(x[i], x[i], ss);
+    }
+    ss = warp_sum(ss);
+    const float rs = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)D), a.eps)));
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const uint32_t e = lane * 8 + i;
+      buf[e] = vi <= G ? __fmul_rn(__fmul_rn(x[i], rs), vi < G ? qg[e] : kg[e]) : __fmul_rn(x[i], rs);
+    }
+    __syncwarp();
+    if (vi <= G) {
+      for (uint32_t e = lane; e < half; e += 32) {
+        const float v0 = buf[e], v1 = buf[e + half];
+        buf[e] = __fsub_rn(__fmul_rn(v0, cs[e]), __fmul_rn(v1, sn[e]));
+        buf[e + half] = __fadd_rn(__fmul_rn(v0, sn[e]), __fmul_rn(v1, cs[e]));
+      }
+      __syncwarp();
+    }
+    if (vi >= G) {
+      void *cache = vi == G ? a.k_cache : a.v_cache;
+      const size_t new_off = (size_t)slot * a.kv_dim + (size_t)kvh * D;
+      for (uint32_t d = lane; d < D; d += 32) {
+        const uint16_t b = bf16_bits_rne(buf[d]);
+        buf[d] = bf16_bits_to_f32(b);
+        if (rank == 0 && slot_ok) reinterpret_cast<uint16_t *>(cache)[new_off + d] = b;
+      }
+    }
+  }
+  cp_async_wait<0>();
+  __syncthreads();
+  // 3. q as bf16 hi / lo rows (8..15 zero); the current slot's row takes the new k / v
+  const uint32_t cur = *cur_s;
+  for (uint32_t p = t; p < 16 * (D / 2); p += W * 32) {
+    const uint32_t row = p / (D / 2), dp = p % (D / 2);
+    float x0 = 0.0f, x1 = 0.0f;
+    if (row < (uint32_t)G) {
+      x0 = qs[row * D + 2 * dp];
+      x1 = qs[row * D + 2 * dp + 1];
+    }
+    uint32_t hi, lo;
+    tca_split(x0, x1, hi, lo);
+    *reinterpret_cast<uint32_t *>(sm + TL::qh + row * kTcaStride + dp * 4) = hi;
+    *reinterpret_cast<uint32_t *>(sm + TL::ql + row * kTcaStride + dp * 4) = lo;
+    if (cur < (uint32_t)kClusterSlots && row == 0) {
+      uint32_t kh, kl, vh, vl;
+      tca_split(kn[2 * dp], kn[2 * dp + 1], kh, kl);  // bf16-exact: the lo half is zero
+      tca_split(vn[2 * dp], vn[2 * dp + 1], vh, vl);
+      *reinterpret_cast<uint32_t *>(sm + TL::kt + cur * kTcaStride + dp * 4) = kh;
+      *reinterpret_cast<uint32_t *>(sm + TL::vt + cur * kTcaStride + dp * 4) = vh;
+    }
   }
   __syncthreads();
-  // this CTA's slice of the G x D outputs: the CL remote values of an output are loaded
-  // together, then summed in record order
-  const uint32_t per = (G * D + ncl - 1) / ncl, lo = rank * per, hi = min(G * D, lo + per);
-  for (uint32_t idx = lo + t; idx < hi; idx += W * 32) {
-    const uint32_t h = idx / D, d = idx % D;
-    float v[kClusterMax];
-#pragma unroll
-    for (uint32_t r = 0; r < (uint32_t)kClusterMax; ++r)
-      v[r] = r < ncl ? cl.map_shared_rank(rec, r)[h * (D + 2) + 2 + d] : 0.0f;
-    float O = 0.0f;
-#pragma unroll
-    for (uint32_t r = 0; r < (uint32_t)kClusterMax; ++r)
-      if (r < ncl) O = fmaf(v[r], fw[h * ncl + r], O);
-    const float L = ls[h];
-    a.out[(size_t)(kvh * G + h) * D + d] = L > 0.0f ? O / L : 0.0f;
+  // 4. S = Q K^T: warp w, keys 8w .. 8w + 7
+  float sc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+  {
+    const uint8_t *q0 = sm + TL::qh + g * kTcaStride + 4 * c, *q1 = q0 + 8 * kTcaStride;
+    const uint8_t *l0 = sm + TL::ql + g * kTcaStride + 4 * c, *l1 = l0 + 8 * kTcaStride;
+    const uint8_t *kr = sm + TL::kt + (8 * warp + g) * kTcaStride + 4 * c;
+#pragma unroll 4
+    for (int kk = 0; kk < 16; ++kk) {
+      const uint32_t off = kk * 32;
+      uint32_t ah[4], al[4];
+      ah[0] = *reinterpret_cast<const uint32_t *>(q0 + off);
+      ah[1] = *reinterpret_cast<const uint32_t *>(q1 + off);
+      ah[2] = *reinterpret_cast<const uint32_t *>(q0 + off + 16);
+      ah[3] = *reinterpret_cast<const uint32_t *>(q1 + off + 16);
+      al[0] = *reinterpret_cast<const uint32_t *>(l0 + off);
+      al[1] = *reinterpret_cast<const uint32_t *>(l1 + off);
+      al[2] = *reinterpret_cast<const uint32_t *>(l0 + off + 16);
+      al[3] = *reinterpret_cast<const uint32_t *>(l1 + off + 16);
+      const uint32_t b0 = *reinterpret_cast<const uint32_t *>(kr + off);
+      const uint32_t b1 = *reinterpret_cast<const uint32_t *>(kr + off + 16);
+      mma_bf16_16816(sc, ah, b0, b1);
+      mma_bf16_16816(sc, al, b0, b1);
+    }
   }
-  cl.sync();  // the records stay readable until every CTA of the cluster is done
+  // rows g (a head) of keys 8w + 2c, + 1; invalid keys and padding rows take no weight
+  float p[2];
+  {
+    float m = -INFINITY;
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      const uint32_t li = 8 * warp + 2 * c + e, sl = slot_s[li];
+      const bool live = li < ns && sl < a.total_slots;
+      if (li < ns && sl >= a.total_slots) raise_error(a.err, kDevBadSlot);
+      p[e] = live ? sc[e] * a.scale : -INFINITY;
+      m = fmaxf(m, p[e]);
+    }
+    m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 1));
+    m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 2));
+    if (c == 0) wmax[warp * G + g] = m;
+  }
+  __syncthreads();
+  float M = -INFINITY;
+#pragma unroll
+  for (int w = 0; w < W; ++w) M = fmaxf(M, wmax[w * G + g]);
+  {
+    float ps = 0.0f;
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      p[e] = p[e] == -INFINITY ? 0.0f : expf(p[e] - M);
+      ps += p[e];
+    }
+    ps += __shfl_xor_sync(0xffffffffu, ps, 1);
+    ps += __shfl_xor_sync(0xffffffffu, ps, 2);
+    if (c == 0) wsum[warp * G + g] = ps;
+    *reinterpret_cast<float2 *>(sp + g * 64 + 8 * warp + 2 * c) = make_float2(p[0], p[1]);
+  }
+  __syncthreads();
+  // 5. O = P V: warp w, head_dim columns 32w .. 32w + 31 (4 tiles of 8)
+  float o[4][4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.0f;
+  const uint32_t vbase = smem_u32(sm + TL::vt) + (lane & 7) * kTcaStride +
+                         ((lane >> 3) & 1) * 8 * kTcaStride + (32 * warp + (lane >> 4) * 8) * 2;
+#pragma unroll
+  for (int s2 = 0; s2 < 4; ++s2) {
+    const float2 pa = *reinterpret_cast<const float2 *>(sp + g * 64 + 16 * s2 + 2 * c);
+    const float2 pb = *reinterpret_cast<const float2 *>(sp + g * 64 + 16 * s2 + 8 + 2 * c);
+    uint32_t ph[4], pl[4];
+    tca_split(pa.x, pa.y, ph[0], pl[0]);
+    tca_split(pb.x, pb.y, ph[2], pl[2]);
+    ph[1] = ph[3] = pl[1] = pl[3] = 0u;  // rows 8..15: padding
+#pragma unroll
+    for (int jd = 0; jd < 4; jd += 2) {
+      uint32_t b00, b01, b10, b11;
+      tca_ldsm_x4_trans(vbase + s2 * 16 * kTcaStride + jd * 16, b00, b01, b10, b11);
+      mma_bf16_16816(o[jd], ph, b00, b01);
+      mma_bf16_16816(o[jd], pl, b00, b01);
+      mma_bf16_16816(o[jd + 1], ph, b10, b11);
+      mma_bf16_16816(o[jd + 1], pl, b10, b11);
+    }
+  }
+  // 6. this CTA's record per head: (M, L, O[D]) for row g
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const uint32_t d = 32 * warp + 8 * j + 2 * c;
+    rec[g * (D + 2) + 2 + d] = o[j][0];
+    rec[g * (D + 2) + 2 + d + 1] = o[j][1];
+  }
+  if (warp == 0 && c == 0) {
+    float L = 0.0f;
+#pragma unroll
+    for (int w = 0; w < W; ++w) L += wsum[w * G + g];
+    rec[g * (D + 2)] = M;
+    rec[g * (D + 2) + 1] = L;
+  }
+  __syncthreads();
+  attn_cluster_merge<G, D, W>(a, kvh, rec, reinterpret_cast<float *>(sm + TL::fw),
+                              reinterpret_cast<float *>(sm + TL::ls),
+                              reinterpret_cast<float *>(sm + TL::fl), t);
 }
 
 }  // namespace

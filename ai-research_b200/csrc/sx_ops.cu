@@ -331,7 +331,10 @@ __global__ void __launch_bounds__(kFusedWarps * 32) attn_cluster_kernel(AttnFuse
   s.slots += (size_t)z * a.total_slots;
   s.step += 4 * z;
   s.out += (size_t)z * a.out_ld;
-  attn_cluster_item<DPL, G, BF16>(s, blockIdx.x, sh, [] { pdl_wait(); });
+  if constexpr (DPL == 8 && G == 8 && BF16)
+    attn_cluster_item_tc(s, blockIdx.x, sh, [] { pdl_wait(); });  // tensor-core form
+  else
+    attn_cluster_item<DPL, G, BF16>(s, blockIdx.x, sh, [] { pdl_wait(); });
 }
 
 static_assert(kClusterSlots * kClusterMax == (int)kAttnClusterMaxSlots, "cluster ring limit");
@@ -343,7 +346,9 @@ cudaError_t launch_attn_fused_t(const AttnFusedArgs &a, cudaStream_t s, bool pdl
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(a.num_kv, ncl, a.sessions > 1 ? a.sessions : 1);
     cfg.blockDim = dim3(kFusedWarps * 32);
-    cfg.dynamicSmemBytes = sizeof(float) * attn_cluster_floats(G, 32 * DPL, ncl);
+    cfg.dynamicSmemBytes = (DPL == 8 && G == 8 && a.kv_bf16)
+                               ? (size_t)TcaLayout::total
+                               : sizeof(float) * attn_cluster_floats(G, 32 * DPL, ncl);
     cfg.stream = s;
     cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeClusterDimension;

@@ -320,6 +320,7 @@ def bf16_bits(a):
     (8, 1, 256, 64, 1e6, 1 / 16, [99999], [96]),   # BASELINE config 3, every recall slot live
     (8, 1, 256, 64, 1e6, 1 / 16, [99999], [0]),    # config 3, recall tier empty
     (8, 1, 256, 64, 1e6, 1 / 16, [600, 31, 54321], [5, 0, 96]),  # 3 instances in one launch
+    (8, 1, 256, 64, 1e6, 1 / 16, [5, 70], [0, 3]),  # young rings: most CTAs hold no live slot
     (16, 8, 256, 256, 1e4, 1.0, [7000], [40]),     # 12B sliding layer, reference scale 1.0
     (4, 2, 128, 32, 1e4, 0.5, [3], [0]),           # young ring: 4 live slots
 ])
