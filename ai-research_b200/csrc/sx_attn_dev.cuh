@@ -440,11 +440,13 @@ SX_DEV void attn_cluster_merge(const AttnFusedArgs &a, uint32_t kvh, float *rec,
   cl.sync();  // the records stay readable until every CTA of the cluster is done
 }
 
-template <int DPL, int G, bool BF16, typename Wait>
+// CP: ring slots per warp (the CTA owns kFusedWarps * CP slots; the cluster kernel uses
+// kClusterPerWarp, the attention + o kernel fewer for more CTAs per kv head)
+template <int DPL, int G, bool BF16, typename Wait, int CP = kClusterPerWarp>
 SX_DEV void attn_cluster_item(const AttnFusedArgs &a, uint32_t kvh, float *sh, Wait wait) {
   namespace cg = cooperative_groups;
   cg::cluster_group cl = cg::this_cluster();
-  constexpr int W = kFusedWarps, P = kClusterPerWarp;
+  constexpr int W = kFusedWarps, P = CP;
   constexpr uint32_t D = 32 * DPL;
   const uint32_t rank = cl.block_rank(), ncl = cl.num_blocks();
   const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
@@ -465,7 +467,7 @@ SX_DEV void attn_cluster_item(const AttnFusedArgs &a, uint32_t kvh, float *sh, W
   S = S > a.total_slots ? a.total_slots : S;
 
   AttnPre<DPL, BF16, P> R;
-  const uint32_t s0 = rank * kClusterSlots, s1 = min(S, s0 + kClusterSlots);
+  const uint32_t s0 = rank * (W * P), s1 = min(S, s0 + W * P);
   attn_fetch<DPL, BF16, P, W>(a, kvh, s0, s1, slot, warp, lane, R);
   wait();
   if (bad_step && t == 0 && rank == 0 && kvh == 0) raise_error(a.err, kDevBadParams);

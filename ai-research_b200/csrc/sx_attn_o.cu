@@ -37,7 +37,7 @@ SX_HD AoLayout ao_layout(int g, uint32_t d, uint32_t cl, uint32_t o_tiles) {
   return L;
 }
 
-template <int DPL, int G, bool BF16>
+template <int DPL, int G, bool BF16, int CP>
 __global__ void __launch_bounds__(kFusedWarps * 32) attn_o_kernel(AttnOArgs a) {
   extern __shared__ __align__(128) float sh[];
   uint8_t *const smem = reinterpret_cast<uint8_t *>(sh);
@@ -68,7 +68,8 @@ __global__ void __launch_bounds__(kFusedWarps * 32) attn_o_kernel(AttnOArgs a) {
                   GP * CB, bar, pol);
   }
   pdl_launch_dependents();
-  attn_cluster_item<DPL, G, BF16>(a.at, kvh, sh, [] { pdl_wait(); });
+  auto wait = [] { pdl_wait(); };
+  attn_cluster_item<DPL, G, BF16, decltype(wait), CP>(a.at, kvh, sh, wait);
   // every CTA of the cluster wrote its slice of the G x D output before the cluster barrier
   // that ends the work item: read all of it back (through L2) and stage it as B fragments
   float *const xo = reinterpret_cast<float *>(smem + L.xo);
@@ -127,7 +128,9 @@ __global__ void __launch_bounds__(kFusedWarps * 32) attn_o_kernel(AttnOArgs a) {
 
 template <int DPL, int G>
 cudaError_t launch_ao_t(const AttnOArgs &a, cudaStream_t s) {
-  const uint32_t ncl = (a.at.total_slots + kClusterSlots - 1) / kClusterSlots;
+  if (a.cta_slots != 40 && a.cta_slots != 64) return cudaErrorInvalidValue;
+  const uint32_t ncl = (a.at.total_slots + a.cta_slots - 1) / a.cta_slots;
+  if (ncl > (uint32_t)kClusterMax) return cudaErrorInvalidValue;
   const AoLayout L = ao_layout(G, 32 * DPL, ncl, a.o_tiles);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(a.at.num_kv, ncl, 1);
@@ -143,8 +146,11 @@ cudaError_t launch_ao_t(const AttnOArgs &a, cudaStream_t s) {
   attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 2;
-  if (a.at.kv_bf16) return cudaLaunchKernelEx(&cfg, attn_o_kernel<DPL, G, true>, a);
-  return cudaLaunchKernelEx(&cfg, attn_o_kernel<DPL, G, false>, a);
+  if (a.cta_slots == 40)
+    return a.at.kv_bf16 ? cudaLaunchKernelEx(&cfg, attn_o_kernel<DPL, G, true, 5>, a)
+                        : cudaLaunchKernelEx(&cfg, attn_o_kernel<DPL, G, false, 5>, a);
+  return a.at.kv_bf16 ? cudaLaunchKernelEx(&cfg, attn_o_kernel<DPL, G, true, 8>, a)
+                      : cudaLaunchKernelEx(&cfg, attn_o_kernel<DPL, G, false, 8>, a);
 }
 
 template <int DPL>
@@ -160,10 +166,14 @@ cudaError_t launch_ao_d(const AttnOArgs &a, cudaStream_t s) {
 
 template <int DPL>
 cudaError_t prepare_ao_d() {
-  for (auto k : {attn_o_kernel<DPL, 1, true>, attn_o_kernel<DPL, 1, false>,
-                 attn_o_kernel<DPL, 2, true>, attn_o_kernel<DPL, 2, false>,
-                 attn_o_kernel<DPL, 4, true>, attn_o_kernel<DPL, 4, false>,
-                 attn_o_kernel<DPL, 8, true>, attn_o_kernel<DPL, 8, false>}) {
+  for (auto k : {attn_o_kernel<DPL, 1, true, 5>, attn_o_kernel<DPL, 1, false, 5>,
+                 attn_o_kernel<DPL, 2, true, 5>, attn_o_kernel<DPL, 2, false, 5>,
+                 attn_o_kernel<DPL, 4, true, 5>, attn_o_kernel<DPL, 4, false, 5>,
+                 attn_o_kernel<DPL, 8, true, 5>, attn_o_kernel<DPL, 8, false, 5>,
+                 attn_o_kernel<DPL, 1, true, 8>, attn_o_kernel<DPL, 1, false, 8>,
+                 attn_o_kernel<DPL, 2, true, 8>, attn_o_kernel<DPL, 2, false, 8>,
+                 attn_o_kernel<DPL, 4, true, 8>, attn_o_kernel<DPL, 4, false, 8>,
+                 attn_o_kernel<DPL, 8, true, 8>, attn_o_kernel<DPL, 8, false, 8>}) {
     cudaError_t e = allow_max_dynamic_smem(k);
     if (e == cudaSuccess) e = cudaFuncSetAttribute(k, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
     if (e != cudaSuccess) return e;
@@ -174,7 +184,8 @@ cudaError_t prepare_ao_d() {
 }  // namespace
 
 bool attn_o_plan(uint32_t o_rows, uint32_t num_q, uint32_t num_kv, uint32_t head_dim,
-                 uint32_t total_slots, uint32_t smem_limit, uint32_t *o_tiles) {
+                 uint32_t total_slots, uint32_t smem_limit, uint32_t *o_tiles,
+                 uint32_t *cta_slots) {
   if (num_kv == 0 || num_q % num_kv != 0 || num_kv > (uint32_t)kProMaxParts) return false;
   const uint32_t g = num_q / num_kv;
   if (g != 1 && g != 2 && g != 4 && g != 8) return false;
@@ -182,10 +193,14 @@ bool attn_o_plan(uint32_t o_rows, uint32_t num_q, uint32_t num_kv, uint32_t head
   if (o_rows % 16 != 0 || (g * head_dim) % 64 != 0 || total_slots == 0 ||
       total_slots > kAttnClusterMaxSlots)
     return false;
-  const uint32_t ncl = (total_slots + kClusterSlots - 1) / kClusterSlots;
+  // 40 slots per CTA (5 per warp) while the cluster stays within 16 CTAs: more CTAs share
+  // the attention and the o projection's tiles; 64 for longer rings
+  const uint32_t cs = total_slots <= 40u * kClusterMax ? 40u : (uint32_t)kClusterSlots;
+  const uint32_t ncl = (total_slots + cs - 1) / cs;
   const uint32_t tiles = (o_rows / 16 + ncl - 1) / ncl;
   if (ao_layout(g, head_dim, ncl, tiles).total > smem_limit) return false;
   *o_tiles = tiles;
+  *cta_slots = cs;
   return true;
 }
 

@@ -212,9 +212,11 @@ struct AttnOArgs {
   float *opart;       // [num_kv][o_rows]
   uint32_t o_rows;    // hidden size
   uint32_t o_tiles;   // W_o tiles per CTA the shared memory holds (attn_o_plan)
+  uint32_t cta_slots; // ring slots per CTA (attn_o_plan: 40 for rings of up to 640 slots, else 64)
 };
 bool attn_o_plan(uint32_t o_rows, uint32_t num_q, uint32_t num_kv, uint32_t head_dim,
-                 uint32_t total_slots, uint32_t smem_limit, uint32_t *o_tiles);
+                 uint32_t total_slots, uint32_t smem_limit, uint32_t *o_tiles,
+                 uint32_t *cta_slots);
 cudaError_t launch_attn_o(const AttnOArgs &a, cudaStream_t s);
 cudaError_t prepare_attn_o_kernels();
 cudaError_t prepare_attn_block_kernels();

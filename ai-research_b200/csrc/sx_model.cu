@@ -33,7 +33,7 @@ struct LayerBufs {
   // the layer's attention block as one kernel (sx_attn_block.cu); ctas == 0: not eligible
   sx::AttnBlockPlan ab{};
   // the cluster attention with the o projection folded in (sx_attn_o.cu); 0: not eligible
-  uint32_t ao_tiles = 0;
+  uint32_t ao_tiles = 0, ao_slots = 0;
 };
 
 enum Tensor : uint32_t {
@@ -189,7 +189,7 @@ sx_status alloc_model(sx_model *m) {
     for (uint32_t l = 0; l < c.num_layers; ++l) {
       LayerBufs &B = m->L[l];
       if (!sx::attn_o_plan(H, m->nq, B.num_kv, B.head_dim, m->total_slots,
-                           sx::kAttnBlockSmemLimit, &B.ao_tiles))
+                           sx::kAttnBlockSmemLimit, &B.ao_tiles, &B.ao_slots))
         B.ao_tiles = 0;
       if (B.ao_tiles && (uint64_t)B.num_kv * H > opart) opart = (uint64_t)B.num_kv * H;
     }
@@ -580,6 +580,7 @@ sx_status record_forward_fused(sx_model *m, sx_cmd *cmd, bool logits, bool io,
       op.ao.opart = (float *)m->ab_opart->d;
       op.ao.o_rows = H;
       op.ao.o_tiles = B.ao_tiles;
+      op.ao.cta_slots = B.ao_slots;
       op.attn_rot = B.rot;
       op.attn_theta = B.theta;
       sx_host_push_op(cmd, op);
